@@ -1,0 +1,162 @@
+/*
+ * nvfp4moe.h -- C ABI of the B200 (sm_100a) NVFP4 MoE library
+ * (libnvfp4moe.so).
+ *
+ * This is the drop-in boundary for the hot path of Layr-Labs/mlxfast-challenge:
+ * the NVFP4 (E2M1 codes, E4M3 group-16 scales) quantized matmuls that carry
+ * Laguna XS 2.1's sparse MoE blocks, plus the BF16 router that feeds them.
+ * Each entry point replaces one operator of the reference's mlx-c surface
+ * (Vendor/mlx-swift/Source/Cmlx/mlx-c/mlx/c/ops.h) for mode "nvfp4",
+ * group_size 16, bits 4, transpose true, or one layer of its Laguna model.
+ *
+ * Conventions
+ *   - Every tensor argument is a DEVICE pointer to row-major, contiguous
+ *     memory.  Packed weights are the reference's own layout: uint32 words of
+ *     8 E2M1 codes (low nibble first) [..., N, K/8] and uint8 E4M3 scales
+ *     [..., N, K/16].  Activations are bf16 (NVFP4_BF16), f16 or f32; outputs
+ *     take the activation dtype (ops.cpp:4568-4572).
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream) and is asynchronous, as MLX evaluation is stream-ordered.
+ *   - Return 0 on success.  On failure nothing is enqueued, a non-zero status
+ *     is returned and nvfp4_last_error() (per calling thread) holds a message
+ *     in the reference's "[op] ..." style (mlx-c returns 1 and routes the
+ *     message to its error handler, mlx-c/mlx/c/error.h:15-33; the handler
+ *     hook is mirrored by nvfp4_set_error_handler).
+ *   - Shape checks follow the reference's validation (ops.cpp:67-175,
+ *     :4549-4600, :5338-5433).  Indices live on the device, so they are
+ *     range-checked on the device: an out-of-range expert or x index skips its
+ *     work and latches NVFP4_ERR_DEVICE_INDEX, read by nvfp4_device_status().
+ *   - No entry point allocates device memory; the MoE block takes a caller
+ *     workspace sized by moe_block_workspace_size().
+ *   - There is no CPU fallback: without a CUDA device every call fails.
+ */
+#ifndef NVFP4MOE_H
+#define NVFP4MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NVFP4MOE_API __attribute__((visibility("default")))
+
+/* Status codes. */
+enum {
+  NVFP4_OK = 0,
+  NVFP4_ERR_INVALID = 1,      /* bad shape / dtype / argument (as mlx-c's 1) */
+  NVFP4_ERR_UNSUPPORTED = 2,  /* valid for the reference, not provided here */
+  NVFP4_ERR_CUDA = 3,         /* CUDA runtime error */
+  NVFP4_ERR_WORKSPACE = 4,    /* workspace missing or too small */
+  NVFP4_ERR_DEVICE_INDEX = 5  /* latched by kernels: index out of range */
+};
+
+/* Activation / output dtypes. */
+enum { NVFP4_BF16 = 0, NVFP4_F16 = 1, NVFP4_F32 = 2 };
+
+typedef void* nvfp4_stream; /* cudaStream_t */
+
+NVFP4MOE_API const char* nvfp4_last_error(void);
+/* mlx_set_error_handler (mlx-c/mlx/c/error.h:15-33): called with the message
+ * and `data` on every failure; NULL restores the default (no callback). */
+typedef void (*nvfp4_error_handler)(const char* msg, void* data);
+NVFP4MOE_API void nvfp4_set_error_handler(nvfp4_error_handler handler, void* data);
+NVFP4MOE_API int nvfp4_version(void);
+/* Synchronises the device, returns and clears the latched device status
+ * (NVFP4_OK or NVFP4_ERR_DEVICE_INDEX). */
+NVFP4MOE_API int nvfp4_device_status(void);
+
+/* mlx_dequantize (mlx-c ops.h:359; ops.cpp:5120-5241 fp_dequantize), mode
+ * "nvfp4": out[rows, K] = LUT[code] * e4m3(scale).  Bit-exact. */
+NVFP4MOE_API int nvfp4_dequantize(void* out, int out_dtype, const uint32_t* w,
+                                  const uint8_t* scales, int64_t rows, int64_t K,
+                                  nvfp4_stream stream);
+
+/* mlx_quantize (mlx-c ops.h:801-808; ops.cpp:4873-4978 fp_quantize), mode
+ * "nvfp4", group 16, no global scale: w[rows, K] (bf16/f16/f32) ->
+ * wq[rows, K/8] uint32 + scales[rows, K/16] uint8, bit-identical to the
+ * reference's CPU evaluation. */
+NVFP4MOE_API int nvfp4_quantize(uint32_t* wq, uint8_t* scales, const void* w, int w_dtype,
+                                int64_t rows, int64_t K, nvfp4_stream stream);
+
+/* mlx_quantized_matmul (mlx-c ops.h:809-818; ops.cpp:4549-4600;
+ * QuantizedMatmul::eval_cpu backend/cpu/quantized.cpp:924-964), transpose:
+ * y[M, N] = x[M, K] @ dequant(w)[N, K]^T. */
+NVFP4MOE_API int nvfp4_quantized_matmul(void* y, const void* x, int dtype, const uint32_t* w,
+                                        const uint8_t* scales, int64_t M, int64_t N, int64_t K,
+                                        nvfp4_stream stream);
+
+/* mlx_gather_qmm (mlx-c ops.h:475-488; ops.cpp:5338-5433; GatherQMM::eval_cpu
+ * backend/cpu/quantized.cpp:966-1047), transpose, lhs/rhs already broadcast
+ * to `pairs` entries:
+ *   out[p] (M x N) = x[lhs[p]] (M x K) @ dequant(w[rhs[p]])^T
+ * x is [n_x_batches, M, K]; w is [n_experts, N, K/8]; out is [pairs, M, N].
+ * lhs_indices NULL means lhs[p] = p (indices_or_default, ops.cpp:67-81);
+ * rhs_indices NULL means expert 0 for every pair.  sorted_indices is the
+ * reference's performance hint; results never depend on it. */
+NVFP4MOE_API int nvfp4_gather_qmm(void* out, const void* x, int dtype, const uint32_t* w,
+                                  const uint8_t* scales, const uint32_t* lhs_indices,
+                                  const uint32_t* rhs_indices, int64_t pairs,
+                                  int64_t n_x_batches, int64_t n_experts, int64_t M, int64_t N,
+                                  int64_t K, int sorted_indices, nvfp4_stream stream);
+
+/* LagunaMoEGate (VLM/MLXLLM/Models/Laguna.swift:149-181): logits = x @ G^T
+ * (bf16 G [E, H]), sigmoid, + e_score_correction_bias for the choice, top-k
+ * (ties to the lower id), weights = sigmoid scores of the chosen experts,
+ * renormalised when norm_topk_prob.  inds [T, k] uint32, weights [T, k] f32.
+ * Needs moe_router_workspace_size() bytes of workspace, zeroed once before
+ * first use (moe_workspace_init); the kernels leave it reusable. */
+NVFP4MOE_API size_t moe_router_workspace_size(int64_t T, int64_t H, int64_t E);
+NVFP4MOE_API int moe_router_topk(uint32_t* inds, float* weights, const void* x, int dtype,
+                                 const uint16_t* gate_w_bf16, const float* bias, int64_t T,
+                                 int64_t H, int64_t E, int k, int norm_topk_prob,
+                                 void* workspace, size_t workspace_bytes, nvfp4_stream stream);
+
+/* One NVFP4 bank: packed codes and scales of [n_experts, rows, K]. */
+typedef struct {
+  const uint32_t* w;
+  const uint8_t* scales;
+} nvfp4_bank;
+
+/* One Laguna sparse MoE layer (LagunaSparseMoeBlock, Laguna.swift:183-213;
+ * runtime LagunaRuntimeSparseMoEBlock, Sources/MLXFastModel/
+ * LagunaRuntimeModel.swift:10498-11002).  Routed banks: gate/up [E, I, H/8],
+ * down [E, H, I/8].  Shared expert banks (LagunaMLP, Laguna.swift:126-145):
+ * gate/up [Is, H/8], down [H, Is/8]; set shared_inter = 0 to omit it. */
+typedef struct {
+  int64_t hidden;        /* H (hidden_size) */
+  int64_t inter;         /* I (moe_intermediate_size) */
+  int64_t n_experts;     /* E (num_experts) */
+  int64_t top_k;         /* k (num_experts_per_tok) */
+  int64_t shared_inter;  /* Is (shared_expert_intermediate_size) or 0 */
+  float routed_scaling;  /* moe_routed_scaling_factor */
+  int norm_topk_prob;
+  const uint16_t* router_w; /* bf16 [E, H] (mlp.gate.weight) */
+  const float* router_bias; /* f32 [E] (e_score_correction_bias) or NULL */
+  nvfp4_bank gate, up, down;
+  nvfp4_bank shared_gate, shared_up, shared_down;
+} moe_layer_desc;
+
+NVFP4MOE_API size_t moe_block_workspace_size(const moe_layer_desc* layer, int64_t T);
+/* Zero a workspace once after allocating it (enqueued on `stream`). */
+NVFP4MOE_API int moe_workspace_init(void* workspace, size_t bytes, nvfp4_stream stream);
+
+/* Sparse MoE block forward:
+ *   y = routed_scaling * sum_j w_j * down_e(silu(gate_e x) * up_e x)
+ *       + shared_down(silu(shared_gate x) * shared_up x) (+ residual)
+ * x, y, residual [T, H] in `dtype`.  When inds_in is NULL the router runs
+ * first (router_w required); otherwise inds_in [T, k] / weights_in [T, k]
+ * are used as given.  inds_out / weights_out (nullable) receive the routing
+ * that was used. */
+NVFP4MOE_API int moe_block_forward(void* y, const void* x, const void* residual, int dtype,
+                                   int64_t T, const moe_layer_desc* layer,
+                                   const uint32_t* inds_in, const float* weights_in,
+                                   uint32_t* inds_out, float* weights_out, void* workspace,
+                                   size_t workspace_bytes, nvfp4_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4MOE_H */

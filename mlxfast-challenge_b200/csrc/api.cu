@@ -1,0 +1,389 @@
+// api.cu -- the C ABI (include/nvfp4moe.h): argument validation in the
+// reference's terms, error reporting, workspace layout and kernel dispatch.
+// No entry point allocates device memory or falls back to the CPU.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/nvfp4moe.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string t_last_error;
+nvfp4_error_handler g_handler = nullptr;
+void* g_handler_data = nullptr;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  if (g_handler) g_handler(buf, g_handler_data);
+  return code;
+}
+
+int check_cuda(cudaError_t e, const char* op) {
+  if (e == cudaSuccess) return NVFP4_OK;
+  return fail(NVFP4_ERR_CUDA, "[%s] CUDA error: %s", op, cudaGetErrorString(e));
+}
+
+bool valid_dtype(int d) { return d == NVFP4_BF16 || d == NVFP4_F16 || d == NVFP4_F32; }
+
+// validate_quantized_input / extract_quantized_matmul_dims (ops.cpp:84-175)
+// for nvfp4, transpose=true: K must be a whole number of 16-element groups.
+int check_qdims(const char* op, int64_t N, int64_t K) {
+  if (K <= 0 || N < 0)
+    return fail(NVFP4_ERR_INVALID, "[%s] Invalid shape: N=%lld K=%lld.", op, (long long)N,
+                (long long)K);
+  if (K % 16 != 0)
+    return fail(NVFP4_ERR_INVALID,
+                "[%s] The last dimension of the matrix needs to be divisible by the "
+                "quantization group size 16. However the provided matrix has K=%lld.",
+                op, (long long)K);
+  return NVFP4_OK;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+struct RouterLayout {
+  size_t counters_off, partial_off, total;
+  int ksplit;
+};
+
+RouterLayout router_layout(int64_t T, int64_t H, int64_t E) {
+  RouterLayout L;
+  L.ksplit = nvfp4::router_ksplit(H);
+  const int64_t groups = (T + 7) / 8;
+  L.counters_off = 0;
+  L.partial_off = align_up((size_t)groups * sizeof(unsigned), 256);
+  L.total = L.partial_off + (size_t)groups * std::max(L.ksplit, 1) * 8 * E * sizeof(float);
+  L.total = align_up(L.total, 256);
+  return L;
+}
+
+struct BlockLayout {
+  RouterLayout router;
+  size_t inds_off, wts_off, act_off, total;
+  int64_t act_ld;
+  int kk;
+};
+
+BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
+  BlockLayout B;
+  B.router = router_layout(T, L->hidden, L->n_experts);
+  B.kk = (int)L->top_k + (L->shared_inter > 0 ? 1 : 0);
+  B.act_ld = align_up((size_t)std::max(L->inter, L->shared_inter), 64);
+  B.inds_off = B.router.total;
+  B.wts_off = align_up(B.inds_off + (size_t)T * L->top_k * sizeof(uint32_t), 256);
+  B.act_off = align_up(B.wts_off + (size_t)T * L->top_k * sizeof(float), 256);
+  B.total = align_up(B.act_off + (size_t)T * B.kk * B.act_ld * sizeof(float), 256);
+  return B;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* nvfp4_last_error(void) { return t_last_error.c_str(); }
+
+void nvfp4_set_error_handler(nvfp4_error_handler handler, void* data) {
+  g_handler = handler;
+  g_handler_data = data;
+}
+
+int nvfp4_version(void) { return 1; }
+
+int nvfp4_device_status(void) {
+  int st = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return check_cuda(e, "device_status");
+  e = nvfp4::read_and_clear_device_error(&st);
+  if (e != cudaSuccess) return check_cuda(e, "device_status");
+  if (st != 0)
+    return fail(NVFP4_ERR_DEVICE_INDEX,
+                "[gather_qmm] an expert or batch index was out of range (kernel site %d); "
+                "the affected outputs were not written.",
+                st);
+  return NVFP4_OK;
+}
+
+int nvfp4_dequantize(void* out, int out_dtype, const uint32_t* w, const uint8_t* scales,
+                     int64_t rows, int64_t K, nvfp4_stream stream) {
+  if (!valid_dtype(out_dtype))
+    return fail(NVFP4_ERR_INVALID, "[dequantize] Only real floating types are supported.");
+  if (int r = check_qdims("dequantize", rows, K)) return r;
+  if (rows > 0 && (!out || !w || !scales))
+    return fail(NVFP4_ERR_INVALID, "[dequantize] null pointer argument.");
+  return check_cuda(nvfp4::launch_dequantize(out, out_dtype, reinterpret_cast<const uint8_t*>(w),
+                                             scales, rows, K, (cudaStream_t)stream),
+                    "dequantize");
+}
+
+int nvfp4_quantize(uint32_t* wq, uint8_t* scales, const void* w, int w_dtype, int64_t rows,
+                   int64_t K, nvfp4_stream stream) {
+  if (!valid_dtype(w_dtype))
+    return fail(NVFP4_ERR_INVALID,
+                "[quantize] Only real floating types can be quantized.");
+  if (int r = check_qdims("quantize", rows, K)) return r;
+  if (rows > 0 && (!wq || !scales || !w))
+    return fail(NVFP4_ERR_INVALID, "[quantize] null pointer argument.");
+  if ((reinterpret_cast<uintptr_t>(wq) & 7) != 0)
+    return fail(NVFP4_ERR_INVALID, "[quantize] wq must be 8-byte aligned.");
+  return check_cuda(nvfp4::launch_quantize(reinterpret_cast<uint8_t*>(wq), scales, w, w_dtype,
+                                           rows, K, (cudaStream_t)stream),
+                    "quantize");
+}
+
+int nvfp4_gather_qmm(void* out, const void* x, int dtype, const uint32_t* w,
+                     const uint8_t* scales, const uint32_t* lhs_indices,
+                     const uint32_t* rhs_indices, int64_t pairs, int64_t n_x_batches,
+                     int64_t n_experts, int64_t M, int64_t N, int64_t K, int sorted_indices,
+                     nvfp4_stream stream) {
+  (void)sorted_indices;
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID, "[gather_qmm] Only real floating types are supported.");
+  if (int r = check_qdims("gather_qmm", N, K)) return r;
+  if (pairs < 0 || M < 0 || n_x_batches < 0 || n_experts <= 0)
+    return fail(NVFP4_ERR_INVALID, "[gather_qmm] Invalid batch sizes.");
+  if (pairs > 0x7fffffff / 8 || M > 0x7fffffff)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[gather_qmm] too many pairs.");
+  if (pairs == 0 || M == 0 || N == 0) return NVFP4_OK;
+  if (!out || !x || !w || !scales)
+    return fail(NVFP4_ERR_INVALID, "[gather_qmm] null pointer argument.");
+  if (!lhs_indices && n_x_batches < pairs)
+    return fail(NVFP4_ERR_INVALID,
+                "[gather_qmm] without lhs_indices x must hold one batch per pair.");
+  nvfp4::QmmArgs a{};
+  a.out = out;
+  a.x = x;
+  a.w = reinterpret_cast<const uint8_t*>(w);
+  a.s = scales;
+  a.lhs = lhs_indices;
+  a.rhs = rhs_indices;
+  a.P = pairs;
+  a.N = N;
+  a.K = K;
+  a.M = (int)M;
+  a.mchunks = (int)((M + 7) / 8);
+  a.dtype = dtype;
+  a.w_stride = N * (K / 2);
+  a.s_stride = N * (K / 16);
+  a.n_x_batches = n_x_batches;
+  a.n_experts = n_experts;
+  if ((int64_t)a.P * a.mchunks > 65535 * 1024LL)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[gather_qmm] too many pairs.");
+  return check_cuda(nvfp4::launch_qmm_gather(a, (cudaStream_t)stream), "gather_qmm");
+}
+
+int nvfp4_quantized_matmul(void* y, const void* x, int dtype, const uint32_t* w,
+                           const uint8_t* scales, int64_t M, int64_t N, int64_t K,
+                           nvfp4_stream stream) {
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID,
+                "[quantized_matmul] Only real floating types are supported.");
+  if (int r = check_qdims("quantized_matmul", N, K)) return r;
+  if (M < 0) return fail(NVFP4_ERR_INVALID, "[quantized_matmul] Invalid M.");
+  // One "pair" whose M rows are the whole activation matrix.
+  return nvfp4_gather_qmm(y, x, dtype, w, scales, nullptr, nullptr, 1, 1, 1, M, N, K, 0,
+                          stream);
+}
+
+size_t moe_router_workspace_size(int64_t T, int64_t H, int64_t E) {
+  return router_layout(T, H, E).total;
+}
+
+static int router_checks(const char* op, int64_t T, int64_t H, int64_t E, int k,
+                         const void* x, const void* G) {
+  if (T < 0 || H <= 0 || E <= 0) return fail(NVFP4_ERR_INVALID, "[%s] Invalid shape.", op);
+  if (k <= 0 || k > E || k > 32)
+    return fail(NVFP4_ERR_INVALID, "[%s] top_k must be in [1, min(E, 32)].", op);
+  if (E > 512) return fail(NVFP4_ERR_UNSUPPORTED, "[%s] at most 512 experts.", op);
+  if (nvfp4::router_ksplit(H) == 0 || H % 8 != 0)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] hidden size must be a multiple of 128.", op);
+  if (T > 0 && (!x || !G)) return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  if (G && !aligned16(G))
+    return fail(NVFP4_ERR_INVALID, "[%s] router weight must be 16-byte aligned.", op);
+  return NVFP4_OK;
+}
+
+int moe_router_topk(uint32_t* inds, float* weights, const void* x, int dtype,
+                    const uint16_t* gate_w_bf16, const float* bias, int64_t T, int64_t H,
+                    int64_t E, int k, int norm_topk_prob, void* workspace,
+                    size_t workspace_bytes, nvfp4_stream stream) {
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID, "[router] Only real floating types are supported.");
+  if (int r = router_checks("router", T, H, E, k, x, gate_w_bf16)) return r;
+  if (T == 0) return NVFP4_OK;
+  if (!inds || !weights) return fail(NVFP4_ERR_INVALID, "[router] null output pointer.");
+  const RouterLayout L = router_layout(T, H, E);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(NVFP4_ERR_WORKSPACE, "[router] workspace of %zu bytes required.", L.total);
+  nvfp4::RouterArgs a{};
+  a.x = x;
+  a.dtype = dtype;
+  a.G = gate_w_bf16;
+  a.bias = bias;
+  a.T = T;
+  a.H = H;
+  a.E = E;
+  a.k = k;
+  a.norm = norm_topk_prob;
+  a.ksplit = L.ksplit;
+  a.counters = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + L.counters_off);
+  a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + L.partial_off);
+  a.inds = inds;
+  a.wts = weights;
+  return check_cuda(nvfp4::launch_router(a, (cudaStream_t)stream), "router");
+}
+
+size_t moe_block_workspace_size(const moe_layer_desc* layer, int64_t T) {
+  if (!layer || T < 0) return 0;
+  return block_layout(layer, T).total;
+}
+
+int moe_workspace_init(void* workspace, size_t bytes, nvfp4_stream stream) {
+  if (!workspace && bytes) return fail(NVFP4_ERR_INVALID, "[workspace] null pointer.");
+  return check_cuda(cudaMemsetAsync(workspace, 0, bytes, (cudaStream_t)stream), "workspace");
+}
+
+int moe_block_forward(void* y, const void* x, const void* residual, int dtype, int64_t T,
+                      const moe_layer_desc* L, const uint32_t* inds_in, const float* weights_in,
+                      uint32_t* inds_out, float* weights_out, void* workspace,
+                      size_t workspace_bytes, nvfp4_stream stream) {
+  const char* op = "moe_block";
+  if (!L) return fail(NVFP4_ERR_INVALID, "[%s] null layer descriptor.", op);
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID, "[%s] Only real floating types are supported.", op);
+  const int64_t H = L->hidden, I = L->inter, E = L->n_experts, Is = L->shared_inter;
+  const int k = (int)L->top_k;
+  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || Is < 0 || k <= 0 || k > E)
+    return fail(NVFP4_ERR_INVALID, "[%s] Invalid layer shape.", op);
+  if (H % 128 || I % 128 || Is % 128)
+    return fail(NVFP4_ERR_UNSUPPORTED,
+                "[%s] hidden and intermediate sizes must be multiples of 128 "
+                "(use nvfp4_gather_qmm for other shapes).",
+                op);
+  if (T == 0) return NVFP4_OK;
+  if (!y || !x) return fail(NVFP4_ERR_INVALID, "[%s] null activation pointer.", op);
+  const nvfp4_bank* banks[3] = {&L->gate, &L->up, &L->down};
+  for (const nvfp4_bank* b : banks)
+    if (!b->w || !b->scales || !aligned16(b->w))
+      return fail(NVFP4_ERR_INVALID, "[%s] routed banks need 16-byte aligned codes.", op);
+  if (Is > 0) {
+    const nvfp4_bank* sb[3] = {&L->shared_gate, &L->shared_up, &L->shared_down};
+    for (const nvfp4_bank* b : sb)
+      if (!b->w || !b->scales || !aligned16(b->w))
+        return fail(NVFP4_ERR_INVALID, "[%s] shared banks need 16-byte aligned codes.", op);
+  }
+  if (!inds_in && !L->router_w)
+    return fail(NVFP4_ERR_INVALID, "[%s] either inds_in or router_w is required.", op);
+  if (inds_in && !weights_in)
+    return fail(NVFP4_ERR_INVALID, "[%s] weights_in is required with inds_in.", op);
+  const BlockLayout B = block_layout(L, T);
+  if (!workspace || workspace_bytes < B.total)
+    return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, B.total);
+  const size_t down_smem = nvfp4::down_smem_bytes(std::max(I, Is), B.kk);
+  if (down_smem > 220 * 1024)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] top_k * intermediate too large.", op);
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t s = (cudaStream_t)stream;
+
+  const uint32_t* inds = inds_in;
+  const float* wts = weights_in;
+  if (!inds_in) {
+    if (int r = router_checks(op, T, H, E, k, x, L->router_w)) return r;
+    uint32_t* ri = inds_out ? inds_out : reinterpret_cast<uint32_t*>(ws + B.inds_off);
+    float* rw = weights_out ? weights_out : reinterpret_cast<float*>(ws + B.wts_off);
+    nvfp4::RouterArgs ra{};
+    ra.x = x;
+    ra.dtype = dtype;
+    ra.G = L->router_w;
+    ra.bias = L->router_bias;
+    ra.T = T;
+    ra.H = H;
+    ra.E = E;
+    ra.k = k;
+    ra.norm = L->norm_topk_prob;
+    ra.ksplit = B.router.ksplit;
+    ra.counters = reinterpret_cast<unsigned*>(ws + B.router.counters_off);
+    ra.partial = reinterpret_cast<float*>(ws + B.router.partial_off);
+    ra.inds = ri;
+    ra.wts = rw;
+    if (int r = check_cuda(nvfp4::launch_router(ra, s), op)) return r;
+    inds = ri;
+    wts = rw;
+  } else if (inds_out || weights_out) {
+    if (inds_out &&
+        cudaMemcpyAsync(inds_out, inds_in, T * k * sizeof(uint32_t), cudaMemcpyDeviceToDevice,
+                        s) != cudaSuccess)
+      return check_cuda(cudaGetLastError(), op);
+    if (weights_out &&
+        cudaMemcpyAsync(weights_out, weights_in, T * k * sizeof(float), cudaMemcpyDeviceToDevice,
+                        s) != cudaSuccess)
+      return check_cuda(cudaGetLastError(), op);
+  }
+  float* act = reinterpret_cast<float*>(ws + B.act_off);
+
+  nvfp4::GateUpArgs ga{};
+  ga.x = x;
+  ga.dtype = dtype;
+  ga.T = T;
+  ga.H = H;
+  ga.I = I;
+  ga.Is = Is;
+  ga.E = E;
+  ga.k = k;
+  ga.kk = B.kk;
+  ga.inds = inds;
+  ga.gw = reinterpret_cast<const uint8_t*>(L->gate.w);
+  ga.gs = L->gate.scales;
+  ga.uw = reinterpret_cast<const uint8_t*>(L->up.w);
+  ga.us = L->up.scales;
+  ga.w_stride = I * (H / 2);
+  ga.s_stride = I * (H / 16);
+  if (Is > 0) {
+    ga.sgw = reinterpret_cast<const uint8_t*>(L->shared_gate.w);
+    ga.sgs = L->shared_gate.scales;
+    ga.suw = reinterpret_cast<const uint8_t*>(L->shared_up.w);
+    ga.sus = L->shared_up.scales;
+  }
+  ga.act = act;
+  ga.act_ld = B.act_ld;
+  if (int r = check_cuda(nvfp4::launch_moe_gateup(ga, s), op)) return r;
+
+  nvfp4::DownArgs da{};
+  da.act = act;
+  da.act_ld = B.act_ld;
+  da.T = T;
+  da.H = H;
+  da.I = I;
+  da.Is = Is;
+  da.E = E;
+  da.k = k;
+  da.kk = B.kk;
+  da.Ipad = (int)std::max(I, Is);
+  da.inds = inds;
+  da.wts = wts;
+  da.scaling = L->routed_scaling;
+  da.dw = reinterpret_cast<const uint8_t*>(L->down.w);
+  da.ds = L->down.scales;
+  da.w_stride = H * (I / 2);
+  da.s_stride = H * (I / 16);
+  if (Is > 0) {
+    da.sdw = reinterpret_cast<const uint8_t*>(L->shared_down.w);
+    da.sds = L->shared_down.scales;
+  }
+  da.residual = residual;
+  da.y = y;
+  da.dtype = dtype;
+  return check_cuda(nvfp4::launch_moe_down(da, s), op);
+}
+
+}  // extern "C"

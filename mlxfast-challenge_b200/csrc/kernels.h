@@ -1,0 +1,83 @@
+// kernels.h -- argument blocks and host launchers of the CUDA kernels.  Only
+// the C ABI (api.cu) includes this; nothing here crosses the library boundary.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace nvfp4 {
+
+// Gather QMM: out[p*M + m][n] = x[lhs[p]*M + m] . dequant(W[rhs[p]])[n].
+struct QmmArgs {
+  void* out;
+  const void* x;
+  const uint8_t* w;    // [E, N, K/2] bytes
+  const uint8_t* s;    // [E, N, K/16]
+  const uint32_t* lhs;  // [P] or null (identity)
+  const uint32_t* rhs;  // [P] or null (expert 0)
+  int64_t P, N, K;
+  int M, mchunks, dtype;
+  int64_t w_stride, s_stride;  // bytes per expert
+  int64_t n_x_batches, n_experts;
+};
+
+struct GateUpArgs {
+  const void* x;  // [T, H]
+  int dtype;
+  int64_t T, H, I, Is, E;
+  int k, kk;
+  const uint32_t* inds;  // [T, k]
+  const uint8_t *gw, *gs, *uw, *us;  // routed banks
+  int64_t w_stride, s_stride;
+  const uint8_t *sgw, *sgs, *suw, *sus;  // shared expert (null when absent)
+  float* act;  // [T*kk, act_ld]
+  int64_t act_ld;
+};
+
+struct DownArgs {
+  const float* act;
+  int64_t act_ld;
+  int64_t T, H, I, Is, E;
+  int k, kk, Ipad;
+  const uint32_t* inds;
+  const float* wts;
+  float scaling;
+  const uint8_t *dw, *ds;
+  int64_t w_stride, s_stride;
+  const uint8_t *sdw, *sds;
+  const void* residual;
+  void* y;
+  int dtype;
+};
+
+struct RouterArgs {
+  const void* x;  // [T, H]
+  int dtype;
+  const uint16_t* G;  // bf16 [E, H]
+  const float* bias;  // [E] or null
+  int64_t T, H, E;
+  int k, norm, ksplit;
+  float* partial;       // [ceil(T/8), ksplit, 8, E]
+  unsigned* counters;   // [ceil(T/8)], zero on entry, left zero on exit
+  uint32_t* inds;       // [T, k]
+  float* wts;           // [T, k]
+};
+
+size_t qmm_smem_bytes(int64_t K);
+bool qmm_fast_path_ok(const QmmArgs& a);
+cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream);
+size_t gateup_smem_bytes(int64_t H);
+cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream);
+size_t down_smem_bytes(int64_t Ipad, int kk);
+cudaError_t launch_moe_down(const DownArgs& a, cudaStream_t stream);
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t stream);
+int router_ksplit(int64_t H);
+cudaError_t launch_dequantize(void* out, int dtype, const uint8_t* w, const uint8_t* s,
+                              int64_t rows, int64_t K, cudaStream_t stream);
+cudaError_t launch_quantize(uint8_t* wq, uint8_t* sq, const void* w, int dtype, int64_t rows,
+                            int64_t K, cudaStream_t stream);
+cudaError_t read_and_clear_device_error(int* out);
+
+}  // namespace nvfp4

@@ -1,0 +1,107 @@
+"""The C-ABI library loads without a GPU, exports every symbol include/*.h
+declares, and rejects invalid arguments on the host before touching CUDA."""
+import ctypes
+import glob
+import importlib
+import os
+import re
+
+import pytest
+
+from conftest import PKG, ROOT
+
+
+def declared_symbols():
+    names = []
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        names += re.findall(r"NVFP4MOE_API\s+[\w\s\*]+?\b(\w+)\s*\(", src)
+    return sorted(set(names))
+
+
+def test_header_declares_the_boundary():
+    names = declared_symbols()
+    for n in ("nvfp4_gather_qmm", "nvfp4_quantized_matmul", "nvfp4_quantize", "nvfp4_dequantize",
+              "moe_router_topk", "moe_block_forward", "nvfp4_last_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(nv):
+    L = ctypes.CDLL(nv.library_path())
+    for n in declared_symbols():
+        assert hasattr(L, n), n
+
+
+def test_python_binding_covers_every_declared_symbol(nv):
+    lib_mod = importlib.import_module(PKG + "._lib")
+    assert set(declared_symbols()) == set(lib_mod.SIGNATURES)
+
+
+def _last(L):
+    return L.nvfp4_last_error().decode()
+
+
+def test_invalid_group_shape_rejected_on_host(nv):
+    L = nv._lib.lib()
+    # K = 40 is not a multiple of the group size 16.
+    st = L.nvfp4_gather_qmm(None, None, 0, None, None, None, None, 1, 1, 1, 1, 8, 40, 0, None)
+    assert st == nv._lib.NVFP4_ERR_INVALID
+    assert "[gather_qmm]" in _last(L) and "group size 16" in _last(L)
+
+
+def test_bad_dtype_rejected(nv):
+    L = nv._lib.lib()
+    assert L.nvfp4_quantized_matmul(None, None, 7, None, None, 1, 16, 16, None) == 1
+    assert "floating" in _last(L)
+
+
+def test_empty_problem_is_a_no_op(nv):
+    L = nv._lib.lib()
+    assert L.nvfp4_gather_qmm(None, None, 0, None, None, None, None, 0, 0, 1, 1, 16, 32, 0,
+                              None) == 0
+
+
+def test_workspace_too_small_rejected(nv):
+    L = nv._lib.lib()
+    st = L.moe_router_topk(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 0,
+                           ctypes.c_void_p(16), None, 4, 2048, 256, 8, 1, ctypes.c_void_p(16), 8,
+                           None)
+    assert st == nv._lib.NVFP4_ERR_WORKSPACE
+    assert L.moe_router_workspace_size(4, 2048, 256) > 8
+
+
+def test_error_handler_called(nv):
+    L = nv._lib.lib()
+    seen = []
+    CB = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.c_void_p)
+    cb = CB(lambda msg, data: seen.append(msg.decode()))
+    L.nvfp4_set_error_handler(ctypes.cast(cb, ctypes.c_void_p), None)
+    try:
+        L.nvfp4_dequantize(None, 9, None, None, 1, 16, None)
+    finally:
+        L.nvfp4_set_error_handler(None, None)
+    assert seen and "[dequantize]" in seen[0]
+
+
+def test_moe_block_rejects_unaligned_shapes(nv):
+    d = nv.MoeLayerDesc()
+    d.hidden, d.inter, d.n_experts, d.top_k = 2000, 512, 256, 8
+    L = nv._lib.lib()
+    st = L.moe_block_forward(ctypes.c_void_p(16), ctypes.c_void_p(16), None, 0, 1,
+                             ctypes.byref(d), None, None, None, None, None, 0, None)
+    assert st == nv._lib.NVFP4_ERR_UNSUPPORTED
+
+
+def test_host_mirror_errors_match_reference_kinds(nv):
+    import torch
+    w = torch.zeros(4, 32)
+    with pytest.raises(ValueError, match="group size 16"):
+        nv.quantize(w, group_size=64)
+    with pytest.raises(ValueError, match="bits to be 4"):
+        nv.quantize(w, bits=3)
+    with pytest.raises(NotImplementedError):
+        nv.quantize(w, mode="affine")
+    with pytest.raises(ValueError, match="Biases must be null"):
+        nv.gather_qmm(w, w, w, biases=w, rhs_indices=torch.zeros(1, dtype=torch.int32))
+    with pytest.raises(ValueError, match="CUDA device"):
+        nv.quantize(w)  # no CPU path
