@@ -1,0 +1,346 @@
+#!/usr/bin/env python
+"""Benchmark of the NVFP4 MoE decode hot path (Laguna XS 2.1 sparse layers).
+
+Workload (the configuration the metric is quoted on): one
+routed-MoE expert layer at decode, T=1 -- 256 experts, top-8 with given
+distinct uniform expert picks and softmax(N(0,1)) routing weights, SwiGLU
+gate/up [512, 2048] and down [2048, 512] NVFP4 group-16, weights quantized
+from bf16 N(0, 0.02), x bf16 N(0, 1).  A "step" runs that layer for each of
+the model's 39 sparse layers back to back (distinct weights per layer, the
+output of one layer is the input of the next), i.e. the routed-MoE work of
+one decode token.  One step streams 39 x 14.16 MB = 552 MB of expert weights,
+far more than the 126 MB L2, so no timed iteration is served from L2.
+
+value   = algorithmic HBM bytes of all ranks' steps / device time (GB/s), the
+          device time measured with CUDA events around K graph replays, max
+          over ranks.
+e2e     = the same metric through the public API MoEDecodeChain(x_host): per
+          step the input is copied from pinned host memory, the layers run and
+          the output is read back to the host.
+roofline= the dominant kernel (fused gate/up + SwiGLU), timed alone.
+
+--impl reference times the reference's own MLX CPU kernel (fp_qmm_t for bf16
+x, compiled from the reference sources into oracle/_ref) on the same layer,
+with all host threads, one sparse layer per step.
+
+Multi-GPU: serial decode does not shard (replicas only): each rank runs its own
+chain; value is the aggregate.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import importlib
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "moe_decode_hbm_gbs"
+UNIT = "GB/s"
+L2_NOTE = "inputs larger than L2 (552 MB of expert weights per step vs 126 MB L2)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=400)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--layers", type=int, default=39)
+    p.add_argument("--cpu-seconds", type=float, default=10.0)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def layer_bytes(cfg, k, T=1):
+    """Algorithmic bytes of one config[1] layer: the k selected experts' packed
+    codes + scales (gate, up, down) plus bf16 x in and y out."""
+    return k * cfg.routed_bytes_per_expert() + 2 * T * cfg.hidden * 2
+
+
+def gateup_bytes(cfg, k, T=1):
+    per_row = cfg.hidden // 2 + cfg.hidden // 16
+    return k * 2 * cfg.inter * per_row + T * cfg.hidden * 2 + T * k * cfg.inter * 2
+
+
+# ----------------------------------------------------------------------------- CPU
+def cpu_reference_gbs(seconds, threads, cfg, steps=None, warmup=0):
+    """The reference's MLX CPU kernel (oracle/_ref) on one config[1] layer per step."""
+    import numpy as np
+    import oracle
+    impl = oracle.ref if oracle.ref is not None else oracle.port
+    kind = "reference" if oracle.ref is not None else "port"
+    rng = np.random.default_rng(0)
+    k, H, I = cfg.top_k, cfg.hidden, cfg.inter
+    # Codes/scales of the 8 selected experts (values do not change CPU timing).
+    gw = rng.integers(0, 2**32, (k, I, H // 8), dtype=np.uint64).astype(np.uint32)
+    gs = rng.integers(0x20, 0x48, (k, I, H // 16)).astype(np.uint8)
+    uw, us = gw[::-1].copy(), gs[::-1].copy()
+    dw = rng.integers(0, 2**32, (k, H, I // 8), dtype=np.uint64).astype(np.uint32)
+    ds = rng.integers(0x20, 0x48, (k, H, I // 16)).astype(np.uint8)
+    x = oracle.bf16_bits_from_f32(rng.standard_normal((1, H)).astype(np.float32))
+    wts = np.full(k, 1.0 / k, np.float32)
+
+    def one_layer():
+        acc = np.zeros(H, np.float32)
+        for j in range(k):
+            if kind == "reference":
+                g = impl.qmm_bf16(x, gw[j], gs[j], threads=threads)
+                u = impl.qmm_bf16(x, uw[j], us[j], threads=threads)
+            else:
+                g = oracle.bf16_bits_from_f32(impl.qmm_f32(oracle.f32_from_bf16_bits(x), gw[j], gs[j]))
+                u = oracle.bf16_bits_from_f32(impl.qmm_f32(oracle.f32_from_bf16_bits(x), uw[j], us[j]))
+            gf, uf = oracle.f32_from_bf16_bits(g), oracle.f32_from_bf16_bits(u)
+            a = oracle.bf16_bits_from_f32(gf / (1 + np.exp(-gf)) * uf)
+            if kind == "reference":
+                d = impl.qmm_bf16(a, dw[j], ds[j], threads=threads)
+            else:
+                d = oracle.bf16_bits_from_f32(impl.qmm_f32(oracle.f32_from_bf16_bits(a), dw[j], ds[j]))
+            acc += wts[j] * oracle.f32_from_bf16_bits(d)[0]
+        return acc * 2.5
+
+    for _ in range(warmup):
+        one_layer()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        one_layer()
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= seconds):
+            break
+    b = layer_bytes(cfg, k)
+    return dict(value=b * n / el / 1e9, unit=UNIT, cores=threads, kind=kind,
+                sample=f"{n} config[1] layers (8 experts x gate/up/down, T=1), bf16 x through "
+                       f"the reference fp_qmm_t<bfloat16_t,16,4> split over {threads} threads; "
+                       f"{el:.2f} s"), n, el
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        self.gpu_index = gpu_index
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(rows)}
+
+
+def measured_peak_hbm():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """dram bytes per launch of the gate/up kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "moe_gateup_decode_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    lag = importlib.import_module("mlxfast-challenge_b200.laguna")
+    cfg = lag.LAGUNA_XS_2_1
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        threads = os.cpu_count() or 1
+        cb, n, el = cpu_reference_gbs(None, threads, cfg, steps=args.steps, warmup=args.warmup)
+        line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / n * 1e3,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "BASELINE config[1]: routed MoE layer decode T=1, "
+                                       "256 experts top-8, H=2048 I=512, one layer per step",
+                           "l2": "CPU"},
+                "impl": "reference", "cpu_baseline": cb,
+                "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    nv = importlib.import_module("mlxfast-challenge_b200")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    # Setup: L random-init sparse layers (routed banks only: config[1]).
+    blocks, routing = [], []
+    for l in range(args.layers):
+        blk, _ = lag.random_sparse_layer(nv, seed=1000 + l, device=dev, with_shared=False)
+        blocks.append(blk)
+        routing.append(lag.random_routing(1, cfg, seed=5000 + l, device=dev))
+    chain = nv.MoEDecodeChain(blocks, routing, T=1, device=dev).capture()
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    chain.x0.copy_(torch.randn(1, cfg.hidden, generator=g, device=dev).to(torch.bfloat16))
+    bytes_step = args.layers * layer_bytes(cfg, cfg.top_k)
+    s = chain.stream
+
+    # Warm-up, then K timed replays bracketed by barrier + synchronize.
+    for _ in range(max(args.warmup, 3)):
+        chain.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_index = int(vis.split(",")[local]) if vis else local
+    sampler = ClockSampler(gpu_index)
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        ev0.record(s)
+        for _ in range(args.steps):
+            chain.graph.replay()
+        ev1.record(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if rank == 0 else None
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps * bytes_step / (ms_max / 1e3) / 1e9
+
+    # Dominant kernel alone: the L gate/up launches captured into one graph.
+    import ctypes
+    L = nv._lib.lib()
+    gu = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(gu, stream=s):
+            sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for l, b in enumerate(blocks):
+                inds, _ = chain.routing[l]
+                nv._lib.check(L.moe_gate_up_swiglu(chain.act.data_ptr(), chain.act_ld,
+                                                   chain.x0.data_ptr(), 0, 1,
+                                                   ctypes.byref(b.desc), inds.data_ptr(), sp))
+        for _ in range(5):
+            gu.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(20, args.steps // 4)
+        e0.record(s)
+        for _ in range(reps):
+            gu.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    gu_ms = e0.elapsed_time(e1) / (reps * args.layers)
+    gu_bytes = gateup_bytes(cfg, cfg.top_k)
+    peak, peak_kind = measured_peak_hbm()
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    traffic = ncu_traffic()
+    roofline = {"bound": "hbm", "kernel": "moe_gateup_kernel (fused gate/up + SwiGLU)",
+                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                if peak_kind == "measured" else "fallback 6650 GB/s",
+                "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes,
+                "us_per_launch": gu_ms * 1e3}
+
+    # End to end through the public API: pinned host x in, host y out, every step.
+    xh = torch.randn(1, cfg.hidden, generator=torch.Generator().manual_seed(3)).to(
+        torch.bfloat16).pin_memory()
+    yh = torch.empty(1, cfg.hidden, dtype=torch.bfloat16).pin_memory()
+    for _ in range(3):
+        chain(xh, yh)
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(10, args.steps // 2)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        chain(xh, yh)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_val = world * e2e_steps * bytes_step / float(te.item()) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu, _, _ = cpu_reference_gbs(args.cpu_seconds, os.cpu_count() or 1, cfg)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config[1]: routed MoE layer decode T=1 (256 experts, "
+                                   "top-8, H=2048, I=512, NVFP4 g16) x 39 sparse layers per step",
+                       "layers_per_step": args.layers, "bytes_per_step": bytes_step,
+                       "l2": L2_NOTE, "parallelism": f"replicas{world}",
+                       "weights": "nvfp4 e2m1/e4m3-g16", "activations": "bf16",
+                       "accumulate": "f32"},
+            "tok_per_s_moe_only": world * args.steps / (ms_max / 1e3),
+            "gpu_launches": args.steps * chain.launches_per_step(),
+            "clocks": clocks,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": cfg.hidden * 2,
+                    "d2h_bytes_per_step": cfg.hidden * 2,
+                    "api": "MoEDecodeChain.__call__ (pinned host x -> device -> host y)"},
+        }
+        print(json.dumps(line), flush=True)
+    del chain, gu
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -155,6 +155,29 @@ NVFP4MOE_API int moe_block_forward(void* y, const void* x, const void* residual,
                                    uint32_t* inds_out, float* weights_out, void* workspace,
                                    size_t workspace_bytes, nvfp4_stream stream);
 
+/* The two fused phases of moe_block_forward, callable on their own.
+ *
+ * moe_gate_up_swiglu -- the routed (and shared) gate/up projections fused
+ * with SwiGLU, as the reference runtime's lagunaRoutedSwiGLUQMV
+ * (Sources/MLXFastModel/LagunaRuntimeModel.swift:7424) and SwitchGLU's
+ * gate/up + compiledSwiGLU (VLM/MLXLMCommon/SwitchLayers.swift:547-571):
+ *   act[t][j][i] = silu(x_t . gate_e[i]) * (x_t . up_e[i]),  e = inds[t][j]
+ * for slots j < k, and slot j = k (when shared_inter > 0) for the shared
+ * expert.  act is f32 [T, k(+1), act_ld], act_ld >= max(I, Is).
+ *
+ * moe_down_combine -- the down projections with the routed weighting,
+ * scaling, shared expert and residual, as lagunaRoutedSharedDownResidual
+ * (LagunaRuntimeModel.swift:8441):
+ *   y_t = scaling * sum_j w[t][j] * down_e(act[t][j]) + shared_down(act[t][k])
+ *         (+ residual_t) */
+NVFP4MOE_API int moe_gate_up_swiglu(float* act, int64_t act_ld, const void* x, int dtype,
+                                    int64_t T, const moe_layer_desc* layer,
+                                    const uint32_t* inds, nvfp4_stream stream);
+NVFP4MOE_API int moe_down_combine(void* y, const float* act, int64_t act_ld,
+                                  const void* residual, int dtype, int64_t T,
+                                  const moe_layer_desc* layer, const uint32_t* inds,
+                                  const float* weights, nvfp4_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -35,7 +35,7 @@ from ._lib import DeviceIndexError, MoeLayerDesc, NvFp4Bank, check, lib
 
 __all__ = [
     "quantize", "dequantize", "quantized_matmul", "gather_qmm", "moe_router_topk",
-    "SparseMoeBlock", "device_status", "DeviceIndexError", "library_path",
+    "SparseMoeBlock", "MoEDecodeChain", "device_status", "DeviceIndexError", "library_path",
 ]
 
 _DT = {torch.bfloat16: _lib.NVFP4_BF16, torch.float16: _lib.NVFP4_F16,
@@ -332,3 +332,6 @@ class SparseMoeBlock:
         if return_routing:
             return y, inds_out, wts_out
         return y
+
+
+from .decode import MoEDecodeChain  # noqa: E402

@@ -253,35 +253,18 @@ int moe_workspace_init(void* workspace, size_t bytes, nvfp4_stream stream) {
   return check_cuda(cudaMemsetAsync(workspace, 0, bytes, (cudaStream_t)stream), "workspace");
 }
 
+static int check_layer(const char* op, const moe_layer_desc* L, int dtype, int64_t T);
+
 int moe_block_forward(void* y, const void* x, const void* residual, int dtype, int64_t T,
                       const moe_layer_desc* L, const uint32_t* inds_in, const float* weights_in,
                       uint32_t* inds_out, float* weights_out, void* workspace,
                       size_t workspace_bytes, nvfp4_stream stream) {
   const char* op = "moe_block";
-  if (!L) return fail(NVFP4_ERR_INVALID, "[%s] null layer descriptor.", op);
-  if (!valid_dtype(dtype))
-    return fail(NVFP4_ERR_INVALID, "[%s] Only real floating types are supported.", op);
-  const int64_t H = L->hidden, I = L->inter, E = L->n_experts, Is = L->shared_inter;
+  if (int r = check_layer(op, L, dtype, T)) return r;
+  const int64_t H = L->hidden, E = L->n_experts;
   const int k = (int)L->top_k;
-  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || Is < 0 || k <= 0 || k > E)
-    return fail(NVFP4_ERR_INVALID, "[%s] Invalid layer shape.", op);
-  if (H % 128 || I % 128 || Is % 128)
-    return fail(NVFP4_ERR_UNSUPPORTED,
-                "[%s] hidden and intermediate sizes must be multiples of 128 "
-                "(use nvfp4_gather_qmm for other shapes).",
-                op);
   if (T == 0) return NVFP4_OK;
   if (!y || !x) return fail(NVFP4_ERR_INVALID, "[%s] null activation pointer.", op);
-  const nvfp4_bank* banks[3] = {&L->gate, &L->up, &L->down};
-  for (const nvfp4_bank* b : banks)
-    if (!b->w || !b->scales || !aligned16(b->w))
-      return fail(NVFP4_ERR_INVALID, "[%s] routed banks need 16-byte aligned codes.", op);
-  if (Is > 0) {
-    const nvfp4_bank* sb[3] = {&L->shared_gate, &L->shared_up, &L->shared_down};
-    for (const nvfp4_bank* b : sb)
-      if (!b->w || !b->scales || !aligned16(b->w))
-        return fail(NVFP4_ERR_INVALID, "[%s] shared banks need 16-byte aligned codes.", op);
-  }
   if (!inds_in && !L->router_w)
     return fail(NVFP4_ERR_INVALID, "[%s] either inds_in or router_w is required.", op);
   if (inds_in && !weights_in)
@@ -289,9 +272,6 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
   const BlockLayout B = block_layout(L, T);
   if (!workspace || workspace_bytes < B.total)
     return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, B.total);
-  const size_t down_smem = nvfp4::down_smem_bytes(std::max(I, Is), B.kk);
-  if (down_smem > 220 * 1024)
-    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] top_k * intermediate too large.", op);
   char* ws = static_cast<char*>(workspace);
   cudaStream_t s = (cudaStream_t)stream;
 
@@ -330,7 +310,41 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
       return check_cuda(cudaGetLastError(), op);
   }
   float* act = reinterpret_cast<float*>(ws + B.act_off);
+  if (int r = moe_gate_up_swiglu(act, B.act_ld, x, dtype, T, L, inds, stream)) return r;
+  return moe_down_combine(y, act, B.act_ld, residual, dtype, T, L, inds, wts, stream);
+}
 
+static int check_layer(const char* op, const moe_layer_desc* L, int dtype, int64_t T) {
+  if (!L) return fail(NVFP4_ERR_INVALID, "[%s] null layer descriptor.", op);
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID, "[%s] Only real floating types are supported.", op);
+  const int64_t H = L->hidden, I = L->inter, E = L->n_experts, Is = L->shared_inter;
+  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || Is < 0 || L->top_k <= 0 || L->top_k > E)
+    return fail(NVFP4_ERR_INVALID, "[%s] Invalid layer shape.", op);
+  if (H % 128 || I % 128 || Is % 128)
+    return fail(NVFP4_ERR_UNSUPPORTED,
+                "[%s] hidden and intermediate sizes must be multiples of 128 "
+                "(use nvfp4_gather_qmm for other shapes).",
+                op);
+  return NVFP4_OK;
+}
+
+int moe_gate_up_swiglu(float* act, int64_t act_ld, const void* x, int dtype, int64_t T,
+                       const moe_layer_desc* L, const uint32_t* inds, nvfp4_stream stream) {
+  const char* op = "moe_gate_up_swiglu";
+  if (int r = check_layer(op, L, dtype, T)) return r;
+  if (T == 0) return NVFP4_OK;
+  if (!act || !x || !inds) return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  if (act_ld < std::max(L->inter, L->shared_inter))
+    return fail(NVFP4_ERR_INVALID, "[%s] act_ld smaller than the intermediate size.", op);
+  if (!L->gate.w || !L->up.w || !L->gate.scales || !L->up.scales || !aligned16(L->gate.w) ||
+      !aligned16(L->up.w))
+    return fail(NVFP4_ERR_INVALID, "[%s] routed banks need 16-byte aligned codes.", op);
+  const int64_t H = L->hidden, I = L->inter, Is = L->shared_inter;
+  if (Is > 0 && (!L->shared_gate.w || !L->shared_up.w || !L->shared_gate.scales ||
+                 !L->shared_up.scales || !aligned16(L->shared_gate.w) ||
+                 !aligned16(L->shared_up.w)))
+    return fail(NVFP4_ERR_INVALID, "[%s] shared banks need 16-byte aligned codes.", op);
   nvfp4::GateUpArgs ga{};
   ga.x = x;
   ga.dtype = dtype;
@@ -338,9 +352,9 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
   ga.H = H;
   ga.I = I;
   ga.Is = Is;
-  ga.E = E;
-  ga.k = k;
-  ga.kk = B.kk;
+  ga.E = L->n_experts;
+  ga.k = (int)L->top_k;
+  ga.kk = (int)L->top_k + (Is > 0 ? 1 : 0);
   ga.inds = inds;
   ga.gw = reinterpret_cast<const uint8_t*>(L->gate.w);
   ga.gs = L->gate.scales;
@@ -355,22 +369,41 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
     ga.sus = L->shared_up.scales;
   }
   ga.act = act;
-  ga.act_ld = B.act_ld;
-  if (int r = check_cuda(nvfp4::launch_moe_gateup(ga, s), op)) return r;
+  ga.act_ld = act_ld;
+  return check_cuda(nvfp4::launch_moe_gateup(ga, (cudaStream_t)stream), op);
+}
 
+int moe_down_combine(void* y, const float* act, int64_t act_ld, const void* residual, int dtype,
+                     int64_t T, const moe_layer_desc* L, const uint32_t* inds,
+                     const float* weights, nvfp4_stream stream) {
+  const char* op = "moe_down_combine";
+  if (int r = check_layer(op, L, dtype, T)) return r;
+  if (T == 0) return NVFP4_OK;
+  if (!y || !act || !inds || !weights)
+    return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  const int64_t H = L->hidden, I = L->inter, Is = L->shared_inter;
+  const int kk = (int)L->top_k + (Is > 0 ? 1 : 0);
+  if (act_ld < std::max(I, Is))
+    return fail(NVFP4_ERR_INVALID, "[%s] act_ld smaller than the intermediate size.", op);
+  if (!L->down.w || !L->down.scales || !aligned16(L->down.w))
+    return fail(NVFP4_ERR_INVALID, "[%s] routed banks need 16-byte aligned codes.", op);
+  if (Is > 0 && (!L->shared_down.w || !L->shared_down.scales || !aligned16(L->shared_down.w)))
+    return fail(NVFP4_ERR_INVALID, "[%s] shared banks need 16-byte aligned codes.", op);
+  if (nvfp4::down_smem_bytes(std::max(I, Is), kk) > 220 * 1024)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] top_k * intermediate too large.", op);
   nvfp4::DownArgs da{};
   da.act = act;
-  da.act_ld = B.act_ld;
+  da.act_ld = act_ld;
   da.T = T;
   da.H = H;
   da.I = I;
   da.Is = Is;
-  da.E = E;
-  da.k = k;
-  da.kk = B.kk;
+  da.E = L->n_experts;
+  da.k = (int)L->top_k;
+  da.kk = kk;
   da.Ipad = (int)std::max(I, Is);
   da.inds = inds;
-  da.wts = wts;
+  da.wts = weights;
   da.scaling = L->routed_scaling;
   da.dw = reinterpret_cast<const uint8_t*>(L->down.w);
   da.ds = L->down.scales;
@@ -383,7 +416,7 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
   da.residual = residual;
   da.y = y;
   da.dtype = dtype;
-  return check_cuda(nvfp4::launch_moe_down(da, s), op);
+  return check_cuda(nvfp4::launch_moe_down(da, (cudaStream_t)stream), op);
 }
 
 }  // extern "C"

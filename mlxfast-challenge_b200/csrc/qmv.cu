@@ -142,7 +142,7 @@ __device__ __forceinline__ void reduce_to_warp0(float (&acc)[4], float* red) {
 
 // ---------------------------------------------------------------------------
 // Gather QMM (also the dense quantized_matmul with one expert and no index).
-// grid = (ceil(N/16), P * mchunks); segment = (pair p, 8-row chunk of M).
+// grid = (P * mchunks, ceil(N/16)); segment = (pair p, 8-row chunk of M).
 template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -152,12 +152,12 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
   float* colscale = reinterpret_cast<float*>(xs + 8 * ldx);
   float* red = colscale + 8;
 
-  const int seg = blockIdx.y;
+  const int seg = blockIdx.x;
   const int p = seg / a.mchunks, mc = seg % a.mchunks;
   const uint32_t e = a.rhs ? a.rhs[p] : 0u;
   const uint32_t xi = a.lhs ? a.lhs[p] : (uint32_t)p;
   if (e >= (uint32_t)a.n_experts || xi >= (uint32_t)a.n_x_batches) {
-    if (threadIdx.x == 0 && blockIdx.x == 0) flag_error(1);
+    if (threadIdx.x == 0 && blockIdx.y == 0) flag_error(1);
     return;
   }
   const int ncols = min(8, a.M - mc * 8);
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
   }
   __syncthreads();
 
-  const int64_t n_lo = (int64_t)blockIdx.x * 16 + g, n_hi = n_lo + 8;
+  const int64_t n_lo = (int64_t)blockIdx.y * 16 + g, n_hi = n_lo + 8;
   const uint8_t* wbase = a.w + (int64_t)e * a.w_stride;
   const uint8_t* sbase = a.s + (int64_t)e * a.s_stride;
   const int64_t rowb = a.K / 2, rows = a.K / 16;
@@ -251,7 +251,7 @@ __global__ void qmm_gather_generic_kernel(QmmArgs a) {
 
 // ---------------------------------------------------------------------------
 // Routed (and shared) expert gate/up projections fused with SwiGLU.
-// grid = (ceil(Imax/8), T * kk), kk = k (+1 with a shared expert).  A warp
+// grid = (T * kk, ceil(Imax/8)), kk = k (+1 with a shared expert).  A warp
 // tile holds gate rows i0..i0+7 in MMA rows 0..7 and the matching up rows in
 // MMA rows 8..15, so every thread ends with (gate, up) of one row.
 template <int WARPS>
@@ -263,11 +263,11 @@ __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
   float* colscale = reinterpret_cast<float*>(xs + ldx);
   float* red = colscale + 4;
 
-  const int seg = blockIdx.y;
+  const int seg = blockIdx.x;
   const int tok = seg / a.kk, slot = seg % a.kk;
   const bool routed = slot < a.k;
   const int64_t Irows = routed ? a.I : a.Is;
-  const int64_t i0 = (int64_t)blockIdx.x * 8;
+  const int64_t i0 = (int64_t)blockIdx.y * 8;
   if (i0 >= Irows) return;
   const uint8_t *gw, *gs, *uw, *us;
   if (routed) {
@@ -483,10 +483,9 @@ cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream) {
   if (qmm_fast_path_ok(a)) {
     const size_t smem = qmm_smem_bytes(a.K);
     auto kern = qmm_gather_kernel<kQmmWarps>;
-    cudaError_t err =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t err = ensure_smem(kern, smem);
     if (err != cudaSuccess) return err;
-    dim3 grid((unsigned)((a.N + 15) / 16), (unsigned)(a.P * a.mchunks));
+    dim3 grid((unsigned)(a.P * a.mchunks), (unsigned)((a.N + 15) / 16));
     kern<<<grid, kQmmWarps * 32, smem, stream>>>(a);
   } else {
     const int64_t total = a.P * (int64_t)a.M * a.N;
@@ -506,11 +505,10 @@ cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream) {
   if (a.T == 0) return cudaSuccess;
   const size_t smem = gateup_smem_bytes(a.H);
   auto kern = moe_gateup_kernel<kGateUpWarps>;
-  cudaError_t err =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = ensure_smem(kern, smem);
   if (err != cudaSuccess) return err;
   const int64_t Imax = std::max(a.I, a.Is);
-  dim3 grid((unsigned)((Imax + 7) / 8), (unsigned)(a.T * a.kk));
+  dim3 grid((unsigned)(a.T * a.kk), (unsigned)((Imax + 7) / 8));
   kern<<<grid, kGateUpWarps * 32, smem, stream>>>(a);
   return cudaGetLastError();
 }
@@ -524,8 +522,7 @@ cudaError_t launch_moe_down(const DownArgs& a, cudaStream_t stream) {
   if (a.T == 0) return cudaSuccess;
   const size_t smem = down_smem_bytes(a.Ipad, a.kk);
   auto kern = moe_down_kernel<kDownWarps>;
-  cudaError_t err =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = ensure_smem(kern, smem);
   if (err != cudaSuccess) return err;
   dim3 grid((unsigned)((a.H + 15) / 16), (unsigned)((a.T + 7) / 8));
   kern<<<grid, kDownWarps * 32, smem, stream>>>(a);

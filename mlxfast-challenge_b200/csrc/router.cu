@@ -173,8 +173,7 @@ cudaError_t launch_router(const RouterArgs& a, cudaStream_t stream) {
   if (a.T == 0) return cudaSuccess;
   const int Kc = (int)(a.H / a.ksplit);
   const size_t smem = (size_t)8 * (Kc + kRouterPad) * sizeof(uint16_t);
-  cudaError_t err = cudaFuncSetAttribute(router_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = ensure_smem(router_kernel, smem);
   if (err != cudaSuccess) return err;
   dim3 grid((unsigned)((a.E + 15) / 16), (unsigned)a.ksplit, (unsigned)((a.T + 7) / 8));
   router_kernel<<<grid, kRouterWarps * 32, smem, stream>>>(a);

@@ -1,0 +1,116 @@
+"""Serial decode of a stack of sparse MoE layers as one CUDA graph.
+
+The reference evaluates each decode step as a lazy MLX graph (eval at
+LagunaRuntimeWorker.swift:369, the per-layer chain at
+LagunaRuntimeModel.swift:11460 -> :11030 -> :10678).  On the B200 the same
+chain is captured once into a CUDA graph: per layer the fused gate/up+SwiGLU
+kernel and the fused down+combine kernel (C ABI moe_gate_up_swiglu /
+moe_down_combine), the output of layer l feeding layer l+1.  A step replays
+the graph, so launch overhead is paid once per step instead of per kernel.
+
+MoEDecodeChain(blocks, routing)(x_host) is the end-to-end call: it copies the
+step's input from pinned host memory, replays the graph and copies the result
+back.  Routing is given per layer; with route=True each
+layer runs the router first (config[2]).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from ._lib import check, lib
+
+
+class MoEDecodeChain:
+    def __init__(self, blocks: Sequence, routing: Optional[Sequence[Tuple[torch.Tensor,
+                                                                           torch.Tensor]]],
+                 T: int = 1, dtype=torch.bfloat16, route: bool = False, device="cuda:0"):
+        self.blocks = list(blocks)
+        self.T = T
+        self.dtype = dtype
+        self.route = route
+        self.device = torch.device(device)
+        H = self.blocks[0].H
+        self.H = H
+        self.x0 = torch.zeros(T, H, dtype=dtype, device=self.device)
+        self.bufs = [torch.zeros(T, H, dtype=dtype, device=self.device) for _ in range(2)]
+        self.routing = []
+        for l, b in enumerate(self.blocks):
+            if route:
+                self.routing.append((torch.empty(T, b.top_k, dtype=torch.uint32, device=self.device),
+                                     torch.empty(T, b.top_k, dtype=torch.float32,
+                                                 device=self.device)))
+            else:
+                i, w = routing[l]
+                self.routing.append((i.to(torch.int32).view(torch.uint32).reshape(T, b.top_k)
+                                     .contiguous(), w.to(torch.float32).reshape(T, b.top_k)
+                                     .contiguous()))
+        kk = max(b.top_k + (1 if b.Is else 0) for b in self.blocks)
+        self.act_ld = max(max(b.I, b.Is) for b in self.blocks)
+        self.act = torch.empty(T * kk * self.act_ld, dtype=torch.float32, device=self.device)
+        nbytes = max(b.workspace_bytes(T) for b in self.blocks)
+        self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+        self.stream = torch.cuda.Stream(device=self.device)
+        self.graph = None
+        self.out = None
+        from . import _dtype_code
+        self._dt = _dtype_code(self.x0, "decode")
+
+    # -- one step as raw launches (captured below) --------------------------------
+    def _launch_step(self, stream_ptr):
+        L = lib()
+        src = self.x0
+        for l, b in enumerate(self.blocks):
+            dst = self.bufs[l % 2]
+            inds, wts = self.routing[l]
+            if self.route:
+                check(L.moe_router_topk(inds.data_ptr(), wts.data_ptr(), src.data_ptr(), self._dt,
+                                        b.router_weight.data_ptr(),
+                                        None if b.router_bias is None else
+                                        b.router_bias.data_ptr(), self.T, b.H, b.E, b.top_k,
+                                        int(b.desc.norm_topk_prob), self.ws.data_ptr(),
+                                        self.ws.numel(), stream_ptr))
+            check(L.moe_gate_up_swiglu(self.act.data_ptr(), self.act_ld, src.data_ptr(),
+                                       self._dt, self.T, ctypes.byref(b.desc), inds.data_ptr(),
+                                       stream_ptr))
+            check(L.moe_down_combine(dst.data_ptr(), self.act.data_ptr(), self.act_ld, None,
+                                     self._dt, self.T, ctypes.byref(b.desc), inds.data_ptr(),
+                                     wts.data_ptr(), stream_ptr))
+            src = dst
+        self.out = src
+
+    def launches_per_step(self) -> int:
+        return len(self.blocks) * (3 if self.route else 2)
+
+    def capture(self):
+        s = self.stream
+        with torch.cuda.stream(s):
+            self._launch_step(ctypes.c_void_p(s.cuda_stream))  # warm (sets kernel attributes)
+        s.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self._launch_step(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return self
+
+    def replay(self):
+        """Enqueue one step on self.stream (inputs already in self.x0)."""
+        if self.graph is None:
+            self.capture()
+        with torch.cuda.stream(self.stream):
+            self.graph.replay()
+        return self.out
+
+    def __call__(self, x_host: torch.Tensor, y_host: Optional[torch.Tensor] = None):
+        """End-to-end step: pinned host x -> device, all layers, device -> host y."""
+        if self.graph is None:
+            self.capture()
+        if y_host is None:
+            y_host = torch.empty(self.T, self.H, dtype=self.dtype, pin_memory=True)
+        with torch.cuda.stream(self.stream):
+            self.x0.copy_(x_host.reshape(self.T, self.H), non_blocking=True)
+            self.graph.replay()
+            y_host.copy_(self.out, non_blocking=True)
+        self.stream.synchronize()
+        return y_host

@@ -1,0 +1,234 @@
+"""GPU parity of every kernel behind the C ABI against the CPU oracle.
+
+Bars: dequantize / quantize bit-exact; matmul outputs within max-abs 2e-2 and
+relative-L2 5e-3 of the fp32-accumulated oracle (tighter where the reference's
+own tests are tighter); router top-k sets equal up to ties closer than 2e-6.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import assert_close, close_report
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def to_dev_u32(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int32)).to(DEV).view(torch.uint32)
+
+
+def to_dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def u32_np(t):
+    return t.view(torch.int32).cpu().numpy().view(np.uint32)
+
+
+def bf16_np_bits(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def rand_bf16(shape, std, seed):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=DEV) * std).to(torch.bfloat16)
+
+
+# --- dequantize / quantize ------------------------------------------------------------
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_dequantize_bit_exact_all_codes_all_scales(nv, orc, dtype):
+    rng = np.random.default_rng(0)
+    rows, K = 256, 512
+    wq = rng.integers(0, 2**32, (rows, K // 8), dtype=np.uint64).astype(np.uint32)
+    sq = np.arange(rows * K // 16, dtype=np.uint32).astype(np.uint8).reshape(rows, K // 16)
+    # Every product LUT[code] * scale is exact in f32, bf16 and f16 (|v| <= 2880).
+    want = orc.port.dequantize(wq, sq)
+    got = nv.dequantize(to_dev_u32(wq), to_dev(sq), dtype=dtype).float().cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.astype(np.float32).view(np.uint32))
+
+
+def test_dequantize_known_answers(nv):
+    w = torch.tensor([[0x76543210, 0xFEDCBA98 - 2**32], [0x76543210, 0xFEDCBA98 - 2**32]],
+                     dtype=torch.int32, device=DEV)
+    s = torch.tensor([[0x38], [0x40]], dtype=torch.uint8, device=DEV)
+    lut = [0, .5, 1, 1.5, 2, 3, 4, 6, -0., -.5, -1, -1.5, -2, -3, -4, -6]
+    out = nv.dequantize(w, s, dtype=torch.float32).cpu().reshape(-1).tolist()
+    assert out == lut + [2 * v for v in lut]
+
+
+@pytest.mark.parametrize("std", [0.02, 1.0, 1e-4, 300.0])
+def test_quantize_bf16_bit_exact(nv, orc, std):
+    w = rand_bf16((128, 2048), std, seed=11)
+    w[0, :16] = 0  # zero group
+    w[1, :32] = 1e-30  # scale encodes to 0
+    wq, sq = nv.quantize(w)
+    owq, osq = orc.port.quantize(bf16_np_bits(w))
+    assert np.array_equal(u32_np(wq), owq)
+    assert np.array_equal(sq.cpu().numpy(), osq)
+
+
+def test_quantize_golden(nv, golden):
+    w = to_dev(golden["quant_w_bf16"].view(np.int16)).view(torch.bfloat16)
+    wq, sq = nv.quantize(w)
+    assert np.array_equal(u32_np(wq), golden["quant_wq"])
+    assert np.array_equal(sq.cpu().numpy(), golden["quant_sq"])
+
+
+def test_quantize_f32_and_f16_bit_exact(nv, orc):
+    g = torch.Generator(device=DEV).manual_seed(5)
+    w = torch.randn(64, 256, generator=g, device=DEV) * 0.5
+    wq, sq = nv.quantize(w)
+    owq, osq = orc.port.quantize(w.cpu().numpy())
+    assert np.array_equal(u32_np(wq), owq) and np.array_equal(sq.cpu().numpy(), osq)
+
+
+# --- quantized_matmul ----------------------------------------------------------------
+
+def _qmm_case(nv, orc, M, N, K, dtype, seed):
+    w = rand_bf16((N, K), 0.02, seed)
+    wq, sq = nv.quantize(w)
+    g = torch.Generator(device=DEV).manual_seed(seed + 1)
+    x = torch.randn(M, K, generator=g, device=DEV).to(dtype)
+    y = nv.quantized_matmul(x, wq, sq)
+    want = orc.port.qmm_f32(x.float().cpu().numpy(), u32_np(wq), sq.cpu().numpy())
+    return y.float().cpu().numpy(), want
+
+
+@pytest.mark.parametrize("M", [1, 2, 5, 8, 9, 32])
+@pytest.mark.parametrize("N,K", [(64, 256), (512, 2048), (2048, 512), (40, 128)])
+def test_quantized_matmul_vs_oracle(nv, orc, M, N, K):
+    got, want = _qmm_case(nv, orc, M, N, K, torch.bfloat16, seed=M * 1000 + N + K)
+    assert_close(got, want, what=f"qmm M={M} N={N} K={K}")
+
+
+@pytest.mark.parametrize("N,K", [(33, 48), (16, 80), (64, 272)])
+def test_quantized_matmul_generic_shapes(nv, orc, N, K):
+    got, want = _qmm_case(nv, orc, 3, N, K, torch.bfloat16, seed=N + K)
+    assert_close(got, want, what=f"generic N={N} K={K}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_quantized_matmul_dtypes(nv, orc, dtype):
+    got, want = _qmm_case(nv, orc, 4, 256, 1024, dtype, seed=3)
+    assert_close(got, want, what=str(dtype))
+
+
+def test_quantized_matmul_golden(nv, golden):
+    x = torch.from_numpy(golden["qmm_x_f32"]).to(DEV)
+    y = nv.quantized_matmul(x, to_dev_u32(golden["qmm_wq"]), to_dev(golden["qmm_sq"]))
+    assert_close(y.cpu().numpy(), golden["qmm_y_f32"], max_abs=1e-4, rel_l2=1e-5,
+                 what="golden f32")
+    xb = to_dev(golden["qmm_x_bf16"].view(np.int16)).view(torch.bfloat16)
+    yb = nv.quantized_matmul(xb, to_dev_u32(golden["qmm_wq"]), to_dev(golden["qmm_sq"]))
+    # Against the reference's own bf16-accumulating CPU path: reported, looser bar.
+    ma, rl = close_report(yb.float().cpu().numpy(),
+                          (golden["qmm_y_bf16"].astype(np.uint32) << 16).view(np.float32))
+    assert rl < 3e-2, rl
+
+
+def test_exact_constant_weights(nv):
+    # LagunaNVFP4KernelTests.swift:8-55 and :93-150: all-ones / 0.5 weights, ones input.
+    for (N, K, val, M) in [(128, 64, 1.0, 32), (512, 2048, 0.5, 1), (2048, 512, 0.5, 32)]:
+        w = torch.full((N, K), val, device=DEV)
+        wq, sq = nv.quantize(w)
+        wd = nv.dequantize(wq, sq, dtype=torch.float32)
+        x = torch.ones(M, K, device=DEV)
+        y = nv.quantized_matmul(x, wq, sq)
+        assert (y - x @ wd.T).abs().max().item() <= 1e-4
+
+
+# --- gather_qmm -------------------------------------------------------------------------
+
+def test_gather_golden(nv, golden):
+    x = torch.from_numpy(golden["gather_x_f32"]).to(DEV)
+    out = nv.gather_qmm(x, to_dev_u32(golden["gather_wq"]), to_dev(golden["gather_sq"]),
+                        lhs_indices=to_dev(golden["gather_lhs"].astype(np.int32)),
+                        rhs_indices=to_dev(golden["gather_rhs"].astype(np.int32)))
+    assert out.shape == (5, 2, 32)
+    assert_close(out.cpu().numpy(), golden["gather_out_f32"], max_abs=1e-4, rel_l2=1e-5)
+
+
+@pytest.mark.parametrize("N,K", [(512, 2048), (2048, 512)])
+def test_gather_routed_decode_shapes(nv, orc, N, K):
+    E = 256
+    w = rand_bf16((E, N, K), 0.02, seed=N)
+    wq, sq = nv.quantize(w)
+    g = torch.Generator(device=DEV).manual_seed(9)
+    x = torch.randn(1, 1, 1, 1, K, generator=g, device=DEV).to(torch.bfloat16)
+    ids = torch.tensor([0, 7, 42, 255, 3, 128, 17, 99], dtype=torch.int32, device=DEV)
+    out = nv.gather_qmm(x, wq, sq, rhs_indices=ids.reshape(1, 1, 8))
+    assert out.shape == (1, 1, 8, 1, N)
+    want = orc.port.gather_qmm_f32(x.float().reshape(1, 1, K).cpu().numpy(),
+                                   u32_np(wq.view(torch.int32)[ids.long()]), sq[ids.long()].cpu().numpy(),
+                                   np.zeros(8, np.uint32), np.arange(8, dtype=np.uint32), M=1)
+    assert_close(out.float().reshape(8, 1, N).cpu().numpy(), want)
+
+
+def test_gather_sorted_prefill_rows(nv, orc):
+    E, N, K, P = 16, 256, 512, 96
+    w = rand_bf16((E, N, K), 0.02, seed=1)
+    wq, sq = nv.quantize(w)
+    g = torch.Generator(device=DEV).manual_seed(2)
+    x = torch.randn(P, 1, K, generator=g, device=DEV).to(torch.bfloat16)
+    rhs = torch.sort(torch.randint(0, E, (P,), generator=g, device=DEV))[0].to(torch.int32)
+    out = nv.gather_qmm(x, wq, sq, rhs_indices=rhs, sorted_indices=True)
+    want = orc.port.gather_qmm_f32(x.float().cpu().numpy(), u32_np(wq), sq.cpu().numpy(), None,
+                                   rhs.cpu().numpy().astype(np.uint32), M=1)
+    assert_close(out.float().cpu().numpy(), want)
+
+
+def test_gather_out_of_range_index_latches_device_status(nv):
+    w = torch.zeros(4, 32, 16, dtype=torch.int32, device=DEV)
+    s = torch.zeros(4, 32, 8, dtype=torch.uint8, device=DEV)
+    x = torch.ones(1, 1, 128, device=DEV, dtype=torch.bfloat16)
+    nv.device_status()  # clear
+    nv.gather_qmm(x, w, s, rhs_indices=torch.tensor([1, 9], dtype=torch.int32, device=DEV))
+    with pytest.raises(nv.DeviceIndexError):
+        nv.device_status()
+    nv.device_status()  # cleared again
+
+
+def test_empty_inputs(nv):
+    w = torch.zeros(4, 32, 16, dtype=torch.int32, device=DEV)
+    s = torch.zeros(4, 32, 8, dtype=torch.uint8, device=DEV)
+    x = torch.ones(0, 1, 128, device=DEV, dtype=torch.bfloat16)
+    out = nv.gather_qmm(x, w, s, lhs_indices=torch.zeros(0, dtype=torch.int32, device=DEV),
+                        rhs_indices=torch.zeros(0, dtype=torch.int32, device=DEV))
+    assert out.shape == (0, 1, 32)
+
+
+# --- router -----------------------------------------------------------------------------
+
+def check_routing(orc, x, G, bias, inds, wts, k):
+    oi, ow, logits = orc.port.router_topk(bf16_np_bits(x), bf16_np_bits(G),
+                                          bias.cpu().numpy(), k)
+    gi = u32_np(inds).reshape(oi.shape)
+    gw = wts.cpu().numpy().reshape(ow.shape)
+    s = 1.0 / (1.0 + np.exp(-logits.astype(np.float64)))
+    choice = s + bias.cpu().numpy()
+    for t in range(oi.shape[0]):
+        if set(gi[t]) != set(oi[t]):
+            # Only a near-tie at the k-th place may differ.
+            kth = np.sort(choice[t])[::-1][k - 1]
+            for e in set(gi[t]) ^ set(oi[t]):
+                assert abs(choice[t, e] - kth) < 2e-6
+        else:
+            order = {e: j for j, e in enumerate(oi[t])}
+            np.testing.assert_allclose(gw[t], ow[t][[order[e] for e in gi[t]]], rtol=1e-5,
+                                       atol=1e-6)
+
+
+@pytest.mark.parametrize("T", [1, 3, 8, 19])
+def test_router_vs_oracle(nv, orc, T):
+    E, H, k = 256, 2048, 8
+    G = rand_bf16((E, H), 0.02, seed=100 + T)
+    x = rand_bf16((T, H), 1.0, seed=200 + T)
+    g = torch.Generator(device=DEV).manual_seed(T)
+    bias = torch.randn(E, generator=g, device=DEV) * 1e-3
+    inds, wts = nv.moe_router_topk(x, G, bias, k)
+    check_routing(orc, x, G, bias, inds, wts, k)
+    # Deterministic: a second call gives the same result.
+    inds2, wts2 = nv.moe_router_topk(x, G, bias, k)
+    assert torch.equal(inds, inds2) and torch.equal(wts, wts2)
