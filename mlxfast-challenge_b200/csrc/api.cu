@@ -335,8 +335,11 @@ int moe_gate_up_swiglu(float* act, int64_t act_ld, const void* x, int dtype, int
   if (int r = check_layer(op, L, dtype, T)) return r;
   if (T == 0) return NVFP4_OK;
   if (!act || !x || !inds) return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
-  if (act_ld < std::max(L->inter, L->shared_inter))
-    return fail(NVFP4_ERR_INVALID, "[%s] act_ld smaller than the intermediate size.", op);
+  if (act_ld < std::max(L->inter, L->shared_inter) || act_ld % 8)
+    return fail(NVFP4_ERR_INVALID,
+                "[%s] act_ld must be a multiple of 8 and >= the intermediate size.", op);
+  if (!aligned16(x) || !aligned16(act))
+    return fail(NVFP4_ERR_INVALID, "[%s] x and act must be 16-byte aligned.", op);
   if (!L->gate.w || !L->up.w || !L->gate.scales || !L->up.scales || !aligned16(L->gate.w) ||
       !aligned16(L->up.w))
     return fail(NVFP4_ERR_INVALID, "[%s] routed banks need 16-byte aligned codes.", op);
@@ -383,8 +386,10 @@ int moe_down_combine(void* y, const float* act, int64_t act_ld, const void* resi
     return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
   const int64_t H = L->hidden, I = L->inter, Is = L->shared_inter;
   const int kk = (int)L->top_k + (Is > 0 ? 1 : 0);
-  if (act_ld < std::max(I, Is))
-    return fail(NVFP4_ERR_INVALID, "[%s] act_ld smaller than the intermediate size.", op);
+  if (act_ld < std::max(I, Is) || act_ld % 8)
+    return fail(NVFP4_ERR_INVALID,
+                "[%s] act_ld must be a multiple of 8 and >= the intermediate size.", op);
+  if (!aligned16(act)) return fail(NVFP4_ERR_INVALID, "[%s] act must be 16-byte aligned.", op);
   if (!L->down.w || !L->down.scales || !aligned16(L->down.w))
     return fail(NVFP4_ERR_INVALID, "[%s] routed banks need 16-byte aligned codes.", op);
   if (Is > 0 && (!L->shared_down.w || !L->shared_down.scales || !aligned16(L->shared_down.w)))

@@ -106,19 +106,72 @@ __device__ __forceinline__ void compute_chunk(float (&acc)[4], const Chunk& c,
   }
 }
 
-// Stage one activation column: f16(v * 2^-e) at swizzled positions, zeros in
-// [K, Kpad).  Executed by one warp; returns 2^e (all lanes).
-template <typename Loader>
-__device__ float stage_column_warp(__half* col, int K, int Kpad, Loader ld) {
-  const int lane = threadIdx.x & 31;
-  float m = 0.0f;
-  for (int k = lane; k < K; k += 32) m = fmaxf(m, fabsf(ld(k)));
-  m = warp_max(m);
-  const int e = pow2_exponent(m);
-  const float inv = ldexpf(1.0f, -e);
-  for (int k = lane; k < Kpad; k += 32)
-    col[xs_swz(k)] = __float2half_rn(k < K ? ld(k) * inv : 0.0f);
-  return ldexpf(1.0f, e);
+// Eight consecutive activation elements (elem_off % 8 == 0, 16-byte aligned).
+__device__ __forceinline__ void load8(const void* x, int dtype, int64_t elem_off, float (&f)[8]) {
+  if (dtype == kF32) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + elem_off);
+    const float4 b =
+        *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + elem_off + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + elem_off);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      if (dtype == kBF16) {
+        const float2 p = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        f[2 * i] = p.x; f[2 * i + 1] = p.y;
+      } else {
+        const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        f[2 * i] = p.x; f[2 * i + 1] = p.y;
+      }
+    }
+  }
+}
+
+// Eight f16 of one staged column, logical elements k..k+7 (k % 8 == 0): the
+// swizzle moves whole 16-byte groups, so they stay contiguous.
+__device__ __forceinline__ void store8_f16(__half* col, int k, const float (&f)[8], float mul) {
+  uint32_t h[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const __half2 v = __floats2half2_rn(f[2 * i] * mul, f[2 * i + 1] * mul);
+    h[i] = *reinterpret_cast<const uint32_t*>(&v);
+  }
+  *reinterpret_cast<uint4*>(col + xs_swz(k)) = make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// Block-cooperative staging of `ncols` activation columns (column j is the K
+// elements at element offset off(j)), each as f16(v * 2^-e_j) with max |v| *
+// 2^-e_j in [1, 2).  colscale[j] = 2^e_j.  Two passes over the (L1/L2-hot)
+// activations: maxima via shared atomics, then the scaled f16 copy.
+template <typename Off>
+__device__ void stage_columns(__half* xs, int ldx, int ncols, int K, const void* x, int dtype,
+                              Off off, float* colscale, int* colmax) {
+  if (threadIdx.x < 8) colmax[threadIdx.x] = 0;
+  __syncthreads();
+  const int per = K / 8;
+  const int items = ncols * per;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int j = it / per, v = it - j * per;
+    float f[8];
+    load8(x, dtype, off(j) + (int64_t)v * 8, f);
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i]));
+    atomicMax(&colmax[j], __float_as_int(m));
+  }
+  __syncthreads();
+  if (threadIdx.x < ncols) colscale[threadIdx.x] =
+      ldexpf(1.0f, pow2_exponent(__int_as_float(colmax[threadIdx.x])));
+  __syncthreads();
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int j = it / per, v = it - j * per;
+    float f[8];
+    load8(x, dtype, off(j) + (int64_t)v * 8, f);
+    store8_f16(xs + j * ldx, v * 8, f, 1.0f / colscale[j]);
+  }
 }
 
 // Deterministic cross-warp reduction of the MMA fragments into warp 0.
@@ -150,7 +203,8 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
   const int ldx = Kpad + kXPad;
   __half* xs = reinterpret_cast<__half*>(smem);
   float* colscale = reinterpret_cast<float*>(xs + 8 * ldx);
-  float* red = colscale + 8;
+  int* colmax = reinterpret_cast<int*>(colscale + 8);
+  float* red = colscale + 16;
 
   const int seg = blockIdx.x;
   const int p = seg / a.mchunks, mc = seg % a.mchunks;
@@ -164,14 +218,6 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
 
-  for (int j = warp; j < ncols; j += WARPS) {
-    const int64_t row = ((int64_t)xi * a.M + mc * 8 + j) * a.K;
-    const float s = stage_column_warp(xs + j * ldx, (int)a.K, Kpad,
-                                      [&](int k) { return load_as_f32(a.x, a.dtype, row + k); });
-    if (lane == 0) colscale[j] = s;
-  }
-  __syncthreads();
-
   const int64_t n_lo = (int64_t)blockIdx.y * 16 + g, n_hi = n_lo + 8;
   const uint8_t* wbase = a.w + (int64_t)e * a.w_stride;
   const uint8_t* sbase = a.s + (int64_t)e * a.s_stride;
@@ -182,13 +228,20 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
   const uint8_t* shi = sbase + n_hi * rows;
   const __half* xcol = g < ncols ? xs + g * ldx : nullptr;
 
+  // Weights do not depend on the activations: put them in flight first.
   const int nch = Kpad / kChunk;
   const int c0 = (warp * nch) / WARPS, c1 = ((warp + 1) * nch) / WARPS;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   Chunk ring[kRing];
 #pragma unroll
   for (int u = 0; u < kRing; u++)
     if (c0 + u < c1) load_chunk(ring[u], clo, chi, slo, shi, c0 + u, t);
+
+  const int64_t xrow0 = ((int64_t)xi * a.M + mc * 8) * a.K;
+  stage_columns(xs, ldx, ncols, (int)a.K, a.x, a.dtype,
+                [&](int j) { return xrow0 + (int64_t)j * a.K; }, colscale, colmax);
+  __syncthreads();
+
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int base = c0; base < c1; base += kRing) {
 #pragma unroll
     for (int u = 0; u < kRing; u++) {
@@ -261,7 +314,8 @@ __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
   const int ldx = Kpad + kXPad;
   __half* xs = reinterpret_cast<__half*>(smem);
   float* colscale = reinterpret_cast<float*>(xs + ldx);
-  float* red = colscale + 4;
+  int* colmax = reinterpret_cast<int*>(colscale + 8);
+  float* red = colscale + 16;
 
   const int seg = blockIdx.x;
   const int tok = seg / a.kk, slot = seg % a.kk;
@@ -288,14 +342,6 @@ __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  if (warp == 0) {
-    const int64_t row = (int64_t)tok * a.H;
-    const float s = stage_column_warp(xs, (int)a.H, Kpad,
-                                      [&](int k) { return load_as_f32(a.x, a.dtype, row + k); });
-    if (lane == 0) colscale[0] = s;
-  }
-  __syncthreads();
-
   const int64_t i = i0 + g;
   const int64_t rowb = a.H / 2, rows = a.H / 16;
   const uint8_t* clo = i < Irows ? gw + i * rowb : nullptr;
@@ -306,11 +352,16 @@ __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
 
   const int nch = Kpad / kChunk;
   const int c0 = (warp * nch) / WARPS, c1 = ((warp + 1) * nch) / WARPS;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   Chunk ring[kRing];
 #pragma unroll
   for (int u = 0; u < kRing; u++)
     if (c0 + u < c1) load_chunk(ring[u], clo, chi, slo, shi, c0 + u, t);
+
+  const int64_t xrow = (int64_t)tok * a.H;
+  stage_columns(xs, ldx, 1, (int)a.H, a.x, a.dtype, [&](int) { return xrow; }, colscale, colmax);
+  __syncthreads();
+
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int base = c0; base < c1; base += kRing) {
 #pragma unroll
     for (int u = 0; u < kRing; u++) {
@@ -345,49 +396,22 @@ __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
   const int nseg = ntok * a.kk;
   __half* xs = reinterpret_cast<__half*>(smem);
   float* colscale = reinterpret_cast<float*>(xs + (size_t)nseg * ldx);
-  float* red = colscale + 8;
+  int* colmax = reinterpret_cast<int*>(colscale + 8);
+  float* segw = colscale + 16;          // [8 * kk] weight of each segment
+  float* red = segw + 8 * a.kk;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-
-  // Per token: power-of-two prescale over all of its weighted segments.
-  for (int tl = warp; tl < ntok; tl += WARPS) {
-    const int tok = t0 + tl;
-    float m = 0.f;
-    for (int sl = 0; sl < a.kk; sl++) {
-      const bool routed = sl < a.k;
-      const int64_t Iseg = routed ? a.I : a.Is;
-      const float wgt = routed ? a.wts[(int64_t)tok * a.k + sl] * a.scaling : 1.0f;
-      const float* src = a.act + ((int64_t)tok * a.kk + sl) * a.act_ld;
-      for (int k = lane; k < Iseg; k += 32) m = fmaxf(m, fabsf(src[k] * wgt));
-    }
-    m = warp_max(m);
-    const int e = pow2_exponent(m);
-    const float inv = ldexpf(1.0f, -e);
-    for (int sl = 0; sl < a.kk; sl++) {
-      const bool routed = sl < a.k;
-      const int64_t Iseg = routed ? a.I : a.Is;
-      const float wgt = (routed ? a.wts[(int64_t)tok * a.k + sl] * a.scaling : 1.0f) * inv;
-      const float* src = a.act + ((int64_t)tok * a.kk + sl) * a.act_ld;
-      __half* col = xs + (size_t)(tl * a.kk + sl) * ldx;
-      for (int k = lane; k < Ipad; k += 32)
-        col[xs_swz(k)] = __float2half_rn(k < Iseg ? src[k] * wgt : 0.0f);
-    }
-    if (lane == 0) colscale[tl] = ldexpf(1.0f, e);
-  }
-  __syncthreads();
-
   const int64_t h_lo = (int64_t)blockIdx.x * 16 + g, h_hi = h_lo + 8;
   const int nch = Ipad / kChunk;
   const int nunits = nseg * nch;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
 
   // Unit u -> (segment, chunk); row pointers resolved per unit.
   auto unit_ptrs = [&](int u, const uint8_t*& clo, const uint8_t*& chi, const uint8_t*& slo,
                        const uint8_t*& shi, int& ch, const __half*& xcol) {
     const int s = u / nch;
-    ch = u % nch;
-    const int tl = s / a.kk, sl = s % a.kk;
+    ch = u - s * nch;
+    const int tl = s / a.kk, sl = s - tl * a.kk;
     const bool routed = sl < a.k;
     const int64_t Iseg = routed ? a.I : a.Is;
     const uint8_t* wb;
@@ -413,6 +437,7 @@ __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
     xcol = (g == tl) ? xs + (size_t)s * ldx : nullptr;
   };
 
+  // Weights first: the first kRing units of this warp go in flight now.
   Chunk ring[kRing];
 #pragma unroll
   for (int r = 0; r < kRing; r++) {
@@ -425,6 +450,46 @@ __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
       load_chunk(ring[r], clo, chi, slo, shi, ch, t);
     }
   }
+
+  // Stage the weighted activations: segment s of token tl is act[t0+tl][sl] *
+  // w (routing weight * scaling, 1 for the shared expert), all segments of a
+  // token under one power-of-two prescale so they share the MMA column.
+  if (threadIdx.x < 8) colmax[threadIdx.x] = 0;
+  for (int s = threadIdx.x; s < nseg; s += blockDim.x) {
+    const int tl = s / a.kk, sl = s - tl * a.kk;
+    segw[s] = sl < a.k ? a.wts[(int64_t)(t0 + tl) * a.k + sl] * a.scaling : 1.0f;
+  }
+  __syncthreads();
+  const int per = Ipad / 8;
+  const int items = nseg * per;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int s = it / per, v = it - s * per;
+    const int tl = s / a.kk, sl = s - tl * a.kk;
+    const int64_t Iseg = sl < a.k ? a.I : a.Is;
+    if ((int64_t)v * 8 >= Iseg) continue;
+    float f[8];
+    load8(a.act, kF32, ((int64_t)(t0 + tl) * a.kk + sl) * a.act_ld + (int64_t)v * 8, f);
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i] * segw[s]));
+    atomicMax(&colmax[tl], __float_as_int(m));
+  }
+  __syncthreads();
+  if (threadIdx.x < ntok)
+    colscale[threadIdx.x] = ldexpf(1.0f, pow2_exponent(__int_as_float(colmax[threadIdx.x])));
+  __syncthreads();
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int s = it / per, v = it - s * per;
+    const int tl = s / a.kk, sl = s - tl * a.kk;
+    const int64_t Iseg = sl < a.k ? a.I : a.Is;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if ((int64_t)v * 8 < Iseg)
+      load8(a.act, kF32, ((int64_t)(t0 + tl) * a.kk + sl) * a.act_ld + (int64_t)v * 8, f);
+    store8_f16(xs + (size_t)s * ldx, v * 8, f, segw[s] / colscale[tl]);
+  }
+  __syncthreads();
+
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
   for (int base = warp; base < nunits; base += kRing * WARPS) {
 #pragma unroll
     for (int r = 0; r < kRing; r++) {
@@ -468,12 +533,13 @@ constexpr int kGateUpWarps = 4;
 constexpr int kDownWarps = 8;
 
 size_t qmm_smem_bytes(int64_t K) {
-  return (size_t)8 * (K + kXPad) * sizeof(__half) + 8 * sizeof(float) +
+  return (size_t)8 * (K + kXPad) * sizeof(__half) + 16 * sizeof(float) +
          (size_t)(kQmmWarps - 1) * 4 * 32 * sizeof(float);
 }
 
 bool qmm_fast_path_ok(const QmmArgs& a) {
   return a.K % kChunk == 0 && qmm_smem_bytes(a.K) <= 200 * 1024 &&
+         (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
          (reinterpret_cast<uintptr_t>(a.w) & 15) == 0 && (a.w_stride & 15) == 0 &&
          (reinterpret_cast<uintptr_t>(a.s) & 1) == 0 && (a.s_stride & 1) == 0;
 }
@@ -497,7 +563,7 @@ cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream) {
 }
 
 size_t gateup_smem_bytes(int64_t H) {
-  return (size_t)(H + kXPad) * sizeof(__half) + 4 * sizeof(float) +
+  return (size_t)(H + kXPad) * sizeof(__half) + 16 * sizeof(float) +
          (size_t)(kGateUpWarps - 1) * 4 * 32 * sizeof(float);
 }
 
@@ -514,7 +580,7 @@ cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream) {
 }
 
 size_t down_smem_bytes(int64_t Ipad, int kk) {
-  return (size_t)8 * kk * (Ipad + kXPad) * sizeof(__half) + 8 * sizeof(float) +
+  return (size_t)8 * kk * (Ipad + kXPad) * sizeof(__half) + (16 + 8 * kk) * sizeof(float) +
          (size_t)(kDownWarps - 1) * 4 * 32 * sizeof(float);
 }
 
