@@ -63,6 +63,19 @@ NVFP4MOE_API const char* nvfp4_last_error(void);
 typedef void (*nvfp4_error_handler)(const char* msg, void* data);
 NVFP4MOE_API void nvfp4_set_error_handler(nvfp4_error_handler handler, void* data);
 NVFP4MOE_API int nvfp4_version(void);
+
+/* Launch flags of the calling thread (no counterpart in the reference, whose
+ * lazy graph schedules launches itself).  NVFP4_LAUNCH_PDL lets the FIRST
+ * kernel of each following call start before the preceding kernel on the
+ * stream has finished (programmatic dependent launch): it streams its weights
+ * immediately and reads the call's activation input only after the
+ * dependency wait.  Set it only when the preceding kernel is one of this
+ * library's (e.g. a decode chain captured into a CUDA graph) and it produced
+ * nothing else this call reads -- in particular not the routing passed in.
+ * Later kernels inside one call always overlap their predecessor.  Returns
+ * the previous flags. */
+#define NVFP4_LAUNCH_PDL 1
+NVFP4MOE_API int nvfp4_set_launch_flags(int flags);
 /* Synchronises the device, returns and clears the latched device status
  * (NVFP4_OK or NVFP4_ERR_DEVICE_INDEX). */
 NVFP4MOE_API int nvfp4_device_status(void);

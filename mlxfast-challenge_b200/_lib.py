@@ -19,6 +19,7 @@ NVFP4_ERR_WORKSPACE = 4
 NVFP4_ERR_DEVICE_INDEX = 5
 
 NVFP4_BF16, NVFP4_F16, NVFP4_F32 = 0, 1, 2
+NVFP4_LAUNCH_PDL = 1
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -45,6 +46,7 @@ SIGNATURES = {
     "nvfp4_last_error": (ctypes.c_char_p, []),
     "nvfp4_set_error_handler": (None, [_P, _P]),
     "nvfp4_version": (_I, []),
+    "nvfp4_set_launch_flags": (_I, [_I]),
     "nvfp4_device_status": (_I, []),
     "nvfp4_dequantize": (_I, [_P, _I, _P, _P, _I64, _I64, _P]),
     "nvfp4_quantize": (_I, [_P, _P, _P, _I, _I64, _I64, _P]),

@@ -13,6 +13,9 @@
 namespace {
 
 thread_local std::string t_last_error;
+thread_local int t_launch_flags = 0;
+
+bool first_pdl() { return (t_launch_flags & NVFP4_LAUNCH_PDL) != 0; }
 nvfp4_error_handler g_handler = nullptr;
 void* g_handler_data = nullptr;
 
@@ -100,6 +103,12 @@ void nvfp4_set_error_handler(nvfp4_error_handler handler, void* data) {
 
 int nvfp4_version(void) { return 1; }
 
+int nvfp4_set_launch_flags(int flags) {
+  const int old = t_launch_flags;
+  t_launch_flags = flags & NVFP4_LAUNCH_PDL;
+  return old;
+}
+
 int nvfp4_device_status(void) {
   int st = 0;
   cudaError_t e = cudaDeviceSynchronize();
@@ -179,7 +188,8 @@ int nvfp4_gather_qmm(void* out, const void* x, int dtype, const uint32_t* w,
   a.n_experts = n_experts;
   if ((int64_t)a.P * a.mchunks > 65535 * 1024LL)
     return fail(NVFP4_ERR_UNSUPPORTED, "[gather_qmm] too many pairs.");
-  return check_cuda(nvfp4::launch_qmm_gather(a, (cudaStream_t)stream), "gather_qmm");
+  return check_cuda(nvfp4::launch_qmm_gather(a, (cudaStream_t)stream, first_pdl()),
+                    "gather_qmm");
 }
 
 int nvfp4_quantized_matmul(void* y, const void* x, int dtype, const uint32_t* w,
@@ -240,7 +250,7 @@ int moe_router_topk(uint32_t* inds, float* weights, const void* x, int dtype,
   a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + L.partial_off);
   a.inds = inds;
   a.wts = weights;
-  return check_cuda(nvfp4::launch_router(a, (cudaStream_t)stream), "router");
+  return check_cuda(nvfp4::launch_router(a, (cudaStream_t)stream, first_pdl()), "router");
 }
 
 size_t moe_block_workspace_size(const moe_layer_desc* layer, int64_t T) {
@@ -254,6 +264,12 @@ int moe_workspace_init(void* workspace, size_t bytes, nvfp4_stream stream) {
 }
 
 static int check_layer(const char* op, const moe_layer_desc* L, int dtype, int64_t T);
+static int gate_up_impl(float* act, int64_t act_ld, const void* x, int dtype, int64_t T,
+                        const moe_layer_desc* L, const uint32_t* inds, nvfp4_stream stream,
+                        bool pdl, bool inds_static);
+static int down_impl(void* y, const float* act, int64_t act_ld, const void* residual, int dtype,
+                     int64_t T, const moe_layer_desc* L, const uint32_t* inds,
+                     const float* weights, nvfp4_stream stream, bool pdl);
 
 int moe_block_forward(void* y, const void* x, const void* residual, int dtype, int64_t T,
                       const moe_layer_desc* L, const uint32_t* inds_in, const float* weights_in,
@@ -296,7 +312,7 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
     ra.partial = reinterpret_cast<float*>(ws + B.router.partial_off);
     ra.inds = ri;
     ra.wts = rw;
-    if (int r = check_cuda(nvfp4::launch_router(ra, s), op)) return r;
+    if (int r = check_cuda(nvfp4::launch_router(ra, s, first_pdl()), op)) return r;
     inds = ri;
     wts = rw;
   } else if (inds_out || weights_out) {
@@ -310,8 +326,15 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
       return check_cuda(cudaGetLastError(), op);
   }
   float* act = reinterpret_cast<float*>(ws + B.act_off);
-  if (int r = moe_gate_up_swiglu(act, B.act_ld, x, dtype, T, L, inds, stream)) return r;
-  return moe_down_combine(y, act, B.act_ld, residual, dtype, T, L, inds, wts, stream);
+  // Kernels after the first overlap their predecessor (PDL).  When the router
+  // ran, the gate/up kernel reads the routing only after its dependency wait.
+  const bool routed_here = inds_in == nullptr;
+  const bool copied = inds_in && (inds_out || weights_out);
+  if (int r = gate_up_impl(act, B.act_ld, x, dtype, T, L, inds, stream,
+                           /*pdl=*/!copied && (routed_here || first_pdl()),
+                           /*inds_static=*/!routed_here))
+    return r;
+  return down_impl(y, act, B.act_ld, residual, dtype, T, L, inds, wts, stream, /*pdl=*/true);
 }
 
 static int check_layer(const char* op, const moe_layer_desc* L, int dtype, int64_t T) {
@@ -331,6 +354,12 @@ static int check_layer(const char* op, const moe_layer_desc* L, int dtype, int64
 
 int moe_gate_up_swiglu(float* act, int64_t act_ld, const void* x, int dtype, int64_t T,
                        const moe_layer_desc* L, const uint32_t* inds, nvfp4_stream stream) {
+  return gate_up_impl(act, act_ld, x, dtype, T, L, inds, stream, first_pdl(), true);
+}
+
+static int gate_up_impl(float* act, int64_t act_ld, const void* x, int dtype, int64_t T,
+                        const moe_layer_desc* L, const uint32_t* inds, nvfp4_stream stream,
+                        bool pdl, bool inds_static) {
   const char* op = "moe_gate_up_swiglu";
   if (int r = check_layer(op, L, dtype, T)) return r;
   if (T == 0) return NVFP4_OK;
@@ -373,12 +402,19 @@ int moe_gate_up_swiglu(float* act, int64_t act_ld, const void* x, int dtype, int
   }
   ga.act = act;
   ga.act_ld = act_ld;
-  return check_cuda(nvfp4::launch_moe_gateup(ga, (cudaStream_t)stream), op);
+  ga.inds_static = inds_static ? 1 : 0;
+  return check_cuda(nvfp4::launch_moe_gateup(ga, (cudaStream_t)stream, pdl), op);
 }
 
 int moe_down_combine(void* y, const float* act, int64_t act_ld, const void* residual, int dtype,
                      int64_t T, const moe_layer_desc* L, const uint32_t* inds,
                      const float* weights, nvfp4_stream stream) {
+  return down_impl(y, act, act_ld, residual, dtype, T, L, inds, weights, stream, first_pdl());
+}
+
+static int down_impl(void* y, const float* act, int64_t act_ld, const void* residual, int dtype,
+                     int64_t T, const moe_layer_desc* L, const uint32_t* inds,
+                     const float* weights, nvfp4_stream stream, bool pdl) {
   const char* op = "moe_down_combine";
   if (int r = check_layer(op, L, dtype, T)) return r;
   if (T == 0) return NVFP4_OK;
@@ -421,7 +457,11 @@ int moe_down_combine(void* y, const float* act, int64_t act_ld, const void* resi
   da.residual = residual;
   da.y = y;
   da.dtype = dtype;
-  return check_cuda(nvfp4::launch_moe_down(da, (cudaStream_t)stream), op);
+  // The down kernel always follows a gate/up kernel (ours or, under
+  // NVFP4_LAUNCH_PDL, by the caller's contract), which waited for whatever
+  // produced the routing before letting this grid launch.
+  da.inds_static = 1;
+  return check_cuda(nvfp4::launch_moe_down(da, (cudaStream_t)stream, pdl), op);
 }
 
 }  // extern "C"

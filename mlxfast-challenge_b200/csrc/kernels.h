@@ -34,6 +34,7 @@ struct GateUpArgs {
   const uint8_t *sgw, *sgs, *suw, *sus;  // shared expert (null when absent)
   float* act;  // [T*kk, act_ld]
   int64_t act_ld;
+  int inds_static;  // inds were not written by the immediately preceding kernel
 };
 
 struct DownArgs {
@@ -50,6 +51,8 @@ struct DownArgs {
   const void* residual;
   void* y;
   int dtype;
+  int inds_static;      // routing complete before this grid starts (see qmv.cu)
+  int max_seg_per_cta;  // set by the launcher
 };
 
 struct RouterArgs {
@@ -67,12 +70,12 @@ struct RouterArgs {
 
 size_t qmm_smem_bytes(int64_t K);
 bool qmm_fast_path_ok(const QmmArgs& a);
-cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream);
+cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream, bool pdl);
 size_t gateup_smem_bytes(int64_t H);
-cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream);
+cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream, bool pdl);
 size_t down_smem_bytes(int64_t Ipad, int kk);
-cudaError_t launch_moe_down(const DownArgs& a, cudaStream_t stream);
-cudaError_t launch_router(const RouterArgs& a, cudaStream_t stream);
+cudaError_t launch_moe_down(const DownArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t stream, bool pdl);
 int router_ksplit(int64_t H);
 cudaError_t launch_dequantize(void* out, int dtype, const uint8_t* w, const uint8_t* s,
                               int64_t rows, int64_t K, cudaStream_t stream);

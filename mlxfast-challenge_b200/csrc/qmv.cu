@@ -8,13 +8,20 @@
 // (rows g and g+8, g = lane/4, t = lane%4) and one 16-bit scale load per row,
 // converts E2M1 pairs to f16x2 with the hardware converter, folds the group
 // scale in with one HMUL2 (exact: see common.cuh) and feeds mma.sync
-// m16n8k16 (f16 x f16 -> f32).  K inside a chunk is permuted: thread t's
-// 32 codes are actual K [32t, 32t+32) and MMA i takes its codes 4i..4i+3;
-// the activation tile in shared memory is laid out with the same permutation
-// (plus an XOR swizzle that keeps the 128-bit B loads bank-conflict free).
-// Activations enter as f16 scaled by a per-column power of two (max |x| is
-// mapped into [1,2)), so no input range can overflow f16; the power is
-// re-applied to the f32 result.  Loads run 4 chunks ahead of the MMAs.
+// m16n8k16 (f16 x f16 -> f32) into two independent accumulator sets.  K
+// inside a chunk is permuted: thread t's 32 codes are actual K [32t, 32t+32)
+// and MMA i takes its codes 4i..4i+3; the activation tile in shared memory is
+// laid out with the same permutation (plus an XOR swizzle that keeps the
+// 128-bit B loads bank-conflict free).  Activations enter as f16 scaled by a
+// per-column power of two (max |x| is mapped into [1,2)), so no input range
+// can overflow f16; the power is re-applied to the f32 result.
+//
+// Latency hiding: every kernel puts its weight loads in flight before it
+// reads anything a preceding kernel produced, and supports programmatic
+// dependent launch (PDL): it waits on the preceding grid (griddepcontrol.wait)
+// only before touching that grid's outputs, and lets its own dependents
+// launch right after that wait.  So in a stream / CUDA graph of these
+// kernels the next kernel's weight streaming overlaps the current one.
 //
 // Reference semantics followed: fp_qmm_t (backend/cpu/quantized.cpp:491-533)
 // for every product, fp_bs_qmm_dispatch_mode (:805-844) for the gather, the
@@ -22,8 +29,12 @@
 // (VLM/MLXLMCommon/SwitchLayers.swift:532-580) and the Laguna sparse block
 // combine  y = scaling * sum_j w_j * expert_j(x) + shared(x)
 // (VLM/MLXLLM/Models/Laguna.swift:204-212).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace nvfp4 {
 
@@ -38,6 +49,12 @@ constexpr int kRing = 4;          // chunks in flight per warp
 __device__ int g_device_error = 0;
 
 __device__ __forceinline__ void flag_error(int code) { atomicCAS(&g_device_error, 0, code); }
+
+// PDL hooks (no-ops when the grid was launched without the PDL attribute).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // Physical f16 index of logical element k of a staged column.
 __device__ __forceinline__ int xs_swz(int k) {
@@ -71,8 +88,20 @@ __device__ __forceinline__ void load_chunk(Chunk& c, const uint8_t* clo, const u
   }
 }
 
-__device__ __forceinline__ void compute_chunk(float (&acc)[4], const Chunk& c,
-                                              const __half* xcol, int ch, int t) {
+struct Acc {
+  float a[4], b[4];
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int r = 0; r < 4; r++) a[r] = b[r] = 0.f;
+  }
+  __device__ __forceinline__ void fold(float (&out)[4]) const {
+#pragma unroll
+    for (int r = 0; r < 4; r++) out[r] = a[r] + b[r];
+  }
+};
+
+__device__ __forceinline__ void compute_chunk(Acc& acc, const Chunk& c, const __half* xcol,
+                                              int ch, int t) {
   uint32_t xb[16];
   if (xcol) {
     const uint4* base = reinterpret_cast<const uint4*>(xcol + ch * kChunk);
@@ -99,9 +128,9 @@ __device__ __forceinline__ void compute_chunk(float (&acc)[4], const Chunk& c,
     e2m1x8_to_f16x2x4(wl[j], hl);
     e2m1x8_to_f16x2x4(wh[j], hh);
     const uint32_t s_l = sl[j >> 1], s_h = sh[j >> 1];
-    mma_f16_16816(acc, hmul2_u32(hl[0], s_l), hmul2_u32(hh[0], s_h), hmul2_u32(hl[1], s_l),
+    mma_f16_16816(acc.a, hmul2_u32(hl[0], s_l), hmul2_u32(hh[0], s_h), hmul2_u32(hl[1], s_l),
                   hmul2_u32(hh[1], s_h), xb[4 * j], xb[4 * j + 1]);
-    mma_f16_16816(acc, hmul2_u32(hl[2], s_l), hmul2_u32(hh[2], s_h), hmul2_u32(hl[3], s_l),
+    mma_f16_16816(acc.b, hmul2_u32(hl[2], s_l), hmul2_u32(hh[2], s_h), hmul2_u32(hl[3], s_l),
                   hmul2_u32(hh[3], s_h), xb[4 * j + 2], xb[4 * j + 3]);
   }
 }
@@ -142,10 +171,19 @@ __device__ __forceinline__ void store8_f16(__half* col, int k, const float (&f)[
   *reinterpret_cast<uint4*>(col + xs_swz(k)) = make_uint4(h[0], h[1], h[2], h[3]);
 }
 
+// Max over a warp, then one shared atomic per warp and column.  Non-negative
+// floats order like their bit patterns.
+__device__ __forceinline__ void warp_atomic_max(int* slot, float m, bool active) {
+  m = warp_max(active ? m : 0.f);
+  if ((threadIdx.x & 31) == 0) atomicMax(slot, __float_as_int(m));
+}
+
 // Block-cooperative staging of `ncols` activation columns (column j is the K
 // elements at element offset off(j)), each as f16(v * 2^-e_j) with max |v| *
 // 2^-e_j in [1, 2).  colscale[j] = 2^e_j.  Two passes over the (L1/L2-hot)
-// activations: maxima via shared atomics, then the scaled f16 copy.
+// activations: maxima via shared atomics, then the scaled f16 copy.  The
+// items of one column are contiguous in `it`, so a warp's items belong to a
+// short run of columns; the max is reduced per column of that run.
 template <typename Off>
 __device__ void stage_columns(__half* xs, int ldx, int ncols, int K, const void* x, int dtype,
                               Off off, float* colscale, int* colmax) {
@@ -153,18 +191,25 @@ __device__ void stage_columns(__half* xs, int ldx, int ncols, int K, const void*
   __syncthreads();
   const int per = K / 8;
   const int items = ncols * per;
-  for (int it = threadIdx.x; it < items; it += blockDim.x) {
-    const int j = it / per, v = it - j * per;
-    float f[8];
-    load8(x, dtype, off(j) + (int64_t)v * 8, f);
+  const int rounds = (items + blockDim.x - 1) / blockDim.x;
+  for (int r = 0; r < rounds; r++) {
+    const int it = r * blockDim.x + threadIdx.x;
+    const bool ok = it < items;
+    const int j = ok ? it / per : 0;
     float m = 0.f;
+    if (ok) {
+      float f[8];
+      load8(x, dtype, off(j) + (int64_t)(it - j * per) * 8, f);
 #pragma unroll
-    for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i]));
-    atomicMax(&colmax[j], __float_as_int(m));
+      for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i]));
+    }
+    const int j0 = __shfl_sync(0xffffffffu, j, 0);
+    const int j1 = __shfl_sync(0xffffffffu, ok ? j : j0, 31);
+    for (int jj = j0; jj <= j1; jj++) warp_atomic_max(&colmax[jj], m, ok && j == jj);
   }
   __syncthreads();
-  if (threadIdx.x < ncols) colscale[threadIdx.x] =
-      ldexpf(1.0f, pow2_exponent(__int_as_float(colmax[threadIdx.x])));
+  if (threadIdx.x < ncols)
+    colscale[threadIdx.x] = ldexpf(1.0f, pow2_exponent(__int_as_float(colmax[threadIdx.x])));
   __syncthreads();
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
     const int j = it / per, v = it - j * per;
@@ -193,6 +238,24 @@ __device__ __forceinline__ void reduce_to_warp0(float (&acc)[4], float* red) {
   }
 }
 
+// Chunks [c0, c1) of one warp's tile: the first kRing loads were issued by
+// the caller into `ring`; later ones are issued as slots free up.
+__device__ __forceinline__ void run_chunks(Acc& acc, Chunk (&ring)[kRing], const uint8_t* clo,
+                                           const uint8_t* chi, const uint8_t* slo,
+                                           const uint8_t* shi, const __half* xcol, int c0,
+                                           int c1, int t) {
+  for (int base = c0; base < c1; base += kRing) {
+#pragma unroll
+    for (int u = 0; u < kRing; u++) {
+      const int ch = base + u;
+      if (ch < c1) {
+        compute_chunk(acc, ring[u], xcol, ch, t);
+        if (ch + kRing < c1) load_chunk(ring[u], clo, chi, slo, shi, ch + kRing, t);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Gather QMM (also the dense quantized_matmul with one expert and no index).
 // grid = (P * mchunks, ceil(N/16)); segment = (pair p, 8-row chunk of M).
@@ -206,6 +269,9 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
   int* colmax = reinterpret_cast<int*>(colscale + 8);
   float* red = colscale + 16;
 
+  // Indices may come from the preceding kernel: wait first.
+  pdl_wait();
+  pdl_trigger();
   const int seg = blockIdx.x;
   const int p = seg / a.mchunks, mc = seg % a.mchunks;
   const uint32_t e = a.rhs ? a.rhs[p] : 0u;
@@ -228,7 +294,6 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
   const uint8_t* shi = sbase + n_hi * rows;
   const __half* xcol = g < ncols ? xs + g * ldx : nullptr;
 
-  // Weights do not depend on the activations: put them in flight first.
   const int nch = Kpad / kChunk;
   const int c0 = (warp * nch) / WARPS, c1 = ((warp + 1) * nch) / WARPS;
   Chunk ring[kRing];
@@ -241,18 +306,12 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
                 [&](int j) { return xrow0 + (int64_t)j * a.K; }, colscale, colmax);
   __syncthreads();
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int base = c0; base < c1; base += kRing) {
-#pragma unroll
-    for (int u = 0; u < kRing; u++) {
-      const int ch = base + u;
-      if (ch < c1) {
-        compute_chunk(acc, ring[u], xcol, ch, t);
-        if (ch + kRing < c1) load_chunk(ring[u], clo, chi, slo, shi, ch + kRing, t);
-      }
-    }
-  }
-  reduce_to_warp0<WARPS>(acc, red);
+  Acc acc;
+  acc.zero();
+  run_chunks(acc, ring, clo, chi, slo, shi, xcol, c0, c1, t);
+  float d[4];
+  acc.fold(d);
+  reduce_to_warp0<WARPS>(d, red);
   if (warp == 0) {
 #pragma unroll
     for (int r = 0; r < 4; r++) {
@@ -260,7 +319,7 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
       const int64_t n = (r < 2) ? n_lo : n_hi;
       if (col < ncols && n < a.N) {
         const int64_t orow = (int64_t)p * a.M + mc * 8 + col;
-        store_from_f32(a.out, a.dtype, orow * a.N + n, acc[r] * colscale[col]);
+        store_from_f32(a.out, a.dtype, orow * a.N + n, d[r] * colscale[col]);
       }
     }
   }
@@ -270,6 +329,8 @@ __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
 // multiple of 128, misaligned pointers): one thread per output element, f32
 // accumulation in the reference's group order.
 __global__ void qmm_gather_generic_kernel(QmmArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = a.P * (int64_t)a.M * a.N;
   const int64_t rowb = a.K / 2, rows = a.K / 16;
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -293,8 +354,7 @@ __global__ void qmm_gather_generic_kernel(QmmArgs a) {
       for (int j = 0; j < 16; j++) {
         const int64_t k = gidx * 16 + j;
         const int code = (wr[k / 2] >> (4 * (k & 1))) & 15;
-        const float lut = fp4_to_f32(code);
-        gs += load_as_f32(a.x, a.dtype, xrow + k) * lut;
+        gs += load_as_f32(a.x, a.dtype, xrow + k) * fp4_to_f32(code);
       }
       sum += scale * gs;
     }
@@ -306,7 +366,8 @@ __global__ void qmm_gather_generic_kernel(QmmArgs a) {
 // Routed (and shared) expert gate/up projections fused with SwiGLU.
 // grid = (T * kk, ceil(Imax/8)), kk = k (+1 with a shared expert).  A warp
 // tile holds gate rows i0..i0+7 in MMA rows 0..7 and the matching up rows in
-// MMA rows 8..15, so every thread ends with (gate, up) of one row.
+// MMA rows 8..15, so every thread ends with (gate, up) of one row.  The
+// WARPS warps of a CTA split K.
 template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -322,12 +383,19 @@ __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
   const bool routed = slot < a.k;
   const int64_t Irows = routed ? a.I : a.Is;
   const int64_t i0 = (int64_t)blockIdx.y * 8;
-  if (i0 >= Irows) return;
+  if (i0 >= Irows) {
+    pdl_trigger();
+    return;
+  }
+  // Routing produced by the preceding kernel is only read after the wait.
+  if (routed && !a.inds_static) pdl_wait();
   const uint8_t *gw, *gs, *uw, *us;
   if (routed) {
     const uint32_t e = a.inds[(int64_t)tok * a.k + slot];
     if (e >= (uint32_t)a.E) {
       if (threadIdx.x == 0) flag_error(2);
+      pdl_wait();
+      pdl_trigger();
       return;
     }
     gw = a.gw + (int64_t)e * a.w_stride;
@@ -357,60 +425,67 @@ __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
   for (int u = 0; u < kRing; u++)
     if (c0 + u < c1) load_chunk(ring[u], clo, chi, slo, shi, c0 + u, t);
 
+  // x is the preceding kernel's output.
+  pdl_wait();
+  pdl_trigger();
   const int64_t xrow = (int64_t)tok * a.H;
   stage_columns(xs, ldx, 1, (int)a.H, a.x, a.dtype, [&](int) { return xrow; }, colscale, colmax);
   __syncthreads();
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int base = c0; base < c1; base += kRing) {
-#pragma unroll
-    for (int u = 0; u < kRing; u++) {
-      const int ch = base + u;
-      if (ch < c1) {
-        compute_chunk(acc, ring[u], xcol, ch, t);
-        if (ch + kRing < c1) load_chunk(ring[u], clo, chi, slo, shi, ch + kRing, t);
-      }
-    }
-  }
-  reduce_to_warp0<WARPS>(acc, red);
+  Acc acc;
+  acc.zero();
+  run_chunks(acc, ring, clo, chi, slo, shi, xcol, c0, c1, t);
+  float d[4];
+  acc.fold(d);
+  reduce_to_warp0<WARPS>(d, red);
   if (warp == 0 && t == 0 && i < Irows) {
     const float cs = colscale[0];
-    const float gate = acc[0] * cs, up = acc[2] * cs;
+    const float gate = d[0] * cs, up = d[2] * cs;
     a.act[(int64_t)seg * a.act_ld + i] = silu_ref(gate) * up;
   }
 }
 
 // ---------------------------------------------------------------------------
 // Down projections of every (token, slot) segment plus the shared expert,
-// weighted, summed, scaled and added to the residual in one pass.
-// grid = (ceil(H/16), ceil(T/8)).  Each segment is one K-range of the
-// accumulation; its activation is pre-multiplied by w_j * scaling (1 for the
-// shared expert) and only the owning token's MMA column is non-zero.
-template <int WARPS>
+// weighted, summed, scaled and added to the residual.
+// grid = (ceil(H/16) * CL, ceil(T/8)) with thread-block clusters of CL CTAs
+// along x: the CL CTAs of a cluster share one 16-row output tile and take
+// every CL-th segment of its K range (segment = one expert's I-long down
+// row for one token).  Each CTA stages only its own segments, pre-multiplied
+// by w_j * scaling (1 for the shared expert) under one power-of-two prescale
+// per token; only the owning token's MMA column is non-zero.  The CL partial
+// tiles are summed in CTA rank 0 through distributed shared memory, in rank
+// order (deterministic).
+template <int WARPS, int CL>
 __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
   const int Ipad = a.Ipad;
   const int ldx = Ipad + kXPad;
   const int t0 = blockIdx.y * 8;
   const int ntok = (int)(a.T - t0 < 8 ? a.T - t0 : 8);
-  const int nseg = ntok * a.kk;
+  const int nseg_all = ntok * a.kk;
+  const int nseg = nseg_all > rank ? (nseg_all - rank + CL - 1) / CL : 0;  // my segments
   __half* xs = reinterpret_cast<__half*>(smem);
-  float* colscale = reinterpret_cast<float*>(xs + (size_t)nseg * ldx);
+  float* colscale = reinterpret_cast<float*>(xs + (size_t)a.max_seg_per_cta * ldx);
   int* colmax = reinterpret_cast<int*>(colscale + 8);
-  float* segw = colscale + 16;          // [8 * kk] weight of each segment
-  float* red = segw + 8 * a.kk;
+  float* segw = colscale + 16;                      // [max_seg_per_cta]
+  float* red = segw + a.max_seg_per_cta;            // [(WARPS-1)*4*32]
+  float* cred = red + (WARPS - 1) * 4 * 32;         // [(CL-1)*4*32], rank 0 only
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int64_t h_lo = (int64_t)blockIdx.x * 16 + g, h_hi = h_lo + 8;
+  const int64_t h_lo = (int64_t)(blockIdx.x / CL) * 16 + g, h_hi = h_lo + 8;
   const int nch = Ipad / kChunk;
   const int nunits = nseg * nch;
 
-  // Unit u -> (segment, chunk); row pointers resolved per unit.
+  // Local segment ls -> global segment rank + ls*CL -> (token, slot).
   auto unit_ptrs = [&](int u, const uint8_t*& clo, const uint8_t*& chi, const uint8_t*& slo,
                        const uint8_t*& shi, int& ch, const __half*& xcol) {
-    const int s = u / nch;
-    ch = u - s * nch;
+    const int ls = u / nch;
+    ch = u - ls * nch;
+    const int s = rank + ls * CL;
     const int tl = s / a.kk, sl = s - tl * a.kk;
     const bool routed = sl < a.k;
     const int64_t Iseg = routed ? a.I : a.Is;
@@ -434,10 +509,13 @@ __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
     chi = (chunk_ok && h_hi < a.H) ? wb + h_hi * rowb : nullptr;
     slo = sb + h_lo * rows;
     shi = sb + h_hi * rows;
-    xcol = (g == tl) ? xs + (size_t)s * ldx : nullptr;
+    xcol = (g == tl) ? xs + (size_t)ls * ldx : nullptr;
   };
 
-  // Weights first: the first kRing units of this warp go in flight now.
+  // The routing was written before the gate/up kernel this grid follows
+  // started its own wait, so it is complete once this grid runs: the weights
+  // go in flight before waiting for the gate/up output.
+  if (!a.inds_static) pdl_wait();
   Chunk ring[kRing];
 #pragma unroll
   for (int r = 0; r < kRing; r++) {
@@ -450,46 +528,60 @@ __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
       load_chunk(ring[r], clo, chi, slo, shi, ch, t);
     }
   }
-
-  // Stage the weighted activations: segment s of token tl is act[t0+tl][sl] *
-  // w (routing weight * scaling, 1 for the shared expert), all segments of a
-  // token under one power-of-two prescale so they share the MMA column.
   if (threadIdx.x < 8) colmax[threadIdx.x] = 0;
-  for (int s = threadIdx.x; s < nseg; s += blockDim.x) {
+  for (int ls = threadIdx.x; ls < nseg; ls += blockDim.x) {
+    const int s = rank + ls * CL;
     const int tl = s / a.kk, sl = s - tl * a.kk;
-    segw[s] = sl < a.k ? a.wts[(int64_t)(t0 + tl) * a.k + sl] * a.scaling : 1.0f;
+    segw[ls] = sl < a.k ? a.wts[(int64_t)(t0 + tl) * a.k + sl] * a.scaling : 1.0f;
   }
+  pdl_wait();  // act is the preceding kernel's output
+  pdl_trigger();
   __syncthreads();
+
+  // Stage my segments: per-token max of |act * w| over my segments, then f16.
   const int per = Ipad / 8;
   const int items = nseg * per;
-  for (int it = threadIdx.x; it < items; it += blockDim.x) {
-    const int s = it / per, v = it - s * per;
-    const int tl = s / a.kk, sl = s - tl * a.kk;
-    const int64_t Iseg = sl < a.k ? a.I : a.Is;
-    if ((int64_t)v * 8 >= Iseg) continue;
-    float f[8];
-    load8(a.act, kF32, ((int64_t)(t0 + tl) * a.kk + sl) * a.act_ld + (int64_t)v * 8, f);
+  const int rounds = (items + blockDim.x - 1) / blockDim.x;
+  for (int r = 0; r < rounds; r++) {
+    const int it = r * blockDim.x + threadIdx.x;
+    const bool ok = it < items;
+    int tl = 0;
     float m = 0.f;
+    if (ok) {
+      const int ls = it / per, v = it - ls * per;
+      const int s = rank + ls * CL;
+      tl = s / a.kk;
+      const int sl = s - tl * a.kk;
+      const int64_t Iseg = sl < a.k ? a.I : a.Is;
+      if ((int64_t)v * 8 < Iseg) {
+        float f[8];
+        load8(a.act, kF32, ((int64_t)(t0 + tl) * a.kk + sl) * a.act_ld + (int64_t)v * 8, f);
 #pragma unroll
-    for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i] * segw[s]));
-    atomicMax(&colmax[tl], __float_as_int(m));
+        for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i] * segw[ls]));
+      }
+    }
+    const int j0 = __shfl_sync(0xffffffffu, tl, 0);
+    const int j1 = __shfl_sync(0xffffffffu, ok ? tl : j0, 31);
+    for (int jj = j0; jj <= j1; jj++) warp_atomic_max(&colmax[jj], m, ok && tl == jj);
   }
   __syncthreads();
   if (threadIdx.x < ntok)
     colscale[threadIdx.x] = ldexpf(1.0f, pow2_exponent(__int_as_float(colmax[threadIdx.x])));
   __syncthreads();
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
-    const int s = it / per, v = it - s * per;
+    const int ls = it / per, v = it - ls * per;
+    const int s = rank + ls * CL;
     const int tl = s / a.kk, sl = s - tl * a.kk;
     const int64_t Iseg = sl < a.k ? a.I : a.Is;
     float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if ((int64_t)v * 8 < Iseg)
       load8(a.act, kF32, ((int64_t)(t0 + tl) * a.kk + sl) * a.act_ld + (int64_t)v * 8, f);
-    store8_f16(xs + (size_t)s * ldx, v * 8, f, segw[s] / colscale[tl]);
+    store8_f16(xs + (size_t)ls * ldx, v * 8, f, segw[ls] / colscale[tl]);
   }
   __syncthreads();
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  Acc acc;
+  acc.zero();
   for (int base = warp; base < nunits; base += kRing * WARPS) {
 #pragma unroll
     for (int r = 0; r < kRing; r++) {
@@ -508,15 +600,35 @@ __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
       }
     }
   }
-  reduce_to_warp0<WARPS>(acc, red);
+  float d[4];
+  acc.fold(d);
+  reduce_to_warp0<WARPS>(d, red);
+  // Apply this CTA's per-token prescale, then combine the cluster in rank 0.
   if (warp == 0) {
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int col = 2 * t + (r & 1);
+      d[r] = col < ntok ? d[r] * colscale[col] : 0.f;
+    }
+    if (rank > 0) {
+      float* dst = cluster.map_shared_rank(cred, 0);
+#pragma unroll
+      for (int r = 0; r < 4; r++) dst[((rank - 1) * 4 + r) * 32 + lane] = d[r];
+    }
+  }
+  cluster.sync();
+  if (rank == 0 && warp == 0) {
+#pragma unroll 1
+    for (int q = 1; q < CL; q++)
+#pragma unroll
+      for (int r = 0; r < 4; r++) d[r] += cred[((q - 1) * 4 + r) * 32 + lane];
 #pragma unroll
     for (int r = 0; r < 4; r++) {
       const int col = 2 * t + (r & 1);
       const int64_t h = (r < 2) ? h_lo : h_hi;
       if (col < ntok && h < a.H) {
         const int64_t o = (int64_t)(t0 + col) * a.H + h;
-        float v = acc[r] * colscale[col];
+        float v = d[r];
         if (a.residual) v += load_as_f32(a.residual, a.dtype, o);
         store_from_f32(a.y, a.dtype, o, v);
       }
@@ -529,8 +641,37 @@ __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
 // ---------------------------------------------------------------------------
 // Host launchers.
 constexpr int kQmmWarps = 4;
-constexpr int kGateUpWarps = 4;
-constexpr int kDownWarps = 8;
+constexpr int kGateUpWarps = 8;
+constexpr int kDownWarps = 4;
+constexpr int kDownCluster = 4;
+
+// Launch with optional programmatic dependent launch and cluster shape.
+template <typename Kern, typename Args>
+static cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             bool pdl, int cluster_x, const Args& args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  if (pdl) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
+  if (cluster_x > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = cluster_x;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = 1;
+    n++;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, args);
+}
 
 size_t qmm_smem_bytes(int64_t K) {
   return (size_t)8 * (K + kXPad) * sizeof(__half) + 16 * sizeof(float) +
@@ -544,7 +685,7 @@ bool qmm_fast_path_ok(const QmmArgs& a) {
          (reinterpret_cast<uintptr_t>(a.s) & 1) == 0 && (a.s_stride & 1) == 0;
 }
 
-cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream) {
+cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream, bool pdl) {
   if (a.P == 0 || a.M == 0 || a.N == 0) return cudaSuccess;
   if (qmm_fast_path_ok(a)) {
     const size_t smem = qmm_smem_bytes(a.K);
@@ -552,12 +693,15 @@ cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream) {
     cudaError_t err = ensure_smem(kern, smem);
     if (err != cudaSuccess) return err;
     dim3 grid((unsigned)(a.P * a.mchunks), (unsigned)((a.N + 15) / 16));
-    kern<<<grid, kQmmWarps * 32, smem, stream>>>(a);
+    err = launch_ex(kern, grid, dim3(kQmmWarps * 32), smem, stream, pdl, 1, a);
+    if (err != cudaSuccess) return err;
   } else {
     const int64_t total = a.P * (int64_t)a.M * a.N;
     const int threads = 256;
     const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 64);
-    qmm_gather_generic_kernel<<<(unsigned)blocks, threads, 0, stream>>>(a);
+    cudaError_t err = launch_ex(qmm_gather_generic_kernel, dim3((unsigned)blocks), dim3(threads),
+                                0, stream, pdl, 1, a);
+    if (err != cudaSuccess) return err;
   }
   return cudaGetLastError();
 }
@@ -567,7 +711,7 @@ size_t gateup_smem_bytes(int64_t H) {
          (size_t)(kGateUpWarps - 1) * 4 * 32 * sizeof(float);
 }
 
-cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream) {
+cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream, bool pdl) {
   if (a.T == 0) return cudaSuccess;
   const size_t smem = gateup_smem_bytes(a.H);
   auto kern = moe_gateup_kernel<kGateUpWarps>;
@@ -575,23 +719,30 @@ cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream) {
   if (err != cudaSuccess) return err;
   const int64_t Imax = std::max(a.I, a.Is);
   dim3 grid((unsigned)(a.T * a.kk), (unsigned)((Imax + 7) / 8));
-  kern<<<grid, kGateUpWarps * 32, smem, stream>>>(a);
+  err = launch_ex(kern, grid, dim3(kGateUpWarps * 32), smem, stream, pdl, 1, a);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 
+int down_max_seg_per_cta(int kk) { return (8 * kk + kDownCluster - 1) / kDownCluster; }
+
 size_t down_smem_bytes(int64_t Ipad, int kk) {
-  return (size_t)8 * kk * (Ipad + kXPad) * sizeof(__half) + (16 + 8 * kk) * sizeof(float) +
-         (size_t)(kDownWarps - 1) * 4 * 32 * sizeof(float);
+  const int ms = down_max_seg_per_cta(kk);
+  return (size_t)ms * (Ipad + kXPad) * sizeof(__half) + (16 + ms) * sizeof(float) +
+         (size_t)(kDownWarps - 1 + kDownCluster - 1) * 4 * 32 * sizeof(float);
 }
 
-cudaError_t launch_moe_down(const DownArgs& a, cudaStream_t stream) {
-  if (a.T == 0) return cudaSuccess;
+cudaError_t launch_moe_down(const DownArgs& a_in, cudaStream_t stream, bool pdl) {
+  if (a_in.T == 0) return cudaSuccess;
+  DownArgs a = a_in;
+  a.max_seg_per_cta = down_max_seg_per_cta(a.kk);
   const size_t smem = down_smem_bytes(a.Ipad, a.kk);
-  auto kern = moe_down_kernel<kDownWarps>;
+  auto kern = moe_down_kernel<kDownWarps, kDownCluster>;
   cudaError_t err = ensure_smem(kern, smem);
   if (err != cudaSuccess) return err;
-  dim3 grid((unsigned)((a.H + 15) / 16), (unsigned)((a.T + 7) / 8));
-  kern<<<grid, kDownWarps * 32, smem, stream>>>(a);
+  dim3 grid((unsigned)((a.H + 15) / 16 * kDownCluster), (unsigned)((a.T + 7) / 8));
+  err = launch_ex(kern, grid, dim3(kDownWarps * 32), smem, stream, pdl, kDownCluster, a);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

@@ -45,6 +45,9 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
   const int ntok = (int)(a.T - t0 < 8 ? a.T - t0 : 8);
   const int64_t k0 = (int64_t)ks * Kc;
 
+  // x is the preceding kernel's output (programmatic dependent launch).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // Stage x[t0 .. t0+ntok) [k0, k0+Kc) as bf16 (exact for bf16 inputs).
   for (int idx = threadIdx.x; idx < 8 * Kc; idx += blockDim.x) {
     const int c = idx / Kc, k = idx % Kc;
@@ -169,14 +172,25 @@ int router_ksplit(int64_t H) {
   return (H % (32 * kRouterWarps) == 0) ? 1 : 0;
 }
 
-cudaError_t launch_router(const RouterArgs& a, cudaStream_t stream) {
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t stream, bool pdl) {
   if (a.T == 0) return cudaSuccess;
   const int Kc = (int)(a.H / a.ksplit);
   const size_t smem = (size_t)8 * (Kc + kRouterPad) * sizeof(uint16_t);
   cudaError_t err = ensure_smem(router_kernel, smem);
   if (err != cudaSuccess) return err;
   dim3 grid((unsigned)((a.E + 15) / 16), (unsigned)a.ksplit, (unsigned)((a.T + 7) / 8));
-  router_kernel<<<grid, kRouterWarps * 32, smem, stream>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kRouterWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  err = cudaLaunchKernelEx(&cfg, router_kernel, a);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

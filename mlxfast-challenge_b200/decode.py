@@ -66,12 +66,14 @@ class MoEDecodeChain:
             dst = self.bufs[l % 2]
             inds, wts = self.routing[l]
             if self.route:
-                check(L.moe_router_topk(inds.data_ptr(), wts.data_ptr(), src.data_ptr(), self._dt,
-                                        b.router_weight.data_ptr(),
-                                        None if b.router_bias is None else
-                                        b.router_bias.data_ptr(), self.T, b.H, b.E, b.top_k,
-                                        int(b.desc.norm_topk_prob), self.ws.data_ptr(),
-                                        self.ws.numel(), stream_ptr))
+                # Router + gate/up + down in one call: the library knows the
+                # gate/up kernel must read the fresh routing after its wait.
+                check(L.moe_block_forward(dst.data_ptr(), src.data_ptr(), None, self._dt, self.T,
+                                          ctypes.byref(b.desc), None, None, inds.data_ptr(),
+                                          wts.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                                          stream_ptr))
+                src = dst
+                continue
             check(L.moe_gate_up_swiglu(self.act.data_ptr(), self.act_ld, src.data_ptr(),
                                        self._dt, self.T, ctypes.byref(b.desc), inds.data_ptr(),
                                        stream_ptr))
@@ -84,14 +86,22 @@ class MoEDecodeChain:
     def launches_per_step(self) -> int:
         return len(self.blocks) * (3 if self.route else 2)
 
-    def capture(self):
+    def capture(self, pdl: bool = True):
+        """Capture one step.  With pdl, every kernel may start while its
+        predecessor drains (programmatic dependent launch): the next layer's
+        weights stream in before the previous layer's output is ready."""
         s = self.stream
         with torch.cuda.stream(s):
             self._launch_step(ctypes.c_void_p(s.cuda_stream))  # warm (sets kernel attributes)
         s.synchronize()
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=s):
-            self._launch_step(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        L = lib()
+        old = L.nvfp4_set_launch_flags(1 if pdl else 0)
+        try:
+            with torch.cuda.graph(self.graph, stream=s):
+                self._launch_step(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        finally:
+            L.nvfp4_set_launch_flags(old)
         return self
 
     def replay(self):

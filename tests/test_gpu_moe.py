@@ -111,3 +111,31 @@ def test_out_of_range_routing_is_latched(nv, layer):
     block(torch.ones(1, 2048, device=DEV, dtype=torch.bfloat16), inds=inds, weights=wts)
     with pytest.raises(nv.DeviceIndexError):
         nv.device_status()
+
+
+@pytest.mark.parametrize("route", [False, True])
+@pytest.mark.parametrize("pdl", [False, True])
+def test_decode_chain_graph_matches_layer_by_layer(nv, route, pdl):
+    """The CUDA-graph chain (with and without programmatic dependent launch)
+    equals running the layers one call at a time, bit for bit."""
+    lag = importlib.import_module(PKG + ".laguna")
+    cfg = lag.LagunaMoEConfig(n_experts=32)
+    blocks = [lag.random_sparse_layer(nv, seed=50 + l, device=DEV, cfg=cfg, n_experts=32)[0]
+              for l in range(4)]
+    routing = [lag.random_routing(2, cfg, seed=60 + l, device=DEV) for l in range(4)]
+    chain = nv.MoEDecodeChain(blocks, None if route else routing, T=2, route=route,
+                              device=DEV).capture(pdl=pdl)
+    x = torch.randn(2, 2048, device=DEV).to(torch.bfloat16)
+    want = x
+    for l, b in enumerate(blocks):
+        if route:
+            want = b(want)
+        else:
+            want = b(want, inds=routing[l][0], weights=routing[l][1])
+    for _ in range(3):  # replays are repeatable
+        chain.x0.copy_(x)
+        out = chain.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+    yh = chain(x.cpu().pin_memory())
+    assert torch.equal(yh, want.cpu())
