@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/nvfp4moe.h"
@@ -91,6 +92,36 @@ BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
 }
 
 }  // namespace
+
+namespace nvfp4 {
+// Per (kernel, device) record of the dynamic shared-memory limit already set.
+cudaError_t ensure_smem_ptr(const void* kern, size_t bytes) {
+  struct Entry {
+    const void* kern;
+    int dev;
+    size_t bytes;
+  };
+  static Entry table[64];
+  static int used = 0;
+  static std::mutex mu;
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; i++)
+    if (table[i].kern == kern && table[i].dev == dev && table[i].bytes >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return e;
+  for (int i = 0; i < used; i++)
+    if (table[i].kern == kern && table[i].dev == dev) {
+      table[i].bytes = bytes;
+      return cudaSuccess;
+    }
+  if (used < 64) table[used++] = Entry{kern, dev, bytes};
+  return cudaSuccess;
+}
+}  // namespace nvfp4
 
 extern "C" {
 

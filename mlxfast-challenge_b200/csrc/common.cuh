@@ -52,11 +52,12 @@ __device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t w, uint32_t (&h)[4]) 
       : "r"(w));
 }
 
-// One E2M1 code -> f32 (exact).
+// One E2M1 code -> f32 (exact), arithmetically: magnitude code m is
+// 0.5*m for m < 2, else (1 + (m&1)/2) * 2^(m/2 - 1); bit 3 is the sign.
 __device__ __forceinline__ float fp4_to_f32(uint32_t code) {
-  uint32_t h[4];
-  e2m1x8_to_f16x2x4(code & 15u, h);
-  return __half2float(__ushort_as_half((unsigned short)(h[0] & 0xFFFFu)));
+  const uint32_t m = code & 7u;
+  const float mag = m < 2u ? 0.5f * (float)m : ldexpf(1.0f + 0.5f * (float)(m & 1u), (int)(m >> 1) - 1);
+  return (code & 8u) ? -mag : mag;
 }
 
 // Scale byte pair (lo byte -> low half) -> f16x2 of the MLX E4M3 decode.

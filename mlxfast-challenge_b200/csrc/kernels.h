@@ -86,17 +86,10 @@ cudaError_t read_and_clear_device_error(int* out);
 // Raise a kernel's dynamic shared-memory limit once per device (the call is
 // not stream-ordered, so it is kept out of the launch path and therefore out
 // of CUDA-graph capture after the first eager launch).
+cudaError_t ensure_smem_ptr(const void* kern, size_t bytes);
 template <typename Kern>
 cudaError_t ensure_smem(Kern kern, size_t bytes) {
-  static int set_bytes[64] = {0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if ((int)bytes <= set_bytes[dev] || bytes <= 48 * 1024) return cudaSuccess;
-  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-  if (e == cudaSuccess) set_bytes[dev] = (int)bytes;
-  return e;
+  return ensure_smem_ptr(reinterpret_cast<const void*>(kern), bytes);
 }
 
 }  // namespace nvfp4

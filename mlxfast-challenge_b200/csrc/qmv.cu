@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -261,7 +262,7 @@ __device__ __forceinline__ void run_chunks(Acc& acc, Chunk (&ring)[kRing], const
 // grid = (P * mchunks, ceil(N/16)); segment = (pair p, 8-row chunk of M).
 template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) qmm_gather_kernel(QmmArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   const int Kpad = (int)a.K;  // fast path: K % 128 == 0
   const int ldx = Kpad + kXPad;
   __half* xs = reinterpret_cast<__half*>(smem);
@@ -370,7 +371,7 @@ __global__ void qmm_gather_generic_kernel(QmmArgs a) {
 // WARPS warps of a CTA split K.
 template <int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   const int Kpad = (int)a.H;
   const int ldx = Kpad + kXPad;
   __half* xs = reinterpret_cast<__half*>(smem);
@@ -458,7 +459,7 @@ __global__ void __launch_bounds__(WARPS * 32) moe_gateup_kernel(GateUpArgs a) {
 // order (deterministic).
 template <int WARPS, int CL>
 __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int Ipad = a.Ipad;
@@ -636,6 +637,434 @@ __global__ void __launch_bounds__(WARPS * 32) moe_down_kernel(DownArgs a) {
   }
 }
 
+
+// ===========================================================================
+// Bulk-copy-fed decode kernels (T <= 8).
+//
+// One CTA per SM-sized share of the tiles: a producer warp streams whole
+// weight tiles into a ring of shared-memory slots with cp.async.bulk (one
+// copy per lane: 16 code rows + 16 scale rows of a 16-row tile), completion
+// tracked by an mbarrier per slot; eight consumer warps compute from shared
+// memory and release the slot through a second mbarrier.  Rows are stored
+// with padded pitches (codes +64 B, scales +16 B) so the consumers' 128-bit
+// and 16-bit shared loads are bank-conflict free.  Many tiles are in flight
+// per SM from the first cycle, independent of register pressure.  Every wait
+// is bounded (tma.cuh): on expiry the kernel latches error 4 and drains.
+// ===========================================================================
+constexpr int kTmaConsumers = 8;
+constexpr int kTmaThreads = (kTmaConsumers + 1) * 32;
+constexpr int kGuSlots = 5;
+constexpr int kDnSlots = 16;
+constexpr int kErrTimeout = 4;
+
+__device__ __forceinline__ int tma_row_pitch(int K) { return K / 2 + 64; }
+__device__ __forceinline__ int tma_scale_pitch(int K) { return K / 16 + 16; }
+
+// Chunk `ch` of a 16-row tile held in shared memory.
+__device__ __forceinline__ void load_chunk_smem(Chunk& c, const uint8_t* tile, int rp, int sp,
+                                                int g, int ch, int t) {
+  c.lo = *reinterpret_cast<const uint4*>(tile + g * rp + ch * kChunkBytes + 16 * t);
+  c.hi = *reinterpret_cast<const uint4*>(tile + (g + 8) * rp + ch * kChunkBytes + 16 * t);
+  const uint8_t* sc = tile + 16 * rp;
+  c.slo = *reinterpret_cast<const uint16_t*>(sc + g * sp + ch * kChunkScales + 2 * t);
+  c.shi = *reinterpret_cast<const uint16_t*>(sc + (g + 8) * sp + ch * kChunkScales + 2 * t);
+}
+
+// Consumer-only staging of T activation rows (no __syncthreads: the
+// producer warp does not take part).  Same numerics as stage_columns.
+__device__ void stage_rows_consumers(__half* xs, int ldx, int ncols, int K, const void* x,
+                                     int dtype, float* colscale, int* colmax) {
+  const int nthr = kTmaConsumers * 32;
+  if (threadIdx.x < 8) colmax[threadIdx.x] = 0;
+  named_sync(1, nthr);
+  const int per = K / 8;
+  const int items = ncols * per;
+  const int rounds = (items + nthr - 1) / nthr;
+  for (int r = 0; r < rounds; r++) {
+    const int it = r * nthr + threadIdx.x;
+    const bool ok = it < items;
+    const int j = ok ? it / per : 0;
+    float m = 0.f;
+    if (ok) {
+      float f[8];
+      load8(x, dtype, (int64_t)j * K + (int64_t)(it - j * per) * 8, f);
+#pragma unroll
+      for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i]));
+    }
+    const int j0 = __shfl_sync(0xffffffffu, j, 0);
+    const int j1 = __shfl_sync(0xffffffffu, ok ? j : j0, 31);
+    for (int jj = j0; jj <= j1; jj++) warp_atomic_max(&colmax[jj], m, ok && j == jj);
+  }
+  named_sync(1, nthr);
+  if (threadIdx.x < ncols)
+    colscale[threadIdx.x] = ldexpf(1.0f, pow2_exponent(__int_as_float(colmax[threadIdx.x])));
+  named_sync(1, nthr);
+  for (int it = threadIdx.x; it < items; it += nthr) {
+    const int j = it / per, v = it - j * per;
+    float f[8];
+    load8(x, dtype, (int64_t)j * K + (int64_t)v * 8, f);
+    store8_f16(xs + j * ldx, v * 8, f, 1.0f / colscale[j]);
+  }
+  named_sync(1, nthr);
+}
+
+struct TmaSmem {
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* red_full;  // [2]
+  uint64_t* red_free;  // [2]
+};
+
+// --------------------------- gate/up + SwiGLU -----------------------------
+// Tiles: u = seg * tps + rg, seg = (token, slot), rg = group of 8 rows (gate
+// rows in tile rows 0..7, up rows in 8..15).  CTA b takes u = b, b+G, ...
+__global__ void __launch_bounds__(kTmaThreads, 1) moe_gateup_tma_kernel(GateUpArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int H = (int)a.H;
+  const int rp = tma_row_pitch(H), sp = tma_scale_pitch(H);
+  const int slot_bytes = (16 * rp + 16 * sp + 127) / 128 * 128;
+  const uint32_t tile_bytes = (uint32_t)(16 * (H / 2) + 16 * (H / 16));
+  const int ldx = H + kXPad;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  TmaSmem B{bars, bars + kGuSlots, bars + 2 * kGuSlots, bars + 2 * kGuSlots + 2};
+  unsigned char* p = smem + 256;
+  uint8_t* slots = p;
+  p += kGuSlots * slot_bytes;
+  __half* xs = reinterpret_cast<__half*>(p);
+  p += (size_t)a.T * ldx * sizeof(__half);
+  float* colscale = reinterpret_cast<float*>(p);
+  int* colmax = reinterpret_cast<int*>(colscale + 8);
+  float* red = colscale + 16;  // [2][kTmaConsumers-1][4][32]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tps = (int)((std::max(a.I, a.Is) + 7) / 8);
+  const int ntiles = (int)a.T * a.kk * tps;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kGuSlots; i++) {
+      mbar_init(&B.full[i], 1);
+      mbar_init(&B.empty[i], kTmaConsumers);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&B.red_full[i], kTmaConsumers - 1);
+      mbar_init(&B.red_free[i], 1);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto tile_of = [&](int u, int& seg, int64_t& i0) {
+    seg = u / tps;
+    i0 = (int64_t)(u - seg * tps) * 8;
+    const int slot = seg % a.kk;
+    return i0 < (slot < a.k ? a.I : a.Is);
+  };
+
+  if (warp == kTmaConsumers) {
+    // ---------------- producer ----------------
+    if (!a.inds_static) pdl_wait();  // routing written by the preceding kernel
+    int j = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < ntiles && ok; u += gridDim.x) {
+      int seg;
+      int64_t i0;
+      if (!tile_of(u, seg, i0)) continue;
+      const int s = j % kGuSlots;
+      if (j >= kGuSlots && !mbar_wait_bounded(&B.empty[s], ((j / kGuSlots) - 1) & 1)) {
+        if (lane == 0) flag_error(kErrTimeout);
+        ok = false;
+        break;
+      }
+      const int tok = seg / a.kk, slot = seg % a.kk;
+      const uint8_t *gw, *gs, *uw, *us;
+      if (slot < a.k) {
+        uint32_t e = a.inds[(int64_t)tok * a.k + slot];
+        if (e >= (uint32_t)a.E) {
+          if (lane == 0) flag_error(2);
+          e = 0;  // keep the pipeline consistent; the output is flagged invalid
+        }
+        gw = a.gw + (int64_t)e * a.w_stride;
+        gs = a.gs + (int64_t)e * a.s_stride;
+        uw = a.uw + (int64_t)e * a.w_stride;
+        us = a.us + (int64_t)e * a.s_stride;
+      } else {
+        gw = a.sgw;
+        gs = a.sgs;
+        uw = a.suw;
+        us = a.sus;
+      }
+      uint8_t* dst = slots + (size_t)s * slot_bytes;
+      if (lane == 0) mbar_arrive_expect_tx(&B.full[s], tile_bytes);
+      __syncwarp();
+      const int r = lane & 15;
+      const int64_t row = i0 + (r & 7);
+      if (lane < 16) {
+        const uint8_t* src = (r < 8 ? gw : uw) + row * (H / 2);
+        bulk_g2s(dst + r * rp, src, (uint32_t)(H / 2), &B.full[s]);
+      } else {
+        const uint8_t* src = (r < 8 ? gs : us) + row * (H / 16);
+        bulk_g2s(dst + 16 * rp + r * sp, src, (uint32_t)(H / 16), &B.full[s]);
+      }
+      j++;
+    }
+    pdl_wait();
+    pdl_trigger();
+    // Drain: never leave the CTA with copies still landing in its memory.
+    for (int jj = (j > kGuSlots ? j - kGuSlots : 0); jj < j; jj++)
+      if (!mbar_wait_bounded(&B.full[jj % kGuSlots], (jj / kGuSlots) & 1) && lane == 0)
+        flag_error(kErrTimeout);
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait();  // x is the preceding kernel's output
+  pdl_trigger();
+  stage_rows_consumers(xs, ldx, (int)a.T, H, a.x, a.dtype, colscale, colmax);
+  const int g = lane >> 2, t = lane & 3;
+  const int nch = H / kChunk;
+  const int c0 = (warp * nch) / kTmaConsumers, c1 = ((warp + 1) * nch) / kTmaConsumers;
+  int j = 0;
+  for (int u = blockIdx.x; u < ntiles; u += gridDim.x) {
+    int seg;
+    int64_t i0;
+    if (!tile_of(u, seg, i0)) continue;
+    const int s = j % kGuSlots;
+    if (!mbar_wait_bounded(&B.full[s], (j / kGuSlots) & 1)) {
+      if (lane == 0) flag_error(kErrTimeout);
+      break;
+    }
+    const int tok = seg / a.kk;
+    const uint8_t* tile = slots + (size_t)s * slot_bytes;
+    const __half* xcol = g == 0 ? xs + tok * ldx : nullptr;
+    Acc acc;
+    acc.zero();
+    for (int ch = c0; ch < c1; ch++) {
+      Chunk c;
+      load_chunk_smem(c, tile, rp, sp, g, ch, t);
+      compute_chunk(acc, c, xcol, ch, t);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&B.empty[s]);
+    float d[4];
+    acc.fold(d);
+    const int rb = j & 1;
+    float* rbuf = red + rb * (kTmaConsumers - 1) * 4 * 32;
+    if (warp > 0) {
+      if (j >= 2 && !mbar_wait_bounded(&B.red_free[rb], ((j >> 1) - 1) & 1)) {
+        if (lane == 0) flag_error(kErrTimeout);
+        break;
+      }
+#pragma unroll
+      for (int r = 0; r < 4; r++) rbuf[((warp - 1) * 4 + r) * 32 + lane] = d[r];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.red_full[rb]);
+    } else {
+      if (!mbar_wait_bounded(&B.red_full[rb], (j >> 1) & 1)) {
+        if (lane == 0) flag_error(kErrTimeout);
+        break;
+      }
+#pragma unroll 1
+      for (int w = 1; w < kTmaConsumers; w++)
+#pragma unroll
+        for (int r = 0; r < 4; r++) d[r] += rbuf[((w - 1) * 4 + r) * 32 + lane];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B.red_free[rb]);
+      if (t == 0) {
+        const float cs = colscale[tok];
+        a.act[(int64_t)seg * a.act_ld + i0 + g] = silu_ref(d[0] * cs) * (d[2] * cs);
+      }
+    }
+    j++;
+  }
+}
+
+// ------------------------------ down + combine ------------------------------
+// One CTA per 16-row output tile.  Units u = 0..nseg-1 are the segments
+// (token, slot) of the tile's K range; unit u's 16 rows of that expert's down
+// matrix go through slot u % S.  Consumer warps 0..3 take even units, 4..7 odd
+// units, warp w%4 the chunks w%4, w%4+4, ... of the unit; all accumulate in
+// registers across units and reduce once at the end.
+__global__ void __launch_bounds__(kTmaThreads, 1) moe_down_tma_kernel(DownArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int Ipad = a.Ipad;
+  const int rp = tma_row_pitch(Ipad), sp = tma_scale_pitch(Ipad);
+  const int slot_bytes = (16 * rp + 16 * sp + 127) / 128 * 128;
+  const int ldx = Ipad + kXPad;
+  const int ntok = (int)a.T;  // <= 8
+  const int nseg = ntok * a.kk;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  TmaSmem B{bars, bars + kDnSlots, bars + 2 * kDnSlots, bars + 2 * kDnSlots + 2};
+  unsigned char* p = smem + 512;
+  uint8_t* slots = p;
+  p += kDnSlots * slot_bytes;
+  __half* xs = reinterpret_cast<__half*>(p);
+  p += (size_t)nseg * ldx * sizeof(__half);
+  float* colscale = reinterpret_cast<float*>(p);
+  int* colmax = reinterpret_cast<int*>(colscale + 8);
+  float* segw = colscale + 16;       // [nseg]
+  float* red = segw + nseg;          // [kTmaConsumers-1][4][32]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t h0 = (int64_t)blockIdx.x * 16;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kDnSlots; i++) {
+      mbar_init(&B.full[i], 1);
+      mbar_init(&B.empty[i], kTmaConsumers / 2);
+    }
+    mbar_init(&B.red_full[0], kTmaConsumers - 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kTmaConsumers) {
+    // ---------------- producer ----------------
+    // The routing is complete before this grid starts (it precedes the
+    // gate/up kernel this one follows), so the weights stream immediately.
+    if (!a.inds_static) pdl_wait();
+    int u = 0;
+    for (; u < nseg; u++) {
+      const int s = u % kDnSlots;
+      if (u >= kDnSlots && !mbar_wait_bounded(&B.empty[s], ((u / kDnSlots) - 1) & 1)) {
+        if (lane == 0) flag_error(kErrTimeout);
+        break;
+      }
+      const int tl = u / a.kk, sl = u - tl * a.kk;
+      const bool routed = sl < a.k;
+      const int Iseg = (int)(routed ? a.I : a.Is);
+      const uint8_t *wb, *sb;
+      if (routed) {
+        uint32_t e = a.inds[(int64_t)tl * a.k + sl];
+        if (e >= (uint32_t)a.E) {
+          if (lane == 0) flag_error(3);
+          e = 0;
+        }
+        wb = a.dw + (int64_t)e * a.w_stride;
+        sb = a.ds + (int64_t)e * a.s_stride;
+      } else {
+        wb = a.sdw;
+        sb = a.sds;
+      }
+      uint8_t* dst = slots + (size_t)s * slot_bytes;
+      if (lane == 0) mbar_arrive_expect_tx(&B.full[s], (uint32_t)(16 * (Iseg / 2 + Iseg / 16)));
+      __syncwarp();
+      const int r = lane & 15;
+      const int64_t row = h0 + r;
+      if (lane < 16)
+        bulk_g2s(dst + r * rp, wb + row * (Iseg / 2), (uint32_t)(Iseg / 2), &B.full[s]);
+      else
+        bulk_g2s(dst + 16 * rp + r * sp, sb + row * (Iseg / 16), (uint32_t)(Iseg / 16),
+                 &B.full[s]);
+    }
+    pdl_wait();
+    pdl_trigger();
+    for (int jj = (u > kDnSlots ? u - kDnSlots : 0); jj < u; jj++)
+      if (!mbar_wait_bounded(&B.full[jj % kDnSlots], (jj / kDnSlots) & 1) && lane == 0)
+        flag_error(kErrTimeout);
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int nthr = kTmaConsumers * 32;
+  for (int s = threadIdx.x; s < nseg; s += nthr) {
+    const int tl = s / a.kk, sl = s - tl * a.kk;
+    segw[s] = sl < a.k ? a.wts[(int64_t)tl * a.k + sl] * a.scaling : 1.0f;
+  }
+  if (threadIdx.x < 8) colmax[threadIdx.x] = 0;
+  pdl_wait();  // act is the preceding kernel's output
+  pdl_trigger();
+  named_sync(1, nthr);
+  const int per = Ipad / 8;
+  const int items = nseg * per;
+  const int rounds = (items + nthr - 1) / nthr;
+  for (int r = 0; r < rounds; r++) {
+    const int it = r * nthr + threadIdx.x;
+    const bool ok = it < items;
+    int tl = 0;
+    float m = 0.f;
+    if (ok) {
+      const int s = it / per, v = it - s * per;
+      tl = s / a.kk;
+      const int sl = s - tl * a.kk;
+      const int64_t Iseg = sl < a.k ? a.I : a.Is;
+      if ((int64_t)v * 8 < Iseg) {
+        float f[8];
+        load8(a.act, kF32, ((int64_t)tl * a.kk + sl) * a.act_ld + (int64_t)v * 8, f);
+#pragma unroll
+        for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i] * segw[s]));
+      }
+    }
+    const int j0 = __shfl_sync(0xffffffffu, tl, 0);
+    const int j1 = __shfl_sync(0xffffffffu, ok ? tl : j0, 31);
+    for (int jj = j0; jj <= j1; jj++) warp_atomic_max(&colmax[jj], m, ok && tl == jj);
+  }
+  named_sync(1, nthr);
+  if (threadIdx.x < ntok)
+    colscale[threadIdx.x] = ldexpf(1.0f, pow2_exponent(__int_as_float(colmax[threadIdx.x])));
+  named_sync(1, nthr);
+  for (int it = threadIdx.x; it < items; it += nthr) {
+    const int s = it / per, v = it - s * per;
+    const int tl = s / a.kk, sl = s - tl * a.kk;
+    const int64_t Iseg = sl < a.k ? a.I : a.Is;
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if ((int64_t)v * 8 < Iseg)
+      load8(a.act, kF32, ((int64_t)tl * a.kk + sl) * a.act_ld + (int64_t)v * 8, f);
+    store8_f16(xs + (size_t)s * ldx, v * 8, f, segw[s] / colscale[tl]);
+  }
+  named_sync(1, nthr);
+
+  const int g = lane >> 2, t = lane & 3;
+  const int grp = warp >> 2, wq = warp & 3;
+  Acc acc;
+  acc.zero();
+  bool alive = true;
+  for (int u = grp; u < nseg; u += 2) {
+    const int s = u % kDnSlots;
+    if (!mbar_wait_bounded(&B.full[s], (u / kDnSlots) & 1)) {
+      if (lane == 0) flag_error(kErrTimeout);
+      alive = false;
+      break;
+    }
+    const int tl = u / a.kk, sl = u - tl * a.kk;
+    const int nch = (int)((sl < a.k ? a.I : a.Is) / kChunk);
+    const uint8_t* tile = slots + (size_t)s * slot_bytes;
+    const __half* xcol = g == tl ? xs + (size_t)u * ldx : nullptr;
+    for (int ch = wq; ch < nch; ch += 4) {
+      Chunk c;
+      load_chunk_smem(c, tile, rp, sp, g, ch, t);
+      compute_chunk(acc, c, xcol, ch, t);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&B.empty[s]);
+  }
+  float d[4];
+  acc.fold(d);
+  if (warp > 0) {
+#pragma unroll
+    for (int r = 0; r < 4; r++) red[((warp - 1) * 4 + r) * 32 + lane] = d[r];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&B.red_full[0]);
+    return;
+  }
+  if (!alive || !mbar_wait_bounded(&B.red_full[0], 0)) {
+    if (lane == 0) flag_error(kErrTimeout);
+    return;
+  }
+#pragma unroll 1
+  for (int w = 1; w < kTmaConsumers; w++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) d[r] += red[((w - 1) * 4 + r) * 32 + lane];
+#pragma unroll
+  for (int r = 0; r < 4; r++) {
+    const int col = 2 * t + (r & 1);
+    const int64_t h = h0 + g + ((r < 2) ? 0 : 8);
+    if (col < ntok && h < a.H) {
+      const int64_t o = (int64_t)col * a.H + h;
+      float v = d[r] * colscale[col];
+      if (a.residual) v += load_as_f32(a.residual, a.dtype, o);
+      store_from_f32(a.y, a.dtype, o, v);
+    }
+  }
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -711,8 +1140,12 @@ size_t gateup_smem_bytes(int64_t H) {
          (size_t)(kGateUpWarps - 1) * 4 * 32 * sizeof(float);
 }
 
+cudaError_t launch_moe_gateup_tma(const GateUpArgs& a, cudaStream_t stream, bool pdl);
+bool gateup_tma_ok(const GateUpArgs& a);
+
 cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream, bool pdl) {
   if (a.T == 0) return cudaSuccess;
+  if (gateup_tma_ok(a)) return launch_moe_gateup_tma(a, stream, pdl);
   const size_t smem = gateup_smem_bytes(a.H);
   auto kern = moe_gateup_kernel<kGateUpWarps>;
   cudaError_t err = ensure_smem(kern, smem);
@@ -732,8 +1165,12 @@ size_t down_smem_bytes(int64_t Ipad, int kk) {
          (size_t)(kDownWarps - 1 + kDownCluster - 1) * 4 * 32 * sizeof(float);
 }
 
+cudaError_t launch_moe_down_tma(const DownArgs& a, cudaStream_t stream, bool pdl);
+bool down_tma_ok(const DownArgs& a);
+
 cudaError_t launch_moe_down(const DownArgs& a_in, cudaStream_t stream, bool pdl) {
   if (a_in.T == 0) return cudaSuccess;
+  if (down_tma_ok(a_in)) return launch_moe_down_tma(a_in, stream, pdl);
   DownArgs a = a_in;
   a.max_seg_per_cta = down_max_seg_per_cta(a.kk);
   const size_t smem = down_smem_bytes(a.Ipad, a.kk);
@@ -742,6 +1179,73 @@ cudaError_t launch_moe_down(const DownArgs& a_in, cudaStream_t stream, bool pdl)
   if (err != cudaSuccess) return err;
   dim3 grid((unsigned)((a.H + 15) / 16 * kDownCluster), (unsigned)((a.T + 7) / 8));
   err = launch_ex(kern, grid, dim3(kDownWarps * 32), smem, stream, pdl, kDownCluster, a);
+  if (err != cudaSuccess) return err;
+  return cudaGetLastError();
+}
+
+
+// ---- bulk-copy-fed decode launchers -----------------------------------------
+static int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (n[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
+  }
+  return n[dev];
+}
+
+static size_t gateup_tma_smem(int64_t H, int64_t T) {
+  const size_t rp = H / 2 + 64, sp = H / 16 + 16;
+  const size_t slot = (16 * rp + 16 * sp + 127) / 128 * 128;
+  return 256 + kGuSlots * slot + (size_t)T * (H + kXPad) * sizeof(__half) +
+         (16 + 2 * (kTmaConsumers - 1) * 4 * 32) * sizeof(float);
+}
+
+static size_t down_tma_smem(int64_t Ipad, int64_t T, int kk) {
+  const size_t rp = Ipad / 2 + 64, sp = Ipad / 16 + 16;
+  const size_t slot = (16 * rp + 16 * sp + 127) / 128 * 128;
+  const size_t nseg = (size_t)T * kk;
+  return 512 + kDnSlots * slot + nseg * (Ipad + kXPad) * sizeof(__half) +
+         (16 + nseg + (kTmaConsumers - 1) * 4 * 32) * sizeof(float);
+}
+
+static bool aligned16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+bool gateup_tma_ok(const GateUpArgs& a) {
+  return a.T >= 1 && a.T <= 8 && a.H % 256 == 0 && a.I % 8 == 0 && a.Is % 8 == 0 &&
+         gateup_tma_smem(a.H, a.T) <= 200 * 1024 && aligned16p(a.gw) && aligned16p(a.gs) &&
+         aligned16p(a.uw) && aligned16p(a.us) &&
+         (a.Is == 0 || (aligned16p(a.sgw) && aligned16p(a.sgs) && aligned16p(a.suw) &&
+                        aligned16p(a.sus)));
+}
+
+bool down_tma_ok(const DownArgs& a) {
+  return a.T >= 1 && a.T <= 8 && a.I % 256 == 0 && a.Is % 256 == 0 && a.H % 16 == 0 &&
+         down_tma_smem(a.Ipad, a.T, a.kk) <= 200 * 1024 && aligned16p(a.dw) &&
+         aligned16p(a.ds) && (a.Is == 0 || (aligned16p(a.sdw) && aligned16p(a.sds)));
+}
+
+cudaError_t launch_moe_gateup_tma(const GateUpArgs& a, cudaStream_t stream, bool pdl) {
+  const size_t smem = gateup_tma_smem(a.H, a.T);
+  cudaError_t err = ensure_smem(moe_gateup_tma_kernel, smem);
+  if (err != cudaSuccess) return err;
+  const int64_t tps = (std::max(a.I, a.Is) + 7) / 8;
+  const int64_t ntiles = a.T * a.kk * tps;
+  const int grid = (int)std::min<int64_t>(ntiles, sm_count());
+  err = launch_ex(moe_gateup_tma_kernel, dim3(grid), dim3(kTmaThreads), smem, stream, pdl, 1, a);
+  if (err != cudaSuccess) return err;
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_down_tma(const DownArgs& a, cudaStream_t stream, bool pdl) {
+  const size_t smem = down_tma_smem(a.Ipad, a.T, a.kk);
+  cudaError_t err = ensure_smem(moe_down_tma_kernel, smem);
+  if (err != cudaSuccess) return err;
+  err = launch_ex(moe_down_tma_kernel, dim3((unsigned)(a.H / 16)), dim3(kTmaThreads), smem,
+                  stream, pdl, 1, a);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }

@@ -30,7 +30,7 @@ constexpr int kRouterWarps = 4;
 constexpr int kRouterPad = 32;  // bf16 elements of padding per staged column
 
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
+  extern __shared__ __align__(128) unsigned char smem[];
   const int Kc = (int)(a.H / a.ksplit);
   const int ldx = Kc + kRouterPad;
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem);
