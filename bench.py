@@ -285,7 +285,7 @@ def main():
     peak, peak_kind = measured_peak_hbm()
     achieved = gu_bytes / (gu_ms / 1e3) / 1e9
     traffic = ncu_traffic()
-    roofline = {"bound": "hbm", "kernel": "moe_gateup_tma_kernel (fused gate/up + SwiGLU, bulk-copy fed)",
+    roofline = {"bound": "hbm", "kernel": "moe_gateup_kernel (fused gate/up + SwiGLU)",
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
                 if peak_kind == "measured" else "fallback 6650 GB/s",

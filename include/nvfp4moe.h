@@ -75,6 +75,10 @@ NVFP4MOE_API int nvfp4_version(void);
  * Later kernels inside one call always overlap their predecessor.  Returns
  * the previous flags. */
 #define NVFP4_LAUNCH_PDL 1
+/* NVFP4_LAUNCH_BULK_COPY selects, for T <= 8, the decode kernels fed by
+ * cp.async.bulk copies into a shared-memory ring (one producer warp, eight
+ * consumer warps) instead of per-thread streaming loads.  Same results. */
+#define NVFP4_LAUNCH_BULK_COPY 2
 NVFP4MOE_API int nvfp4_set_launch_flags(int flags);
 /* Synchronises the device, returns and clears the latched device status
  * (NVFP4_OK or NVFP4_ERR_DEVICE_INDEX). */

@@ -35,7 +35,7 @@ from ._lib import DeviceIndexError, MoeLayerDesc, NvFp4Bank, check, lib
 
 __all__ = [
     "quantize", "dequantize", "quantized_matmul", "gather_qmm", "moe_router_topk",
-    "SparseMoeBlock", "MoEDecodeChain", "device_status", "DeviceIndexError", "library_path",
+    "SparseMoeBlock", "MoEDecodeChain", "device_status", "launch_flags", "DeviceIndexError", "library_path",
 ]
 
 _DT = {torch.bfloat16: _lib.NVFP4_BF16, torch.float16: _lib.NVFP4_F16,
@@ -216,6 +216,24 @@ def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases=No
                                  _ptr(sb), _ptr(lhs), _ptr(rhs), P, nxb, E, M, N, K,
                                  int(bool(sorted_indices)), _stream(x.device)))
     return out
+
+
+class launch_flags:
+    """Context manager setting the calling thread's C-ABI launch flags
+    (nvfp4_set_launch_flags): pdl=True lets the first kernel of each call
+    overlap its predecessor; bulk_copy=True selects the bulk-copy fed decode
+    kernels."""
+
+    def __init__(self, pdl: bool = False, bulk_copy: bool = False):
+        self.flags = (_lib.NVFP4_LAUNCH_PDL if pdl else 0) | (
+            _lib.NVFP4_LAUNCH_BULK_COPY if bulk_copy else 0)
+
+    def __enter__(self):
+        self.old = lib().nvfp4_set_launch_flags(self.flags)
+        return self
+
+    def __exit__(self, *exc):
+        lib().nvfp4_set_launch_flags(self.old)
 
 
 def device_status() -> None:

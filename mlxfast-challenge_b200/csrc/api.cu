@@ -17,6 +17,7 @@ thread_local std::string t_last_error;
 thread_local int t_launch_flags = 0;
 
 bool first_pdl() { return (t_launch_flags & NVFP4_LAUNCH_PDL) != 0; }
+bool use_bulk() { return (t_launch_flags & NVFP4_LAUNCH_BULK_COPY) != 0; }
 nvfp4_error_handler g_handler = nullptr;
 void* g_handler_data = nullptr;
 
@@ -136,7 +137,7 @@ int nvfp4_version(void) { return 1; }
 
 int nvfp4_set_launch_flags(int flags) {
   const int old = t_launch_flags;
-  t_launch_flags = flags & NVFP4_LAUNCH_PDL;
+  t_launch_flags = flags & (NVFP4_LAUNCH_PDL | NVFP4_LAUNCH_BULK_COPY);
   return old;
 }
 
@@ -434,6 +435,7 @@ static int gate_up_impl(float* act, int64_t act_ld, const void* x, int dtype, in
   ga.act = act;
   ga.act_ld = act_ld;
   ga.inds_static = inds_static ? 1 : 0;
+  ga.bulk = use_bulk() ? 1 : 0;
   return check_cuda(nvfp4::launch_moe_gateup(ga, (cudaStream_t)stream, pdl), op);
 }
 
@@ -492,6 +494,7 @@ static int down_impl(void* y, const float* act, int64_t act_ld, const void* resi
   // NVFP4_LAUNCH_PDL, by the caller's contract), which waited for whatever
   // produced the routing before letting this grid launch.
   da.inds_static = 1;
+  da.bulk = use_bulk() ? 1 : 0;
   return check_cuda(nvfp4::launch_moe_down(da, (cudaStream_t)stream, pdl), op);
 }
 

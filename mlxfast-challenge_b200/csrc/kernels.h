@@ -35,6 +35,7 @@ struct GateUpArgs {
   float* act;  // [T*kk, act_ld]
   int64_t act_ld;
   int inds_static;  // inds were not written by the immediately preceding kernel
+  int bulk;         // use the bulk-copy fed kernel when the shape allows
 };
 
 struct DownArgs {
@@ -53,6 +54,7 @@ struct DownArgs {
   int dtype;
   int inds_static;      // routing complete before this grid starts (see qmv.cu)
   int max_seg_per_cta;  // set by the launcher
+  int bulk;             // use the bulk-copy fed kernel when the shape allows
 };
 
 struct RouterArgs {

@@ -1145,7 +1145,7 @@ bool gateup_tma_ok(const GateUpArgs& a);
 
 cudaError_t launch_moe_gateup(const GateUpArgs& a, cudaStream_t stream, bool pdl) {
   if (a.T == 0) return cudaSuccess;
-  if (gateup_tma_ok(a)) return launch_moe_gateup_tma(a, stream, pdl);
+  if (a.bulk && gateup_tma_ok(a)) return launch_moe_gateup_tma(a, stream, pdl);
   const size_t smem = gateup_smem_bytes(a.H);
   auto kern = moe_gateup_kernel<kGateUpWarps>;
   cudaError_t err = ensure_smem(kern, smem);
@@ -1170,7 +1170,7 @@ bool down_tma_ok(const DownArgs& a);
 
 cudaError_t launch_moe_down(const DownArgs& a_in, cudaStream_t stream, bool pdl) {
   if (a_in.T == 0) return cudaSuccess;
-  if (down_tma_ok(a_in)) return launch_moe_down_tma(a_in, stream, pdl);
+  if (a_in.bulk && down_tma_ok(a_in)) return launch_moe_down_tma(a_in, stream, pdl);
   DownArgs a = a_in;
   a.max_seg_per_cta = down_max_seg_per_cta(a.kk);
   const size_t smem = down_smem_bytes(a.Ipad, a.kk);

@@ -96,7 +96,8 @@ class MoEDecodeChain:
         s.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         L = lib()
-        old = L.nvfp4_set_launch_flags(1 if pdl else 0)
+        old = L.nvfp4_set_launch_flags(0)
+        L.nvfp4_set_launch_flags((old & ~1) | (1 if pdl else 0))  # keep other flag bits
         try:
             with torch.cuda.graph(self.graph, stream=s):
                 self._launch_step(ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
@@ -105,11 +106,15 @@ class MoEDecodeChain:
         return self
 
     def replay(self):
-        """Enqueue one step on self.stream (inputs already in self.x0)."""
+        """Enqueue one step (inputs already in self.x0), ordered after the
+        caller's current stream; the caller's stream then waits for it."""
         if self.graph is None:
             self.capture()
+        cur = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(cur)
         with torch.cuda.stream(self.stream):
             self.graph.replay()
+        cur.wait_stream(self.stream)
         return self.out
 
     def __call__(self, x_host: torch.Tensor, y_host: Optional[torch.Tensor] = None):

@@ -43,24 +43,28 @@ def oracle_block(orc, raw, x, inds, wts, residual=None, with_shared=True):
                                   routed, shared, scaling=2.5, residual=res)
 
 
+@pytest.mark.parametrize("bulk", [False, True])
 @pytest.mark.parametrize("T", [1, 2, 8])
-def test_routed_layer_given_routing_config1(nv, orc, layer, T):
+def test_routed_layer_given_routing_config1(nv, orc, layer, T, bulk):
     lag, block, raw = layer
     inds, wts = lag.random_routing(T, lag.LAGUNA_XS_2_1, seed=T)
     g = torch.Generator(device=DEV).manual_seed(T)
     x = torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16)
-    y = block(x, inds=inds, weights=wts)
+    with nv.launch_flags(bulk_copy=bulk):
+        y = block(x, inds=inds, weights=wts)
     want = oracle_block(orc, raw, x, inds, wts)
     assert_close(y.float().cpu().numpy(), want, what=f"block T={T}")
 
 
+@pytest.mark.parametrize("bulk", [False, True])
 @pytest.mark.parametrize("T", [1, 3, 8, 11])
-def test_full_block_with_router_config2(nv, orc, layer, T):
+def test_full_block_with_router_config2(nv, orc, layer, T, bulk):
     lag, block, raw = layer
     g = torch.Generator(device=DEV).manual_seed(100 + T)
     x = torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16)
     res = torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16)
-    y, inds, wts = block(x, residual=res, return_routing=True)
+    with nv.launch_flags(bulk_copy=bulk):
+        y, inds, wts = block(x, residual=res, return_routing=True)
     # The routing the block used is the router's (checked against the oracle router).
     ri, rw = nv.moe_router_topk(x, raw["router_w"], raw["router_b"], 8)
     assert torch.equal(inds, ri) and torch.equal(wts, rw)
@@ -123,8 +127,9 @@ def test_decode_chain_graph_matches_layer_by_layer(nv, route, pdl):
     blocks = [lag.random_sparse_layer(nv, seed=50 + l, device=DEV, cfg=cfg, n_experts=32)[0]
               for l in range(4)]
     routing = [lag.random_routing(2, cfg, seed=60 + l, device=DEV) for l in range(4)]
-    chain = nv.MoEDecodeChain(blocks, None if route else routing, T=2, route=route,
-                              device=DEV).capture(pdl=pdl)
+    with nv.launch_flags(bulk_copy=pdl):  # cover both kernel families
+        chain = nv.MoEDecodeChain(blocks, None if route else routing, T=2, route=route,
+                                  device=DEV).capture(pdl=pdl)
     x = torch.randn(2, 2048, device=DEV).to(torch.bfloat16)
     want = x
     for l, b in enumerate(blocks):
