@@ -127,20 +127,22 @@ def test_decode_chain_graph_matches_layer_by_layer(nv, route, pdl):
     blocks = [lag.random_sparse_layer(nv, seed=50 + l, device=DEV, cfg=cfg, n_experts=32)[0]
               for l in range(4)]
     routing = [lag.random_routing(2, cfg, seed=60 + l, device=DEV) for l in range(4)]
-    with nv.launch_flags(bulk_copy=pdl):  # cover both kernel families
+    # Cover both kernel families (bulk-copy fed with PDL, per-thread loads
+    # without); the layer-by-layer reference uses the same family.
+    with nv.launch_flags(bulk_copy=pdl):
         chain = nv.MoEDecodeChain(blocks, None if route else routing, T=2, route=route,
                                   device=DEV).capture(pdl=pdl)
-    x = torch.randn(2, 2048, device=DEV).to(torch.bfloat16)
-    want = x
-    for l, b in enumerate(blocks):
-        if route:
-            want = b(want)
-        else:
-            want = b(want, inds=routing[l][0], weights=routing[l][1])
-    for _ in range(3):  # replays are repeatable
-        chain.x0.copy_(x)
-        out = chain.replay()
-        torch.cuda.synchronize()
-        assert torch.equal(out, want)
-    yh = chain(x.cpu().pin_memory())
-    assert torch.equal(yh, want.cpu())
+        x = torch.randn(2, 2048, device=DEV).to(torch.bfloat16)
+        want = x
+        for l, b in enumerate(blocks):
+            if route:
+                want = b(want)
+            else:
+                want = b(want, inds=routing[l][0], weights=routing[l][1])
+        for _ in range(3):  # replays are repeatable
+            chain.x0.copy_(x)
+            out = chain.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(out, want)
+        yh = chain(x.cpu().pin_memory())
+        assert torch.equal(yh, want.cpu())
