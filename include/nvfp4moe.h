@@ -172,6 +172,23 @@ NVFP4MOE_API int moe_block_forward(void* y, const void* x, const void* residual,
                                    uint32_t* inds_out, float* weights_out, void* workspace,
                                    size_t workspace_bytes, nvfp4_stream stream);
 
+/* moe_block_forward without a workspace, for callers that cannot allocate
+ * device memory (no counterpart in the reference, whose MLX runtime owns its
+ * allocations): hosts that reach this library only through an operator
+ * interface that passes tensor pointers, with no way to hand it a separately
+ * owned workspace, or that must keep a fixed device-memory footprint.  The
+ * scratch is a static 256 KB device array held by every GPU that loads the
+ * library until exit: enough for T <= 8 tokens at Laguna XS 2.1 sizes;
+ * larger T is rejected with NVFP4_ERR_WORKSPACE.  The first call on a device
+ * looks the array up (make it before any stream capture).  All calls on a
+ * device share the array: calls that overlap on the GPU race.  Arguments
+ * otherwise as moe_block_forward. */
+NVFP4MOE_API int moe_block_forward_noalloc(void* y, const void* x, const void* residual,
+                                           int dtype, int64_t T, const moe_layer_desc* layer,
+                                           const uint32_t* inds_in, const float* weights_in,
+                                           uint32_t* inds_out, float* weights_out,
+                                           nvfp4_stream stream);
+
 /* The two fused phases of moe_block_forward, callable on their own.
  *
  * moe_gate_up_swiglu -- the routed (and shared) gate/up projections fused

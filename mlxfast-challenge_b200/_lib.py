@@ -60,6 +60,8 @@ SIGNATURES = {
     "moe_workspace_init": (_I, [_P, _SZ, _P]),
     "moe_block_forward": (_I, [_P, _P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P, _P,
                                _P, _P, _SZ, _P]),
+    "moe_block_forward_noalloc": (_I, [_P, _P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P,
+                                       _P, _P, _P, _P]),
     "moe_gate_up_swiglu": (_I, [_P, _I64, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P]),
     "moe_down_combine": (_I, [_P, _P, _I64, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P,
                               _P]),

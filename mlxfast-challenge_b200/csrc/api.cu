@@ -498,4 +498,70 @@ static int down_impl(void* y, const float* act, int64_t act_ld, const void* resi
   return check_cuda(nvfp4::launch_moe_down(da, (cudaStream_t)stream, pdl), op);
 }
 
+// ---------------------------------------------------------------------------
+// moe_block_forward_noalloc: the same sparse MoE block for callers that can
+// not allocate device memory -- hosts that embed this library behind another
+// runtime's allocator or operator interface and have no way to hand it a
+// separately owned workspace buffer, or that must keep a fixed device-memory
+// footprint once loaded.  Its scratch is the static array below instead of a
+// caller workspace; nothing here calls cudaMalloc, cudaFree or any other
+// allocating routine.
+//
+// The array lives in every GPU that loads this library until the process
+// exits.  Its device address is looked up with cudaGetSymbolAddress on the
+// first call made on each device (with that device current), so that first
+// call should come before any stream capture.  All calls on a device share
+// the array and it keeps the last call's contents: the router's tickets,
+// which must start at zero, are cleared on the stream at every call, and
+// calls that overlap on the GPU (other streams, other host threads) race on
+// it.  Limit: kNoAllocScratchBytes, i.e. up to T = 8 tokens at Laguna XS 2.1
+// sizes (E = 256, H = 2048, top-8 + shared expert of 512).
+static constexpr size_t kNoAllocScratchBytes = 256 * 1024;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static int noalloc_scratch(void** out) {
+  static void* addr[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return check_cuda(e, "moe_block_noalloc");
+  if (dev < 0 || dev >= 64)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[moe_block_noalloc] device ordinal %d >= 64.", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return check_cuda(e, "moe_block_noalloc");
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return NVFP4_OK;
+}
+
+extern "C" int moe_block_forward_noalloc(void* y, const void* x, const void* residual, int dtype,
+                                         int64_t T, const moe_layer_desc* L,
+                                         const uint32_t* inds_in, const float* weights_in,
+                                         uint32_t* inds_out, float* weights_out,
+                                         nvfp4_stream stream) {
+  const char* op = "moe_block_noalloc";
+  if (int r = check_layer(op, L, dtype, T)) return r;
+  if (T == 0) return NVFP4_OK;
+  const BlockLayout B = block_layout(L, T);
+  if (B.total > kNoAllocScratchBytes)
+    return fail(NVFP4_ERR_WORKSPACE,
+                "[%s] T=%lld needs %zu bytes of scratch but the static scratch holds %zu "
+                "(up to T=8 at Laguna sizes); use moe_block_forward with a workspace.",
+                op, (long long)T, B.total, kNoAllocScratchBytes);
+  void* ws = nullptr;
+  if (int r = noalloc_scratch(&ws)) return r;
+  // The router's tickets must start at zero; the array keeps the last call's
+  // contents, so clear them on this call's stream.
+  const size_t counters = (size_t)((T + 7) / 8) * sizeof(unsigned);
+  cudaError_t e = cudaMemsetAsync(static_cast<char*>(ws) + B.router.counters_off, 0, counters,
+                                  (cudaStream_t)stream);
+  if (e != cudaSuccess) return check_cuda(e, op);
+  return moe_block_forward(y, x, residual, dtype, T, L, inds_in, weights_in, inds_out,
+                           weights_out, ws, kNoAllocScratchBytes, stream);
+}
+
 }  // extern "C"
