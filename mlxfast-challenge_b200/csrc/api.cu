@@ -78,7 +78,18 @@ struct BlockLayout {
   size_t inds_off, wts_off, act_off, total;
   int64_t act_ld;
   int kk;
+  // Prefill (T > 8) buffers: sorted slot maps, tile list, bf16 act, f32 Y.
+  bool prefill;
+  int64_t P, S, max_tiles;
+  size_t brow_off, pos_off, tiles_off, ntiles_off, act16_off, y_off;
 };
+
+// The tensor-core prefill path: T > 8 tokens, 64-aligned sizes, and a shared
+// expert (if any) as wide as a routed one (one K for the down GEMM).
+bool prefill_shape_ok(const moe_layer_desc* L, int64_t T) {
+  return T > 8 && L->hidden % 64 == 0 && L->inter % 64 == 0 &&
+         (L->shared_inter == 0 || L->shared_inter == L->inter) && L->n_experts <= 1024;
+}
 
 BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
   BlockLayout B;
@@ -89,6 +100,21 @@ BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
   B.wts_off = align_up(B.inds_off + (size_t)T * L->top_k * sizeof(uint32_t), 256);
   B.act_off = align_up(B.wts_off + (size_t)T * L->top_k * sizeof(float), 256);
   B.total = align_up(B.act_off + (size_t)T * B.kk * B.act_ld * sizeof(float), 256);
+  B.prefill = prefill_shape_ok(L, T);
+  if (B.prefill) {
+    const int64_t tile = nvfp4::gemm_tile_tokens();
+    B.P = T * L->top_k;
+    const bool sh = L->shared_inter > 0;
+    B.S = B.P + (sh ? T : 0);
+    B.max_tiles = L->n_experts + (B.P + tile - 1) / tile + (sh ? (T + tile - 1) / tile : 0);
+    B.brow_off = B.total;
+    B.pos_off = align_up(B.brow_off + (size_t)B.S * sizeof(int), 256);
+    B.tiles_off = align_up(B.pos_off + (size_t)B.P * sizeof(int), 256);
+    B.ntiles_off = align_up(B.tiles_off + (size_t)B.max_tiles * 16, 256);
+    B.act16_off = align_up(B.ntiles_off + 16, 256);
+    B.y_off = align_up(B.act16_off + (size_t)B.S * B.act_ld * 2, 256);
+    B.total = align_up(B.y_off + (size_t)B.S * L->hidden * sizeof(float), 256);
+  }
   return B;
 }
 
@@ -147,6 +173,10 @@ int nvfp4_device_status(void) {
   if (e != cudaSuccess) return check_cuda(e, "device_status");
   e = nvfp4::read_and_clear_device_error(&st);
   if (e != cudaSuccess) return check_cuda(e, "device_status");
+  int st2 = 0;
+  e = nvfp4::read_and_clear_prefill_error(&st2);
+  if (e != cudaSuccess) return check_cuda(e, "device_status");
+  if (st == 0) st = st2;
   if (st != 0)
     return fail(NVFP4_ERR_DEVICE_INDEX,
                 "[gather_qmm] an expert or batch index was out of range (kernel site %d); "
@@ -232,6 +262,29 @@ int nvfp4_quantized_matmul(void* y, const void* x, int dtype, const uint32_t* w,
                 "[quantized_matmul] Only real floating types are supported.");
   if (int r = check_qdims("quantized_matmul", N, K)) return r;
   if (M < 0) return fail(NVFP4_ERR_INVALID, "[quantized_matmul] Invalid M.");
+  // Many rows: the tcgen05 GEMM streams W once for all of them.
+  if (M > 8 && K % 64 == 0 && N > 0 && M <= 0x7fffffff && x && y && w && scales &&
+      aligned16(x) && aligned16(w) && (K * (dtype == NVFP4_F32 ? 4 : 2)) % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(scales) & 3) == 0) {
+    nvfp4::GemmArgs g{};
+    g.mode = 0;
+    g.K = (int)K;
+    g.Mrows = (int)N;
+    g.Mrows_shared = 0;
+    g.w0 = g.w1 = reinterpret_cast<const uint8_t*>(w);
+    g.s0 = g.s1 = scales;
+    g.shared_group = -1;
+    g.b = x;
+    g.b_dtype = dtype;
+    g.b_ld = K;
+    g.implicit_M = (int)M;
+    g.out = y;
+    g.out_dtype = dtype;
+    g.out_ld = N;
+    const int tiles = (int)((M + nvfp4::gemm_tile_tokens() - 1) / nvfp4::gemm_tile_tokens());
+    return check_cuda(nvfp4::launch_nvfp4_gemm(g, tiles, (cudaStream_t)stream, first_pdl()),
+                      "quantized_matmul");
+  }
   // One "pair" whose M rows are the whole activation matrix.
   return nvfp4_gather_qmm(y, x, dtype, w, scales, nullptr, nullptr, 1, 1, 1, M, N, K, 0,
                           stream);
@@ -296,6 +349,9 @@ int moe_workspace_init(void* workspace, size_t bytes, nvfp4_stream stream) {
 }
 
 static int check_layer(const char* op, const moe_layer_desc* L, int dtype, int64_t T);
+static int prefill_impl(void* y, const void* x, const void* residual, int dtype, int64_t T,
+                        const moe_layer_desc* L, const uint32_t* inds, const float* wts, char* ws,
+                        const BlockLayout& B, nvfp4_stream stream, bool pdl_first);
 static int gate_up_impl(float* act, int64_t act_ld, const void* x, int dtype, int64_t T,
                         const moe_layer_desc* L, const uint32_t* inds, nvfp4_stream stream,
                         bool pdl, bool inds_static);
@@ -357,6 +413,14 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
                         s) != cudaSuccess)
       return check_cuda(cudaGetLastError(), op);
   }
+  if (B.prefill) {
+    if (!aligned16(x))
+      return fail(NVFP4_ERR_INVALID, "[%s] x must be 16-byte aligned.", op);
+    const bool routed_here = inds_in == nullptr;
+    const bool copied = inds_in && (inds_out || weights_out);
+    return prefill_impl(y, x, residual, dtype, T, L, inds, wts, ws, B, stream,
+                        /*pdl_first=*/!copied && (routed_here || first_pdl()));
+  }
   float* act = reinterpret_cast<float*>(ws + B.act_off);
   // Kernels after the first overlap their predecessor (PDL).  When the router
   // ran, the gate/up kernel reads the routing only after its dependency wait.
@@ -367,6 +431,106 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
                            /*inds_static=*/!routed_here))
     return r;
   return down_impl(y, act, B.act_ld, residual, dtype, T, L, inds, wts, stream, /*pdl=*/true);
+}
+
+// Prefill: sort pairs by expert, gate/up + SwiGLU and down as tcgen05
+// grouped GEMMs over expert-sorted token slots (the shared expert is one more
+// group holding every token), then the weighted per-token combine.
+static int prefill_impl(void* y, const void* x, const void* residual, int dtype, int64_t T,
+                        const moe_layer_desc* L, const uint32_t* inds, const float* wts, char* ws,
+                        const BlockLayout& B, nvfp4_stream stream, bool pdl_first) {
+  const char* op = "moe_block";
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t H = L->hidden, I = L->inter, E = L->n_experts;
+  const bool sh = L->shared_inter > 0;
+  int* brow = reinterpret_cast<int*>(ws + B.brow_off);
+  int* pos = reinterpret_cast<int*>(ws + B.pos_off);
+  int4* tiles = reinterpret_cast<int4*>(ws + B.tiles_off);
+  int* ntiles = reinterpret_cast<int*>(ws + B.ntiles_off);
+  void* act16 = ws + B.act16_off;
+  float* Y = reinterpret_cast<float*>(ws + B.y_off);
+
+  nvfp4::SortArgs sa{};
+  sa.inds = inds;
+  sa.T = (int)T;
+  sa.k = (int)L->top_k;
+  sa.E = (int)E;
+  sa.P = (int)B.P;
+  sa.with_shared = sh ? 1 : 0;
+  sa.brow = brow;
+  sa.pos = pos;
+  sa.tiles = tiles;
+  sa.ntiles = ntiles;
+  if (int r = check_cuda(nvfp4::launch_moe_sort(sa, s, pdl_first), op)) return r;
+
+  nvfp4::GemmArgs g{};
+  g.mode = 1;
+  g.K = (int)H;
+  g.Mrows = (int)I;
+  g.Mrows_shared = (int)L->shared_inter;
+  g.w0 = reinterpret_cast<const uint8_t*>(L->gate.w);
+  g.s0 = L->gate.scales;
+  g.w1 = reinterpret_cast<const uint8_t*>(L->up.w);
+  g.s1 = L->up.scales;
+  g.w_stride = I * (H / 2);
+  g.s_stride = I * (H / 16);
+  g.shared_group = sh ? (int)E : -1;
+  if (sh) {
+    g.sw0 = reinterpret_cast<const uint8_t*>(L->shared_gate.w);
+    g.ss0 = L->shared_gate.scales;
+    g.sw1 = reinterpret_cast<const uint8_t*>(L->shared_up.w);
+    g.ss1 = L->shared_up.scales;
+  }
+  g.b = x;
+  g.b_dtype = dtype;
+  g.b_ld = H;
+  g.brow = brow;
+  g.tiles = tiles;
+  g.ntiles = ntiles;
+  g.out = act16;
+  g.out_dtype = NVFP4_BF16;
+  g.out_ld = B.act_ld;
+  if (int r = check_cuda(nvfp4::launch_nvfp4_gemm(g, (int)B.max_tiles, s, true), op)) return r;
+
+  nvfp4::GemmArgs d{};
+  d.mode = 2;
+  d.K = (int)I;
+  d.Mrows = (int)H;
+  d.Mrows_shared = (int)H;
+  d.w0 = d.w1 = reinterpret_cast<const uint8_t*>(L->down.w);
+  d.s0 = d.s1 = L->down.scales;
+  d.w_stride = H * (I / 2);
+  d.s_stride = H * (I / 16);
+  d.shared_group = sh ? (int)E : -1;
+  if (sh) {
+    d.sw0 = d.sw1 = reinterpret_cast<const uint8_t*>(L->shared_down.w);
+    d.ss0 = d.ss1 = L->shared_down.scales;
+  }
+  d.b = act16;
+  d.b_dtype = NVFP4_BF16;
+  d.b_ld = B.act_ld;
+  d.brow = nullptr;  // the down GEMM reads act by slot
+  d.tiles = tiles;
+  d.ntiles = ntiles;
+  d.out = Y;
+  d.out_dtype = NVFP4_F32;
+  d.out_ld = H;
+  if (int r = check_cuda(nvfp4::launch_nvfp4_gemm(d, (int)B.max_tiles, s, true), op)) return r;
+
+  nvfp4::CombineArgs c{};
+  c.Y = Y;
+  c.pos = pos;
+  c.wts = wts;
+  c.T = (int)T;
+  c.k = (int)L->top_k;
+  c.P = (int)B.P;
+  c.H = (int)H;
+  c.with_shared = sh ? 1 : 0;
+  c.scaling = L->routed_scaling;
+  c.residual = residual;
+  c.y = y;
+  c.dtype = dtype;
+  return check_cuda(nvfp4::launch_moe_combine(c, s, true), op);
 }
 
 static int check_layer(const char* op, const moe_layer_desc* L, int dtype, int64_t T) {

@@ -70,6 +70,55 @@ struct RouterArgs {
   float* wts;           // [T, k]
 };
 
+// Grouped NVFP4 GEMM on tcgen05 (prefill.cu).
+struct GemmArgs {
+  int mode;          // 0 plain (y[brow][row]), 1 gate/up + SwiGLU -> bf16 act, 2 down -> f32 Y
+  int K;             // reduction length (multiple of 64)
+  int Mrows;         // rows of one bank per group
+  int Mrows_shared;  // rows of the shared group's bank
+  const uint8_t *w0, *s0, *w1, *s1;  // routed banks (w1/s1: the up bank in mode 1)
+  int64_t w_stride, s_stride;        // bytes per group
+  int shared_group;                  // group id served by the shared banks, -1 none
+  const uint8_t *sw0, *ss0, *sw1, *ss1;
+  const void* b;     // activation rows [*, b_ld]
+  int b_dtype;
+  int64_t b_ld;
+  const int* brow;   // slot -> activation row (null: slot itself)
+  const int4* tiles; // (group, first slot, count, 0)
+  const int* ntiles;
+  int implicit_M;    // > 0: one group, slots 0..implicit_M-1, tiles of 64 (no tiles/brow)
+  void* out;
+  int out_dtype;
+  int64_t out_ld;
+};
+
+struct SortArgs {
+  const uint32_t* inds;  // [T, k]
+  int T, k, E, P, with_shared;
+  int* brow;   // [P + T]
+  int* pos;    // [P]
+  int4* tiles;
+  int* ntiles;
+};
+
+struct CombineArgs {
+  const float* Y;  // [P + T, H]
+  const int* pos;
+  const float* wts;
+  int T, k, P, H, with_shared;
+  float scaling;
+  const void* residual;
+  void* y;
+  int dtype;
+};
+
+size_t gemm_smem_bytes();
+int gemm_tile_tokens();
+cudaError_t launch_nvfp4_gemm(const GemmArgs& a, int max_tiles, cudaStream_t stream, bool pdl);
+cudaError_t launch_moe_sort(const SortArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t launch_moe_combine(const CombineArgs& a, cudaStream_t stream, bool pdl);
+cudaError_t read_and_clear_prefill_error(int* out);
+
 size_t qmm_smem_bytes(int64_t K);
 bool qmm_fast_path_ok(const QmmArgs& a);
 cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream, bool pdl);
