@@ -93,10 +93,12 @@ def test_prefill_block_vs_oracle_and_decode_path(nv, orc, layer, T):
     want = oracle_tokens(orc, raw, x, inds, wts, tokens, residual=res)
     assert_close(y.float().cpu().numpy()[tokens], want, what=f"prefill T={T} vs oracle")
     # Every token against the decode-path kernels, 8 tokens per call, same routing.
+    # Both results are rounded to bf16, so two outputs may sit one bf16 ulp apart
+    # (0.031 at |y| in [4, 8)): max-abs 4e-2, relative-L2 at the usual 5e-3.
     parts = [block(x[i:i + 8], residual=res[i:i + 8], inds=inds[i:i + 8].view(torch.int32),
                    weights=wts[i:i + 8]) for i in range(0, T, 8)]
     assert_close(y.float().cpu().numpy(), torch.cat(parts).float().cpu().numpy(),
-                 what=f"prefill T={T} vs decode path")
+                 max_abs=4e-2, what=f"prefill T={T} vs decode path")
 
 
 def test_prefill_given_routing_with_skew(nv, orc, layer):
