@@ -8,15 +8,18 @@
 //
 // GEMM shape: D[weight rows, tokens] = W[rows, K] x X[tokens, K]^T per tile of
 // 128 weight rows (UMMA M) and up to 64 tokens (UMMA N), K in stages of 64.
-// Four producer warps dequantise NVFP4 to bf16 straight into the 128-byte
-// swizzled K-major UMMA layout (E2M1 pairs by the hardware converter, times
-// the E4M3 group scale: exact in bf16) and stage the bf16 activation rows of
-// the tile's tokens (gathered through a slot -> row map, so no sorted copy of
-// the activations is ever written); one thread issues tcgen05.mma kind::f16
-// (bf16 x bf16 -> f32 in TMEM) and commits each stage back to its producers
-// through an mbarrier.  Activations stay bf16 (exact for bf16 inputs, the
-// full bf16 range).  After the K loop the producer warps read TMEM
-// (tcgen05.ld 32x32b) and run the epilogue:
+// A three-stage pipeline per CTA: a raw-loader warp streams the packed codes
+// and scales of the tile rows into an 8-deep shared ring with 16-byte
+// cp.async copies (mbarrier arrivals on completion); four dequantiser warps
+// turn each stage into bf16 straight in the 128-byte swizzled K-major UMMA
+// layout (E2M1 pairs by the hardware converter, times the E4M3 group scale:
+// exact in bf16); an activation-loader warp gathers the tile's token rows
+// (through a slot -> row map, so no sorted copy of the activations is ever
+// written) with cp.async into the swizzled B stage; one thread issues
+// tcgen05.mma kind::f16 (bf16 x bf16 -> f32 in TMEM) and commits each stage
+// back to its producers through an mbarrier.  Activations stay bf16 (exact
+// for bf16 inputs, the full bf16 range).  After the K loop the dequantiser
+// warps read TMEM (tcgen05.ld 32x32b) and run the epilogue:
 //   mode 0 (plain)   y[row of token][n] = D                      (dense qmm)
 //   mode 1 (gate/up) tile rows interleave gate row i / up row i, so adjacent
 //                    TMEM lanes pair up: act = silu(gate) * up -> bf16
@@ -33,11 +36,15 @@ namespace {
 constexpr int kBM = 128;                          // weight rows per tile
 constexpr int kBN = 64;                           // tokens per tile (max UMMA N used)
 constexpr int kBK = 64;                           // K per stage: one 128 B swizzle atom of bf16
-constexpr int kStages = 4;
-constexpr int kProducerWarps = 4;
-constexpr int kGemmThreads = 32 * (1 + kProducerWarps);
+constexpr int kStages = 3;                        // bf16 A/B stages fed to the MMA
+constexpr int kRawSlots = 5;                      // packed-weight stages in flight (2 CTAs / SM)
+constexpr int kDeqWarps = 4;
+constexpr int kGemmThreads = 32 * (3 + kDeqWarps);
 constexpr int kStageA = kBM * kBK * 2;            // 16 KB
 constexpr int kStageB = kBN * kBK * 2;            // 8 KB
+constexpr int kRawPitch = 48;                     // 32 code bytes + pad: conflict-free reads
+constexpr int kRawCodes = kBM * kRawPitch;        // 6 KB
+constexpr int kRawSlot = kRawCodes + kBM * 4;     // + 4 scale bytes per row
 constexpr int kTmemCols = 64;
 constexpr int kErrTimeout = 4;
 
@@ -89,6 +96,34 @@ __device__ __forceinline__ uint4 load8_as_bf16(const void* x, int dtype, int64_t
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// cp.async helpers (16-byte L2-only copies, 4-byte copies, zero-fill).
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
+// One arrival on `bar` once all of this thread's prior cp.async copies landed.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Warp roles: 0 = TMEM owner + MMA issuer (lane 0), 1 = raw weight loader,
+// 2 = activation loader, 3..6 = dequantisers, then the epilogue.
+constexpr int kWarpMma = 0, kWarpRaw = 1, kWarpAct = 2, kWarpDeq0 = 3;
+
 __global__ void __launch_bounds__(kGemmThreads, 1) nvfp4_gemm_kernel(GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // UMMA swizzle atoms need 1024-byte alignment.
@@ -96,9 +131,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) nvfp4_gemm_kernel(GemmArgs a)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + kStages * kStageA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kStageB);
+  uint8_t* sRaw = sB + kStages * kStageB;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sRaw + kRawSlots * kRawSlot);
   uint64_t* empty = full + kStages;
-  uint64_t* done = empty + kStages;
+  uint64_t* raw_full = empty + kStages;
+  uint64_t* raw_empty = raw_full + kRawSlots;
+  uint64_t* done = raw_empty + kRawSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   // Tiles, token maps and activations come from preceding kernels.
@@ -124,20 +162,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1) nvfp4_gemm_kernel(GemmArgs a)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
-      mbar_init(&full[i], kProducerWarps);
-      mbar_init(&empty[i], 1);
+      mbar_init(&full[i], kDeqWarps + 32);  // dequant warps + activation-loader lanes
+      mbar_init(&empty[i], 1);              // MMA commit
+    }
+    for (int i = 0; i < kRawSlots; i++) {
+      mbar_init(&raw_full[i], 32);          // raw-loader lanes (cp.async arrivals)
+      mbar_init(&raw_empty[i], kDeqWarps);
     }
     mbar_init(done, 1);
     fence_barrier_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == kWarpMma) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int nkb = a.K / kBK;
 
-  if (warp == 0) {
+  // Bank row behind tile row r (gate/up interleave in mode 1).
+  auto bank_row = [&](int r, const uint8_t*& wb, const uint8_t*& sb, int64_t& row) {
+    const uint8_t* w0 = is_shared ? a.sw0 : a.w0 + (int64_t)grp * a.w_stride;
+    const uint8_t* s0 = is_shared ? a.ss0 : a.s0 + (int64_t)grp * a.s_stride;
+    const uint8_t* w1 = is_shared ? a.sw1 : a.w1 + (int64_t)grp * a.w_stride;
+    const uint8_t* s1 = is_shared ? a.ss1 : a.s1 + (int64_t)grp * a.s_stride;
+    if (a.mode == 1) {
+      row = (int64_t)m_tile * 64 + (r >> 1);
+      wb = (r & 1) ? w1 : w0;
+      sb = (r & 1) ? s1 : s0;
+    } else {
+      row = (int64_t)m_tile * 128 + r;
+      wb = w0;
+      sb = s0;
+    }
+  };
+
+  if (warp == kWarpMma) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(kBM, N) | (1u << 7) | (1u << 10);  // A, B bf16
@@ -158,59 +217,101 @@ __global__ void __launch_bounds__(kGemmThreads, 1) nvfp4_gemm_kernel(GemmArgs a)
       umma_commit(done);  // fires when every MMA issued above has completed
     }
     __syncwarp();
-  } else {
-    // ------------------------------ producers -------------------------------
-    const int pt = threadIdx.x - 32;  // 0..127: this thread's A row
-    // A row -> bank row.
-    const uint8_t *wb, *sb;
-    int64_t row;
-    {
-      const uint8_t* w0 = is_shared ? a.sw0 : a.w0 + (int64_t)grp * a.w_stride;
-      const uint8_t* s0 = is_shared ? a.ss0 : a.s0 + (int64_t)grp * a.s_stride;
-      const uint8_t* w1 = is_shared ? a.sw1 : a.w1 + (int64_t)grp * a.w_stride;
-      const uint8_t* s1 = is_shared ? a.ss1 : a.s1 + (int64_t)grp * a.s_stride;
-      if (a.mode == 1) {
-        row = (int64_t)m_tile * 64 + (pt >> 1);
-        wb = (pt & 1) ? w1 : w0;
-        sb = (pt & 1) ? s1 : s0;
-      } else {
-        row = (int64_t)m_tile * 128 + pt;
-        wb = w0;
-        sb = s0;
-      }
-    }
-    const bool row_ok = row < Mrows;
-    const uint8_t* codes = wb + row * (a.K / 2);
-    const uint8_t* scal = sb + row * (a.K / 16);
-    // B rows: chunk q = pt + 128 i -> token n = (pt >> 3) + 16 i, chunk c = pt & 7.
-    const int c8 = pt & 7;
-    int64_t brow[4];
+  } else if (warp == kWarpRaw) {
+    // --------------------------- raw weight loader ---------------------------
+    // Lane l copies rows l, l+32, l+64, l+96: 32 code bytes (two 16 B copies)
+    // and 4 scale bytes per row and stage, R stages ahead of the dequantisers.
+    const uint8_t* cptr[4];
+    const uint8_t* sptr[4];
+    bool rok[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-      const int n = (pt >> 3) + 16 * i;
+      const uint8_t *wb, *sb;
+      int64_t row;
+      bank_row(lane + 32 * i, wb, sb, row);
+      rok[i] = row < Mrows;
+      cptr[i] = rok[i] ? wb + row * (a.K / 2) : a.w0;
+      sptr[i] = rok[i] ? sb + row * (a.K / 16) : a.s0;
+    }
+    for (int kb = 0; kb < nkb; kb++) {
+      const int r = kb % kRawSlots;
+      if (kb >= kRawSlots && !mbar_wait_bounded(&raw_empty[r], ((kb / kRawSlots) - 1) & 1)) {
+        flag(kErrTimeout);
+        break;
+      }
+      uint8_t* slot = sRaw + r * kRawSlot;
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int tr = lane + 32 * i;
+        cp_async16(slot + tr * kRawPitch, cptr[i] + kb * 32, rok[i]);
+        cp_async16(slot + tr * kRawPitch + 16, cptr[i] + kb * 32 + 16, rok[i]);
+        cp_async4(slot + kRawCodes + tr * 4, sptr[i] + kb * 4, rok[i]);
+      }
+      cp_async_arrive_noinc(&raw_full[r]);
+    }
+    cp_async_wait<0>();
+  } else if (warp == kWarpAct) {
+    // --------------------------- activation loader ---------------------------
+    // Lane l copies 16-byte chunks q = l + 32 i (token n = q / 8, chunk q % 8)
+    // of the tile's rows into the swizzled B stage.  Copies of stage kb are
+    // one commit group; the stage is handed to the MMA (proxy fence + arrive)
+    // once its group has landed, kStages - 1 stages later.
+    const bool direct = a.b_dtype == kBF16;
+    int64_t brow[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const int n = (lane + 32 * i) >> 3;
       brow[i] = n < count ? (int64_t)(a.brow ? a.brow[start + n] : start + n) : -1;
     }
-    uint4 cw0 = make_uint4(0, 0, 0, 0), cw1 = cw0;
-    uint32_t sw = 0;
-    if (row_ok) {
-      cw0 = ldg_stream_u4(codes);
-      cw1 = ldg_stream_u4(codes + 16);
-      sw = *reinterpret_cast<const uint32_t*>(scal);
-    }
-    bool ok = true;
-    for (int kb = 0; kb < nkb && ok; kb++) {
+    int issued = 0, handed = 0;
+    for (int kb = 0; kb < nkb; kb++) {
       const int s = kb % kStages;
-      // Prefetch the next stage's codes while this one is converted.
-      uint4 nw0 = make_uint4(0, 0, 0, 0), nw1 = nw0;
-      uint32_t nsw = 0;
-      if (row_ok && kb + 1 < nkb) {
-        nw0 = ldg_stream_u4(codes + (kb + 1) * 32);
-        nw1 = ldg_stream_u4(codes + (kb + 1) * 32 + 16);
-        nsw = *reinterpret_cast<const uint32_t*>(scal + (kb + 1) * 4);
-      }
       if (kb >= kStages && !mbar_wait_bounded(&empty[s], ((kb / kStages) - 1) & 1)) {
         flag(kErrTimeout);
-        ok = false;
+        break;
+      }
+      uint8_t* stage = sB + s * kStageB;
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const int q = lane + 32 * i, n = q >> 3, c = q & 7;
+        uint8_t* dst = stage + n * 128 + ((c ^ (n & 7)) << 4);
+        const int64_t off = (brow[i] >= 0 ? brow[i] : 0) * a.b_ld + kb * kBK + c * 8;
+        if (direct) {
+          cp_async16(dst, reinterpret_cast<const uint16_t*>(a.b) + off, brow[i] >= 0);
+        } else {
+          *reinterpret_cast<uint4*>(dst) =
+              brow[i] >= 0 ? load8_as_bf16(a.b, a.b_dtype, off) : make_uint4(0, 0, 0, 0);
+        }
+      }
+      cp_async_commit();
+      issued++;
+      if (issued - handed == kStages - 1) {
+        cp_async_wait<kStages - 2>();
+        fence_proxy_async();
+        mbar_arrive(&full[handed % kStages]);
+        handed++;
+      }
+    }
+    cp_async_wait<0>();
+    fence_proxy_async();
+    for (; handed < issued; handed++) mbar_arrive(&full[handed % kStages]);
+  } else {
+    // ------------------------------ dequantisers ------------------------------
+    const int pt = threadIdx.x - 32 * kWarpDeq0;  // 0..127: this thread's A row
+    for (int kb = 0; kb < nkb; kb++) {
+      const int r = kb % kRawSlots, s = kb % kStages;
+      if (!mbar_wait_bounded(&raw_full[r], (kb / kRawSlots) & 1)) {
+        flag(kErrTimeout);
+        break;
+      }
+      const uint8_t* slot = sRaw + r * kRawSlot;
+      const uint4 cw0 = *reinterpret_cast<const uint4*>(slot + pt * kRawPitch);
+      const uint4 cw1 = *reinterpret_cast<const uint4*>(slot + pt * kRawPitch + 16);
+      const uint32_t sw = *reinterpret_cast<const uint32_t*>(slot + kRawCodes + pt * 4);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&raw_empty[r]);
+      if (kb >= kStages && !mbar_wait_bounded(&empty[s], ((kb / kStages) - 1) & 1)) {
+        flag(kErrTimeout);
         break;
       }
       uint8_t* arow = sA + s * kStageA + pt * 128;
@@ -221,26 +322,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) nvfp4_gemm_kernel(GemmArgs a)
         const float scale = scale_to_f32((sw >> (8 * (j >> 1))) & 0xFFu);
         *reinterpret_cast<uint4*>(arow + ((j ^ sw7) << 4)) = dequant8_bf16(wds[j], scale);
       }
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int n = (pt >> 3) + 16 * i;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (brow[i] >= 0) v = load8_as_bf16(a.b, a.b_dtype, brow[i] * a.b_ld + kb * kBK + c8 * 8);
-        *reinterpret_cast<uint4*>(sB + s * kStageB + n * 128 + ((c8 ^ (n & 7)) << 4)) = v;
-      }
       fence_proxy_async();  // generic-proxy smem writes -> tensor-core reads
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[s]);
-      cw0 = nw0;
-      cw1 = nw1;
-      sw = nsw;
     }
     // ------------------------------ epilogue --------------------------------
     // Warp-uniform decision: the TMEM loads below are .sync.aligned.
     const bool have = __all_sync(0xffffffffu, mbar_wait_bounded(done, 0));
     if (!have && lane == 0) flag(kErrTimeout);
     tc_fence_after();
-    const int sp = warp & 3;  // TMEM sub-partition this warp may read
+    const int sp = warp & 3;       // TMEM sub-partition this warp may read
     const int r = sp * 32 + lane;  // tile row = TMEM lane
     for (int c0 = 0; c0 < N && have; c0 += 16) {
       float v[16];
@@ -275,7 +366,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) nvfp4_gemm_kernel(GemmArgs a)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+  if (warp == kWarpMma) tmem_dealloc(tmem, kTmemCols);
 }
 
 // ---------------------------------------------------------------------------
@@ -382,7 +473,8 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream
 }  // namespace
 
 size_t gemm_smem_bytes() {
-  return 1024 + (size_t)kStages * (kStageA + kStageB) + (2 * kStages + 1) * 8 + 16;
+  return 1024 + (size_t)kStages * (kStageA + kStageB) + (size_t)kRawSlots * kRawSlot +
+         (2 * kStages + 2 * kRawSlots + 1) * 8 + 16;
 }
 
 int gemm_tile_tokens() { return kBN; }
