@@ -5,6 +5,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <initializer_list>
 #include <mutex>
 #include <string>
 
@@ -78,17 +79,27 @@ struct BlockLayout {
   size_t inds_off, wts_off, act_off, total;
   int64_t act_ld;
   int kk;
-  // Prefill (T > 8) buffers: sorted slot maps, tile list, bf16 act, f32 Y.
+  // Prefill (T > 8) buffers: sorted slot maps, tile list, x rows in slot order
+  // as pre-scaled f16, f32 act, act as pre-scaled f16 rows, f32 Y.
   bool prefill;
   int64_t P, S, max_tiles;
-  size_t brow_off, pos_off, tiles_off, ntiles_off, act16_off, y_off;
+  size_t brow_off, pos_off, tiles_off, ntiles_off, x16_off, xscale_off, act32_off, act16_off,
+      ascale_off, y_off;
 };
 
-// The tensor-core prefill path: T > 8 tokens, 64-aligned sizes, and a shared
-// expert (if any) as wide as a routed one (one K for the down GEMM).
+// The tensor-core prefill path: T > 8 tokens, K slabs of 256 on both GEMMs,
+// a shared expert (if any) as wide as a routed one (one K for the down GEMM),
+// and 16-byte aligned banks (TMA tensor-map bases).
 bool prefill_shape_ok(const moe_layer_desc* L, int64_t T) {
-  return T > 8 && L->hidden % 64 == 0 && L->inter % 64 == 0 &&
-         (L->shared_inter == 0 || L->shared_inter == L->inter) && L->n_experts <= 1024;
+  const int64_t slab = nvfp4::gemm_slab_k();
+  bool ok = T > 8 && L->hidden % slab == 0 && L->inter % slab == 0 &&
+            (L->shared_inter == 0 || L->shared_inter == L->inter) && L->n_experts <= 1024 &&
+            (int64_t)L->n_experts * std::max(L->hidden, L->inter) < (1ll << 31);
+  const nvfp4_bank* banks[6] = {&L->gate, &L->up, &L->down,
+                                &L->shared_gate, &L->shared_up, &L->shared_down};
+  for (int i = 0; i < (L->shared_inter > 0 ? 6 : 3); i++)
+    ok = ok && aligned16(banks[i]->w) && aligned16(banks[i]->scales);
+  return ok;
 }
 
 BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
@@ -111,8 +122,12 @@ BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
     B.pos_off = align_up(B.brow_off + (size_t)B.S * sizeof(int), 256);
     B.tiles_off = align_up(B.pos_off + (size_t)B.P * sizeof(int), 256);
     B.ntiles_off = align_up(B.tiles_off + (size_t)B.max_tiles * 16, 256);
-    B.act16_off = align_up(B.ntiles_off + 16, 256);
-    B.y_off = align_up(B.act16_off + (size_t)B.S * B.act_ld * 2, 256);
+    B.x16_off = align_up(B.ntiles_off + 16, 256);
+    B.xscale_off = align_up(B.x16_off + (size_t)B.S * L->hidden * 2, 256);
+    B.act32_off = align_up(B.xscale_off + (size_t)B.S * sizeof(float), 256);
+    B.act16_off = align_up(B.act32_off + (size_t)B.S * B.act_ld * sizeof(float), 256);
+    B.ascale_off = align_up(B.act16_off + (size_t)B.S * B.act_ld * 2, 256);
+    B.y_off = align_up(B.ascale_off + (size_t)B.S * sizeof(float), 256);
     B.total = align_up(B.y_off + (size_t)B.S * L->hidden * sizeof(float), 256);
   }
   return B;
@@ -262,28 +277,28 @@ int nvfp4_quantized_matmul(void* y, const void* x, int dtype, const uint32_t* w,
                 "[quantized_matmul] Only real floating types are supported.");
   if (int r = check_qdims("quantized_matmul", N, K)) return r;
   if (M < 0) return fail(NVFP4_ERR_INVALID, "[quantized_matmul] Invalid M.");
-  // Many rows: the tcgen05 GEMM streams W once for all of them.
-  if (M > 8 && K % 64 == 0 && N > 0 && M <= 0x7fffffff && x && y && w && scales &&
-      aligned16(x) && aligned16(w) && (K * (dtype == NVFP4_F32 ? 4 : 2)) % 16 == 0 &&
-      (reinterpret_cast<uintptr_t>(scales) & 3) == 0) {
+  // Many 16-bit rows: the tcgen05 GEMM streams W once per 64 rows.
+  if (M > 8 && dtype != NVFP4_F32 && K % nvfp4::gemm_slab_k() == 0 && N > 0 &&
+      N < (1ll << 31) && M < (1ll << 31) && x && y && w && scales && aligned16(x) &&
+      aligned16(w) && aligned16(scales)) {
     nvfp4::GemmArgs g{};
     g.mode = 0;
     g.K = (int)K;
     g.Mrows = (int)N;
     g.Mrows_shared = 0;
-    g.w0 = g.w1 = reinterpret_cast<const uint8_t*>(w);
-    g.s0 = g.s1 = scales;
     g.shared_group = -1;
-    g.b = x;
-    g.b_dtype = dtype;
-    g.b_ld = K;
     g.implicit_M = (int)M;
     g.out = y;
     g.out_dtype = dtype;
     g.out_ld = N;
-    const int tiles = (int)((M + nvfp4::gemm_tile_tokens() - 1) / nvfp4::gemm_tile_tokens());
-    return check_cuda(nvfp4::launch_nvfp4_gemm(g, tiles, (cudaStream_t)stream, first_pdl()),
-                      "quantized_matmul");
+    if (nvfp4::map_codes(&g.mc0, w, N, K, 128) == cudaSuccess &&
+        nvfp4::map_scales(&g.ms0, scales, N, K, 128) == cudaSuccess &&
+        nvfp4::map_rows16(&g.mb, x, dtype == NVFP4_BF16, M, K, K) == cudaSuccess) {
+      const int tiles = (int)((M + nvfp4::gemm_tile_tokens() - 1) / nvfp4::gemm_tile_tokens());
+      return check_cuda(nvfp4::launch_nvfp4_gemm(g, dtype == NVFP4_F16, tiles,
+                                                 (cudaStream_t)stream, first_pdl()),
+                        "quantized_matmul");
+    }
   }
   // One "pair" whose M rows are the whole activation matrix.
   return nvfp4_gather_qmm(y, x, dtype, w, scales, nullptr, nullptr, 1, 1, 1, M, N, K, 0,
@@ -435,7 +450,9 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
 
 // Prefill: sort pairs by expert, gate/up + SwiGLU and down as tcgen05
 // grouped GEMMs over expert-sorted token slots (the shared expert is one more
-// group holding every token), then the weighted per-token combine.
+// group holding every token), then the weighted per-token combine.  Both GEMMs
+// take f16 operands: x and the intermediate go through rows_to_f16 first
+// (per-row power-of-two scale, re-applied in the GEMM epilogue).
 static int prefill_impl(void* y, const void* x, const void* residual, int dtype, int64_t T,
                         const moe_layer_desc* L, const uint32_t* inds, const float* wts, char* ws,
                         const BlockLayout& B, nvfp4_stream stream, bool pdl_first) {
@@ -447,7 +464,11 @@ static int prefill_impl(void* y, const void* x, const void* residual, int dtype,
   int* pos = reinterpret_cast<int*>(ws + B.pos_off);
   int4* tiles = reinterpret_cast<int4*>(ws + B.tiles_off);
   int* ntiles = reinterpret_cast<int*>(ws + B.ntiles_off);
-  void* act16 = ws + B.act16_off;
+  __half* x16 = reinterpret_cast<__half*>(ws + B.x16_off);
+  float* xscale = reinterpret_cast<float*>(ws + B.xscale_off);
+  float* act32 = reinterpret_cast<float*>(ws + B.act32_off);
+  __half* act16 = reinterpret_cast<__half*>(ws + B.act16_off);
+  float* ascale = reinterpret_cast<float*>(ws + B.ascale_off);
   float* Y = reinterpret_cast<float*>(ws + B.y_off);
 
   nvfp4::SortArgs sa{};
@@ -463,59 +484,86 @@ static int prefill_impl(void* y, const void* x, const void* residual, int dtype,
   sa.ntiles = ntiles;
   if (int r = check_cuda(nvfp4::launch_moe_sort(sa, s, pdl_first), op)) return r;
 
+  // x rows in slot order (shared-expert slots P.. hold tokens 0..T-1).
+  nvfp4::RowsArgs rx{};
+  rx.src = x;
+  rx.src_dtype = dtype;
+  rx.src_map = brow;
+  rx.rows = (int)B.S;
+  rx.K = (int)H;
+  rx.src_ld = H;
+  rx.dst = x16;
+  rx.dst_ld = H;
+  rx.scale = xscale;
+  if (int r = check_cuda(nvfp4::launch_rows_to_f16(rx, s, true), op)) return r;
+
+  // Tensor maps: routed banks stack E groups of rows; 64-row boxes for the
+  // gate/up halves of a gate/up tile, 128-row boxes for down.
+  const int64_t Is = L->shared_inter;
+  auto maps_ok = [](std::initializer_list<cudaError_t> l) {
+    for (cudaError_t e : l)
+      if (e != cudaSuccess) return false;
+    return true;
+  };
   nvfp4::GemmArgs g{};
   g.mode = 1;
   g.K = (int)H;
   g.Mrows = (int)I;
-  g.Mrows_shared = (int)L->shared_inter;
-  g.w0 = reinterpret_cast<const uint8_t*>(L->gate.w);
-  g.s0 = L->gate.scales;
-  g.w1 = reinterpret_cast<const uint8_t*>(L->up.w);
-  g.s1 = L->up.scales;
-  g.w_stride = I * (H / 2);
-  g.s_stride = I * (H / 16);
+  g.Mrows_shared = (int)Is;
   g.shared_group = sh ? (int)E : -1;
-  if (sh) {
-    g.sw0 = reinterpret_cast<const uint8_t*>(L->shared_gate.w);
-    g.ss0 = L->shared_gate.scales;
-    g.sw1 = reinterpret_cast<const uint8_t*>(L->shared_up.w);
-    g.ss1 = L->shared_up.scales;
-  }
-  g.b = x;
-  g.b_dtype = dtype;
-  g.b_ld = H;
-  g.brow = brow;
+  bool ok = maps_ok({nvfp4::map_codes(&g.mc0, L->gate.w, E * I, H, 64),
+                     nvfp4::map_scales(&g.ms0, L->gate.scales, E * I, H, 64),
+                     nvfp4::map_codes(&g.mc1, L->up.w, E * I, H, 64),
+                     nvfp4::map_scales(&g.ms1, L->up.scales, E * I, H, 64),
+                     nvfp4::map_rows16(&g.mb, x16, false, B.S, H, H)});
+  if (sh)
+    ok = ok && maps_ok({nvfp4::map_codes(&g.mcs0, L->shared_gate.w, Is, H, 64),
+                        nvfp4::map_scales(&g.mss0, L->shared_gate.scales, Is, H, 64),
+                        nvfp4::map_codes(&g.mcs1, L->shared_up.w, Is, H, 64),
+                        nvfp4::map_scales(&g.mss1, L->shared_up.scales, Is, H, 64)});
+  g.bscale = xscale;
   g.tiles = tiles;
   g.ntiles = ntiles;
-  g.out = act16;
-  g.out_dtype = NVFP4_BF16;
+  g.out = act32;
+  g.out_dtype = NVFP4_F32;
   g.out_ld = B.act_ld;
-  if (int r = check_cuda(nvfp4::launch_nvfp4_gemm(g, (int)B.max_tiles, s, true), op)) return r;
 
   nvfp4::GemmArgs d{};
   d.mode = 2;
   d.K = (int)I;
   d.Mrows = (int)H;
   d.Mrows_shared = (int)H;
-  d.w0 = d.w1 = reinterpret_cast<const uint8_t*>(L->down.w);
-  d.s0 = d.s1 = L->down.scales;
-  d.w_stride = H * (I / 2);
-  d.s_stride = H * (I / 16);
   d.shared_group = sh ? (int)E : -1;
-  if (sh) {
-    d.sw0 = d.sw1 = reinterpret_cast<const uint8_t*>(L->shared_down.w);
-    d.ss0 = d.ss1 = L->shared_down.scales;
-  }
-  d.b = act16;
-  d.b_dtype = NVFP4_BF16;
-  d.b_ld = B.act_ld;
-  d.brow = nullptr;  // the down GEMM reads act by slot
+  ok = ok && maps_ok({nvfp4::map_codes(&d.mc0, L->down.w, E * H, I, 128),
+                      nvfp4::map_scales(&d.ms0, L->down.scales, E * H, I, 128),
+                      nvfp4::map_rows16(&d.mb, act16, false, B.S, I, B.act_ld)});
+  if (sh)
+    ok = ok && maps_ok({nvfp4::map_codes(&d.mcs0, L->shared_down.w, H, I, 128),
+                        nvfp4::map_scales(&d.mss0, L->shared_down.scales, H, I, 128)});
+  d.bscale = ascale;
   d.tiles = tiles;
   d.ntiles = ntiles;
   d.out = Y;
   d.out_dtype = NVFP4_F32;
   d.out_ld = H;
-  if (int r = check_cuda(nvfp4::launch_nvfp4_gemm(d, (int)B.max_tiles, s, true), op)) return r;
+  if (!ok) return fail(NVFP4_ERR_CUDA, "[%s] tensor-map encoding failed.", op);
+
+  if (int r = check_cuda(nvfp4::launch_nvfp4_gemm(g, true, (int)B.max_tiles, s, true), op))
+    return r;
+
+  nvfp4::RowsArgs ra{};
+  ra.src = act32;
+  ra.src_dtype = NVFP4_F32;
+  ra.rows = (int)B.S;
+  ra.K = (int)I;
+  ra.src_ld = B.act_ld;
+  ra.dst = act16;
+  ra.dst_ld = B.act_ld;
+  ra.scale = ascale;
+  if (int r = check_cuda(nvfp4::launch_rows_to_f16(ra, s, true), op)) return r;
+
+  if (int r = check_cuda(nvfp4::launch_nvfp4_gemm(d, true, (int)B.max_tiles, s, true), op))
+    return r;
 
   nvfp4::CombineArgs c{};
   c.Y = Y;

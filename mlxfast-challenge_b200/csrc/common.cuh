@@ -123,6 +123,30 @@ __device__ __forceinline__ uint32_t ldg_stream_u16(const void* p) {
   return r;
 }
 
+// Eight consecutive activation elements (elem_off % 8 == 0, 16-byte aligned).
+__device__ __forceinline__ void load8(const void* x, int dtype, int64_t elem_off, float (&f)[8]) {
+  if (dtype == kF32) {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + elem_off);
+    const float4 b =
+        *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + elem_off + 4);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + elem_off);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      if (dtype == kBF16) {
+        const float2 p = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        f[2 * i] = p.x; f[2 * i + 1] = p.y;
+      } else {
+        const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        f[2 * i] = p.x; f[2 * i + 1] = p.y;
+      }
+    }
+  }
+}
+
 // Power-of-two exponent e with max_abs * 2^-e in [1, 2); 0 for zero / non-finite.
 __device__ __forceinline__ int pow2_exponent(float max_abs) {
   if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 0;

@@ -2,6 +2,8 @@
 // the C ABI (api.cu) includes this; nothing here crosses the library boundary.
 #pragma once
 
+#include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -71,25 +73,49 @@ struct RouterArgs {
 };
 
 // Grouped NVFP4 GEMM on tcgen05 (prefill.cu).
-struct GemmArgs {
-  int mode;          // 0 plain (y[brow][row]), 1 gate/up + SwiGLU -> bf16 act, 2 down -> f32 Y
-  int K;             // reduction length (multiple of 64)
-  int Mrows;         // rows of one bank per group
-  int Mrows_shared;  // rows of the shared group's bank
-  const uint8_t *w0, *s0, *w1, *s1;  // routed banks (w1/s1: the up bank in mode 1)
-  int64_t w_stride, s_stride;        // bytes per group
-  int shared_group;                  // group id served by the shared banks, -1 none
-  const uint8_t *sw0, *ss0, *sw1, *ss1;
-  const void* b;     // activation rows [*, b_ld]
-  int b_dtype;
-  int64_t b_ld;
-  const int* brow;   // slot -> activation row (null: slot itself)
-  const int4* tiles; // (group, first slot, count, 0)
+// Sorted-slot grouped GEMM (prefill.cu).  Operands arrive by TMA through
+// 2-D tensor maps: packed codes [rows, K/2] bytes (box 128 bytes x 64 or 128
+// rows, 128-byte swizzle), scales [rows, K/16] bytes (box 16 x rows), and
+// 16-bit activation rows in slot order [slots, K] (box 64 elements x 16 rows,
+// 128-byte swizzle).  Routed banks stack the groups' rows (row = group *
+// Mrows + r); the shared group has its own maps.
+struct alignas(64) GemmArgs {
+  CUtensorMap mc0, ms0, mc1, ms1;      // routed codes / scales (mc1, ms1: up bank, mode 1)
+  CUtensorMap mcs0, mss0, mcs1, mss1;  // shared-group codes / scales
+  CUtensorMap mb;                      // activation rows, slot order
+  int mode;          // 0 plain (out[row of slot][n]), 1 gate/up + SwiGLU -> f32 act, 2 down -> f32 Y
+  int K;             // reduction length (multiple of 256)
+  int Mrows;         // rows of one routed group
+  int Mrows_shared;  // rows of the shared group
+  int shared_group;  // group id served by the shared maps, -1 none
+  int implicit_M;    // > 0: one group, slots 0..implicit_M-1, tiles of 64 (no tile list)
+  const float* bscale;  // per slot: true activation row = row * bscale[slot] (null: 1)
+  const int* brow;      // mode 0: slot -> output row (null: the slot itself)
+  const int4* tiles;    // (group, first slot, count, 0)
   const int* ntiles;
-  int implicit_M;    // > 0: one group, slots 0..implicit_M-1, tiles of 64 (no tiles/brow)
   void* out;
   int out_dtype;
   int64_t out_ld;
+};
+
+// Tensor maps for GemmArgs (cuTensorMapEncodeTiled through the runtime's
+// driver entry point).  rows: rows of the whole bank / activation matrix.
+cudaError_t map_codes(CUtensorMap* m, const void* w, int64_t rows, int64_t K, int box_rows);
+cudaError_t map_scales(CUtensorMap* m, const void* s, int64_t rows, int64_t K, int box_rows);
+cudaError_t map_rows16(CUtensorMap* m, const void* b, bool bf16, int64_t rows, int64_t K,
+                       int64_t ld);
+
+// Rows of any activation dtype -> f16 rows scaled by a per-row power of two
+// (rows_to_f16_kernel); scale[r] receives the factor that undoes it.
+struct RowsArgs {
+  const void* src;
+  int src_dtype;
+  const int* src_map;  // dst row r <- src row src_map[r] (null: r)
+  int rows, K;
+  int64_t src_ld;
+  __half* dst;
+  int64_t dst_ld;
+  float* scale;
 };
 
 struct SortArgs {
@@ -114,7 +140,10 @@ struct CombineArgs {
 
 size_t gemm_smem_bytes();
 int gemm_tile_tokens();
-cudaError_t launch_nvfp4_gemm(const GemmArgs& a, int max_tiles, cudaStream_t stream, bool pdl);
+cudaError_t launch_nvfp4_gemm(const GemmArgs& a, bool f16, int max_tiles, cudaStream_t stream,
+                              bool pdl);
+int gemm_slab_k();
+cudaError_t launch_rows_to_f16(const RowsArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t launch_moe_sort(const SortArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t launch_moe_combine(const CombineArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t read_and_clear_prefill_error(int* out);

@@ -1,52 +1,68 @@
 // prefill.cu -- the sorted-expert (grouped) NVFP4 GEMM on sm_100a tensor
-// cores (tcgen05, TMEM accumulators) and the MoE prefill plumbing around it.
+// cores (tcgen05, TMEM accumulators, TMA operand feeds) and the MoE prefill
+// plumbing around it.
 //
 // Reference semantics: gather_qmm over tokens sorted by expert
 // (VMLX/backend/cpu/quantized.cpp:805-844 per pair; SwitchGLU with
 // sortedIndices, VLM/MLXLMCommon/SwitchLayers.swift:532-580; gatherSort /
 // scatterUnsort :385-428), the Laguna block combine (Laguna.swift:204-212).
 //
-// GEMM shape: D[weight rows, tokens] = W[rows, K] x X[tokens, K]^T per tile of
-// 128 weight rows (UMMA M) and up to 64 tokens (UMMA N), K in stages of 64.
-// A three-stage pipeline per CTA: a raw-loader warp streams the packed codes
-// and scales of the tile rows into an 8-deep shared ring with 16-byte
-// cp.async copies (mbarrier arrivals on completion); four dequantiser warps
-// turn each stage into bf16 straight in the 128-byte swizzled K-major UMMA
-// layout (E2M1 pairs by the hardware converter, times the E4M3 group scale:
-// exact in bf16); an activation-loader warp gathers the tile's token rows
-// (through a slot -> row map, so no sorted copy of the activations is ever
-// written) with cp.async into the swizzled B stage; one thread issues
-// tcgen05.mma kind::f16 (bf16 x bf16 -> f32 in TMEM) and commits each stage
-// back to its producers through an mbarrier.  Activations stay bf16 (exact
-// for bf16 inputs, the full bf16 range).  After the K loop the dequantiser
-// warps read TMEM (tcgen05.ld 32x32b) and run the epilogue:
-//   mode 0 (plain)   y[row of token][n] = D                      (dense qmm)
-//   mode 1 (gate/up) tile rows interleave gate row i / up row i, so adjacent
-//                    TMEM lanes pair up: act = silu(gate) * up -> bf16
-//   mode 2 (down)    Y[slot][n] = D  (f32, combined per token afterwards)
-// All mbarrier waits are bounded (tma.cuh); on expiry error 4 is latched and
-// the CTA drains before releasing TMEM.
+// GEMM: D[weight rows, tokens] = W[rows, K] x X[tokens, K]^T in tiles of 128
+// weight rows (UMMA M) by up to 64 tokens (UMMA N), K in MMA stages of 64.
+// One persistent CTA per SM walks its tiles; warp roles form a pipeline that
+// runs across tile boundaries:
+//   weight TMA (1 thread)  per 256-wide K slab, the tile rows' packed codes
+//                          (16 KB, 128-byte swizzle) and E4M3 scales (2 KB)
+//                          into a 4-deep ring;
+//   dequantisers (8 warps) per MMA stage, each thread a half row: E2M1 pairs
+//                          by the hardware converter times the group scale
+//                          (exact in f16 / bf16), stored straight into the
+//                          128-byte swizzled K-major UMMA layout;
+//   activation TMA         16-row boxes of the tile's slot-ordered 16-bit
+//   (1 thread)             activation rows into the B stage;
+//   MMA issuer (1 thread)  tcgen05.mma kind::f16 into one of two TMEM
+//                          accumulators; each stage committed back to the
+//                          producers through an mbarrier;
+//   epilogue (4 warps)     tcgen05.ld of the finished accumulator (one TMEM
+//                          sub-partition each) while the next tile runs.
+// Operand type: f16 for pre-scaled activation rows (rows_to_f16: per-row power
+// of two, exact for bf16 inputs, re-applied in the epilogue) and for f16
+// inputs; bf16 for bf16 inputs (dense quantized_matmul, no workspace).
+// Epilogue modes: 0 plain out[row of slot][n] = D; 1 gate/up: tile rows
+// interleave gate row i / up row i, adjacent TMEM lanes pair up and
+// act = silu(gate) * up (f32); 2 down: Y[slot][n] = D (f32, combined per token
+// afterwards).  All mbarrier waits are bounded (tma.cuh): on expiry error 4 is
+// latched and every role leaves its loop before TMEM is released.
 #include "common.cuh"
 #include "kernels.h"
 #include "umma.cuh"
 
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
 namespace nvfp4 {
 namespace {
 
-constexpr int kBM = 128;                          // weight rows per tile
-constexpr int kBN = 64;                           // tokens per tile (max UMMA N used)
-constexpr int kBK = 64;                           // K per stage: one 128 B swizzle atom of bf16
-constexpr int kStages = 3;                        // bf16 A/B stages fed to the MMA
-constexpr int kRawSlots = 5;                      // packed-weight stages in flight (2 CTAs / SM)
-constexpr int kDeqWarps = 4;
-constexpr int kGemmThreads = 32 * (3 + kDeqWarps);
-constexpr int kStageA = kBM * kBK * 2;            // 16 KB
-constexpr int kStageB = kBN * kBK * 2;            // 8 KB
-constexpr int kRawPitch = 48;                     // 32 code bytes + pad: conflict-free reads
-constexpr int kRawCodes = kBM * kRawPitch;        // 6 KB
-constexpr int kRawSlot = kRawCodes + kBM * 4;     // + 4 scale bytes per row
-constexpr int kTmemCols = 64;
+constexpr int kBM = 128;                     // weight rows per tile
+constexpr int kBN = 64;                      // tokens per tile (max UMMA N used)
+constexpr int kBK = 64;                      // K per MMA stage: one 128 B swizzle row of 16-bit
+constexpr int kSlabK = 256;                  // K per weight slab (128 code bytes per row)
+constexpr int kStages = 4;                   // A/B stages fed to the MMA
+constexpr int kRawSlots = 4;                 // weight slabs in flight
+constexpr int kDeqWarps = 8;
+constexpr int kEpiWarps = 4;
+constexpr int kWarpMma = 0, kWarpRaw = 1, kWarpAct = 2, kWarpDeq0 = 3;
+constexpr int kWarpEpi0 = kWarpDeq0 + kDeqWarps;  // 11..14: TMEM sub-partitions 3,0,1,2
+constexpr int kGemmThreads = 32 * (kWarpEpi0 + kEpiWarps);
+constexpr int kStageA = kBM * kBK * 2;       // 16 KB
+constexpr int kStageB = kBN * kBK * 2;       // 8 KB
+constexpr int kBoxB = 16 * kBK * 2;          // one 16-row activation box, 2 KB
+constexpr int kRawCodes = kBM * 128;         // 16 KB
+constexpr int kRawSlot = kRawCodes + kBM * 16;  // + 16 scale bytes per row
+constexpr int kTmemCols = 2 * kBN;           // two accumulators
 constexpr int kErrTimeout = 4;
+constexpr long long kDrainBudget = 200000000LL;  // ~0.1 s: in-flight copies on an error path
 
 __device__ int g_prefill_error = 0;
 __device__ __forceinline__ void flag(int code) { atomicCAS(&g_prefill_error, 0, code); }
@@ -56,77 +72,81 @@ __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// 8 bf16 (16 bytes) from eight E2M1 codes of one word and their f32 scale.
-__device__ __forceinline__ uint4 dequant8_bf16(uint32_t word, float scale) {
+// 2-D tiled TMA load of this GPU's memory into this CTA's shared memory
+// (no multicast); x is the inner coordinate in elements.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ---- dequantisation of 8 codes (one word) into 16 bytes of operand ----------
+__device__ __forceinline__ uint4 dequant8_f16(uint32_t word, uint32_t scale_f16x2) {
   uint32_t h[4];
   e2m1x8_to_f16x2x4(word, h);
+  return make_uint4(hmul2_u32(h[0], scale_f16x2), hmul2_u32(h[1], scale_f16x2),
+                    hmul2_u32(h[2], scale_f16x2), hmul2_u32(h[3], scale_f16x2));
+}
+
+__device__ __forceinline__ uint4 dequant8_bf16(uint32_t word, uint32_t scale_f16x2) {
+  uint32_t h[4];
+  e2m1x8_to_f16x2x4(word, h);
+  const float s = __half2float(__ushort_as_half((unsigned short)(scale_f16x2 & 0xFFFFu)));
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; i++) {
     const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[i]));
-    const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * scale, f.y * scale);
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f.x * s, f.y * s);
     o[i] = *reinterpret_cast<const uint32_t*>(&b);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Eight activation values of one row as bf16x8 (16 bytes).
-__device__ __forceinline__ uint4 load8_as_bf16(const void* x, int dtype, int64_t off) {
-  if (dtype == kBF16) return *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + off);
-  uint32_t o[4];
-  if (dtype == kF16) {
-    const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + off);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-      const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
-      o[i] = *reinterpret_cast<const uint32_t*>(&b);
-    }
+// ---- tile bookkeeping (identical in every role) --------------------------------
+struct TileInfo {
+  int grp, start, count, N, m_tile, Mrows;
+  bool is_shared;
+};
+
+__device__ __forceinline__ int total_tiles(const GemmArgs& a, int m_tiles) {
+  const int ngt = a.implicit_M > 0 ? (a.implicit_M + kBN - 1) / kBN : *a.ntiles;
+  return ngt * m_tiles;
+}
+
+// Tile u: token tile u / m_tiles, weight-row tile u % m_tiles (consecutive
+// CTAs share a token tile, so its activation rows are read from L2).  Returns
+// false when that weight-row tile lies beyond the group's rows.
+__device__ __forceinline__ bool tile_info(const GemmArgs& a, int u, int m_tiles, TileInfo& ti) {
+  const int gt = u / m_tiles;
+  ti.m_tile = u - gt * m_tiles;
+  if (a.implicit_M > 0) {
+    ti.grp = 0;
+    ti.start = gt * kBN;
+    ti.count = min(kBN, a.implicit_M - gt * kBN);
   } else {
-    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + off);
-    const float4 c = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + off + 4);
-    const float f[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-      o[i] = *reinterpret_cast<const uint32_t*>(&b);
-    }
+    const int4 td = a.tiles[gt];
+    ti.grp = td.x;
+    ti.start = td.y;
+    ti.count = td.z;
   }
-  return make_uint4(o[0], o[1], o[2], o[3]);
+  ti.N = (ti.count + 15) & ~15;
+  ti.is_shared = ti.grp == a.shared_group;
+  ti.Mrows = ti.is_shared ? a.Mrows_shared : a.Mrows;
+  return ti.m_tile * (a.mode == 1 ? 64 : 128) < ti.Mrows;
 }
 
-// cp.async helpers (16-byte L2-only copies, 4-byte copies, zero-fill).
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
-               "r"(valid ? 4 : 0)
-               : "memory");
-}
-// One arrival on `bar` once all of this thread's prior cp.async copies landed.
-__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// Warp roles: 0 = TMEM owner + MMA issuer (lane 0), 1 = raw weight loader,
-// 2 = activation loader, 3..6 = dequantisers, then the epilogue.
-constexpr int kWarpMma = 0, kWarpRaw = 1, kWarpAct = 2, kWarpDeq0 = 3;
-
-__global__ void __launch_bounds__(kGemmThreads, 1) nvfp4_gemm_kernel(GemmArgs a) {
+template <bool F16>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ GemmArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  // UMMA swizzle atoms need 1024-byte alignment.
+  // Swizzle atoms (TMA and UMMA) need 1024-byte alignment.
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
@@ -136,237 +156,306 @@ __global__ void __launch_bounds__(kGemmThreads, 1) nvfp4_gemm_kernel(GemmArgs a)
   uint64_t* empty = full + kStages;
   uint64_t* raw_full = empty + kStages;
   uint64_t* raw_empty = raw_full + kRawSlots;
-  uint64_t* done = raw_empty + kRawSlots;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-
-  // Tiles, token maps and activations come from preceding kernels.
-  pdl_wait();
-  pdl_trigger();
-  const int tile = blockIdx.y;
-  int4 td;
-  if (a.implicit_M > 0) {
-    if (tile * kBN >= a.implicit_M) return;
-    td = make_int4(0, tile * kBN, min(kBN, a.implicit_M - tile * kBN), 0);
-  } else {
-    if (tile >= *a.ntiles) return;
-    td = a.tiles[tile];
-  }
-  const int grp = td.x, start = td.y, count = td.z;
-  const int N = (count + 15) & ~15;
-  const int m_tile = blockIdx.x;
-  const bool is_shared = grp == a.shared_group;
-  const int Mrows = is_shared ? a.Mrows_shared : a.Mrows;
-  const int row_step = a.mode == 1 ? 64 : 128;
-  if (m_tile * row_step >= Mrows) return;
+  uint64_t* acc_full = raw_empty + kRawSlots;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; i++) {
-      mbar_init(&full[i], kDeqWarps + 32);  // dequant warps + activation-loader lanes
-      mbar_init(&empty[i], 1);              // MMA commit
+      mbar_init(&full[i], kDeqWarps + 1);  // dequantiser warps + activation TMA (with tx)
+      mbar_init(&empty[i], 1);             // MMA commit
     }
     for (int i = 0; i < kRawSlots; i++) {
-      mbar_init(&raw_full[i], 32);          // raw-loader lanes (cp.async arrivals)
+      mbar_init(&raw_full[i], 1);          // weight TMA (with tx)
       mbar_init(&raw_empty[i], kDeqWarps);
     }
-    mbar_init(done, 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&acc_full[i], 1);          // MMA commit at the end of a tile
+      mbar_init(&acc_empty[i], kEpiWarps);
+    }
+    mbar_init(drain, 1);
     fence_barrier_init();
   }
+  if (warp == kWarpRaw && lane == 0) {
+    prefetch_map(&a.mc0);
+    prefetch_map(&a.ms0);
+  }
+  // Tiles, slot maps and activations come from preceding kernels.
+  pdl_wait();
+  pdl_trigger();
+  const int m_tiles = a.mode == 1 ? (max(a.Mrows, a.Mrows_shared) + 63) / 64
+                                  : (max(a.Mrows, a.Mrows_shared) + 127) / 128;
+  const int ntot = total_tiles(a, m_tiles);
+  if ((int)blockIdx.x >= ntot) return;  // uniform per CTA, before any barrier use
   if (warp == kWarpMma) tmem_alloc(tmem_slot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int nkb = a.K / kBK;
-
-  // Bank row behind tile row r (gate/up interleave in mode 1).
-  auto bank_row = [&](int r, const uint8_t*& wb, const uint8_t*& sb, int64_t& row) {
-    const uint8_t* w0 = is_shared ? a.sw0 : a.w0 + (int64_t)grp * a.w_stride;
-    const uint8_t* s0 = is_shared ? a.ss0 : a.s0 + (int64_t)grp * a.s_stride;
-    const uint8_t* w1 = is_shared ? a.sw1 : a.w1 + (int64_t)grp * a.w_stride;
-    const uint8_t* s1 = is_shared ? a.ss1 : a.s1 + (int64_t)grp * a.s_stride;
-    if (a.mode == 1) {
-      row = (int64_t)m_tile * 64 + (r >> 1);
-      wb = (r & 1) ? w1 : w0;
-      sb = (r & 1) ? s1 : s0;
-    } else {
-      row = (int64_t)m_tile * 128 + r;
-      wb = w0;
-      sb = s0;
-    }
-  };
+  const int nslab = a.K / kSlabK;
 
   if (warp == kWarpMma) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16_f32(kBM, N) | (1u << 7) | (1u << 10);  // A, B bf16
-      for (int kb = 0; kb < nkb; kb++) {
-        const int s = kb % kStages;
-        if (!mbar_wait_bounded(&full[s], (kb / kStages) & 1)) {
+      uint32_t it = 0;
+      int j = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
+        TileInfo ti;
+        if (!tile_info(a, u, m_tiles, ti)) continue;
+        const int buf = j & 1;
+        if (j >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((j >> 1) - 1) & 1)) {
           flag(kErrTimeout);
           break;
         }
         tc_fence_after();
-        const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * kStageA));
-        const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * kStageB));
+        const uint32_t idesc =
+            idesc_f16_f32(kBM, ti.N) | (F16 ? 0u : ((1u << 7) | (1u << 10)));
+        const uint32_t d = tmem + (uint32_t)(buf * kBN);
+        for (int kb = 0; kb < nkb; kb++, it++) {
+          const int s = it % kStages;
+          if (!mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
+            flag(kErrTimeout);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * kStageA));
+          const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * kStageB));
 #pragma unroll
-        for (int ks = 0; ks < kBK / 16; ks++)  // 16 bf16 = 32 bytes = 2 descriptor units
-          umma_f16(tmem, ad + 2 * ks, bd + 2 * ks, idesc, (kb | ks) != 0);
-        umma_commit(&empty[s]);
+          for (int ks = 0; ks < kBK / 16; ks++)  // 16 elements = 32 bytes = 2 descriptor units
+            umma_f16(d, ad + 2 * ks, bd + 2 * ks, idesc, (kb | ks) != 0);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[buf]);  // the accumulator is complete once these MMAs are
+        j++;
       }
-      umma_commit(done);  // fires when every MMA issued above has completed
+      // No MMA may still write TMEM when it is released.
+      umma_commit(drain);
+      if (!mbar_wait_bounded(drain, 0)) flag(kErrTimeout);
     }
     __syncwarp();
   } else if (warp == kWarpRaw) {
-    // --------------------------- raw weight loader ---------------------------
-    // Lane l copies rows l, l+32, l+64, l+96: 32 code bytes (two 16 B copies)
-    // and 4 scale bytes per row and stage, R stages ahead of the dequantisers.
-    const uint8_t* cptr[4];
-    const uint8_t* sptr[4];
-    bool rok[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const uint8_t *wb, *sb;
-      int64_t row;
-      bank_row(lane + 32 * i, wb, sb, row);
-      rok[i] = row < Mrows;
-      cptr[i] = rok[i] ? wb + row * (a.K / 2) : a.w0;
-      sptr[i] = rok[i] ? sb + row * (a.K / 16) : a.s0;
-    }
-    for (int kb = 0; kb < nkb; kb++) {
-      const int r = kb % kRawSlots;
-      if (kb >= kRawSlots && !mbar_wait_bounded(&raw_empty[r], ((kb / kRawSlots) - 1) & 1)) {
-        flag(kErrTimeout);
-        break;
-      }
-      uint8_t* slot = sRaw + r * kRawSlot;
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int tr = lane + 32 * i;
-        cp_async16(slot + tr * kRawPitch, cptr[i] + kb * 32, rok[i]);
-        cp_async16(slot + tr * kRawPitch + 16, cptr[i] + kb * 32 + 16, rok[i]);
-        cp_async4(slot + kRawCodes + tr * 4, sptr[i] + kb * 4, rok[i]);
-      }
-      cp_async_arrive_noinc(&raw_full[r]);
-    }
-    cp_async_wait<0>();
-  } else if (warp == kWarpAct) {
-    // --------------------------- activation loader ---------------------------
-    // Lane l copies 16-byte chunks q = l + 32 i (token n = q / 8, chunk q % 8)
-    // of the tile's rows into the swizzled B stage.  Copies of stage kb are
-    // one commit group; the stage is handed to the MMA (proxy fence + arrive)
-    // once its group has landed, kStages - 1 stages later.
-    const bool direct = a.b_dtype == kBF16;
-    int64_t brow[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) {
-      const int n = (lane + 32 * i) >> 3;
-      brow[i] = n < count ? (int64_t)(a.brow ? a.brow[start + n] : start + n) : -1;
-    }
-    int issued = 0, handed = 0;
-    for (int kb = 0; kb < nkb; kb++) {
-      const int s = kb % kStages;
-      if (kb >= kStages && !mbar_wait_bounded(&empty[s], ((kb / kStages) - 1) & 1)) {
-        flag(kErrTimeout);
-        break;
-      }
-      uint8_t* stage = sB + s * kStageB;
-#pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const int q = lane + 32 * i, n = q >> 3, c = q & 7;
-        uint8_t* dst = stage + n * 128 + ((c ^ (n & 7)) << 4);
-        const int64_t off = (brow[i] >= 0 ? brow[i] : 0) * a.b_ld + kb * kBK + c * 8;
-        if (direct) {
-          cp_async16(dst, reinterpret_cast<const uint16_t*>(a.b) + off, brow[i] >= 0);
-        } else {
-          *reinterpret_cast<uint4*>(dst) =
-              brow[i] >= 0 ? load8_as_bf16(a.b, a.b_dtype, off) : make_uint4(0, 0, 0, 0);
-        }
-      }
-      cp_async_commit();
-      issued++;
-      if (issued - handed == kStages - 1) {
-        cp_async_wait<kStages - 2>();
-        fence_proxy_async();
-        mbar_arrive(&full[handed % kStages]);
-        handed++;
-      }
-    }
-    cp_async_wait<0>();
-    fence_proxy_async();
-    for (; handed < issued; handed++) mbar_arrive(&full[handed % kStages]);
-  } else {
-    // ------------------------------ dequantisers ------------------------------
-    const int pt = threadIdx.x - 32 * kWarpDeq0;  // 0..127: this thread's A row
-    for (int kb = 0; kb < nkb; kb++) {
-      const int r = kb % kRawSlots, s = kb % kStages;
-      if (!mbar_wait_bounded(&raw_full[r], (kb / kRawSlots) & 1)) {
-        flag(kErrTimeout);
-        break;
-      }
-      const uint8_t* slot = sRaw + r * kRawSlot;
-      const uint4 cw0 = *reinterpret_cast<const uint4*>(slot + pt * kRawPitch);
-      const uint4 cw1 = *reinterpret_cast<const uint4*>(slot + pt * kRawPitch + 16);
-      const uint32_t sw = *reinterpret_cast<const uint32_t*>(slot + kRawCodes + pt * 4);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&raw_empty[r]);
-      if (kb >= kStages && !mbar_wait_bounded(&empty[s], ((kb / kStages) - 1) & 1)) {
-        flag(kErrTimeout);
-        break;
-      }
-      uint8_t* arow = sA + s * kStageA + pt * 128;
-      const int sw7 = pt & 7;
-      const uint32_t wds[8] = {cw0.x, cw0.y, cw0.z, cw0.w, cw1.x, cw1.y, cw1.z, cw1.w};
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const float scale = scale_to_f32((sw >> (8 * (j >> 1))) & 0xFFu);
-        *reinterpret_cast<uint4*>(arow + ((j ^ sw7) << 4)) = dequant8_bf16(wds[j], scale);
-      }
-      fence_proxy_async();  // generic-proxy smem writes -> tensor-core reads
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full[s]);
-    }
-    // ------------------------------ epilogue --------------------------------
-    // Warp-uniform decision: the TMEM loads below are .sync.aligned.
-    const bool have = __all_sync(0xffffffffu, mbar_wait_bounded(done, 0));
-    if (!have && lane == 0) flag(kErrTimeout);
-    tc_fence_after();
-    const int sp = warp & 3;       // TMEM sub-partition this warp may read
-    const int r = sp * 32 + lane;  // tile row = TMEM lane
-    for (int c0 = 0; c0 < N && have; c0 += 16) {
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)c0, v);
-      if (a.mode == 1) {
-        const int64_t i = (int64_t)m_tile * 64 + (r >> 1);
-#pragma unroll
-        for (int q = 0; q < 16; q++) {
-          const float other = __shfl_xor_sync(0xffffffffu, v[q], 1);
-          const int n = c0 + q;
-          if (!(r & 1) && n < count && i < Mrows)
-            reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)(start + n) * a.out_ld + i] =
-                __float2bfloat16_rn(silu_ref(v[q]) * other);
-        }
-      } else {
-        const int64_t rr = (int64_t)m_tile * 128 + r;
-#pragma unroll
-        for (int q = 0; q < 16; q++) {
-          const int n = c0 + q;
-          if (n < count && rr < Mrows) {
-            if (a.mode == 2)
-              reinterpret_cast<float*>(a.out)[(int64_t)(start + n) * a.out_ld + rr] = v[q];
-            else
-              store_from_f32(a.out, a.out_dtype,
-                             (int64_t)(a.brow ? a.brow[start + n] : start + n) * a.out_ld + rr,
-                             v[q]);
+    // ------------------------------ weight TMA ------------------------------
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
+        TileInfo ti;
+        if (!tile_info(a, u, m_tiles, ti)) continue;
+        const CUtensorMap* c0 = ti.is_shared ? &a.mcs0 : &a.mc0;
+        const CUtensorMap* s0 = ti.is_shared ? &a.mss0 : &a.ms0;
+        const CUtensorMap* c1 = ti.is_shared ? &a.mcs1 : &a.mc1;
+        const CUtensorMap* s1 = ti.is_shared ? &a.mss1 : &a.ms1;
+        const int row0 =
+            (ti.is_shared ? 0 : ti.grp * a.Mrows) + ti.m_tile * (a.mode == 1 ? 64 : 128);
+        for (int sl = 0; sl < nslab; sl++, g++) {
+          const int r = g % kRawSlots;
+          if (g >= kRawSlots &&
+              !mbar_wait_bounded(&raw_empty[r], ((g / kRawSlots) - 1) & 1)) {
+            flag(kErrTimeout);
+            ok = false;
+            break;
+          }
+          uint8_t* slot = sRaw + r * kRawSlot;
+          mbar_arrive_expect_tx(&raw_full[r], kRawSlot);
+          if (a.mode == 1) {
+            tma_load_2d(slot, c0, sl * 128, row0, &raw_full[r]);
+            tma_load_2d(slot + kRawCodes / 2, c1, sl * 128, row0, &raw_full[r]);
+            tma_load_2d(slot + kRawCodes, s0, sl * 16, row0, &raw_full[r]);
+            tma_load_2d(slot + kRawCodes + 64 * 16, s1, sl * 16, row0, &raw_full[r]);
+          } else {
+            tma_load_2d(slot, c0, sl * 128, row0, &raw_full[r]);
+            tma_load_2d(slot + kRawCodes, s0, sl * 16, row0, &raw_full[r]);
           }
         }
       }
+      // No copy may still be in flight when the CTA exits (immediate unless a
+      // wait above gave up).
+      for (uint32_t i = 0; i < min(g, (uint32_t)kRawSlots); i++) {
+        const uint32_t gg = g - 1 - i;
+        mbar_wait_bounded(&raw_full[gg % kRawSlots], (gg / kRawSlots) & 1, kDrainBudget);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kWarpAct) {
+    // ---------------------------- activation TMA ----------------------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
+        TileInfo ti;
+        if (!tile_info(a, u, m_tiles, ti)) continue;
+        const int nbox = ti.N / 16;
+        for (int kb = 0; kb < nkb; kb++, it++) {
+          const int s = it % kStages;
+          if (it >= kStages && !mbar_wait_bounded(&empty[s], ((it / kStages) - 1) & 1)) {
+            flag(kErrTimeout);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], nbox * kBoxB);
+          for (int b = 0; b < nbox; b++)
+            tma_load_2d(sB + s * kStageB + b * kBoxB, &a.mb, kb * kBK, ti.start + 16 * b,
+                        &full[s]);
+        }
+      }
+      for (uint32_t i = 0; i < min(it, (uint32_t)kStages); i++) {
+        const uint32_t ii = it - 1 - i;
+        mbar_wait_bounded(&full[ii % kStages], (ii / kStages) & 1, kDrainBudget);
+      }
+    }
+    __syncwarp();
+  } else if (warp < kWarpEpi0) {
+    // ------------------------------ dequantisers ------------------------------
+    // Thread -> tile row r, half h (32 of the stage's 64 K).  The slab row sr
+    // holding tile row r: gate rows 0..63 then up rows 64..127 in mode 1.
+    const int pt = threadIdx.x - 32 * kWarpDeq0;  // 0..255
+    const int r = pt & 127, h = pt >> 7;
+    const int sr = a.mode == 1 ? ((r & 1) * 64 + (r >> 1)) : r;
+    const int sw_r = r & 7, sw_sr = sr & 7;
+    uint32_t it = 0, g = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
+      TileInfo ti;
+      if (!tile_info(a, u, m_tiles, ti)) continue;
+      for (int kb = 0; kb < nkb; kb++, it++) {
+        const int q = kb & 3;
+        const int rs = g % kRawSlots, s = it % kStages;
+        if (q == 0 && !mbar_wait_bounded(&raw_full[rs], (g / kRawSlots) & 1)) {
+          flag(kErrTimeout);
+          ok = false;
+          break;
+        }
+        const uint8_t* slot = sRaw + rs * kRawSlot;
+        const int c = 2 * q + h;  // 16-byte code chunk of the slab row
+        const uint4 cw = *reinterpret_cast<const uint4*>(slot + sr * 128 + ((c ^ sw_sr) << 4));
+        const uint32_t sc2 =
+            *reinterpret_cast<const uint16_t*>(slot + kRawCodes + sr * 16 + q * 4 + h * 2);
+        if (q == 3) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&raw_empty[rs]);
+          g++;
+        }
+        if (it >= kStages && !mbar_wait_bounded(&empty[s], ((it / kStages) - 1) & 1)) {
+          flag(kErrTimeout);
+          ok = false;
+          break;
+        }
+        const uint32_t S2 = scale2_to_f16x2(sc2);
+        const uint32_t s_lo = bcast_lo(S2), s_hi = bcast_hi(S2);
+        uint8_t* arow = sA + s * kStageA + r * 128;
+        const uint32_t wds[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+          const int j = h * 4 + jj;  // 16-byte chunk of the 128-byte operand row
+          const uint32_t sc = jj < 2 ? s_lo : s_hi;
+          *reinterpret_cast<uint4*>(arow + ((j ^ sw_r) << 4)) =
+              F16 ? dequant8_f16(wds[jj], sc) : dequant8_bf16(wds[jj], sc);
+        }
+        fence_proxy_async();  // generic-proxy smem writes -> tensor-core reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+      }
+    }
+  } else {
+    // ------------------------------ epilogue --------------------------------
+    const int sp = warp & 3;       // TMEM sub-partition this warp may read
+    const int r = sp * 32 + lane;  // tile row = TMEM lane
+    int j = 0;
+    for (int u = blockIdx.x; u < ntot; u += gridDim.x) {
+      TileInfo ti;
+      if (!tile_info(a, u, m_tiles, ti)) continue;
+      const int buf = j & 1;
+      // Warp-uniform decision: the TMEM loads below are .sync.aligned.
+      const bool have =
+          __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1));
+      if (!have) {
+        if (lane == 0) flag(kErrTimeout);
+        break;
+      }
+      tc_fence_after();
+      for (int c0 = 0; c0 < ti.N; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)(buf * kBN + c0), v);
+#pragma unroll
+        for (int q = 0; q < 16; q++) {
+          const int n = c0 + q;
+          const bool col_ok = n < ti.count;
+          const int slot = ti.start + n;
+          const float cs = (a.bscale && col_ok) ? a.bscale[slot] : 1.0f;
+          const float val = v[q] * cs;
+          if (a.mode == 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, val, 1);
+            const int64_t i = (int64_t)ti.m_tile * 64 + (r >> 1);
+            if (!(r & 1) && col_ok && i < ti.Mrows)
+              reinterpret_cast<float*>(a.out)[(int64_t)slot * a.out_ld + i] =
+                  silu_ref(val) * other;
+          } else {
+            const int64_t rr = (int64_t)ti.m_tile * 128 + r;
+            if (col_ok && rr < ti.Mrows) {
+              if (a.mode == 2) {
+                reinterpret_cast<float*>(a.out)[(int64_t)slot * a.out_ld + rr] = val;
+              } else {
+                const int64_t orow = a.brow ? (int64_t)a.brow[slot] : (int64_t)slot;
+                store_from_f32(a.out, a.out_dtype, orow * a.out_ld + rr, val);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      j++;
     }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == kWarpMma) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// Activation rows -> f16(v * 2^-e) with max |v| * 2^-e in [1, 2) per row, and
+// 2^e in scale[row] (exact for bf16 inputs; no input overflows f16).  dst row r
+// reads src row src_map[r] (the expert-sorted slot order).  One warp per row;
+// K a multiple of 8.
+__global__ void rows_to_f16_kernel(RowsArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int nwarps = (gridDim.x * blockDim.x) >> 5;
+  for (int r = warp; r < a.rows; r += nwarps) {
+    const int64_t src = (int64_t)(a.src_map ? a.src_map[r] : r) * a.src_ld;
+    float m = 0.f;
+    for (int k = lane * 8; k < a.K; k += 256) {
+      float f[8];
+      load8(a.src, a.src_dtype, src + k, f);
+#pragma unroll
+      for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i]));
+    }
+    m = warp_max(m);
+    const int e = pow2_exponent(m);
+    const float inv = ldexpf(1.0f, -e);
+    for (int k = lane * 8; k < a.K; k += 256) {
+      float f[8];
+      load8(a.src, a.src_dtype, src + k, f);
+      uint32_t hv[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const __half2 v = __floats2half2_rn(f[2 * i] * inv, f[2 * i + 1] * inv);
+        hv[i] = *reinterpret_cast<const uint32_t*>(&v);
+      }
+      *reinterpret_cast<uint4*>(a.dst + (int64_t)r * a.dst_ld + k) =
+          make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    }
+    if (lane == 0) a.scale[r] = ldexpf(1.0f, e);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -470,24 +559,97 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream
   return cudaGetLastError();
 }
 
+int gemm_sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (n[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
+  }
+  return n[dev];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+cudaError_t encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                      uint64_t rows, uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows,
+                      CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || rows == 0 || inner == 0)
+    return cudaErrorInvalidValue;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 }  // namespace
+
+cudaError_t map_codes(CUtensorMap* m, const void* w, int64_t rows, int64_t K, int box_rows) {
+  return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)rows,
+                   (uint64_t)K / 2, 128, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+cudaError_t map_scales(CUtensorMap* m, const void* s, int64_t rows, int64_t K, int box_rows) {
+  return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, s, (uint64_t)K / 16, (uint64_t)rows,
+                   (uint64_t)K / 16, 16, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+cudaError_t map_rows16(CUtensorMap* m, const void* b, bool bf16, int64_t rows, int64_t K,
+                       int64_t ld) {
+  return encode_2d(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                   b, (uint64_t)K, (uint64_t)rows, (uint64_t)ld * 2, kBK, 16,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
 
 size_t gemm_smem_bytes() {
   return 1024 + (size_t)kStages * (kStageA + kStageB) + (size_t)kRawSlots * kRawSlot +
-         (2 * kStages + 2 * kRawSlots + 1) * 8 + 16;
+         (2 * kStages + 2 * kRawSlots + 5) * 8 + 16;
 }
 
 int gemm_tile_tokens() { return kBN; }
+int gemm_slab_k() { return kSlabK; }
 
-cudaError_t launch_nvfp4_gemm(const GemmArgs& a, int max_tiles, cudaStream_t stream, bool pdl) {
+// f16: the activation map holds f16 rows (A is dequantised to f16), else bf16.
+cudaError_t launch_nvfp4_gemm(const GemmArgs& a, bool f16, int max_tiles, cudaStream_t stream,
+                              bool pdl) {
   if (max_tiles <= 0) return cudaSuccess;
+  if (a.K % kSlabK) return cudaErrorInvalidValue;
   const size_t smem = gemm_smem_bytes();
-  cudaError_t e = ensure_smem(nvfp4_gemm_kernel, smem);
+  auto kern = f16 ? nvfp4_gemm_kernel<true> : nvfp4_gemm_kernel<false>;
+  cudaError_t e = ensure_smem(kern, smem);
   if (e != cudaSuccess) return e;
   const int mrows = std::max(a.Mrows, a.Mrows_shared);
   const int m_tiles = a.mode == 1 ? (mrows + 63) / 64 : (mrows + 127) / 128;
-  return launch_pdl(nvfp4_gemm_kernel, dim3(m_tiles, max_tiles), dim3(kGemmThreads), smem,
-                    stream, pdl, a);
+  const int64_t upper = (int64_t)m_tiles * max_tiles;
+  const int grid = (int)std::min<int64_t>(upper, gemm_sm_count());
+  return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), smem, stream, pdl, a);
+}
+
+cudaError_t launch_rows_to_f16(const RowsArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.rows <= 0) return cudaSuccess;
+  const int threads = 256;
+  const int blocks = std::min(std::max(1, (a.rows + 7) / 8), gemm_sm_count() * 8);
+  return launch_pdl(rows_to_f16_kernel, dim3(blocks), dim3(threads), 0, stream, pdl, a);
 }
 
 cudaError_t launch_moe_sort(const SortArgs& a, cudaStream_t stream, bool pdl) {

@@ -136,30 +136,6 @@ __device__ __forceinline__ void compute_chunk(Acc& acc, const Chunk& c, const __
   }
 }
 
-// Eight consecutive activation elements (elem_off % 8 == 0, 16-byte aligned).
-__device__ __forceinline__ void load8(const void* x, int dtype, int64_t elem_off, float (&f)[8]) {
-  if (dtype == kF32) {
-    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + elem_off);
-    const float4 b =
-        *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + elem_off + 4);
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-  } else {
-    const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + elem_off);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      if (dtype == kBF16) {
-        const float2 p = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-        f[2 * i] = p.x; f[2 * i + 1] = p.y;
-      } else {
-        const float2 p = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        f[2 * i] = p.x; f[2 * i + 1] = p.y;
-      }
-    }
-  }
-}
-
 // Eight f16 of one staged column, logical elements k..k+7 (k % 8 == 0): the
 // swizzle moves whole 16-byte groups, so they stay contiguous.
 __device__ __forceinline__ void store8_f16(__half* col, int k, const float (&f)[8], float mul) {
