@@ -428,9 +428,8 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
                         s) != cudaSuccess)
       return check_cuda(cudaGetLastError(), op);
   }
-  if (B.prefill) {
-    if (!aligned16(x))
-      return fail(NVFP4_ERR_INVALID, "[%s] x must be 16-byte aligned.", op);
+  // The prefill kernels move activations 16 bytes at a time.
+  if (B.prefill && aligned16(x) && aligned16(y) && (!residual || aligned16(residual))) {
     const bool routed_here = inds_in == nullptr;
     const bool copied = inds_in && (inds_out || weights_out);
     return prefill_impl(y, x, residual, dtype, T, L, inds, wts, ws, B, stream,

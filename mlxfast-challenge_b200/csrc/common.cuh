@@ -147,6 +147,30 @@ __device__ __forceinline__ void load8(const void* x, int dtype, int64_t elem_off
   }
 }
 
+// Eight consecutive output elements (elem_off % 8 == 0, 16-byte aligned).
+__device__ __forceinline__ void store8_from_f32(void* y, int dtype, int64_t elem_off,
+                                                const float (&f)[8]) {
+  if (dtype == kF32) {
+    float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + elem_off);
+    d[0] = make_float4(f[0], f[1], f[2], f[3]);
+    d[1] = make_float4(f[4], f[5], f[6], f[7]);
+  } else {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      if (dtype == kBF16) {
+        const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&b);
+      } else {
+        const __half2 b = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+    }
+    *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(y) + elem_off) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // Power-of-two exponent e with max_abs * 2^-e in [1, 2); 0 for zero / non-finite.
 __device__ __forceinline__ int pow2_exponent(float max_abs) {
   if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 0;

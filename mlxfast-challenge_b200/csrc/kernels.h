@@ -72,8 +72,7 @@ struct RouterArgs {
   float* wts;           // [T, k]
 };
 
-// Grouped NVFP4 GEMM on tcgen05 (prefill.cu).
-// Sorted-slot grouped GEMM (prefill.cu).  Operands arrive by TMA through
+// Sorted-slot grouped GEMM on tcgen05 (prefill.cu).  Operands arrive by TMA through
 // 2-D tensor maps: packed codes [rows, K/2] bytes (box 128 bytes x 64 or 128
 // rows, 128-byte swizzle), scales [rows, K/16] bytes (box 16 x rows), and
 // 16-bit activation rows in slot order [slots, K] (box 64 elements x 16 rows,
@@ -90,12 +89,12 @@ struct alignas(64) GemmArgs {
   int shared_group;  // group id served by the shared maps, -1 none
   int implicit_M;    // > 0: one group, slots 0..implicit_M-1, tiles of 64 (no tile list)
   const float* bscale;  // per slot: true activation row = row * bscale[slot] (null: 1)
-  const int* brow;      // mode 0: slot -> output row (null: the slot itself)
   const int4* tiles;    // (group, first slot, count, 0)
   const int* ntiles;
   void* out;
   int out_dtype;
   int64_t out_ld;
+  int out_bulk;  // set by the launcher: output rows written by bulk copies
 };
 
 // Tensor maps for GemmArgs (cuTensorMapEncodeTiled through the runtime's

@@ -13,24 +13,32 @@
 // runs across tile boundaries:
 //   weight TMA (1 thread)  per 256-wide K slab, the tile rows' packed codes
 //                          (16 KB, 128-byte swizzle) and E4M3 scales (2 KB)
-//                          into a 4-deep ring;
-//   dequantisers (8 warps) per MMA stage, each thread a half row: E2M1 pairs
-//                          by the hardware converter times the group scale
-//                          (exact in f16 / bf16), stored straight into the
-//                          128-byte swizzled K-major UMMA layout;
+//                          into a 6-deep shared-memory ring;
+//   dequantisers          4 groups of 4 warps; group q owns K quarter q of
+//   (16 warps)            every slab, one thread per tile row (= TMEM lane):
+//                          E2M1 pairs by the hardware converter times the group
+//                          scale (exact in f16 / bf16), written to one of two
+//                          A slabs in tensor memory (tcgen05.st);
 //   activation TMA         16-row boxes of the tile's slot-ordered 16-bit
-//   (1 thread)             activation rows into the B stage;
-//   MMA issuer (1 thread)  tcgen05.mma kind::f16 into one of two TMEM
-//                          accumulators; each stage committed back to the
-//                          producers through an mbarrier;
+//   (1 thread)             activation rows, a whole slab at a time, into a
+//                          3-deep B ring (128-byte swizzled K-major);
+//   MMA issuer (1 thread)  per slab 16 tcgen05.mma kind::f16 (A from TMEM, B
+//                          from shared memory) into one of two TMEM
+//                          accumulators, then one commit per freed buffer.
+// The MMA issue costs a fixed ~46 cycles per instruction for N <= 96, so the
+// per-slab granularity keeps the issuing thread's bookkeeping off that path.
 //   epilogue (4 warps)     tcgen05.ld of the finished accumulator (one TMEM
-//                          sub-partition each) while the next tile runs.
+//                          sub-partition each; the accumulator is released at
+//                          once), staged in shared memory one slot row per
+//                          tile column, written out by bulk copies
+//                          (cp.async.bulk shared -> global) while the next
+//                          tile runs.
 // Operand type: f16 for pre-scaled activation rows (rows_to_f16: per-row power
 // of two, exact for bf16 inputs, re-applied in the epilogue) and for f16
 // inputs; bf16 for bf16 inputs (dense quantized_matmul, no workspace).
-// Epilogue modes: 0 plain out[row of slot][n] = D; 1 gate/up: tile rows
-// interleave gate row i / up row i, adjacent TMEM lanes pair up and
-// act = silu(gate) * up (f32); 2 down: Y[slot][n] = D (f32, combined per token
+// Epilogue modes: 0 plain out[slot][n] = D; 1 gate/up: tile rows
+// alternate blocks of 8 gate rows and the same 8 up rows, so TMEM lanes r and
+// r ^ 8 pair up in one warp and act = silu(gate) * up (f32); 2 down: Y[slot][n] = D (f32, combined per token
 // afterwards).  All mbarrier waits are bounded (tma.cuh): on expiry error 4 is
 // latched and every role leaves its loop before TMEM is released.
 #include "common.cuh"
@@ -48,19 +56,28 @@ constexpr int kBM = 128;                     // weight rows per tile
 constexpr int kBN = 64;                      // tokens per tile (max UMMA N used)
 constexpr int kBK = 64;                      // K per MMA stage: one 128 B swizzle row of 16-bit
 constexpr int kSlabK = 256;                  // K per weight slab (128 code bytes per row)
-constexpr int kStages = 4;                   // A/B stages fed to the MMA
-constexpr int kRawSlots = 4;                 // weight slabs in flight
-constexpr int kDeqWarps = 8;
+constexpr int kStages = 4;                   // 64-wide K stages per slab
+constexpr int kASlabs = 2;                   // A slabs in TMEM
+constexpr int kBSlabs = 3;                   // B (activation) slabs in shared memory
+constexpr int kRawSlots = 5;                 // weight slabs in flight
+constexpr int kOutPitch = 512;               // staged output: bytes per tile column (slot)
+constexpr int kGroupWarps = 4;               // one dequantiser group: 128 threads = 128 rows
+constexpr int kDeqWarps = kStages * kGroupWarps;
 constexpr int kEpiWarps = 4;
 constexpr int kWarpMma = 0, kWarpRaw = 1, kWarpAct = 2, kWarpDeq0 = 3;
-constexpr int kWarpEpi0 = kWarpDeq0 + kDeqWarps;  // 11..14: TMEM sub-partitions 3,0,1,2
+constexpr int kWarpEpi0 = kWarpDeq0 + kDeqWarps;  // 19..22: TMEM sub-partitions 3,0,1,2
+static_assert(kStages * kBK == kSlabK, "dequantiser group q owns stage q of each slab");
 constexpr int kGemmThreads = 32 * (kWarpEpi0 + kEpiWarps);
-constexpr int kStageA = kBM * kBK * 2;       // 16 KB
 constexpr int kStageB = kBN * kBK * 2;       // 8 KB
+constexpr int kSlabB = kStages * kStageB;    // 32 KB
 constexpr int kBoxB = 16 * kBK * 2;          // one 16-row activation box, 2 KB
 constexpr int kRawCodes = kBM * 128;         // 16 KB
 constexpr int kRawSlot = kRawCodes + kBM * 16;  // + 16 scale bytes per row
-constexpr int kTmemCols = 2 * kBN;           // two accumulators
+constexpr int kAccCols = 2 * kBN;            // two f32 accumulators
+constexpr int kACols = kBK / 2;              // one A stage: 64 16-bit K per lane
+constexpr int kASlabCols = kStages * kACols; // 128
+constexpr int kTmemCols = 512;               // accumulators + A slabs, power of two
+static_assert(kAccCols + kASlabs * kASlabCols <= kTmemCols, "TMEM budget");
 constexpr int kErrTimeout = 4;
 constexpr long long kDrainBudget = 200000000LL;  // ~0.1 s: in-flight copies on an error path
 
@@ -120,10 +137,34 @@ __device__ __forceinline__ int total_tiles(const GemmArgs& a, int m_tiles) {
   return ngt * m_tiles;
 }
 
+// Tile-list entry of tile u (read one tile ahead by every role: a global
+// load costs ~1 us while the weight stream fills the memory system).
+__device__ __forceinline__ int4 fetch_td(const GemmArgs& a, int u, int m_tiles, int ntot) {
+  if (a.implicit_M > 0 || u >= ntot) return make_int4(0, 0, 0, 0);
+  return a.tiles[u / m_tiles];
+}
+
+// The CTA's tile-list entries, read two tiles ahead.
+struct TileStream {
+  int4 td0, td1;
+  __device__ __forceinline__ void start(const GemmArgs& a, int m_tiles, int ntot) {
+    td0 = fetch_td(a, blockIdx.x, m_tiles, ntot);
+    td1 = fetch_td(a, blockIdx.x + gridDim.x, m_tiles, ntot);
+  }
+  // Entry of tile u (the loop's current tile); queues the one two tiles on.
+  __device__ __forceinline__ int4 next(const GemmArgs& a, int u, int m_tiles, int ntot) {
+    const int4 td = td0;
+    td0 = td1;
+    td1 = fetch_td(a, u + 2 * gridDim.x, m_tiles, ntot);
+    return td;
+  }
+};
+
 // Tile u: token tile u / m_tiles, weight-row tile u % m_tiles (consecutive
 // CTAs share a token tile, so its activation rows are read from L2).  Returns
 // false when that weight-row tile lies beyond the group's rows.
-__device__ __forceinline__ bool tile_info(const GemmArgs& a, int u, int m_tiles, TileInfo& ti) {
+__device__ __forceinline__ bool tile_info(const GemmArgs& a, int u, int m_tiles, int4 td,
+                                          TileInfo& ti) {
   const int gt = u / m_tiles;
   ti.m_tile = u - gt * m_tiles;
   if (a.implicit_M > 0) {
@@ -131,7 +172,6 @@ __device__ __forceinline__ bool tile_info(const GemmArgs& a, int u, int m_tiles,
     ti.start = gt * kBN;
     ti.count = min(kBN, a.implicit_M - gt * kBN);
   } else {
-    const int4 td = a.tiles[gt];
     ti.grp = td.x;
     ti.start = td.y;
     ti.count = td.z;
@@ -142,6 +182,14 @@ __device__ __forceinline__ bool tile_info(const GemmArgs& a, int u, int m_tiles,
   return ti.m_tile * (a.mode == 1 ? 64 : 128) < ti.Mrows;
 }
 
+// silu(x) = x * sigmoid(x), sigmoid composed as the reference does
+// (x < 0 ? y : 1 - y with y = 1 / (1 + e^|x|)), with the fast exponential and
+// division intrinsics (a few ulp; the tolerance is 5e-3 relative-L2).
+__device__ __forceinline__ float silu_fast(float x) {
+  const float y = __fdividef(1.0f, 1.0f + __expf(fabsf(x)));
+  return x * (x < 0.0f ? y : 1.0f - y);
+}
+
 template <bool F16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     nvfp4_gemm_kernel(const __grid_constant__ GemmArgs a) {
@@ -149,23 +197,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // Swizzle atoms (TMA and UMMA) need 1024-byte alignment.
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = sA + kStages * kStageA;
-  uint8_t* sRaw = sB + kStages * kStageB;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sRaw + kRawSlots * kRawSlot);
-  uint64_t* empty = full + kStages;
-  uint64_t* raw_full = empty + kStages;
+  uint8_t* sB = smem;
+  uint8_t* sRaw = sB + kBSlabs * kSlabB;
+  uint8_t* sOut = sRaw + kRawSlots * kRawSlot;  // [kBN][kOutPitch]
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(sOut + kBN * kOutPitch);
+  uint64_t* a_empty = a_full + kASlabs;
+  uint64_t* b_full = a_empty + kASlabs;
+  uint64_t* b_empty = b_full + kBSlabs;
+  uint64_t* raw_full = b_empty + kBSlabs;
   uint64_t* raw_empty = raw_full + kRawSlots;
   uint64_t* acc_full = raw_empty + kRawSlots;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
+  uint64_t* sc_full = acc_empty + 2;
+  uint64_t* sc_empty = sc_full + 2;
+  uint64_t* drain = sc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  float* s_scale = reinterpret_cast<float*>(tmem_slot + 4);  // [2][kBN] per-column scales
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; i++) {
-      mbar_init(&full[i], kDeqWarps + 1);  // dequantiser warps + activation TMA (with tx)
-      mbar_init(&empty[i], 1);             // MMA commit
+    for (int i = 0; i < kASlabs; i++) {
+      mbar_init(&a_full[i], kDeqWarps);    // every dequantiser warp
+      mbar_init(&a_empty[i], 1);           // MMA commit
+    }
+    for (int i = 0; i < kBSlabs; i++) {
+      mbar_init(&b_full[i], 1);            // activation TMA (with tx)
+      mbar_init(&b_empty[i], 1);           // MMA commit
     }
     for (int i = 0; i < kRawSlots; i++) {
       mbar_init(&raw_full[i], 1);          // weight TMA (with tx)
@@ -174,6 +231,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);          // MMA commit at the end of a tile
       mbar_init(&acc_empty[i], kEpiWarps);
+      mbar_init(&sc_full[i], 1);           // activation warp: the tile's column scales
+      mbar_init(&sc_empty[i], kEpiWarps);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -194,18 +253,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int nkb = a.K / kBK;
   const int nslab = a.K / kSlabK;
 
   if (warp == kWarpMma) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t g = 0;
       int j = 0;
       bool ok = true;
+      TileStream ts;
+      ts.start(a, m_tiles, ntot);
       for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
         TileInfo ti;
-        if (!tile_info(a, u, m_tiles, ti)) continue;
+        if (!tile_info(a, u, m_tiles, ts.next(a, u, m_tiles, ntot), ti)) continue;
         const int buf = j & 1;
         if (j >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((j >> 1) - 1) & 1)) {
           flag(kErrTimeout);
@@ -215,20 +275,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t idesc =
             idesc_f16_f32(kBM, ti.N) | (F16 ? 0u : ((1u << 7) | (1u << 10)));
         const uint32_t d = tmem + (uint32_t)(buf * kBN);
-        for (int kb = 0; kb < nkb; kb++, it++) {
-          const int s = it % kStages;
-          if (!mbar_wait_bounded(&full[s], (it / kStages) & 1)) {
+        for (int sl = 0; sl < nslab; sl++, g++) {
+          const int as = g % kASlabs, bs = g % kBSlabs;
+          if (!mbar_wait_bounded(&a_full[as], (g / kASlabs) & 1) ||
+              !mbar_wait_bounded(&b_full[bs], (g / kBSlabs) & 1)) {
             flag(kErrTimeout);
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t ad = smem_desc_sw128(smem_u32(sA + s * kStageA));
-          const uint64_t bd = smem_desc_sw128(smem_u32(sB + s * kStageB));
+          const uint32_t ta = tmem + (uint32_t)(kAccCols + as * kASlabCols);
+          const uint64_t bd = smem_desc_sw128(smem_u32(sB + bs * kSlabB));
 #pragma unroll
-          for (int ks = 0; ks < kBK / 16; ks++)  // 16 elements = 32 bytes = 2 descriptor units
-            umma_f16(d, ad + 2 * ks, bd + 2 * ks, idesc, (kb | ks) != 0);
-          umma_commit(&empty[s]);
+          for (int s = 0; s < kStages; s++)
+#pragma unroll
+            for (int ks = 0; ks < kBK / 16; ks++)  // 16 K: 8 TMEM columns of A, 32 bytes of B
+              umma_f16_ts(d, ta + s * kACols + 8 * ks, bd + s * (kStageB >> 4) + 2 * ks, idesc,
+                          (sl | s | ks) != 0);
+          umma_commit(&a_empty[as]);
+          umma_commit(&b_empty[bs]);
         }
         if (!ok) break;
         umma_commit(&acc_full[buf]);  // the accumulator is complete once these MMAs are
@@ -244,9 +309,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       uint32_t g = 0;
       bool ok = true;
+      TileStream ts;
+      ts.start(a, m_tiles, ntot);
       for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
         TileInfo ti;
-        if (!tile_info(a, u, m_tiles, ti)) continue;
+        if (!tile_info(a, u, m_tiles, ts.next(a, u, m_tiles, ntot), ti)) continue;
         const CUtensorMap* c0 = ti.is_shared ? &a.mcs0 : &a.mc0;
         const CUtensorMap* s0 = ti.is_shared ? &a.mss0 : &a.ms0;
         const CUtensorMap* c1 = ti.is_shared ? &a.mcs1 : &a.mc1;
@@ -284,135 +351,218 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else if (warp == kWarpAct) {
     // ---------------------------- activation TMA ----------------------------
-    if (lane == 0) {
-      uint32_t it = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
-        TileInfo ti;
-        if (!tile_info(a, u, m_tiles, ti)) continue;
+    // Lane 0 issues the B slabs; with pre-scaled rows the whole warp also
+    // stages the tile's per-column scales (read one tile ahead) for the
+    // epilogue.
+    uint32_t g = 0;
+    int j = 0;
+    bool ok = true;
+    TileStream ts;
+    ts.start(a, m_tiles, ntot);
+    float sc_next[2] = {1.0f, 1.0f};
+    auto load_scales = [&](int4 td, int u, float (&dst)[2]) {
+      TileInfo tn;
+      const bool valid = u < ntot && tile_info(a, u, m_tiles, td, tn);
+#pragma unroll
+      for (int h2 = 0; h2 < 2; h2++) {
+        const int n = 32 * h2 + lane;
+        dst[h2] = (a.bscale && valid && n < tn.count) ? a.bscale[tn.start + n] : 1.0f;
+      }
+    };
+    load_scales(ts.td0, blockIdx.x, sc_next);
+    for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
+      const int4 td = ts.next(a, u, m_tiles, ntot);
+      const float sc_cur[2] = {sc_next[0], sc_next[1]};
+      load_scales(ts.td0, u + gridDim.x, sc_next);
+      TileInfo ti;
+      if (!tile_info(a, u, m_tiles, td, ti)) continue;
+      const int sb = j & 1;
+      if (j >= 2 && !mbar_wait_bounded(&sc_empty[sb], ((j >> 1) - 1) & 1)) {
+        if (lane == 0) flag(kErrTimeout);
+        break;
+      }
+      s_scale[sb * kBN + lane] = sc_cur[0];
+      s_scale[sb * kBN + 32 + lane] = sc_cur[1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sc_full[sb]);
+      j++;
+      if (lane == 0) {
         const int nbox = ti.N / 16;
-        for (int kb = 0; kb < nkb; kb++, it++) {
-          const int s = it % kStages;
-          if (it >= kStages && !mbar_wait_bounded(&empty[s], ((it / kStages) - 1) & 1)) {
+        for (int sl = 0; sl < nslab; sl++, g++) {
+          const int bs = g % kBSlabs;
+          if (g >= kBSlabs && !mbar_wait_bounded(&b_empty[bs], ((g / kBSlabs) - 1) & 1)) {
             flag(kErrTimeout);
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], nbox * kBoxB);
-          for (int b = 0; b < nbox; b++)
-            tma_load_2d(sB + s * kStageB + b * kBoxB, &a.mb, kb * kBK, ti.start + 16 * b,
-                        &full[s]);
+          mbar_arrive_expect_tx(&b_full[bs], kStages * nbox * kBoxB);
+          for (int s = 0; s < kStages; s++)
+            for (int b = 0; b < nbox; b++)
+              tma_load_2d(sB + bs * kSlabB + s * kStageB + b * kBoxB, &a.mb,
+                          (sl * kStages + s) * kBK, ti.start + 16 * b, &b_full[bs]);
         }
       }
-      for (uint32_t i = 0; i < min(it, (uint32_t)kStages); i++) {
-        const uint32_t ii = it - 1 - i;
-        mbar_wait_bounded(&full[ii % kStages], (ii / kStages) & 1, kDrainBudget);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (lane == 0) {
+      for (uint32_t i = 0; i < min(g, (uint32_t)kBSlabs); i++) {
+        const uint32_t gg = g - 1 - i;
+        mbar_wait_bounded(&b_full[gg % kBSlabs], (gg / kBSlabs) & 1, kDrainBudget);
       }
     }
     __syncwarp();
   } else if (warp < kWarpEpi0) {
     // ------------------------------ dequantisers ------------------------------
-    // Thread -> tile row r, half h (32 of the stage's 64 K).  The slab row sr
-    // holding tile row r: gate rows 0..63 then up rows 64..127 in mode 1.
-    const int pt = threadIdx.x - 32 * kWarpDeq0;  // 0..255
-    const int r = pt & 127, h = pt >> 7;
-    const int sr = a.mode == 1 ? ((r & 1) * 64 + (r >> 1)) : r;
-    const int sw_r = r & 7, sw_sr = sr & 7;
-    uint32_t it = 0, g = 0;
+    // Group q, thread -> tile row r = the TMEM lane this warp may write; slab
+    // row sr holds tile row r (mode 1: tile rows [16b, 16b+8) are gate rows
+    // 8b.., [16b+8, 16b+16) the same up rows, and the slab has gate rows 0..63
+    // then up rows 64..127).  Eight consecutive rows read eight distinct
+    // 16-byte bank groups of the swizzled slab.
+    const int q = (warp - kWarpDeq0) / kGroupWarps;
+    const int r = 32 * (warp & 3) + lane;
+    const int sr = a.mode == 1 ? (((r >> 3) & 1) * 64 + (r >> 4) * 8 + (r & 7)) : r;
+    const int sw_sr = sr & 7;
+    const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(kAccCols + q * kACols);
+    uint32_t g = 0;
     bool ok = true;
+    TileStream ts;
+    ts.start(a, m_tiles, ntot);
     for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
       TileInfo ti;
-      if (!tile_info(a, u, m_tiles, ti)) continue;
-      for (int kb = 0; kb < nkb; kb++, it++) {
-        const int q = kb & 3;
-        const int rs = g % kRawSlots, s = it % kStages;
-        if (q == 0 && !mbar_wait_bounded(&raw_full[rs], (g / kRawSlots) & 1)) {
+      if (!tile_info(a, u, m_tiles, ts.next(a, u, m_tiles, ntot), ti)) continue;
+      for (int sl = 0; sl < nslab; sl++, g++) {
+        const int rs = g % kRawSlots;
+        if (!mbar_wait_bounded(&raw_full[rs], (g / kRawSlots) & 1)) {
           flag(kErrTimeout);
           ok = false;
           break;
         }
         const uint8_t* slot = sRaw + rs * kRawSlot;
-        const int c = 2 * q + h;  // 16-byte code chunk of the slab row
-        const uint4 cw = *reinterpret_cast<const uint4*>(slot + sr * 128 + ((c ^ sw_sr) << 4));
-        const uint32_t sc2 =
-            *reinterpret_cast<const uint16_t*>(slot + kRawCodes + sr * 16 + q * 4 + h * 2);
-        if (q == 3) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&raw_empty[rs]);
-          g++;
+        const uint4 cw0 =
+            *reinterpret_cast<const uint4*>(slot + sr * 128 + (((2 * q) ^ sw_sr) << 4));
+        const uint4 cw1 =
+            *reinterpret_cast<const uint4*>(slot + sr * 128 + (((2 * q + 1) ^ sw_sr) << 4));
+        const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(slot + kRawCodes + sr * 16 + q * 4);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
+        const uint32_t S01 = scale2_to_f16x2(sc4 & 0xFFFFu), S23 = scale2_to_f16x2(sc4 >> 16);
+        const uint32_t sc[4] = {bcast_lo(S01), bcast_hi(S01), bcast_lo(S23), bcast_hi(S23)};
+        const uint32_t wds[8] = {cw0.x, cw0.y, cw0.z, cw0.w, cw1.x, cw1.y, cw1.z, cw1.w};
+        uint32_t o[32];  // column c = K elements 2c, 2c+1 of the stage
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const uint4 v = F16 ? dequant8_f16(wds[j], sc[j >> 1]) : dequant8_bf16(wds[j], sc[j >> 1]);
+          o[4 * j] = v.x;
+          o[4 * j + 1] = v.y;
+          o[4 * j + 2] = v.z;
+          o[4 * j + 3] = v.w;
         }
-        if (it >= kStages && !mbar_wait_bounded(&empty[s], ((it / kStages) - 1) & 1)) {
-          flag(kErrTimeout);
+        // Warp-uniform: tcgen05.st below is .sync.aligned.
+        const int as = g % kASlabs;
+        if (g >= kASlabs &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(&a_empty[as], ((g / kASlabs) - 1) & 1))) {
+          if (lane == 0) flag(kErrTimeout);
           ok = false;
           break;
         }
-        const uint32_t S2 = scale2_to_f16x2(sc2);
-        const uint32_t s_lo = bcast_lo(S2), s_hi = bcast_hi(S2);
-        uint8_t* arow = sA + s * kStageA + r * 128;
-        const uint32_t wds[4] = {cw.x, cw.y, cw.z, cw.w};
-#pragma unroll
-        for (int jj = 0; jj < 4; jj++) {
-          const int j = h * 4 + jj;  // 16-byte chunk of the 128-byte operand row
-          const uint32_t sc = jj < 2 ? s_lo : s_hi;
-          *reinterpret_cast<uint4*>(arow + ((j ^ sw_r) << 4)) =
-              F16 ? dequant8_f16(wds[jj], sc) : dequant8_bf16(wds[jj], sc);
-        }
-        fence_proxy_async();  // generic-proxy smem writes -> tensor-core reads
+        tc_fence_after();
+        tmem_st32(ta + as * kASlabCols, o);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);
+        if (lane == 0) mbar_arrive(&a_full[as]);
       }
     }
   } else {
     // ------------------------------ epilogue --------------------------------
     const int sp = warp & 3;       // TMEM sub-partition this warp may read
     const int r = sp * 32 + lane;  // tile row = TMEM lane
+    const bool issuer = warp == kWarpEpi0 && lane == 0;  // bulk copies
     int j = 0;
+    TileStream ts;
+    ts.start(a, m_tiles, ntot);
     for (int u = blockIdx.x; u < ntot; u += gridDim.x) {
       TileInfo ti;
-      if (!tile_info(a, u, m_tiles, ti)) continue;
+      if (!tile_info(a, u, m_tiles, ts.next(a, u, m_tiles, ntot), ti)) continue;
       const int buf = j & 1;
       // Warp-uniform decision: the TMEM loads below are .sync.aligned.
       const bool have =
-          __all_sync(0xffffffffu, mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1));
+          __all_sync(0xffffffffu, mbar_wait_bounded(&sc_full[buf], (j >> 1) & 1) &&
+                                      mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1));
       if (!have) {
         if (lane == 0) flag(kErrTimeout);
         break;
       }
       tc_fence_after();
-      for (int c0 = 0; c0 < ti.N; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)(buf * kBN + c0), v);
-#pragma unroll
-        for (int q = 0; q < 16; q++) {
-          const int n = c0 + q;
-          const bool col_ok = n < ti.count;
-          const int slot = ti.start + n;
-          const float cs = (a.bscale && col_ok) ? a.bscale[slot] : 1.0f;
-          const float val = v[q] * cs;
-          if (a.mode == 1) {
-            const float other = __shfl_xor_sync(0xffffffffu, val, 1);
-            const int64_t i = (int64_t)ti.m_tile * 64 + (r >> 1);
-            if (!(r & 1) && col_ok && i < ti.Mrows)
-              reinterpret_cast<float*>(a.out)[(int64_t)slot * a.out_ld + i] =
-                  silu_ref(val) * other;
-          } else {
-            const int64_t rr = (int64_t)ti.m_tile * 128 + r;
-            if (col_ok && rr < ti.Mrows) {
-              if (a.mode == 2) {
-                reinterpret_cast<float*>(a.out)[(int64_t)slot * a.out_ld + rr] = val;
-              } else {
-                const int64_t orow = a.brow ? (int64_t)a.brow[slot] : (int64_t)slot;
-                store_from_f32(a.out, a.out_dtype, orow * a.out_ld + rr, val);
-              }
-            }
-          }
-        }
-      }
+      // Per-column scales, one column per lane, broadcast by shuffle.
+      const float cs_l[2] = {s_scale[buf * kBN + lane], s_scale[buf * kBN + 32 + lane]};
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sc_empty[buf]);
+      // The whole accumulator (N <= 64 columns) into registers; TMEM is then
+      // handed back to the MMA before any output work.
+      uint32_t v[2][32];
+      const uint32_t taddr = tmem + ((uint32_t)(sp * 32) << 16) + (uint32_t)(buf * kBN);
+      tmem_ld32_nowait(taddr, v[0]);
+      if (ti.N > 32) tmem_ld32_nowait(taddr + 32, v[1]);
+      tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      // Staging buffer free: the previous tile's bulk copies have read it.
+      if (issuer) bulk_wait_read0();
+      named_sync(1, 32 * kEpiWarps);
+#pragma unroll
+      for (int h2 = 0; h2 < 2; h2++) {
+        if (h2 == 1 && ti.N <= 32) break;  // warp-uniform
+#pragma unroll
+        for (int q = 0; q < 32; q++) {
+          const int n = 32 * h2 + q;
+          const float val = __uint_as_float(v[h2][q]) * __shfl_sync(0xffffffffu, cs_l[h2], q);
+          uint8_t* row = sOut + n * kOutPitch;
+          if (a.mode == 1) {
+            const float other = __shfl_xor_sync(0xffffffffu, val, 8);
+            if (!(r & 8))
+              reinterpret_cast<float*>(row)[(r >> 4) * 8 + (r & 7)] = silu_fast(val) * other;
+          } else if (a.mode == 2 || a.out_dtype == kF32) {
+            reinterpret_cast<float*>(row)[r] = val;
+          } else if (a.out_dtype == kBF16) {
+            reinterpret_cast<__nv_bfloat16*>(row)[r] = __float2bfloat16_rn(val);
+          } else {
+            reinterpret_cast<__half*>(row)[r] = __float2half_rn(val);
+          }
+        }
+      }
+      const int esz = (a.mode != 0 || a.out_dtype == kF32) ? 4 : 2;
+      const int row_elems = a.mode == 1 ? 64 : 128;
+      const int64_t col0 = (int64_t)ti.m_tile * row_elems;
+      if (a.out_bulk) {
+        fence_proxy_async();  // staged rows -> bulk-copy reads
+        named_sync(1, 32 * kEpiWarps);
+        if (issuer) {
+          for (int n = 0; n < ti.count; n++)
+            bulk_s2g(reinterpret_cast<uint8_t*>(a.out) +
+                         ((int64_t)(ti.start + n) * a.out_ld + col0) * esz,
+                     sOut + n * kOutPitch, (uint32_t)(row_elems * esz));
+          bulk_commit();
+        }
+      } else {
+        named_sync(1, 32 * kEpiWarps);
+        const int et = threadIdx.x - 32 * kWarpEpi0;
+        const int64_t rows_left = ti.Mrows - col0;
+        const int ncol = rows_left < row_elems ? (int)rows_left : row_elems;
+        for (int idx = et; idx < ti.count * row_elems; idx += 32 * kEpiWarps) {
+          const int n = idx / row_elems, c = idx - n * row_elems;
+          if (c >= ncol) continue;
+          const uint8_t* src = sOut + n * kOutPitch + c * esz;
+          uint8_t* dst = reinterpret_cast<uint8_t*>(a.out) +
+                         ((int64_t)(ti.start + n) * a.out_ld + col0 + c) * esz;
+          if (esz == 4) *reinterpret_cast<float*>(dst) = *reinterpret_cast<const float*>(src);
+          else *reinterpret_cast<uint16_t*>(dst) = *reinterpret_cast<const uint16_t*>(src);
+        }
+      }
       j++;
     }
+    if (issuer) bulk_wait0();  // every output row written before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -521,23 +671,42 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(SortArgs a) {
 }
 
 // y[t] = scaling * sum_j w[t][j] * Y[pos[t*k+j]] + Y[P + t] (shared) + residual
-// in a fixed j order (deterministic).
+// in a fixed j order (deterministic).  Each thread owns 8 consecutive h of one
+// token (H a multiple of 8): two 16-byte loads per expert row, one store.
 __global__ void moe_combine_kernel(CombineArgs a) {
   pdl_wait();
   pdl_trigger();
-  const int64_t total = (int64_t)a.T * a.H;
+  const int H8 = a.H / 8;
+  const int64_t total = (int64_t)a.T * H8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t t = i / a.H, h = i - t * a.H;
-    float acc = 0.f;
+    const int64_t t = i / H8, h = (i - t * H8) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     for (int j = 0; j < a.k; j++) {
       const int slot = a.pos[t * a.k + j];
-      if (slot >= 0) acc += a.wts[t * a.k + j] * a.Y[(int64_t)slot * a.H + h];
+      if (slot < 0) continue;
+      const float w = a.wts[t * a.k + j];
+      const float4* src = reinterpret_cast<const float4*>(a.Y + (int64_t)slot * a.H + h);
+      const float4 u = src[0], v = src[1];
+      acc[0] += w * u.x; acc[1] += w * u.y; acc[2] += w * u.z; acc[3] += w * u.w;
+      acc[4] += w * v.x; acc[5] += w * v.y; acc[6] += w * v.z; acc[7] += w * v.w;
     }
-    acc *= a.scaling;
-    if (a.with_shared) acc += a.Y[(int64_t)(a.P + t) * a.H + h];
-    if (a.residual) acc += load_as_f32(a.residual, a.dtype, i);
-    store_from_f32(a.y, a.dtype, i, acc);
+#pragma unroll
+    for (int q = 0; q < 8; q++) acc[q] *= a.scaling;
+    if (a.with_shared) {
+      const float4* src = reinterpret_cast<const float4*>(a.Y + (int64_t)(a.P + t) * a.H + h);
+      const float4 u = src[0], v = src[1];
+      acc[0] += u.x; acc[1] += u.y; acc[2] += u.z; acc[3] += u.w;
+      acc[4] += v.x; acc[5] += v.y; acc[6] += v.z; acc[7] += v.w;
+    }
+    const int64_t off = t * a.H + h;
+    if (a.residual) {
+      float r[8];
+      load8(a.residual, a.dtype, off, r);
+#pragma unroll
+      for (int q = 0; q < 8; q++) acc[q] += r[q];
+    }
+    store8_from_f32(a.y, a.dtype, off, acc);
   }
 }
 
@@ -622,8 +791,8 @@ cudaError_t map_rows16(CUtensorMap* m, const void* b, bool bf16, int64_t rows, i
 }
 
 size_t gemm_smem_bytes() {
-  return 1024 + (size_t)kStages * (kStageA + kStageB) + (size_t)kRawSlots * kRawSlot +
-         (2 * kStages + 2 * kRawSlots + 5) * 8 + 16;
+  return 1024 + (size_t)kBSlabs * kSlabB + (size_t)kRawSlots * kRawSlot + (size_t)kBN * kOutPitch +
+         (2 * kASlabs + 2 * kBSlabs + 2 * kRawSlots + 9) * 8 + 16 + 2 * kBN * sizeof(float);
 }
 
 int gemm_tile_tokens() { return kBN; }
@@ -636,13 +805,19 @@ cudaError_t launch_nvfp4_gemm(const GemmArgs& a, bool f16, int max_tiles, cudaSt
   if (a.K % kSlabK) return cudaErrorInvalidValue;
   const size_t smem = gemm_smem_bytes();
   auto kern = f16 ? nvfp4_gemm_kernel<true> : nvfp4_gemm_kernel<false>;
+  // Bulk output copies need 16-byte aligned rows and only whole row tiles.
+  GemmArgs args = a;
+  const int esz = (a.mode != 0 || a.out_dtype == kF32) ? 4 : 2;
+  const int tile_rows = a.mode == 1 ? 64 : 128;
+  args.out_bulk = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) && (a.out_ld * esz) % 16 == 0 &&
+                  a.Mrows % tile_rows == 0 && a.Mrows_shared % tile_rows == 0;
   cudaError_t e = ensure_smem(kern, smem);
   if (e != cudaSuccess) return e;
   const int mrows = std::max(a.Mrows, a.Mrows_shared);
   const int m_tiles = a.mode == 1 ? (mrows + 63) / 64 : (mrows + 127) / 128;
   const int64_t upper = (int64_t)m_tiles * max_tiles;
   const int grid = (int)std::min<int64_t>(upper, gemm_sm_count());
-  return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), smem, stream, pdl, a);
+  return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), smem, stream, pdl, args);
 }
 
 cudaError_t launch_rows_to_f16(const RowsArgs& a, cudaStream_t stream, bool pdl) {
@@ -657,7 +832,7 @@ cudaError_t launch_moe_sort(const SortArgs& a, cudaStream_t stream, bool pdl) {
 }
 
 cudaError_t launch_moe_combine(const CombineArgs& a, cudaStream_t stream, bool pdl) {
-  const int64_t total = (int64_t)a.T * a.H;
+  const int64_t total = (int64_t)a.T * (a.H / 8);
   const int threads = 256;
   const int blocks = (int)std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
   return launch_pdl(moe_combine_kernel, dim3(blocks), dim3(threads), 0, stream, pdl, a);

@@ -13,7 +13,7 @@
 //   w      = s[top] / sum(s[top]) when norm_topk_prob
 // Slots are written in descending choice order.
 //
-// Layout of the launch: grid (E/16 expert tiles, ksplit K slices, ceil(T/8)
+// Decode (T <= 8) launch: grid (E/16 expert tiles, ksplit K slices, ceil(T/8)
 // token groups).  Each CTA computes a 16-expert x 8-token tile of partial
 // logits over its K slice with mma.sync m16n8k16 bf16 (the router weights
 // are bf16 already: no dequantisation) and writes it to the workspace.  The
@@ -28,6 +28,69 @@ namespace {
 
 constexpr int kRouterWarps = 4;
 constexpr int kRouterPad = 32;  // bf16 elements of padding per staged column
+
+// Route one token (called by a whole warp): logit(e) = sum over `slices`
+// of lg[s * stride + e], rounded to the activation dtype as the reference's
+// matmul returns it; sigmoid; bias for choice; top-k by choice (ties to the
+// lower id); weights s / sum(s) when norm.
+__device__ void route_token(const RouterArgs& a, int64_t tok, const float* lg, int64_t stride,
+                            int slices, int lane) {
+  // Each lane owns experts lane, lane+32, ... (E <= 32 * 16).
+  float sc[16], ch[16];
+  const int per = (int)((a.E + 31) / 32);
+  for (int j = 0; j < 16; j++) {
+    sc[j] = 0.f;
+    ch[j] = -INFINITY;
+  }
+  for (int j = 0; j < per && j < 16; j++) {
+    const int64_t e = lane + 32 * j;
+    if (e >= a.E) break;
+    float l = 0.f;
+    for (int s = 0; s < slices; s++) l += __ldcg(lg + (int64_t)s * stride + e);
+    if (a.dtype == kBF16) l = __bfloat162float(__float2bfloat16_rn(l));
+    else if (a.dtype == kF16) l = __half2float(__float2half_rn(l));
+    const float s = sigmoid_ref(l);
+    sc[j] = s;
+    ch[j] = s + (a.bias ? a.bias[e] : 0.f);
+  }
+  float wsum = 0.f;
+  float wsel = 0.f;
+  uint32_t isel = 0;
+  for (int r = 0; r < a.k; r++) {
+    // Lane-local best (highest choice, then lowest id).
+    float bv = -INFINITY;
+    int bj = -1;
+    for (int j = 0; j < per && j < 16; j++) {
+      if (lane + 32 * j >= a.E) break;
+      if (ch[j] > bv) {
+        bv = ch[j];
+        bj = j;
+      }
+    }
+    int bid = bj >= 0 ? lane + 32 * bj : 0x7fffffff;
+    float bs = bj >= 0 ? sc[bj] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      if (ov > bv || (ov == bv && oid < bid)) {
+        bv = ov;
+        bid = oid;
+        bs = os;
+      }
+    }
+    if (bid != 0x7fffffff && (bid & 31) == lane) ch[bid >> 5] = -INFINITY;
+    wsum += bs;
+    if (lane == r) {
+      wsel = bs;
+      isel = (uint32_t)bid;
+    }
+  }
+  if (lane < a.k) {
+    a.inds[tok * a.k + lane] = isel;
+    a.wts[tok * a.k + lane] = a.norm ? wsel / wsum : wsel;
+  }
+}
 
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -103,64 +166,78 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a)
 
   // One warp per token: sum slices, sigmoid, top-k.
   const float* part0 = a.partial + (tg * a.ksplit * 8) * a.E;
-  for (int c = warp; c < ntok; c += kRouterWarps) {
-    const int64_t tok = t0 + c;
-    // Each lane owns experts lane, lane+32, ... (E <= 32 * 16).
-    float sc[16], ch[16];
-    const int per = (int)((a.E + 31) / 32);
-    for (int j = 0; j < 16; j++) {
-      sc[j] = 0.f;
-      ch[j] = -INFINITY;
-    }
-    for (int j = 0; j < per && j < 16; j++) {
-      const int64_t e = lane + 32 * j;
-      if (e >= a.E) break;
-      float l = 0.f;
-      for (int s = 0; s < a.ksplit; s++) l += __ldcg(part0 + ((int64_t)s * 8 + c) * a.E + e);
-      if (a.dtype == kBF16) l = __bfloat162float(__float2bfloat16_rn(l));
-      else if (a.dtype == kF16) l = __half2float(__float2half_rn(l));
-      const float s = sigmoid_ref(l);
-      sc[j] = s;
-      ch[j] = s + (a.bias ? a.bias[e] : 0.f);
-    }
-    float wsum = 0.f;
-    float wsel = 0.f;
-    uint32_t isel = 0;
-    for (int r = 0; r < a.k; r++) {
-      // Lane-local best (highest choice, then lowest id).
-      float bv = -INFINITY;
-      int bj = -1;
-      for (int j = 0; j < per && j < 16; j++) {
-        if (lane + 32 * j >= a.E) break;
-        if (ch[j] > bv) {
-          bv = ch[j];
-          bj = j;
+  for (int c = warp; c < ntok; c += kRouterWarps)
+    route_token(a, t0 + c, part0 + (int64_t)c * a.E, 8 * a.E, a.ksplit, lane);
+}
+
+// Prefill logits: grid (ceil(E/32), ceil(T/32)); warp w covers experts
+// 16*(w&1).. and tokens 16*(w>>1).. of the CTA's 32 x 32 tile with mma.sync
+// m16n8k16 bf16 (A = router rows, B = token rows), fragments loaded straight
+// from global memory (each 32-wide K chunk uses the same element permutation
+// in A and B, so the dot products are unchanged).  logits[T, E] f32.
+__global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t e0 = (int64_t)blockIdx.x * 32 + (warp & 1) * 16;
+  const int64_t tk0 = (int64_t)blockIdx.y * 32 + (warp >> 1) * 16;
+  const int64_t r_lo = e0 + g, r_hi = e0 + g + 8;
+  const bool ok_lo = r_lo < a.E, ok_hi = r_hi < a.E;
+  const uint16_t* glo = a.G + (ok_lo ? r_lo : 0) * a.H;
+  const uint16_t* ghi = a.G + (ok_hi ? r_hi : 0) * a.H;
+  int64_t tok[2];
+  bool tok_ok[2];
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    tok[j] = tk0 + 8 * j + g;
+    tok_ok[j] = tok[j] < a.T;
+  }
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll 4
+  for (int64_t c = 0; c < a.H; c += 32) {
+    const uint4 wl = ok_lo ? *reinterpret_cast<const uint4*>(glo + c + 8 * t) : make_uint4(0, 0, 0, 0);
+    const uint4 wh = ok_hi ? *reinterpret_cast<const uint4*>(ghi + c + 8 * t) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      uint4 xv = make_uint4(0, 0, 0, 0);
+      if (tok_ok[j]) {
+        const int64_t off = tok[j] * a.H + c + 8 * t;
+        if (a.dtype == kBF16) {
+          xv = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.x) + off);
+        } else {
+          float f[8];
+          load8(a.x, a.dtype, off, f);
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<const uint32_t*>(&b);
+          }
+          xv = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-      int bid = bj >= 0 ? lane + 32 * bj : 0x7fffffff;
-      float bs = bj >= 0 ? sc[bj] : 0.f;
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-        const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-        if (ov > bv || (ov == bv && oid < bid)) {
-          bv = ov;
-          bid = oid;
-          bs = os;
-        }
-      }
-      if (bid != 0x7fffffff && (bid & 31) == lane) ch[bid >> 5] = -INFINITY;
-      wsum += bs;
-      if (lane == r) {
-        wsel = bs;
-        isel = (uint32_t)bid;
-      }
-    }
-    if (lane < a.k) {
-      a.inds[tok * a.k + lane] = isel;
-      a.wts[tok * a.k + lane] = a.norm ? wsel / wsum : wsel;
+      mma_bf16_16816(acc[j], wl.x, wh.x, wl.y, wh.y, xv.x, xv.y);
+      mma_bf16_16816(acc[j], wl.z, wh.z, wl.w, wh.w, xv.z, xv.w);
     }
   }
+#pragma unroll
+  for (int j = 0; j < 2; j++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int64_t tk = tk0 + 8 * j + 2 * t + (r & 1);
+      const int64_t e = (r < 2) ? r_lo : r_hi;
+      if (tk < a.T && e < a.E) a.partial[tk * a.E + e] = acc[j][r];
+    }
+}
+
+// Prefill routing: one warp per token over logits[T, E].
+__global__ void __launch_bounds__(256) router_topk_kernel(RouterArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (tok < a.T) route_token(a, tok, a.partial + tok * a.E, 0, 1, lane);
 }
 
 }  // namespace
@@ -172,8 +249,36 @@ int router_ksplit(int64_t H) {
   return (H % (32 * kRouterWarps) == 0) ? 1 : 0;
 }
 
+template <typename Kern>
+cudaError_t launch_plain(Kern kern, dim3 grid, dim3 block, cudaStream_t stream, bool pdl,
+                         const RouterArgs& a) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kern, a);
+  if (err != cudaSuccess) return err;
+  return cudaGetLastError();
+}
+
+// T > 8: logits GEMM then one warp per token (the partial workspace, sized
+// ceil(T/8) * 8 * ksplit * E floats, holds the [T, E] logits).  T <= 8: the
+// split-K single-launch kernel.
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t stream, bool pdl) {
   if (a.T == 0) return cudaSuccess;
+  if (a.T > 8) {
+    cudaError_t err = launch_plain(router_logits_kernel,
+                                   dim3((unsigned)((a.E + 31) / 32), (unsigned)((a.T + 31) / 32)),
+                                   dim3(128), stream, pdl, a);
+    if (err != cudaSuccess) return err;
+    return launch_plain(router_topk_kernel, dim3((unsigned)((a.T + 7) / 8)), dim3(256), stream,
+                        true, a);
+  }
   const int Kc = (int)(a.H / a.ksplit);
   const size_t smem = (size_t)8 * (Kc + kRouterPad) * sizeof(uint16_t);
   cudaError_t err = ensure_smem(router_kernel, smem);

@@ -52,6 +52,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may stay suspended in hardware for up to
+// `ns` nanoseconds waiting for the phase (it resumes as soon as the phase
+// completes), so waiting warps do not take issue slots from working ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete, for at most ~`budget` cycles
 // (default ~1 s at 2 GHz).  Returns false on timeout.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
@@ -74,6 +91,26 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
           "r"(smem_u32(dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) from
+// this CTA's shared memory to global memory, in the thread's current bulk
+// group.
+__device__ __forceinline__ void bulk_s2g(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst),
+               "r"(smem_u32(ssrc)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// The source shared memory of every committed bulk group has been read.
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Every committed bulk group has completed.
+__device__ __forceinline__ void bulk_wait0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // Named barrier among `count` threads (multiple of 32), id 1..15.
