@@ -257,7 +257,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == kWarpMma) {
     // ------------------------------ MMA issuer ------------------------------
-    if (lane == 0) {
+    uint32_t elected;
+    asm volatile("{\n.reg .pred p;\nelect.sync _|p, 0xffffffff;\nselp.u32 %0, 1, 0, p;\n}\n" : "=r"(elected));
+    {
       uint32_t g = 0;
       int j = 0;
       bool ok = true;
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!tile_info(a, u, m_tiles, ts.next(a, u, m_tiles, ntot), ti)) continue;
         const int buf = j & 1;
         if (j >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((j >> 1) - 1) & 1)) {
-          flag(kErrTimeout);
+          if (elected) flag(kErrTimeout);
           break;
         }
         tc_fence_after();
@@ -279,13 +281,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int as = g % kASlabs, bs = g % kBSlabs;
           if (!mbar_wait_bounded(&a_full[as], (g / kASlabs) & 1) ||
               !mbar_wait_bounded(&b_full[bs], (g / kBSlabs) & 1)) {
-            flag(kErrTimeout);
+            if (elected) flag(kErrTimeout);
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t ta = tmem + (uint32_t)(kAccCols + as * kASlabCols);
           const uint64_t bd = smem_desc_sw128(smem_u32(sB + bs * kSlabB));
+          if (elected) {
 #pragma unroll
           for (int s = 0; s < kStages; s++)
 #pragma unroll
@@ -294,19 +297,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                           (sl | s | ks) != 0);
           umma_commit(&a_empty[as]);
           umma_commit(&b_empty[bs]);
+          }
+          __syncwarp();
         }
         if (!ok) break;
-        umma_commit(&acc_full[buf]);  // the accumulator is complete once these MMAs are
+        if (elected) umma_commit(&acc_full[buf]);
+        __syncwarp();
         j++;
       }
-      // No MMA may still write TMEM when it is released.
-      umma_commit(drain);
-      if (!mbar_wait_bounded(drain, 0)) flag(kErrTimeout);
+      if (elected) umma_commit(drain);
+      __syncwarp();
+      if (!mbar_wait_bounded(drain, 0) && elected) flag(kErrTimeout);
     }
     __syncwarp();
   } else if (warp == kWarpRaw) {
     // ------------------------------ weight TMA ------------------------------
-    if (lane == 0) {
+    uint32_t elected;
+    asm volatile("{\n.reg .pred p;\nelect.sync _|p, 0xffffffff;\nselp.u32 %0, 1, 0, p;\n}\n" : "=r"(elected));
+    {
       uint32_t g = 0;
       bool ok = true;
       TileStream ts;
@@ -324,11 +332,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int r = g % kRawSlots;
           if (g >= kRawSlots &&
               !mbar_wait_bounded(&raw_empty[r], ((g / kRawSlots) - 1) & 1)) {
-            flag(kErrTimeout);
+            if (elected) flag(kErrTimeout);
             ok = false;
             break;
           }
           uint8_t* slot = sRaw + r * kRawSlot;
+          if (!elected) continue;
           mbar_arrive_expect_tx(&raw_full[r], kRawSlot);
           if (a.mode == 1) {
             tma_load_2d(slot, c0, sl * 128, row0, &raw_full[r]);
@@ -386,25 +395,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sc_full[sb]);
       j++;
-      if (lane == 0) {
+      {
         const int nbox = ti.N / 16;
         for (int sl = 0; sl < nslab; sl++, g++) {
           const int bs = g % kBSlabs;
           if (g >= kBSlabs && !mbar_wait_bounded(&b_empty[bs], ((g / kBSlabs) - 1) & 1)) {
-            flag(kErrTimeout);
+            if (lane == 0) flag(kErrTimeout);
             ok = false;
             break;
           }
+          if (lane != 0) continue;
           mbar_arrive_expect_tx(&b_full[bs], kStages * nbox * kBoxB);
           for (int s = 0; s < kStages; s++)
             for (int b = 0; b < nbox; b++)
               tma_load_2d(sB + bs * kSlabB + s * kStageB + b * kBoxB, &a.mb,
                           (sl * kStages + s) * kBK, ti.start + 16 * b, &b_full[bs]);
         }
+        __syncwarp();
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
-    if (lane == 0) {
+    {
       for (uint32_t i = 0; i < min(g, (uint32_t)kBSlabs); i++) {
         const uint32_t gg = g - 1 - i;
         mbar_wait_bounded(&b_full[gg % kBSlabs], (gg / kBSlabs) & 1, kDrainBudget);
