@@ -94,7 +94,7 @@ struct alignas(64) GemmArgs {
   void* out;
   int out_dtype;
   int64_t out_ld;
-  int out_bulk;  // set by the launcher: output rows written by bulk copies
+  int out_vec;  // set by the launcher: output rows written as 16-byte chunks
 };
 
 // Tensor maps for GemmArgs (cuTensorMapEncodeTiled through the runtime's

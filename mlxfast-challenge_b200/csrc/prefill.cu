@@ -30,9 +30,8 @@
 //   epilogue (4 warps)     tcgen05.ld of the finished accumulator (one TMEM
 //                          sub-partition each; the accumulator is released at
 //                          once), staged in shared memory one slot row per
-//                          tile column, written out by bulk copies
-//                          (cp.async.bulk shared -> global) while the next
-//                          tile runs.
+//                          tile column, written out with coalesced 16-byte
+//                          stores while the next tile runs.
 // Operand type: f16 for pre-scaled activation rows (rows_to_f16: per-row power
 // of two, exact for bf16 inputs, re-applied in the epilogue) and for f16
 // inputs; bf16 for bf16 inputs (dense quantized_matmul, no workspace).
@@ -488,7 +487,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------ epilogue --------------------------------
     const int sp = warp & 3;       // TMEM sub-partition this warp may read
     const int r = sp * 32 + lane;  // tile row = TMEM lane
-    const bool issuer = warp == kWarpEpi0 && lane == 0;  // bulk copies
     int j = 0;
     TileStream ts;
     ts.start(a, m_tiles, ntot);
@@ -519,8 +517,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      // Staging buffer free: the previous tile's bulk copies have read it.
-      if (issuer) bulk_wait_read0();
+      // Staging buffer free: every epilogue thread has copied out the
+      // previous tile.
       named_sync(1, 32 * kEpiWarps);
 #pragma unroll
       for (int h2 = 0; h2 < 2; h2++) {
@@ -546,19 +544,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int esz = (a.mode != 0 || a.out_dtype == kF32) ? 4 : 2;
       const int row_elems = a.mode == 1 ? 64 : 128;
       const int64_t col0 = (int64_t)ti.m_tile * row_elems;
-      if (a.out_bulk) {
-        fence_proxy_async();  // staged rows -> bulk-copy reads
+      const int et = threadIdx.x - 32 * kWarpEpi0;
+      if (a.out_vec) {
+        // Coalesced 16-byte copies of the staged rows (the TMA queue stays
+        // with the operand loads).
         named_sync(1, 32 * kEpiWarps);
-        if (issuer) {
-          for (int n = 0; n < ti.count; n++)
-            bulk_s2g(reinterpret_cast<uint8_t*>(a.out) +
-                         ((int64_t)(ti.start + n) * a.out_ld + col0) * esz,
-                     sOut + n * kOutPitch, (uint32_t)(row_elems * esz));
-          bulk_commit();
+        const int chunks = row_elems * esz / 16;
+        for (int idx = et; idx < ti.count * chunks; idx += 32 * kEpiWarps) {
+          const int n = idx / chunks, c = idx - n * chunks;
+          const uint4 v4 = *reinterpret_cast<const uint4*>(sOut + n * kOutPitch + c * 16);
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.out) +
+                                    ((int64_t)(ti.start + n) * a.out_ld + col0) * esz + c * 16) = v4;
         }
       } else {
         named_sync(1, 32 * kEpiWarps);
-        const int et = threadIdx.x - 32 * kWarpEpi0;
         const int64_t rows_left = ti.Mrows - col0;
         const int ncol = rows_left < row_elems ? (int)rows_left : row_elems;
         for (int idx = et; idx < ti.count * row_elems; idx += 32 * kEpiWarps) {
@@ -573,7 +572,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       j++;
     }
-    if (issuer) bulk_wait0();  // every output row written before the CTA retires
   }
   tc_fence_before();
   __syncthreads();
@@ -816,11 +814,11 @@ cudaError_t launch_nvfp4_gemm(const GemmArgs& a, bool f16, int max_tiles, cudaSt
   if (a.K % kSlabK) return cudaErrorInvalidValue;
   const size_t smem = gemm_smem_bytes();
   auto kern = f16 ? nvfp4_gemm_kernel<true> : nvfp4_gemm_kernel<false>;
-  // Bulk output copies need 16-byte aligned rows and only whole row tiles.
+  // 16-byte output copies need 16-byte aligned rows and only whole row tiles.
   GemmArgs args = a;
   const int esz = (a.mode != 0 || a.out_dtype == kF32) ? 4 : 2;
   const int tile_rows = a.mode == 1 ? 64 : 128;
-  args.out_bulk = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) && (a.out_ld * esz) % 16 == 0 &&
+  args.out_vec = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) && (a.out_ld * esz) % 16 == 0 &&
                   a.Mrows % tile_rows == 0 && a.Mrows_shared % tile_rows == 0;
   cudaError_t e = ensure_smem(kern, smem);
   if (e != cudaSuccess) return e;
