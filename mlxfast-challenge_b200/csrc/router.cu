@@ -35,40 +35,38 @@ constexpr int kRouterPad = 32;  // bf16 elements of padding per staged column
 // lower id); weights s / sum(s) when norm.
 __device__ void route_token(const RouterArgs& a, int64_t tok, const float* lg, int64_t stride,
                             int slices, int lane) {
-  // Each lane owns experts lane, lane+32, ... (E <= 32 * 16).
-  float sc[16], ch[16];
-  const int per = (int)((a.E + 31) / 32);
-  for (int j = 0; j < 16; j++) {
-    sc[j] = 0.f;
-    ch[j] = -INFINITY;
-  }
-  for (int j = 0; j < per && j < 16; j++) {
+  // Lane owns experts lane + 32 j, j < 16 (E <= 512); fully unrolled so the
+  // per-lane arrays stay in registers.
+  constexpr int kPer = 16;
+  float sc[kPer], ch[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; j++) {
     const int64_t e = lane + 32 * j;
-    if (e >= a.E) break;
-    float l = 0.f;
-    for (int s = 0; s < slices; s++) l += __ldcg(lg + (int64_t)s * stride + e);
+    const bool live = e < a.E;
+    float l = live ? __ldcg(lg + e) : 0.f;
+    for (int s = 1; s < slices; s++)
+      if (live) l += __ldcg(lg + (int64_t)s * stride + e);
     if (a.dtype == kBF16) l = __bfloat162float(__float2bfloat16_rn(l));
     else if (a.dtype == kF16) l = __half2float(__float2half_rn(l));
     const float s = sigmoid_ref(l);
-    sc[j] = s;
-    ch[j] = s + (a.bias ? a.bias[e] : 0.f);
+    sc[j] = live ? s : 0.f;
+    ch[j] = live ? s + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
   }
   float wsum = 0.f;
   float wsel = 0.f;
   uint32_t isel = 0;
   for (int r = 0; r < a.k; r++) {
-    // Lane-local best (highest choice, then lowest id).
-    float bv = -INFINITY;
+    // Lane-local best (highest choice, then lowest id = lowest j).
+    float bv = -INFINITY, bs = 0.f;
     int bj = -1;
-    for (int j = 0; j < per && j < 16; j++) {
-      if (lane + 32 * j >= a.E) break;
+#pragma unroll
+    for (int j = 0; j < kPer; j++)
       if (ch[j] > bv) {
         bv = ch[j];
+        bs = sc[j];
         bj = j;
       }
-    }
     int bid = bj >= 0 ? lane + 32 * bj : 0x7fffffff;
-    float bs = bj >= 0 ? sc[bj] : 0.f;
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
       const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
@@ -79,7 +77,11 @@ __device__ void route_token(const RouterArgs& a, int64_t tok, const float* lg, i
         bs = os;
       }
     }
-    if (bid != 0x7fffffff && (bid & 31) == lane) ch[bid >> 5] = -INFINITY;
+    if (bid != 0x7fffffff && (bid & 31) == lane) {
+#pragma unroll
+      for (int j = 0; j < kPer; j++)
+        if (j == (bid >> 5)) ch[j] = -INFINITY;
+    }
     wsum += bs;
     if (lane == r) {
       wsel = bs;
@@ -231,6 +233,82 @@ __global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
     }
 }
 
+// Prefill logits for bf16 x: grid (ceil(E/32), ceil(T/32)), 128 threads.  The
+// CTA's 32 router rows and 32 token rows stream through shared memory in
+// 64-wide K chunks (cp.async, kLgStages deep; rows padded to 192 bytes so the
+// 16-byte fragment reads are conflict-free); warp w computes experts
+// 16*(w&1).. x tokens 16*(w>>1).. with mma.sync m16n8k16 bf16 (same K
+// permutation in A and B as above).
+constexpr int kLgStages = 4;
+constexpr int kLgPitch = 192;                   // bytes per staged row (128 + pad)
+constexpr int kLgTile = 32 * kLgPitch;          // one 32-row operand tile
+__device__ __forceinline__ void cp_async16_lg(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(dst)),
+               "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__global__ void __launch_bounds__(128) router_logits_smem_kernel(RouterArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int64_t eb = (int64_t)blockIdx.x * 32, tb = (int64_t)blockIdx.y * 32;
+  const int nk = (int)(a.H / 64);
+  const uint16_t* x = reinterpret_cast<const uint16_t*>(a.x);
+  auto load_stage = [&](int st, int kc) {
+    uint8_t* sg = smem + st * 2 * kLgTile;
+    uint8_t* sx = sg + kLgTile;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      const int q = threadIdx.x + 128 * i;  // 256 chunks of 16 bytes per tile
+      const int row = q >> 3, c = q & 7;
+      const int64_t e = eb + row, tk = tb + row;
+      cp_async16_lg(sg + row * kLgPitch + c * 16,
+                    a.G + (e < a.E ? e : 0) * a.H + (int64_t)kc * 64 + c * 8, e < a.E);
+      cp_async16_lg(sx + row * kLgPitch + c * 16,
+                    x + (tk < a.T ? tk : 0) * a.H + (int64_t)kc * 64 + c * 8, tk < a.T);
+    }
+  };
+#pragma unroll
+  for (int s = 0; s < kLgStages - 1; s++) {
+    if (s < nk) load_stage(s, s);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  const int erow = (warp & 1) * 16, trow = (warp >> 1) * 16;
+  for (int kc = 0; kc < nk; kc++) {
+    asm volatile("cp.async.wait_group %0;" ::"n"(kLgStages - 2) : "memory");
+    __syncthreads();
+    if (kc + kLgStages - 1 < nk) load_stage((kc + kLgStages - 1) % kLgStages, kc + kLgStages - 1);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint8_t* sg = smem + (kc % kLgStages) * 2 * kLgTile;
+    const uint8_t* sx = sg + kLgTile;
+#pragma unroll
+    for (int sub = 0; sub < 2; sub++) {  // two 32-wide K pieces of the chunk
+      const int cb = sub * 64 + t * 16;
+      const uint4 wl = *reinterpret_cast<const uint4*>(sg + (erow + g) * kLgPitch + cb);
+      const uint4 wh = *reinterpret_cast<const uint4*>(sg + (erow + g + 8) * kLgPitch + cb);
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(sx + (trow + 8 * j + g) * kLgPitch + cb);
+        mma_bf16_16816(acc[j], wl.x, wh.x, wl.y, wh.y, xv.x, xv.y);
+        mma_bf16_16816(acc[j], wl.z, wh.z, wl.w, wh.w, xv.z, xv.w);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < 2; j++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      const int64_t tk = tb + trow + 8 * j + 2 * t + (r & 1);
+      const int64_t e = eb + erow + g + ((r < 2) ? 0 : 8);
+      if (tk < a.T && e < a.E) a.partial[tk * a.E + e] = acc[j][r];
+    }
+}
+
 // Prefill routing: one warp per token over logits[T, E].
 __global__ void __launch_bounds__(256) router_topk_kernel(RouterArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -272,9 +350,30 @@ cudaError_t launch_plain(Kern kern, dim3 grid, dim3 block, cudaStream_t stream, 
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t stream, bool pdl) {
   if (a.T == 0) return cudaSuccess;
   if (a.T > 8) {
-    cudaError_t err = launch_plain(router_logits_kernel,
-                                   dim3((unsigned)((a.E + 31) / 32), (unsigned)((a.T + 31) / 32)),
-                                   dim3(128), stream, pdl, a);
+    const dim3 grid((unsigned)((a.E + 31) / 32), (unsigned)((a.T + 31) / 32));
+    cudaError_t err;
+    const bool staged = a.dtype == kBF16 && a.H % 64 == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.G) & 15) == 0;
+    if (staged) {
+      const size_t smem = (size_t)kLgStages * 2 * kLgTile;
+      err = ensure_smem(router_logits_smem_kernel, smem);
+      if (err != cudaSuccess) return err;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = grid;
+      cfg.blockDim = dim3(128);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr.val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = pdl ? 1 : 0;
+      err = cudaLaunchKernelEx(&cfg, router_logits_smem_kernel, a);
+      if (err == cudaSuccess) err = cudaGetLastError();
+    } else {
+      err = launch_plain(router_logits_kernel, grid, dim3(128), stream, pdl, a);
+    }
     if (err != cudaSuccess) return err;
     return launch_plain(router_topk_kernel, dim3((unsigned)((a.T + 7) / 8)), dim3(256), stream,
                         true, a);
