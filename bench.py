@@ -23,6 +23,20 @@ roofline= the dominant kernel (fused gate/up + SwiGLU), timed alone.
 x, compiled from the reference sources into oracle/_ref) on the same layer,
 with all host threads, one sparse layer per step.
 
+Also reported on the same line (rank 0, N=1 runs):
+prefill = BASELINE config[3] on one GPU: the full sparse block (BF16 router
+          top-8, 256 routed experts, shared expert, residual) at T=512 tokens,
+          39 sparse layers per step (4 distinct random-init layers cycled, 452 MB
+          of NVFP4 weights each, > L2), through SparseMoeBlock; 512-token
+          prefill tok/s of the MoE blocks and the HBM GB/s that moving every
+          used weight once would need in that time.
+dense   = BASELINE config[0]: quantized_matmul x[M, 2048] @ W[4096, 2048]^T,
+          M = 512 (tensor-core GEMM, TFLOP/s) and M = 1 (GEMV, GB/s), cycling 32
+          weight copies (150 MB > L2).
+
+--workload prefill|dense prints only that measurement (used by the committed
+ncu profiling commands).
+
 Multi-GPU: serial decode does not shard (replicas only): each rank runs its own
 chain; value is the aggregate.
 """
@@ -56,6 +70,8 @@ def parse():
     p.add_argument("--layers", type=int, default=39)
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", choices=["all", "decode", "prefill", "dense"], default="all")
+    p.add_argument("--prefill-steps", type=int, default=10)
     return p.parse_args()
 
 
@@ -68,6 +84,73 @@ def layer_bytes(cfg, k, T=1):
 def gateup_bytes(cfg, k, T=1):
     per_row = cfg.hidden // 2 + cfg.hidden // 16
     return k * 2 * cfg.inter * per_row + T * cfg.hidden * 2 + T * k * cfg.inter * 2
+
+
+# ----------------------------------------------------------------------------- prefill / dense
+def bench_prefill(torch, nv, lag, cfg, dev, steps, warmup, layers, distinct=4, T=512):
+    """config[3] on one GPU: the full sparse block at T tokens, `layers` per step."""
+    distinct = max(1, min(distinct, layers))
+    blocks = [lag.random_sparse_layer(nv, seed=2000 + l, device=dev)[0] for l in range(distinct)]
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+    res = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty_like(x)
+
+    def step():
+        for l in range(layers):
+            blocks[l % distinct](x, residual=res, out=y)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_step = e0.elapsed_time(e1) / steps
+    us_layer = ms_step * 1e3 / layers
+    # Every expert is hit at T=512 (4096 random pairs over 256 experts).
+    layer_w = (cfg.n_experts * cfg.routed_bytes_per_expert() + cfg.shared_bytes() +
+               cfg.router_bytes())
+    layer_b = layer_w + 3 * T * cfg.hidden * 2
+    return {"workload": f"BASELINE config[3] on 1 GPU: sparse block T={T} (router top-8, 256 "
+                        f"experts, shared expert, residual), {layers} layers per step "
+                        f"({distinct} distinct layers cycled)",
+            "tok_per_s": T / (ms_step / 1e3), "us_per_layer": us_layer,
+            "hbm_gbs_equiv": layer_b / (us_layer / 1e6) / 1e9,
+            "bytes_per_layer": layer_b, "steps": steps, "layers_per_step": layers,
+            "unit": "tok/s"}
+
+
+def bench_dense(torch, nv, dev, reps=50, copies=32):
+    """config[0]: quantized_matmul [M, 2048] x [4096, 2048]^T for M = 512 and M = 1."""
+    N, K = 4096, 2048
+    g = torch.Generator(device=dev).manual_seed(5)
+    w = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wq, sq = nv.quantize(w)
+    wqs = [wq.clone() for _ in range(copies)]
+    sqs = [sq.clone() for _ in range(copies)]
+    out = {}
+    for M in (512, 1):
+        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+        for i in range(3):
+            nv.quantized_matmul(x, wqs[i], sqs[i])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            nv.quantized_matmul(x, wqs[i % copies], sqs[i % copies])
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        wbytes = N * K // 2 + N * K // 16
+        out[f"M{M}"] = {"us": us, "tflops": 2 * M * N * K / (us / 1e6) / 1e12,
+                        "hbm_gbs": (wbytes + M * K * 2 + M * N * 2) / (us / 1e6) / 1e9}
+    out["workload"] = ("BASELINE config[0]: x bf16 [M, 2048] @ nvfp4 W[4096, 2048]^T, "
+                       f"{copies} weight copies cycled (> L2)")
+    return out
 
 
 # ----------------------------------------------------------------------------- CPU
@@ -216,6 +299,17 @@ def main():
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
 
+    if args.workload in ("prefill", "dense"):
+        if rank == 0:
+            if args.workload == "prefill":
+                r = bench_prefill(torch, nv, lag, cfg, dev, args.steps, args.warmup, args.layers)
+            else:
+                r = bench_dense(torch, nv, dev)
+            print(json.dumps({"workload": args.workload, "result": r}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
     # Setup: L random-init sparse layers (routed banks only: config[1]).
     blocks, routing = [], []
     for l in range(args.layers):
@@ -310,9 +404,17 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_val = world * e2e_steps * bytes_step / float(te.item()) / 1e9
 
+    launches = args.steps * chain.launches_per_step()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu, _, _ = cpu_reference_gbs(args.cpu_seconds, os.cpu_count() or 1, cfg)
+    prefill = dense = None
+    if rank == 0 and world == 1 and args.workload == "all":
+        del chain, gu
+        torch.cuda.empty_cache()
+        prefill = bench_prefill(torch, nv, lag, cfg, dev, args.prefill_steps, 3,
+                                cfg.num_sparse_layers)
+        dense = bench_dense(torch, nv, dev)
 
     if rank == 0:
         line = {
@@ -327,16 +429,19 @@ def main():
                        "weights": "nvfp4 e2m1/e4m3-g16", "activations": "bf16",
                        "accumulate": "f32"},
             "tok_per_s_moe_only": world * args.steps / (ms_max / 1e3),
-            "gpu_launches": args.steps * chain.launches_per_step(),
+            "gpu_launches": launches,
             "clocks": clocks,
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": cfg.hidden * 2,
                     "d2h_bytes_per_step": cfg.hidden * 2,
                     "api": "MoEDecodeChain.__call__ (pinned host x -> device -> host y)"},
+            "prefill": prefill,
+            "dense": dense,
         }
         print(json.dumps(line), flush=True)
-    del chain, gu
+    if prefill is None:
+        del chain, gu
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
