@@ -17,7 +17,9 @@ value   = algorithmic HBM bytes of all ranks' steps / device time (GB/s), the
 e2e     = the same metric through the public API MoEDecodeChain(x_host): per
           step the input is copied from pinned host memory, the layers run and
           the output is read back to the host.
-roofline= the dominant kernel (fused gate/up + SwiGLU), timed alone.
+roofline= the dominant kernel timed alone: moe_decode_stack_kernel, which runs
+          all 39 layers in one persistent launch (or, where the stack does
+          not apply, the per-layer fused gate/up + SwiGLU kernel).
 
 --impl reference times the reference's own MLX CPU kernel (fp_qmm_t for bf16
 x, compiled from the reference sources into oracle/_ref) on the same layer,
@@ -253,6 +255,19 @@ def measured_peak_hbm():
         return 6650.0, "fallback"
 
 
+def stack_traffic(layers):
+    """DRAM bytes of one moe_decode_stack_kernel launch over `layers` layers,
+    scaled from the committed ncu capture (taken on fewer layers; the kernel
+    moves the same bytes per layer)."""
+    p = os.path.join(ROOT, "profiles", "moe_decode_stack_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d["dram_bytes_per_layer"] * layers
+    except Exception:
+        return None
+
+
 def ncu_traffic():
     """dram bytes per launch of the gate/up kernel from the committed ncu summary."""
     p = os.path.join(ROOT, "profiles", "moe_gateup_decode_traffic.json")
@@ -353,38 +368,62 @@ def main():
     ms_max = float(t.item())
     value = world * args.steps * bytes_step / (ms_max / 1e3) / 1e9
 
-    # Dominant kernel alone: the L gate/up launches captured into one graph.
+    # Dominant kernel alone.  With the persistent stack (one launch per step)
+    # that kernel is the whole step: time moe_decode_stack_forward calls alone
+    # (its tiny counter reset included); otherwise the L gate/up launches in
+    # one graph.
     import ctypes
     L = nv._lib.lib()
-    gu = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(gu, stream=s):
-            sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-            for l, b in enumerate(blocks):
-                inds, _ = chain.routing[l]
-                nv._lib.check(L.moe_gate_up_swiglu(chain.act.data_ptr(), chain.act_ld,
-                                                   chain.x0.data_ptr(), 0, 1,
-                                                   ctypes.byref(b.desc), inds.data_ptr(), sp))
-        for _ in range(5):
-            gu.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = max(20, args.steps // 4)
-        e0.record(s)
-        for _ in range(reps):
-            gu.replay()
-        e1.record(s)
-    torch.cuda.synchronize()
-    gu_ms = e0.elapsed_time(e1) / (reps * args.layers)
-    gu_bytes = gateup_bytes(cfg, cfg.top_k)
     peak, peak_kind = measured_peak_hbm()
-    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
-    traffic = ncu_traffic()
-    roofline = {"bound": "hbm", "kernel": "moe_gateup_kernel (fused gate/up + SwiGLU)",
-                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
-                if peak_kind == "measured" else "fallback 6650 GB/s",
-                "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes,
-                "us_per_launch": gu_ms * 1e3}
+    peak_src = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6650 GB/s")
+    if chain.stack:
+        reps = max(20, args.steps // 4)
+        with torch.cuda.stream(s):
+            sp = ctypes.c_void_p(s.cuda_stream)
+            for _ in range(3):
+                nv._lib.check(chain._stack_call(sp))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(reps):
+                nv._lib.check(chain._stack_call(sp))
+            e1.record(s)
+        torch.cuda.synchronize()
+        k_ms = e0.elapsed_time(e1) / reps
+        achieved = bytes_step / (k_ms / 1e3) / 1e9
+        tr = stack_traffic(args.layers)
+        roofline = {"bound": "hbm", "kernel": f"moe_decode_stack_kernel ({args.layers} layers, "
+                                              "one persistent launch)",
+                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "peak_source": peak_src, "traffic": tr,
+                    "algorithmic_bytes_per_launch": bytes_step, "us_per_launch": k_ms * 1e3}
+        gu = None
+    else:
+        gu = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gu, stream=s):
+                sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+                for l, b in enumerate(blocks):
+                    inds, _ = chain.routing[l]
+                    nv._lib.check(L.moe_gate_up_swiglu(chain.act.data_ptr(), chain.act_ld,
+                                                       chain.x0.data_ptr(), 0, 1,
+                                                       ctypes.byref(b.desc), inds.data_ptr(), sp))
+            for _ in range(5):
+                gu.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = max(20, args.steps // 4)
+            e0.record(s)
+            for _ in range(reps):
+                gu.replay()
+            e1.record(s)
+        torch.cuda.synchronize()
+        gu_ms = e0.elapsed_time(e1) / (reps * args.layers)
+        gu_bytes = gateup_bytes(cfg, cfg.top_k)
+        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+        roofline = {"bound": "hbm", "kernel": "moe_gateup_kernel (fused gate/up + SwiGLU)",
+                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "peak_source": peak_src, "traffic": ncu_traffic(),
+                    "algorithmic_bytes_per_launch": gu_bytes, "us_per_launch": gu_ms * 1e3}
 
     # End to end through the public API: pinned host x in, host y out, every step.
     xh = torch.randn(1, cfg.hidden, generator=torch.Generator().manual_seed(3)).to(
@@ -410,7 +449,7 @@ def main():
         cpu, _, _ = cpu_reference_gbs(args.cpu_seconds, os.cpu_count() or 1, cfg)
     prefill = dense = None
     if rank == 0 and world == 1 and args.workload == "all":
-        del chain, gu
+        del chain
         torch.cuda.empty_cache()
         prefill = bench_prefill(torch, nv, lag, cfg, dev, args.prefill_steps, 3,
                                 cfg.num_sparse_layers)
@@ -441,7 +480,7 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if prefill is None:
-        del chain, gu
+        del chain
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

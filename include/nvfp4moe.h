@@ -212,6 +212,31 @@ NVFP4MOE_API int moe_down_combine(void* y, const float* act, int64_t act_ld,
                                   const moe_layer_desc* layer, const uint32_t* inds,
                                   const float* weights, nvfp4_stream stream);
 
+/* Serial decode through a stack of sparse MoE layers, T = 1, routing given
+ * per layer: for l = 0 .. n_layers-1
+ *   x_{l+1} = moe_block(x_l; layers[l], inds[l], weights[l])   (no residual)
+ * and y = x_{n_layers}.  This is the MoE part of the reference runtime's
+ * decode step over the sparse layers (Sources/MLXFastModel/
+ * LagunaRuntimeModel.swift:11460 -> :11030 -> :10678), which the reference
+ * evaluates layer by layer; it has no single-operator counterpart.  Run as one
+ * persistent cooperative launch that streams the next layers' expert weights
+ * while the current layer's dependent chain runs; results equal a loop of
+ * moe_gate_up_swiglu + moe_down_combine.  Requirements: every layer has the
+ * same hidden / inter / n_experts / top_k (<= 16), shared_inter 0 or equal to
+ * inter, hidden and inter multiples of 256, 16-byte aligned banks,
+ * n_layers <= 64; otherwise NVFP4_ERR_UNSUPPORTED (use the per-layer calls).
+ * inds[l] / weights[l] are device pointers to [top_k] entries.  The call runs
+ * as many CTAs as the GPU has SMs and they wait on one another inside the
+ * launch (co-residency is guaranteed by the cooperative launch); do not
+ * overlap it with other work that needs whole SMs. */
+NVFP4MOE_API size_t moe_decode_stack_workspace_size(const moe_layer_desc* layers,
+                                                    int64_t n_layers);
+NVFP4MOE_API int moe_decode_stack_forward(void* y, const void* x, int dtype, int64_t n_layers,
+                                          const moe_layer_desc* layers,
+                                          const uint32_t* const* inds,
+                                          const float* const* weights, void* workspace,
+                                          size_t workspace_bytes, nvfp4_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -65,6 +65,9 @@ SIGNATURES = {
     "moe_gate_up_swiglu": (_I, [_P, _I64, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P]),
     "moe_down_combine": (_I, [_P, _P, _I64, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P,
                               _P]),
+    "moe_decode_stack_workspace_size": (_SZ, [ctypes.POINTER(MoeLayerDesc), _I64]),
+    "moe_decode_stack_forward": (_I, [_P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P, _P,
+                                      _SZ, _P]),
 }
 
 _lib = None

@@ -192,6 +192,10 @@ int nvfp4_device_status(void) {
   e = nvfp4::read_and_clear_prefill_error(&st2);
   if (e != cudaSuccess) return check_cuda(e, "device_status");
   if (st == 0) st = st2;
+  int st3 = 0;
+  e = nvfp4::read_and_clear_stack_error(&st3);
+  if (e != cudaSuccess) return check_cuda(e, "device_status");
+  if (st == 0) st = st3;
   if (st != 0)
     return fail(NVFP4_ERR_DEVICE_INDEX,
                 "[gather_qmm] an expert or batch index was out of range (kernel site %d); "
@@ -776,3 +780,115 @@ extern "C" int moe_block_forward_noalloc(void* y, const void* x, const void* res
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Serial decode through a stack of sparse layers in one persistent launch.
+namespace {
+struct StackLayout {
+  size_t act_off, xb0_off, xb1_off, bar_off, total;
+};
+
+StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
+  StackLayout S;
+  const int64_t kk = L0->top_k + (L0->shared_inter > 0 ? 1 : 0);
+  S.act_off = 0;
+  S.xb0_off = align_up((size_t)kk * L0->inter * sizeof(float), 256);
+  S.xb1_off = align_up(S.xb0_off + (size_t)L0->hidden * dtype_bytes, 256);
+  S.bar_off = align_up(S.xb1_off + (size_t)L0->hidden * dtype_bytes, 256);
+  S.total = align_up(S.bar_off + (2 + 2 * nvfp4::kStackMaxLayers) * sizeof(unsigned), 256);
+  return S;
+}
+}  // namespace
+
+extern "C" size_t moe_decode_stack_workspace_size(const moe_layer_desc* layers,
+                                                  int64_t n_layers) {
+  if (!layers || n_layers <= 0) return 0;
+  return stack_layout(&layers[0], 4).total;  // sized for the widest dtype
+}
+
+extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64_t n_layers,
+                                        const moe_layer_desc* layers,
+                                        const uint32_t* const* inds, const float* const* weights,
+                                        void* workspace, size_t workspace_bytes,
+                                        nvfp4_stream stream) {
+  const char* op = "moe_decode_stack";
+  if (!layers || n_layers <= 0) return fail(NVFP4_ERR_INVALID, "[%s] no layers.", op);
+  if (!y || !x || !inds || !weights)
+    return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  if (n_layers > nvfp4::kStackMaxLayers)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] at most %d layers per call.", op,
+                nvfp4::kStackMaxLayers);
+  const moe_layer_desc* L0 = &layers[0];
+  for (int64_t l = 0; l < n_layers; l++)
+    if (int r = check_layer(op, &layers[l], dtype, 1)) return r;
+  const int64_t H = L0->hidden, I = L0->inter, E = L0->n_experts, k = L0->top_k;
+  const int64_t Is = L0->shared_inter;
+  for (int64_t l = 1; l < n_layers; l++) {
+    const moe_layer_desc* Ll = &layers[l];
+    if (Ll->hidden != H || Ll->inter != I || Ll->n_experts != E || Ll->top_k != k ||
+        (Ll->shared_inter > 0) != (Is > 0))
+      return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layers must share one shape.", op);
+  }
+  if (H % 256 || I % 256 || (Is != 0 && Is != I) || k > 16 || E > 0x7fffffff)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] unsupported layer shape.", op);
+  const int esz = dtype == NVFP4_F32 ? 4 : 2;
+  if (!aligned16(x) || !aligned16(y))
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] x and y must be 16-byte aligned.", op);
+  const StackLayout S = stack_layout(L0, esz);
+  if (!workspace || workspace_bytes < S.total)
+    return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, S.total);
+  const int kk = (int)(k + (Is > 0 ? 1 : 0));
+  if (nvfp4::decode_stack_smem_bytes((int)H, (int)I, kk) > 227 * 1024)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layer too large for the on-chip rings.", op);
+  nvfp4::StackArgs A{};
+  A.L = (int)n_layers;
+  A.H = (int)H;
+  A.I = (int)I;
+  A.E = (int)E;
+  A.k = (int)k;
+  A.kk = kk;
+  A.dtype = dtype;
+  A.gw_stride = I * (H / 2);
+  A.gs_stride = I * (H / 16);
+  A.dw_stride = H * (I / 2);
+  A.ds_stride = H * (I / 16);
+  A.x0 = x;
+  A.y = y;
+  char* ws = static_cast<char*>(workspace);
+  A.act = reinterpret_cast<float*>(ws + S.act_off);
+  A.xb[0] = ws + S.xb0_off;
+  A.xb[1] = ws + S.xb1_off;
+  A.bar = reinterpret_cast<unsigned*>(ws + S.bar_off);
+  A.xmax = A.bar + 2;
+  A.amax = A.xmax + nvfp4::kStackMaxLayers;
+  for (int64_t l = 0; l < n_layers; l++) {
+    const moe_layer_desc* Ll = &layers[l];
+    const nvfp4_bank* banks[6] = {&Ll->gate, &Ll->up, &Ll->down,
+                                  &Ll->shared_gate, &Ll->shared_up, &Ll->shared_down};
+    for (int b = 0; b < (Is > 0 ? 6 : 3); b++)
+      if (!banks[b]->w || !banks[b]->scales || !aligned16(banks[b]->w) ||
+          !aligned16(banks[b]->scales))
+        return fail(NVFP4_ERR_UNSUPPORTED, "[%s] banks must be 16-byte aligned.", op);
+    if (!inds[l] || !weights[l])
+      return fail(NVFP4_ERR_INVALID, "[%s] null routing for layer %lld.", op, (long long)l);
+    nvfp4::StackLayer& d = A.layer[l];
+    d.gw = reinterpret_cast<const uint8_t*>(Ll->gate.w);
+    d.gs = Ll->gate.scales;
+    d.uw = reinterpret_cast<const uint8_t*>(Ll->up.w);
+    d.us = Ll->up.scales;
+    d.dw = reinterpret_cast<const uint8_t*>(Ll->down.w);
+    d.ds = Ll->down.scales;
+    if (Is > 0) {
+      d.sgw = reinterpret_cast<const uint8_t*>(Ll->shared_gate.w);
+      d.sgs = Ll->shared_gate.scales;
+      d.suw = reinterpret_cast<const uint8_t*>(Ll->shared_up.w);
+      d.sus = Ll->shared_up.scales;
+      d.sdw = reinterpret_cast<const uint8_t*>(Ll->shared_down.w);
+      d.sds = Ll->shared_down.scales;
+    }
+    d.inds = inds[l];
+    d.wts = weights[l];
+    d.scaling = Ll->routed_scaling;
+  }
+  return check_cuda(nvfp4::launch_decode_stack(A, (cudaStream_t)stream), op);
+}

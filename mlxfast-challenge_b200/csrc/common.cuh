@@ -39,7 +39,7 @@ __device__ __forceinline__ void store_from_f32(void* p, int dtype, int64_t i, fl
 // E2M1 pairs -> f16x2.  One hardware conversion per byte: the low nibble
 // lands in the low half.  Four bytes of a 32-bit word give four f16x2.
 __device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t w, uint32_t (&h)[4]) {
-  asm volatile(
+  asm(
       "{\n"
       ".reg .b8 b0, b1, b2, b3;\n"
       "mov.b32 {b0, b1, b2, b3}, %4;\n"
@@ -91,7 +91,7 @@ __device__ __forceinline__ uint32_t bcast_hi(uint32_t v) { return __byte_perm(v,
 __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
                                               uint32_t a2, uint32_t a3, uint32_t b0,
                                               uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -101,7 +101,7 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
                                                uint32_t a2, uint32_t a3, uint32_t b0,
                                                uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
       "{%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

@@ -117,6 +117,32 @@ struct RowsArgs {
   float* scale;
 };
 
+// Serial decode through a stack of sparse MoE layers in one persistent
+// cooperative launch (decode_stack.cu).  T = 1, routing given per layer.
+constexpr int kStackMaxLayers = 64;
+struct StackLayer {
+  const uint8_t *gw, *gs, *uw, *us, *dw, *ds;        // routed banks
+  const uint8_t *sgw, *sgs, *suw, *sus, *sdw, *sds;  // shared expert (null: none)
+  const uint32_t* inds;                              // [k] device
+  const float* wts;                                  // [k] device
+  float scaling;
+};
+struct StackArgs {
+  int L, H, I, E, k, kk, dtype;
+  int64_t gw_stride, gs_stride, dw_stride, ds_stride;  // bytes per expert
+  const void* x0;   // [H] input
+  void* y;          // [H] output of the last layer
+  void* xb[2];      // [H] ping-pong activations between layers
+  float* act;       // [kk, I] gate/up output of the current layer
+  unsigned* bar;    // [2] grid-barrier counters, zero at launch
+  unsigned* xmax;   // [L] max |x_l| (float bits), zero at launch
+  unsigned* amax;   // [L] max |act_l * w|, zero at launch
+  StackLayer layer[kStackMaxLayers];
+};
+size_t decode_stack_smem_bytes(int H, int I, int kk);
+cudaError_t launch_decode_stack(const StackArgs& a, cudaStream_t stream);
+cudaError_t read_and_clear_stack_error(int* out);
+
 struct SortArgs {
   const uint32_t* inds;  // [T, k]
   int T, k, E, P, with_shared;

@@ -8,6 +8,11 @@ kernel and the fused down+combine kernel (C ABI moe_gate_up_swiglu /
 moe_down_combine), the output of layer l feeding layer l+1.  A step replays
 the graph, so launch overhead is paid once per step instead of per kernel.
 
+With given routing and uniform layer shapes (the Laguna case) the step is
+instead ONE persistent launch over all layers (C ABI moe_decode_stack_forward),
+which streams the next layers' expert weights while the current layer's
+dependent chain runs; stack=False keeps the per-layer kernels.
+
 MoEDecodeChain(blocks, routing)(x_host) is the end-to-end call: it copies the
 step's input from pinned host memory, replays the graph and copies the result
 back.  Routing is given per layer; with route=True each
@@ -26,7 +31,8 @@ from ._lib import check, lib
 class MoEDecodeChain:
     def __init__(self, blocks: Sequence, routing: Optional[Sequence[Tuple[torch.Tensor,
                                                                            torch.Tensor]]],
-                 T: int = 1, dtype=torch.bfloat16, route: bool = False, device="cuda:0"):
+                 T: int = 1, dtype=torch.bfloat16, route: bool = False, device="cuda:0",
+                 stack: bool = True):
         self.blocks = list(blocks)
         self.T = T
         self.dtype = dtype
@@ -57,10 +63,39 @@ class MoEDecodeChain:
         self.out = None
         from . import _dtype_code
         self._dt = _dtype_code(self.x0, "decode")
+        # One persistent launch for the whole stack when the library accepts it.
+        self.stack = False
+        if stack and not route and T == 1 and len(self.blocks) <= 64:
+            from ._lib import MoeLayerDesc
+            n = len(self.blocks)
+            self._descs = (MoeLayerDesc * n)(*[b.desc for b in self.blocks])
+            self._inds = (ctypes.c_void_p * n)(*[r[0].data_ptr() for r in self.routing])
+            self._wts = (ctypes.c_void_p * n)(*[r[1].data_ptr() for r in self.routing])
+            sb = lib().moe_decode_stack_workspace_size(self._descs, n)
+            self._stack_ws = torch.zeros(max(sb, 256), dtype=torch.uint8, device=self.device)
+            self.stack = self._try_stack()
+
+    def _stack_call(self, stream_ptr) -> int:
+        return lib().moe_decode_stack_forward(
+            self.bufs[0].data_ptr(), self.x0.data_ptr(), self._dt, len(self.blocks), self._descs,
+            ctypes.cast(self._inds, ctypes.c_void_p), ctypes.cast(self._wts, ctypes.c_void_p),
+            self._stack_ws.data_ptr(), self._stack_ws.numel(), stream_ptr)
+
+    def _try_stack(self) -> bool:
+        """Whether the library runs this stack as one launch (shape checks only)."""
+        s = torch.cuda.Stream(device=self.device)
+        with torch.cuda.stream(s):
+            st = self._stack_call(ctypes.c_void_p(s.cuda_stream))
+        s.synchronize()
+        return st == 0
 
     # -- one step as raw launches (captured below) --------------------------------
     def _launch_step(self, stream_ptr):
         L = lib()
+        if self.stack:
+            check(self._stack_call(stream_ptr))
+            self.out = self.bufs[0]
+            return
         src = self.x0
         for l, b in enumerate(self.blocks):
             dst = self.bufs[l % 2]
@@ -84,6 +119,8 @@ class MoEDecodeChain:
         self.out = src
 
     def launches_per_step(self) -> int:
+        if self.stack:
+            return 1
         return len(self.blocks) * (3 if self.route else 2)
 
     def capture(self, pdl: bool = True):

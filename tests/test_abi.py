@@ -105,3 +105,20 @@ def test_host_mirror_errors_match_reference_kinds(nv):
         nv.gather_qmm(w, w, w, biases=w, rhs_indices=torch.zeros(1, dtype=torch.int32))
     with pytest.raises(ValueError, match="CUDA device"):
         nv.quantize(w)  # no CPU path
+
+
+def test_decode_stack_rejects_unsupported_shapes(nv):
+    d = (nv.MoeLayerDesc * 2)()
+    for i in range(2):
+        d[i].hidden, d[i].inter, d[i].n_experts, d[i].top_k = 2048, 512, 256, 8
+    d[1].inter = 256  # layers must share one shape
+    L = nv._lib.lib()
+    ptrs = (ctypes.c_void_p * 2)(16, 16)
+    st = L.moe_decode_stack_forward(ctypes.c_void_p(16), ctypes.c_void_p(16), 0, 2, d,
+                                    ctypes.cast(ptrs, ctypes.c_void_p),
+                                    ctypes.cast(ptrs, ctypes.c_void_p), None, 0, None)
+    assert st in (nv._lib.NVFP4_ERR_UNSUPPORTED, nv._lib.NVFP4_ERR_INVALID)
+    st = L.moe_decode_stack_forward(ctypes.c_void_p(16), ctypes.c_void_p(16), 0, 65, d,
+                                    ctypes.cast(ptrs, ctypes.c_void_p),
+                                    ctypes.cast(ptrs, ctypes.c_void_p), None, 0, None)
+    assert st == nv._lib.NVFP4_ERR_UNSUPPORTED
