@@ -237,6 +237,33 @@ NVFP4MOE_API int moe_decode_stack_forward(void* y, const void* x, int dtype, int
                                           const float* const* weights, void* workspace,
                                           size_t workspace_bytes, nvfp4_stream stream);
 
+/* Expert parallelism (no reference counterpart: the reference runs every
+ * expert on one device; its single-device analogue is SwitchGLU's gatherSort /
+ * scatterUnsort, VLM/MLXLMCommon/SwitchLayers.swift:385-428).  Rank r of
+ * `world` owns experts [r * experts_per_rank, (r + 1) * experts_per_rank).
+ *
+ * moe_ep_dispatch -- for every (token, slot) pair p of inds [T, k]:
+ *   pos[p] = its row of send_x, rows grouped by destination rank in rank
+ *   order and, within a rank, in pair order; send_x[pos[p]] = x[p / k];
+ *   send_ids[pos[p]] = the expert's id on its owner; send_counts[r] = rows for
+ *   rank r.  An out-of-range expert gets pos -1 and is reported by
+ *   nvfp4_device_status.  The host then exchanges rows with an all-to-all.
+ *
+ * moe_ep_combine -- after the owners' expert outputs come back in send order:
+ *   y_t = scaling * sum_j w[t][j] * y_pairs[pos[t*k + j]]
+ *         + shared_t + residual_t   (nullable), f32 accumulation in slot order,
+ * the Laguna combine (VLM/MLXLLM/Models/Laguna.swift:204-212).
+ * x / y / y_pairs / shared / residual in `dtype`; rows 16-byte aligned for
+ * dispatch (H * element size a multiple of 16). */
+NVFP4MOE_API int moe_ep_dispatch(void* send_x, int32_t* send_ids, int32_t* pos,
+                                 int32_t* send_counts, const void* x, int dtype,
+                                 const uint32_t* inds, int64_t T, int k, int64_t H,
+                                 int64_t experts_per_rank, int world, nvfp4_stream stream);
+NVFP4MOE_API int moe_ep_combine(void* y, const void* y_pairs, const int32_t* pos,
+                                const float* weights, const void* shared, const void* residual,
+                                int dtype, int64_t T, int k, int64_t H, float scaling,
+                                nvfp4_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

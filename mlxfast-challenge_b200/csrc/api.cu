@@ -196,6 +196,10 @@ int nvfp4_device_status(void) {
   e = nvfp4::read_and_clear_stack_error(&st3);
   if (e != cudaSuccess) return check_cuda(e, "device_status");
   if (st == 0) st = st3;
+  int st4 = 0;
+  e = nvfp4::read_and_clear_ep_error(&st4);
+  if (e != cudaSuccess) return check_cuda(e, "device_status");
+  if (st == 0) st = st4;
   if (st != 0)
     return fail(NVFP4_ERR_DEVICE_INDEX,
                 "[gather_qmm] an expert or batch index was out of range (kernel site %d); "
@@ -891,4 +895,73 @@ extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64
     d.scaling = Ll->routed_scaling;
   }
   return check_cuda(nvfp4::launch_decode_stack(A, (cudaStream_t)stream), op);
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel dispatch / combine.
+extern "C" int moe_ep_dispatch(void* send_x, int32_t* send_ids, int32_t* pos,
+                               int32_t* send_counts, const void* x, int dtype,
+                               const uint32_t* inds, int64_t T, int k, int64_t H,
+                               int64_t experts_per_rank, int world, nvfp4_stream stream) {
+  const char* op = "moe_ep_dispatch";
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID, "[%s] Only real floating types are supported.", op);
+  if (T < 0 || k <= 0 || H <= 0 || experts_per_rank <= 0 || world <= 0)
+    return fail(NVFP4_ERR_INVALID, "[%s] Invalid shape.", op);
+  if (world > 64) return fail(NVFP4_ERR_UNSUPPORTED, "[%s] at most 64 ranks.", op);
+  const int esz = dtype == NVFP4_F32 ? 4 : 2;
+  if ((H * esz) % 16 || !aligned16(x) || !aligned16(send_x))
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] rows must be 16-byte aligned.", op);
+  if (T == 0) {
+    return check_cuda(cudaMemsetAsync(send_counts, 0, world * sizeof(int32_t),
+                                      (cudaStream_t)stream),
+                      op);
+  }
+  if (!send_x || !send_ids || !pos || !send_counts || !x || !inds)
+    return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  nvfp4::EpPlanArgs pa{};
+  pa.inds = inds;
+  pa.T = T;
+  pa.k = k;
+  pa.experts_per_rank = experts_per_rank;
+  pa.world = world;
+  pa.pos = pos;
+  pa.ids = send_ids;
+  pa.counts = send_counts;
+  if (int r = check_cuda(nvfp4::launch_ep_plan(pa, (cudaStream_t)stream), op)) return r;
+  nvfp4::EpPackArgs ka{};
+  ka.x = x;
+  ka.T = T;
+  ka.k = k;
+  ka.H = H;
+  ka.esz = esz;
+  ka.pos = pos;
+  ka.send_x = send_x;
+  return check_cuda(nvfp4::launch_ep_pack(ka, (cudaStream_t)stream), op);
+}
+
+extern "C" int moe_ep_combine(void* y, const void* y_pairs, const int32_t* pos,
+                              const float* weights, const void* shared, const void* residual,
+                              int dtype, int64_t T, int k, int64_t H, float scaling,
+                              nvfp4_stream stream) {
+  const char* op = "moe_ep_combine";
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID, "[%s] Only real floating types are supported.", op);
+  if (T < 0 || k <= 0 || H <= 0) return fail(NVFP4_ERR_INVALID, "[%s] Invalid shape.", op);
+  if (T == 0) return NVFP4_OK;
+  if (!y || !y_pairs || !pos || !weights)
+    return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  nvfp4::EpCombineArgs c{};
+  c.y = y;
+  c.yp = y_pairs;
+  c.pos = pos;
+  c.wts = weights;
+  c.T = T;
+  c.k = k;
+  c.H = H;
+  c.scaling = scaling;
+  c.shared = shared;
+  c.residual = residual;
+  c.dtype = dtype;
+  return check_cuda(nvfp4::launch_ep_combine(c, (cudaStream_t)stream), op);
 }

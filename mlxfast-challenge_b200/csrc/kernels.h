@@ -143,6 +143,44 @@ size_t decode_stack_smem_bytes(int H, int I, int kk);
 cudaError_t launch_decode_stack(const StackArgs& a, cudaStream_t stream);
 cudaError_t read_and_clear_stack_error(int* out);
 
+// Expert-parallel dispatch / combine (ep.cu).
+struct EpPlanArgs {
+  const uint32_t* inds;      // [T, k] global expert ids
+  int64_t T;
+  int k;
+  int64_t experts_per_rank;
+  int world;
+  int32_t* pos;     // [T*k] slot of each pair in the send buffer (-1: none)
+  int32_t* ids;     // [T*k] local expert id per send slot
+  int32_t* counts;  // [world] pairs per destination rank
+};
+struct EpPackArgs {
+  const void* x;    // [T, H]
+  int64_t T;
+  int k;
+  int64_t H;
+  int esz;          // bytes per element
+  const int32_t* pos;
+  void* send_x;     // [T*k, H] in destination order
+};
+struct EpCombineArgs {
+  void* y;            // [T, H]
+  const void* yp;     // [T*k, H] expert outputs in send order
+  const int32_t* pos;
+  const float* wts;   // [T, k]
+  int64_t T;
+  int k;
+  int64_t H;
+  float scaling;
+  const void* shared;    // [T, H] or null
+  const void* residual;  // [T, H] or null
+  int dtype;
+};
+cudaError_t launch_ep_plan(const EpPlanArgs& a, cudaStream_t stream);
+cudaError_t launch_ep_pack(const EpPackArgs& a, cudaStream_t stream);
+cudaError_t launch_ep_combine(const EpCombineArgs& a, cudaStream_t stream);
+cudaError_t read_and_clear_ep_error(int* out);
+
 struct SortArgs {
   const uint32_t* inds;  // [T, k]
   int T, k, E, P, with_shared;

@@ -1,0 +1,161 @@
+"""Expert parallelism for the Laguna sparse MoE block over torch.distributed.
+
+The 256 routed experts are split over the N ranks of a process group (one
+process per GPU): rank r holds experts [r*E/N, (r+1)*E/N), every rank holds
+the router and the shared expert.  Each rank runs the block for its own tokens:
+
+1. route its tokens (BF16 router top-k, moe_router_topk);
+2. build the send buffer: every (token, slot) pair's activation row grouped by
+   the rank that owns the pair's expert (moe_ep_dispatch);
+3. exchange the per-rank row counts, then the rows and their local expert ids
+   (all-to-all; NCCL over NVLink on the GPUs);
+4. run its local experts over the rows it received, one expert per row, with
+   the grouped NVFP4 GEMM path (moe_block_forward, top-1, weight 1);
+5. send the expert outputs back (all-to-all, the reverse splits);
+6. combine in the Laguna order: y = 2.5 * sum_j w_j e_j(x) + shared(x)
+   (+ residual) (moe_ep_combine).
+
+Reference semantics: the single-device block (VLM/MLXLLM/Models/Laguna.swift:
+183-213, SwitchGLU with sorted indices VLM/MLXLMCommon/SwitchLayers.swift:
+532-580); the exchange has no reference counterpart.  Expert outputs travel as
+the activation dtype (bf16), as the reference's gather_qmm returns them.
+
+The exchange logic (ExpertParallelBlock) only moves tensors; the compute goes
+through an ops object.  CudaEPOps is the product (C ABI kernels on the GPU, no
+CPU fallback); tests may drive the same exchange with CPU ops on gloo ranks.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ._lib import check, lib
+
+
+def exchange(send: torch.Tensor, send_counts, recv_counts, group=None) -> torch.Tensor:
+    """Rows of `send` (grouped by destination rank, send_counts[r] rows for
+    rank r) to their ranks; returns the rows received, grouped by source rank."""
+    shape = (int(sum(recv_counts)),) + tuple(send.shape[1:])
+    recv = torch.empty(shape, dtype=send.dtype, device=send.device)
+    dist.all_to_all_single(recv, send, output_split_sizes=[int(c) for c in recv_counts],
+                           input_split_sizes=[int(c) for c in send_counts], group=group)
+    return recv
+
+
+def exchange_counts(send_counts: torch.Tensor, group=None) -> torch.Tensor:
+    recv = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv, send_counts, group=group)
+    return recv
+
+
+class ExpertParallelBlock:
+    """One sparse block, expert-parallel over `group` (see the module doc)."""
+
+    def __init__(self, ops, group=None):
+        self.ops = ops
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                 routing: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+        ops = self.ops
+        inds, wts = routing if routing is not None else ops.route(x)
+        send_x, send_ids, pos, send_counts = ops.dispatch(x, inds, self.world)
+        # Counts travel as int64 on the exchange's device; the row splits are
+        # host integers (one small device-to-host copy per layer).
+        sc = send_counts.to(torch.int64)
+        rc = exchange_counts(sc, self.group)
+        sc_h, rc_h = sc.tolist(), rc.tolist()
+        recv_x = exchange(send_x, sc_h, rc_h, self.group)
+        recv_ids = exchange(send_ids, sc_h, rc_h, self.group)
+        y_recv = ops.experts(recv_x, recv_ids)
+        y_back = exchange(y_recv, rc_h, sc_h, self.group)
+        shared = ops.shared(x)
+        return ops.combine(y_back, pos, wts, shared, residual)
+
+
+class CudaEPOps:
+    """The device side of one rank: router, dispatch / combine kernels, local
+    experts through moe_block_forward (C ABI).  `routed` holds this rank's
+    expert slice (gate_w [E/N, I, H/8], ...), `shared` the shared expert."""
+
+    def __init__(self, routed: dict, shared: Optional[dict], router_w: torch.Tensor,
+                 router_b: Optional[torch.Tensor], n_experts: int, rank: int, world: int,
+                 top_k: int = 8, routed_scaling: float = 2.5, norm_topk_prob: bool = True):
+        from . import SparseMoeBlock
+        self.E, self.rank, self.world = n_experts, rank, world
+        self.epr = n_experts // world
+        self.top_k, self.scaling, self.norm = top_k, float(routed_scaling), bool(norm_topk_prob)
+        # Local experts as a top-1 block: scaling and weights are applied by the
+        # source rank's combine.
+        self.local = SparseMoeBlock(routed, None, None, None, top_k=1, routed_scaling=1.0,
+                                    norm_topk_prob=False)
+        self.shared_block = None
+        if shared is not None:
+            one = {k: v.unsqueeze(0) for k, v in shared.items()}
+            self.shared_block = SparseMoeBlock(one, None, None, None, top_k=1,
+                                               routed_scaling=1.0, norm_topk_prob=False)
+        self.router_w = router_w.contiguous()
+        self.router_b = None if router_b is None else router_b.to(torch.float32).contiguous()
+        self.H = self.local.H
+
+    def _stream(self, t):
+        return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+    def route(self, x):
+        from . import moe_router_topk
+        return moe_router_topk(x, self.router_w, self.router_b, self.top_k, self.norm)
+
+    def dispatch(self, x, inds, world):
+        from . import _dtype_code
+        T, k = inds.shape
+        P = T * k
+        send_x = torch.empty(P, self.H, dtype=x.dtype, device=x.device)
+        send_ids = torch.empty(P, dtype=torch.int32, device=x.device)
+        pos = torch.empty(P, dtype=torch.int32, device=x.device)
+        counts = torch.empty(world, dtype=torch.int32, device=x.device)
+        xi = (inds if inds.dtype == torch.uint32 else inds.to(torch.int32).view(torch.uint32))
+        xi = xi.contiguous()
+        check(lib().moe_ep_dispatch(send_x.data_ptr(), send_ids.data_ptr(), pos.data_ptr(),
+                                    counts.data_ptr(), x.contiguous().data_ptr(),
+                                    _dtype_code(x, "moe_ep_dispatch"), xi.data_ptr(), T, k, self.H,
+                                    self.epr, world, self._stream(x)))
+        return send_x, send_ids, pos, counts
+
+    def experts(self, rows, ids):
+        if rows.shape[0] == 0:
+            return torch.empty_like(rows)
+        w = torch.ones(rows.shape[0], 1, dtype=torch.float32, device=rows.device)
+        return self.local(rows, inds=ids.view(-1, 1), weights=w)
+
+    def shared(self, x):
+        if self.shared_block is None:
+            return None
+        T = x.shape[0]
+        z = torch.zeros(T, 1, dtype=torch.int32, device=x.device)
+        w = torch.ones(T, 1, dtype=torch.float32, device=x.device)
+        return self.shared_block(x, inds=z, weights=w)
+
+    def combine(self, y_pairs, pos, wts, shared, residual):
+        from . import _dtype_code
+        T, k = wts.shape
+        y = torch.empty(T, self.H, dtype=y_pairs.dtype, device=y_pairs.device)
+        res = None if residual is None else residual.to(y.dtype).contiguous()
+        check(lib().moe_ep_combine(y.data_ptr(), y_pairs.data_ptr(), pos.data_ptr(),
+                                   wts.to(torch.float32).contiguous().data_ptr(),
+                                   None if shared is None else shared.data_ptr(),
+                                   None if res is None else res.data_ptr(),
+                                   _dtype_code(y, "moe_ep_combine"), T, k, self.H, self.scaling,
+                                   self._stream(y)))
+        return y
+
+
+def local_slice(raw_routed: dict, rank: int, world: int) -> dict:
+    """This rank's expert slice of full routed banks (views, no copy)."""
+    E = next(iter(raw_routed.values())).shape[0]
+    epr = E // world
+    return {k: v[rank * epr:(rank + 1) * epr] for k, v in raw_routed.items()}
