@@ -36,6 +36,11 @@ dense   = BASELINE config[0]: quantized_matmul x[M, 2048] @ W[4096, 2048]^T,
           M = 512 (tensor-core GEMM, TFLOP/s) and M = 1 (GEMV, GB/s), cycling 32
           weight copies (150 MB > L2).
 
+prefill_ep (N > 1 only) = config[3] expert-parallel: each GPU holds 256/N
+          experts (+ router and shared expert) and its own 512 tokens; pair
+          rows go to their experts' GPU and back by NCCL all-to-all; total
+          tok/s over all GPUs, device time max over ranks.
+
 --workload prefill|dense prints only that measurement (used by the committed
 ncu profiling commands).
 
@@ -124,6 +129,56 @@ def bench_prefill(torch, nv, lag, cfg, dev, steps, warmup, layers, distinct=4, T
             "hbm_gbs_equiv": layer_b / (us_layer / 1e6) / 1e9,
             "bytes_per_layer": layer_b, "steps": steps, "layers_per_step": layers,
             "unit": "tok/s"}
+
+
+def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers, distinct=2,
+                     T=512):
+    """config[3] expert-parallel: every rank holds E/world experts, the router
+    and the shared expert, and runs the sparse block for its own T tokens; the
+    (token, slot) rows cross to their experts' ranks and back by NCCL
+    all-to-all.  Weak scaling: T tokens per rank.  Device time per step, max
+    over ranks."""
+    ep = importlib.import_module("mlxfast-challenge_b200.ep")
+    blocks = []
+    for l in range(distinct):
+        _, raw = lag.random_sparse_layer(nv, seed=3000 + l, device=dev)
+        # this rank's expert slice as its own tensors, so the other experts
+        # are freed (256/world experts resident per GPU)
+        local = {k: v.clone() for k, v in ep.local_slice(raw["routed"], rank, world).items()}
+        ops = ep.CudaEPOps(local, raw["shared"], raw["router_w"], raw["router_b"],
+                           cfg.n_experts, rank, world)
+        del raw
+        torch.cuda.empty_cache()
+        blocks.append(ep.ExpertParallelBlock(ops))
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    x = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+    res = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+
+    def step():
+        for l in range(layers):
+            blocks[l % distinct](x, residual=res)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item())
+    return {"workload": f"BASELINE config[3] expert-parallel over {world} GPUs: sparse block "
+                        f"T={T} tokens per GPU (router top-8, {cfg.n_experts // world} experts "
+                        f"per GPU, shared expert, residual), {layers} layers per step, NCCL "
+                        f"all-to-all dispatch/combine", "n_gpus": world,
+            "tok_per_s": world * T / (ms_step / 1e3), "us_per_layer": ms_step * 1e3 / layers,
+            "scaling": "weak", "unit": "tok/s", "steps": steps}
 
 
 def bench_dense(torch, nv, dev, reps=50, copies=32):
@@ -447,7 +502,11 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu, _, _ = cpu_reference_gbs(args.cpu_seconds, os.cpu_count() or 1, cfg)
-    prefill = dense = None
+    prefill = dense = prefill_ep = None
+    if world > 1 and args.workload == "all":
+        # every rank takes part (the exchange is collective)
+        prefill_ep = bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world,
+                                      args.prefill_steps, cfg.num_sparse_layers)
     if rank == 0 and world == 1 and args.workload == "all":
         del chain
         torch.cuda.empty_cache()
@@ -476,6 +535,7 @@ def main():
                     "d2h_bytes_per_step": cfg.hidden * 2,
                     "api": "MoEDecodeChain.__call__ (pinned host x -> device -> host y)"},
             "prefill": prefill,
+            "prefill_ep": prefill_ep,
             "dense": dense,
         }
         print(json.dumps(line), flush=True)
