@@ -182,7 +182,9 @@ def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers,
 
 
 def bench_dense(torch, nv, dev, reps=50, copies=32):
-    """config[0]: quantized_matmul [M, 2048] x [4096, 2048]^T for M = 512 and M = 1."""
+    """config[0]: quantized_matmul [M, 2048] x [4096, 2048]^T for M = 512 and M = 1,
+    and the same shapes through qqmm (activations fake-quantised to NVFP4, the
+    block-scaled tcgen05 kind::mxf4nvf4 path; a separately reported variant)."""
     N, K = 4096, 2048
     g = torch.Generator(device=dev).manual_seed(5)
     w = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
@@ -190,23 +192,26 @@ def bench_dense(torch, nv, dev, reps=50, copies=32):
     wqs = [wq.clone() for _ in range(copies)]
     sqs = [sq.clone() for _ in range(copies)]
     out = {}
-    for M in (512, 1):
-        x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
-        for i in range(3):
-            nv.quantized_matmul(x, wqs[i], sqs[i])
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(reps):
-            nv.quantized_matmul(x, wqs[i % copies], sqs[i % copies])
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / reps
-        wbytes = N * K // 2 + N * K // 16
-        out[f"M{M}"] = {"us": us, "tflops": 2 * M * N * K / (us / 1e6) / 1e12,
-                        "hbm_gbs": (wbytes + M * K * 2 + M * N * 2) / (us / 1e6) / 1e9}
+    for name, op in (("", nv.quantized_matmul), ("qqmm_", nv.qqmm)):
+        for M in (512, 1):
+            x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+            for i in range(3):
+                op(x, wqs[i], sqs[i])
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(reps):
+                op(x, wqs[i % copies], sqs[i % copies])
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            wbytes = N * K // 2 + N * K // 16
+            out[f"{name}M{M}"] = {"us": us, "tflops": 2 * M * N * K / (us / 1e6) / 1e12,
+                                  "hbm_gbs": (wbytes + M * K * 2 + M * N * 2) / (us / 1e6) / 1e9}
     out["workload"] = ("BASELINE config[0]: x bf16 [M, 2048] @ nvfp4 W[4096, 2048]^T, "
-                       f"{copies} weight copies cycled (> L2)")
+                       f"{copies} weight copies cycled (> L2); qqmm_* = the same through "
+                       "qqmm (x fake-quantised to NVFP4 in the timed call, tcgen05 "
+                       "kind::mxf4nvf4)")
     return out
 
 

@@ -97,6 +97,32 @@ NVFP4MOE_API int nvfp4_dequantize(void* out, int out_dtype, const uint32_t* w,
 NVFP4MOE_API int nvfp4_quantize(uint32_t* wq, uint8_t* scales, const void* w, int w_dtype,
                                 int64_t rows, int64_t K, nvfp4_stream stream);
 
+/* The activation half of MLX's fp_quantize_dequantize
+ * (backend/cpu/quantized.cpp:1093-1129, bits 4, group 16), which QQMatmul
+ * applies to x before its matmul: per row group of 16, scale =
+ * ToFP8(max|x| / 6), code = to_fp4_e2m1(x / FromFP8(scale)) (:1064-1091).
+ * x[M, K] (bf16/f16/f32, 16-byte aligned) -> xq[M, K/8] uint32 (low nibble
+ * first) + scales[M, K/16]; dequantising them gives MLX's xhat bit for bit.
+ * (A group whose max is NaN gets scale byte ToFP8(-inf) = 0xFE in MLX; it is
+ * written as 0x7E with every code's sign flipped, the same xhat.) */
+NVFP4MOE_API int nvfp4_quantize_activations(uint32_t* xq, uint8_t* scales, const void* x,
+                                            int dtype, int64_t M, int64_t K,
+                                            nvfp4_stream stream);
+
+/* mlx_qqmm (mlx-c ops.h:790-800; ops.cpp:4691-4757), mode "nvfp4", w
+ * quantized, no global scales; QQMatmul::eval_cpu (quantized.cpp:1322-1360):
+ * y[M, N] = xhat[M, K] @ dequant(w)[N, K]^T with xhat the fake-quantised x
+ * above; y has x's dtype.  Runs on the block-scaled tensor cores
+ * (tcgen05.mma kind::mxf4nvf4, UE4M3 scales per 16): products are exact, the
+ * sum is f32.  The reference's CPU path accepts only M == 1 ("NYI for the
+ * general case"); any M is accepted here, as MLX's CUDA qqmm does.
+ * K % 256 == 0; x, w and scales 16-byte aligned.  Workspace:
+ * nvfp4_qqmm_workspace_size(M, N, K) bytes, 256-byte aligned. */
+NVFP4MOE_API size_t nvfp4_qqmm_workspace_size(int64_t M, int64_t N, int64_t K);
+NVFP4MOE_API int nvfp4_qqmm(void* y, const void* x, int dtype, const uint32_t* w,
+                            const uint8_t* scales, int64_t M, int64_t N, int64_t K,
+                            void* workspace, size_t workspace_bytes, nvfp4_stream stream);
+
 /* mlx_quantized_matmul (mlx-c ops.h:809-818; ops.cpp:4549-4600;
  * QuantizedMatmul::eval_cpu backend/cpu/quantized.cpp:924-964), transpose:
  * y[M, N] = x[M, K] @ dequant(w)[N, K]^T. */

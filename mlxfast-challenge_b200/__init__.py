@@ -34,7 +34,8 @@ from . import _lib
 from ._lib import DeviceIndexError, MoeLayerDesc, NvFp4Bank, check, lib
 
 __all__ = [
-    "quantize", "dequantize", "quantized_matmul", "gather_qmm", "moe_router_topk",
+    "quantize", "dequantize", "quantized_matmul", "gather_qmm", "moe_router_topk", "qqmm",
+    "quantize_activations",
     "SparseMoeBlock", "MoEDecodeChain", "device_status", "launch_flags", "DeviceIndexError", "library_path",
 ]
 
@@ -175,6 +176,52 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
                                        _ptr(w.contiguous()), _ptr(scales.contiguous()), M, N, K,
                                        _stream(x.device)))
     return y
+
+
+def quantize_activations(x: torch.Tensor):
+    """The activation quantisation QQMatmul applies to x (fp_quantize_dequantize,
+    backend/cpu/quantized.cpp:1093-1129): x [..., K] -> (codes uint32 [..., K/8],
+    scales uint8 [..., K/16]); dequantize() of them is MLX's xhat bit for bit."""
+    _require_cuda("qqmm", x)
+    K = x.shape[-1]
+    if K % 16:
+        raise ValueError("[qqmm] The last dimension of the matrix needs to be divisible by the "
+                         f"quantization group size 16. However the provided matrix has K={K}.")
+    xc = x.contiguous()
+    M = xc.numel() // K if K else 0
+    xq = torch.empty(x.shape[:-1] + (K // 8,), dtype=torch.uint32, device=x.device)
+    sc = torch.empty(x.shape[:-1] + (K // 16,), dtype=torch.uint8, device=x.device)
+    check(lib().nvfp4_quantize_activations(_ptr(xq), _ptr(sc), _ptr(xc), _dtype_code(x, "qqmm"),
+                                           M, K, _stream(x.device)))
+    return xq, sc
+
+
+def qqmm(x: torch.Tensor, w: torch.Tensor, scales: Optional[torch.Tensor] = None,
+         group_size: int = 16, bits: int = 4, mode: str = "nvfp4", global_scale_x=None,
+         global_scale_w=None) -> torch.Tensor:
+    """mlx.core.qqmm (ops.cpp:4691-4757) for mode "nvfp4" with quantized w:
+    y = fake_quant(x) @ dequant(w)^T in x.dtype, on the block-scaled tensor
+    cores.  x is 1-D or 2-D (qqmm's own rule); w [N, K/8] uint32."""
+    _check_mode("qqmm", group_size, bits, mode)
+    if global_scale_x is not None or global_scale_w is not None:
+        raise ValueError("[qqmm] global scales are not supported by this build.")
+    if scales is None:
+        raise ValueError("[qqmm] Scales must be provided if second argument is quantized.")
+    _require_cuda("qqmm", x, w, scales)
+    if x.dim() > 2 or w.dim() > 2:
+        raise ValueError(f"[qqmm] Only 2D inputs are supported but x.ndim() == {x.dim()} and "
+                         f"w.ndim() == {w.dim()}.")
+    x2 = x.unsqueeze(0) if x.dim() == 1 else x
+    w, K, N = _qdims("qqmm", x2, w, scales)
+    xc = x2.contiguous()
+    M = xc.shape[0]
+    y = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    ws_bytes = lib().nvfp4_qqmm_workspace_size(M, N, K)
+    ws = torch.empty(max(int(ws_bytes), 256), dtype=torch.uint8, device=x.device)
+    check(lib().nvfp4_qqmm(_ptr(y), _ptr(xc), _dtype_code(x, "qqmm"), _ptr(w.contiguous()),
+                           _ptr(scales.contiguous()), M, N, K, _ptr(ws), ws.numel(),
+                           _stream(x.device)))
+    return y.squeeze(0) if x.dim() == 1 else y
 
 
 def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases=None,

@@ -52,6 +52,9 @@ SIGNATURES = {
     "nvfp4_dequantize": (_I, [_P, _I, _P, _P, _I64, _I64, _P]),
     "nvfp4_quantize": (_I, [_P, _P, _P, _I, _I64, _I64, _P]),
     "nvfp4_quantized_matmul": (_I, [_P, _P, _I, _P, _P, _I64, _I64, _I64, _P]),
+    "nvfp4_quantize_activations": (_I, [_P, _P, _P, _I, _I64, _I64, _P]),
+    "nvfp4_qqmm_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64]),
+    "nvfp4_qqmm": (_I, [_P, _P, _I, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     "nvfp4_gather_qmm": (_I, [_P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                               _I, _P]),
     "moe_router_workspace_size": (_SZ, [_I64, _I64, _I64]),

@@ -200,6 +200,10 @@ int nvfp4_device_status(void) {
   e = nvfp4::read_and_clear_ep_error(&st4);
   if (e != cudaSuccess) return check_cuda(e, "device_status");
   if (st == 0) st = st4;
+  int st5 = 0;
+  e = nvfp4::read_and_clear_qqmm_error(&st5);
+  if (e != cudaSuccess) return check_cuda(e, "device_status");
+  if (st == 0) st = st5;
   if (st != 0)
     return fail(NVFP4_ERR_DEVICE_INDEX,
                 "[gather_qmm] an expert or batch index was out of range (kernel site %d); "
@@ -275,6 +279,100 @@ int nvfp4_gather_qmm(void* out, const void* x, int dtype, const uint32_t* w,
     return fail(NVFP4_ERR_UNSUPPORTED, "[gather_qmm] too many pairs.");
   return check_cuda(nvfp4::launch_qmm_gather(a, (cudaStream_t)stream, first_pdl()),
                     "gather_qmm");
+}
+
+int nvfp4_quantize_activations(uint32_t* xq, uint8_t* scales, const void* x, int dtype,
+                               int64_t M, int64_t K, nvfp4_stream stream) {
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID,
+                "[qqmm] Only real floating types except float64 are supported.");
+  if (int r = check_qdims("qqmm", M, K)) return r;
+  if (M == 0) return NVFP4_OK;
+  if (!xq || !scales || !x) return fail(NVFP4_ERR_INVALID, "[qqmm] null pointer argument.");
+  if (!aligned16(x) || (reinterpret_cast<uintptr_t>(xq) & 7) != 0)
+    return fail(NVFP4_ERR_INVALID, "[qqmm] x must be 16-byte and xq 8-byte aligned.");
+  return check_cuda(nvfp4::launch_qx_quantize(reinterpret_cast<uint8_t*>(xq), scales, x, dtype,
+                                              M, K, (cudaStream_t)stream),
+                    "qqmm");
+}
+
+struct QqmmLayout {
+  size_t qx_off, sx_off, part_off, ticket_off, total;
+  int bn, n_tiles, m_tiles, splits;
+};
+
+static int device_sm_count() {
+  int dev = 0, v = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+    return 148;
+  return v;
+}
+
+static QqmmLayout qqmm_layout(int64_t M, int64_t N, int64_t K) {
+  QqmmLayout L{};
+  nvfp4::qqmm_plan(M, N, K, device_sm_count(), &L.bn, &L.n_tiles, &L.m_tiles, &L.splits);
+  L.qx_off = 0;
+  L.sx_off = align_up((size_t)M * (size_t)(K / 2), 256);
+  L.part_off = align_up(L.sx_off + (size_t)M * (size_t)(K / 16), 256);
+  const size_t tiles = (size_t)L.n_tiles * L.m_tiles;
+  const size_t part = L.splits > 1 ? tiles * L.splits * (size_t)L.bn * 128 * sizeof(float) : 0;
+  L.ticket_off = align_up(L.part_off + part, 256);
+  L.total = align_up(L.ticket_off + tiles * sizeof(unsigned), 256);
+  return L;
+}
+
+size_t nvfp4_qqmm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % 256 != 0) return 0;
+  return qqmm_layout(M, N, K).total;
+}
+
+int nvfp4_qqmm(void* y, const void* x, int dtype, const uint32_t* w, const uint8_t* scales,
+               int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
+               nvfp4_stream stream) {
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID,
+                "[qqmm] Only real floating types except float64 are supported but first "
+                "argument dtype is not.");
+  if (int r = check_qdims("qqmm", N, K)) return r;
+  if (M < 0) return fail(NVFP4_ERR_INVALID, "[qqmm] Invalid M.");
+  if (M == 0 || N == 0) return NVFP4_OK;
+  if (K % 256 != 0)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[qqmm] K=%lld: the tensor-core path needs K %% 256 == 0.",
+                (long long)K);
+  if (M >= (1ll << 31) || N >= (1ll << 31))
+    return fail(NVFP4_ERR_UNSUPPORTED, "[qqmm] M and N must be below 2^31.");
+  if (!y || !x || !w || !scales) return fail(NVFP4_ERR_INVALID, "[qqmm] null pointer argument.");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(scales))
+    return fail(NVFP4_ERR_INVALID, "[qqmm] x, w and scales must be 16-byte aligned.");
+  const QqmmLayout L = qqmm_layout(M, N, K);
+  if (!workspace || workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(NVFP4_ERR_WORKSPACE, "[qqmm] workspace needs %zu bytes, 256-byte aligned.",
+                L.total);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint8_t* qx = ws + L.qx_off;
+  uint8_t* sx = ws + L.sx_off;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = nvfp4::launch_qx_quantize(qx, sx, x, dtype, M, K, st);
+  if (e != cudaSuccess) return check_cuda(e, "qqmm");
+  nvfp4::QqmmArgs a{};
+  if (nvfp4::map_codes(&a.ma, w, N, K, 128) != cudaSuccess ||
+      nvfp4::map_scales(&a.msa, scales, N, K, 128) != cudaSuccess ||
+      nvfp4::map_codes(&a.mb, qx, M, K, L.bn) != cudaSuccess ||
+      nvfp4::map_scales(&a.msb, sx, M, K, L.bn) != cudaSuccess)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[qqmm] tensor map encoding failed.");
+  a.out = y;
+  a.dtype = dtype;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.bn = L.bn;
+  a.n_tiles = L.n_tiles;
+  a.m_tiles = L.m_tiles;
+  a.splits = L.splits;
+  a.partial = reinterpret_cast<float*>(ws + L.part_off);
+  a.ticket = reinterpret_cast<unsigned*>(ws + L.ticket_off);
+  return check_cuda(nvfp4::launch_qqmm(a, st), "qqmm");
 }
 
 int nvfp4_quantized_matmul(void* y, const void* x, int dtype, const uint32_t* w,

@@ -77,6 +77,27 @@ __device__ __forceinline__ float scale_to_f32(uint32_t b) {
   return (b & 0x80u) ? -v : v;
 }
 
+// f32 -> E4M3 byte as MLX's ToFP8 rounds it (backend/cpu/unary_ops.h:120-151):
+// round-to-nearest-even on the bit pattern, subnormals through a float add,
+// saturation at 0x7E, the sign copied.
+__device__ __forceinline__ uint32_t e4m3_encode(float f) {
+  uint32_t bits = __float_as_uint(f);
+  const uint32_t sign = bits & 0x80000000u;
+  bits ^= sign;
+  uint32_t r;
+  if (bits >= (543u << 21)) {
+    r = 0x7Eu;
+  } else if (bits < (121u << 23)) {
+    const uint32_t magic = 141u << 23;
+    r = (__float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(magic))) - magic) &
+        0xFFu;
+  } else {
+    const uint32_t odd = (bits >> 20) & 1u;
+    r = ((bits + ((uint32_t)(7 - 127) << 23) + 0x7FFFFu + odd) >> 20) & 0xFFu;
+  }
+  return r | (sign >> 24);
+}
+
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);

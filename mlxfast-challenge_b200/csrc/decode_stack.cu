@@ -117,6 +117,7 @@ struct StackSmem {
   int* colmax;
   volatile int* abort;     // consumers -> producer: stop
   volatile int* bar_ok;    // grid-barrier outcome, thread 0 -> consumers
+  volatile int* hold;      // consumers in a grid barrier: producer holds refills
   uint32_t* inds;          // [L][k] routing of every layer, staged at start
   float* wts;              // [L][k]
 };
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
   S.emptyD = S.fullD + kDSlots;
   S.abort = reinterpret_cast<volatile int*>(S.emptyD + kDSlots);
   S.bar_ok = S.abort + 1;
+  S.hold = S.abort + 2;
   unsigned char* p = smem + 512;
   S.slotsG = p;
   p += (size_t)kGSlots * slotG;
@@ -191,6 +193,7 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
       mbar_init(&S.emptyD[i], 4);  // the 4 warps of the segment's group
     }
     *S.abort = 0;
+    *S.hold = 0;
     fence_barrier_init();
   }
   // Every layer's routing into shared memory once: a global load costs ~1 us
@@ -209,6 +212,19 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
     // gate/up units of layer 0, its down units, gate/up units of layer 1, ...
     uint32_t jg = 0, jd = 0;
     bool ok = true;
+    // While this CTA's consumers wait in a grid barrier, the barrier's atomics
+    // and polls are the critical path; a refill burst issued at that moment
+    // (the slots the finished phase released) queues ahead of them in the
+    // memory system.  The refills are for units needed a layer later, so they
+    // wait until the barrier has passed (bounded: a missed release only costs
+    // time).
+    auto hold_refills = [&]() {
+      if (lane == 0) {
+        const long long h0 = clock64();
+        while (*S.hold && !*S.abort && clock64() - h0 < 400000) __nanosleep(64);
+      }
+      __syncwarp();
+    };
     for (int l = 0; l < a.L && ok; l++) {
       const StackLayer& ly = a.layer[l];
       for (int u = blockIdx.x; u < nG && ok; u += G) {
@@ -237,6 +253,7 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
           uw = ly.suw;
           us = ly.sus;
         }
+        hold_refills();
         uint8_t* dst = S.slotsG + (size_t)s * slotG;
         // rows 0..7 gate rows i0.., rows 8..15 the same up rows; then scales
         if (lane == 0) {
@@ -267,6 +284,7 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
             wb = ly.sdw;
             sb = ly.sds;
           }
+          hold_refills();
           uint8_t* dst = S.slotsD + (size_t)s * slotD;
           if (lane == 0) {
             const int64_t row0 = (int64_t)dt * 16;
@@ -304,6 +322,7 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
   // One grid barrier: every consumer thread's global writes, then this CTA's
   // arrival; thread 0 waits (bounded) for all G CTAs.  Returns false on expiry.
   auto grid_barrier = [&](unsigned* ctr) -> bool {
+    if (threadIdx.x == 0) *S.hold = 1;
     named_sync(1, nthr);
     if (threadIdx.x == 0) {
       red_release_add(ctr, 1u);  // orders this CTA's writes (bar.sync above) first
@@ -320,6 +339,7 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
         }
       }
       *S.bar_ok = ok;
+      *S.hold = 0;
       if (!ok) sflag(kErrTimeout);
     }
     named_sync(1, nthr);
@@ -475,34 +495,31 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
 
       const int grp = warp >> 2, wq = warp & 3;  // kDGroups groups of 4 warps
       for (int dt = blockIdx.x; dt < nD && alive; dt += G) {
-        // this group's segments grp, grp+2, ...: wait for all, then chunks
-        // with the segments interleaved over four accumulator sets
-        for (int seg = grp; seg < kk && alive; seg += kDGroups) {
-          const uint32_t q = jd + seg;
-          if (!mbar_wait_bounded(&S.fullD[q % kDSlots], (q / kDSlots) & 1)) {
-            if (lane == 0) sflag(kErrTimeout);
-            alive = false;
-          }
-        }
+        // this group's segments grp, grp + kDGroups, ... one at a time (wait,
+        // compute, release: no ring size can stall it), alternating between
+        // two accumulator sets
         Acc accd[kDAcc];
 #pragma unroll
         for (int i = 0; i < kDAcc; i++) accd[i].zero();
-        if (alive) {
+        int ai = 0;
+        for (int seg = grp; seg < kk; seg += kDGroups, ai ^= 1) {
+          const uint32_t q = jd + seg;
+          const int s = q % kDSlots;
+          if (!mbar_wait_bounded(&S.fullD[s], (q / kDSlots) & 1)) {
+            if (lane == 0) sflag(kErrTimeout);
+            alive = false;
+            break;
+          }
+          const uint8_t* tile = S.slotsD + (size_t)s * slotD;
+          const __half* xcol = g == 0 ? S.xa + (size_t)seg * ldxD : nullptr;
           for (int ch = wq; ch < nchD; ch += 4) {
-            int i = 0;
-            for (int seg = grp; seg < kk; seg += kDGroups, i ^= 1) {
-              const uint8_t* tile = S.slotsD + (size_t)((jd + seg) % kDSlots) * slotD;
-              const __half* xcol = g == 0 ? S.xa + (size_t)seg * ldxD : nullptr;
-              Chunk c;
-              load_chunk_smem(c, tile, rpD, spD, g, ch, t);
-              if (i == 0) compute_chunk(accd[0], c, xcol, ch, t);
-              else compute_chunk(accd[1], c, xcol, ch, t);
-            }
+            Chunk c;
+            load_chunk_smem(c, tile, rpD, spD, g, ch, t);
+            if (ai == 0) compute_chunk(accd[0], c, xcol, ch, t);
+            else compute_chunk(accd[1], c, xcol, ch, t);
           }
           __syncwarp();
-          if (lane == 0)
-            for (int seg = grp; seg < kk; seg += kDGroups)
-              mbar_arrive(&S.emptyD[(jd + seg) % kDSlots]);
+          if (lane == 0) mbar_arrive(&S.emptyD[s]);
         }
         jd += kk;
         alive = named_sync_and(1, nthr, alive);

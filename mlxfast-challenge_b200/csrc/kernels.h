@@ -211,6 +211,26 @@ cudaError_t launch_moe_sort(const SortArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t launch_moe_combine(const CombineArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t read_and_clear_prefill_error(int* out);
 
+// NVFP4 x NVFP4 matmul (qqmm): y[M, N] = xhat[M, K] . dequant(W)[N, K]^T.
+struct alignas(64) QqmmArgs {
+  CUtensorMap ma, msa;  // W codes [N, K/2] (128 x 128 B boxes, 128 B swizzle), W scales
+  CUtensorMap mb, msb;  // x codes [M, K/2] (bn x 128 B boxes), x scales
+  void* out;            // [M, N], dtype
+  int dtype;
+  int64_t M, N, K;
+  int bn, n_tiles, m_tiles, splits;
+  float* partial;   // [tiles][splits][bn][128] when splits > 1
+  unsigned* ticket; // [tiles] when splits > 1
+};
+int qqmm_tile_tokens(int64_t M);
+size_t qqmm_smem_bytes(int bn);
+void qqmm_plan(int64_t M, int64_t N, int64_t K, int sms, int* bn, int* n_tiles, int* m_tiles,
+               int* splits);
+cudaError_t launch_qx_quantize(uint8_t* qx, uint8_t* sx, const void* x, int dtype, int64_t M,
+                               int64_t K, cudaStream_t stream);
+cudaError_t launch_qqmm(const QqmmArgs& a, cudaStream_t stream);
+cudaError_t read_and_clear_qqmm_error(int* out);
+
 size_t qmm_smem_bytes(int64_t K);
 bool qmm_fast_path_ok(const QmmArgs& a);
 cudaError_t launch_qmm_gather(const QmmArgs& a, cudaStream_t stream, bool pdl);

@@ -26,24 +26,6 @@ __device__ __forceinline__ float round_to(float v, int dtype) {
   return v;
 }
 
-__device__ __forceinline__ uint32_t e4m3_encode(float f) {
-  uint32_t bits = __float_as_uint(f);
-  const uint32_t sign = bits & 0x80000000u;
-  bits ^= sign;
-  uint32_t r;
-  if (bits >= (543u << 21)) {
-    r = 0x7Eu;
-  } else if (bits < (121u << 23)) {
-    const uint32_t magic = 141u << 23;
-    r = (__float_as_uint(__fadd_rn(__uint_as_float(bits), __uint_as_float(magic))) - magic) &
-        0xFFu;
-  } else {
-    const uint32_t odd = (bits >> 20) & 1u;
-    r = ((bits + ((uint32_t)(7 - 127) << 23) + 0x7FFFFu + odd) >> 20) & 0xFFu;
-  }
-  return r | (sign >> 24);
-}
-
 __device__ __forceinline__ int argmin_fp4(float q) {
   int best = 0;
   float bv = fabsf(q - fp4_to_f32(0));

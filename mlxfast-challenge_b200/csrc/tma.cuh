@@ -6,6 +6,7 @@
 // CTA-local bulk copies of this GPU's own memory are used (no multicast).
 #pragma once
 
+#include <cuda.h>
 #include <stdint.h>
 
 namespace nvfp4 {
@@ -116,6 +117,21 @@ __device__ __forceinline__ void bulk_wait0() {
 // Named barrier among `count` threads (multiple of 32), id 1..15.
 __device__ __forceinline__ void named_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// 2-D tiled TMA load of this GPU's memory into this CTA's shared memory
+// (no multicast); x is the inner coordinate in elements.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 }  // namespace nvfp4

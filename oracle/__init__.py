@@ -56,6 +56,11 @@ class _Port:
         L.orc_router_topk.argtypes = [_P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P]
         L.orc_moe_block_f32.argtypes = ([_P, _P, _P, _I64, _I64, _I64, _I, _F] + [_P] * 6 +
                                         [_I64] + [_P] * 6 + [_P, _P])
+        L.orc_to_fp4_e2m1.restype = ctypes.c_uint8
+        L.orc_to_fp4_e2m1.argtypes = [_F]
+        L.orc_quantize_dequantize_x.argtypes = [_P, _I64, _I64, _P]
+        L.orc_quantize_x.argtypes = [_P, _I64, _I64, _P, _P]
+        L.orc_qqmm_f32.argtypes = [_P, _P, _P, _I64, _I64, _I64, _P]
 
     # -- scalar conversions -------------------------------------------------
     def e4m3_decode(self, b):
@@ -129,6 +134,37 @@ class _Port:
                                     K, _ptr(out))
         return out
 
+    # -- QQMatmul: activation fake-quant + NVFP4 matmul ---------------------
+    def to_fp4_e2m1(self, f):
+        return self.lib.orc_to_fp4_e2m1(float(f))
+
+    def fake_quant_x(self, x):
+        """xhat = fp_quantize_dequantize(x) (f32 values, groups of 16 along the last axis)."""
+        x = np.ascontiguousarray(x, np.float32)
+        K = x.shape[-1]
+        out = np.empty_like(x)
+        self.lib.orc_quantize_dequantize_x(_ptr(x), x.size // K, K, _ptr(out))
+        return out
+
+    def quantize_x(self, x):
+        """x f32 [..., K] -> (codes u32 [..., K/8], scale bytes u8 [..., K/16])."""
+        x = np.ascontiguousarray(x, np.float32)
+        K = x.shape[-1]
+        xq = np.empty(x.shape[:-1] + (K // 8,), np.uint32)
+        s = np.empty(x.shape[:-1] + (K // 16,), np.uint8)
+        self.lib.orc_quantize_x(_ptr(x), x.size // K, K, _ptr(xq), _ptr(s))
+        return xq, s
+
+    def qqmm_f32(self, x, wq, sq):
+        x = np.ascontiguousarray(x, np.float32)
+        K = x.shape[-1]
+        M = x.size // K
+        N = wq.shape[-2]
+        y = np.empty(x.shape[:-1] + (N,), np.float32)
+        self.lib.orc_qqmm_f32(_ptr(x), _ptr(np.ascontiguousarray(wq)),
+                              _ptr(np.ascontiguousarray(sq)), M, N, K, _ptr(y))
+        return y
+
     def router_topk(self, x_bits, G_bits, bias, k, norm=True, round_logits=True):
         x = np.ascontiguousarray(x_bits, np.uint16)
         G = np.ascontiguousarray(G_bits, np.uint16)
@@ -186,6 +222,36 @@ class _Ref:
         for n in ("ref_bf16_mul", "ref_bf16_div"):
             getattr(L, n).restype = ctypes.c_uint16
             getattr(L, n).argtypes = [ctypes.c_uint16, ctypes.c_uint16]
+        L.ref_fake_quant_f32.argtypes = [_P, _I, _I, _P]
+        L.ref_qqmm_f32.argtypes = [_P, _P, _P, _I, _I, _I, _P]
+        L.ref_qqmm_bf16.argtypes = [_P, _P, _P, _I, _I, _I, _P]
+
+    def fake_quant_x(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        K = x.shape[-1]
+        out = np.empty_like(x)
+        self.lib.ref_fake_quant_f32(_ptr(x), x.size // K, K, _ptr(out))
+        return out
+
+    def qqmm_f32(self, x, wq, sq):
+        x = np.ascontiguousarray(x, np.float32)
+        K = x.shape[-1]
+        M = x.size // K
+        N = wq.shape[-2]
+        y = np.empty(x.shape[:-1] + (N,), np.float32)
+        self.lib.ref_qqmm_f32(_ptr(x), _ptr(np.ascontiguousarray(wq)),
+                              _ptr(np.ascontiguousarray(sq)), M, N, K, _ptr(y))
+        return y
+
+    def qqmm_bf16(self, x_bits, wq, sq):
+        x = np.ascontiguousarray(x_bits, np.uint16)
+        K = x.shape[-1]
+        M = x.size // K
+        N = wq.shape[-2]
+        y = np.empty(x.shape[:-1] + (N,), np.uint16)
+        self.lib.ref_qqmm_bf16(_ptr(x), _ptr(np.ascontiguousarray(wq)),
+                               _ptr(np.ascontiguousarray(sq)), M, N, K, _ptr(y))
+        return y
 
     def qmm_f32(self, x, wq, sq):
         x = np.ascontiguousarray(x, np.float32)

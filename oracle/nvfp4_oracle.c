@@ -223,6 +223,87 @@ ORC_API void orc_qmm_bf16(const uint16_t *x, const uint32_t *w, const uint8_t *s
 }
 
 /* ------------------------------------------------------------------------ */
+/* Activation fake-quantisation for QQMatmul (backend/cpu/quantized.cpp:    */
+/* 1064-1091 to_fp4_e2m1, 1093-1129 fp_quantize_dequantize, bits 4, group   */
+/* 16), in f32 on the values of x:                                           */
+/*   amax = std::max over |x| starting from -inf (a NaN operand never wins) */
+/*   s    = FromFP8(ToFP8(amax / 6))                                        */
+/*   code = to_fp4_e2m1(s == 0 ? 0 : x / s); xhat = s * LUT[code]           */
+/* to_fp4_e2m1 rounds |v| to the nearest E2M1 magnitude, ties to the even   */
+/* code (0.25 -> 0, 0.75 -> 1, 1.25 -> 1, 1.75 -> 2, 2.5 -> 2, 3.5 -> 4,     */
+/* 5 -> 4), saturates at 6, maps NaN to code 7, and takes the sign bit.      */
+/* ------------------------------------------------------------------------ */
+ORC_API uint8_t orc_to_fp4_e2m1(float v) {
+  if (isnan(v)) return 0x7;
+  uint8_t sign = signbit(v) ? 0x8 : 0x0;
+  float a = fabsf(v);
+  uint8_t m;
+  if (a > 5.0f) m = 7;
+  else if (a >= 3.5f) m = 6;
+  else if (a > 2.5f) m = 5;
+  else if (a >= 1.75f) m = 4;
+  else if (a > 1.25f) m = 3;
+  else if (a >= 0.75f) m = 2;
+  else if (a > 0.25f) m = 1;
+  else m = 0;
+  return (uint8_t)(m | sign);
+}
+
+/* Codes and raw scale bytes of one row group (the scale byte as MLX forms  */
+/* it, sign included), and xhat.                                            */
+static void qx_group(const float *v, uint8_t *codes, uint8_t *sbyte, float *xhat) {
+  float amax = -INFINITY;
+  for (int j = 0; j < 16; j++) {
+    float a = fabsf(v[j]);
+    amax = (amax < a) ? a : amax; /* std::max(amax, a) */
+  }
+  uint8_t sb = orc_e4m3_encode(amax / 6.0f);
+  float s = orc_e4m3_decode(sb);
+  for (int j = 0; j < 16; j++) {
+    uint8_t c = orc_to_fp4_e2m1(s == 0.0f ? 0.0f : v[j] / s);
+    codes[j] = c;
+    if (xhat) xhat[j] = s * FP4_VALUES[c];
+  }
+  *sbyte = sb;
+}
+
+/* xhat[M, K] = fp_quantize_dequantize(x) in f32. */
+ORC_API void orc_quantize_dequantize_x(const float *x, int64_t M, int64_t K, float *xhat) {
+  uint8_t codes[16], sb;
+  for (int64_t i = 0; i < M * (K / 16); i++) qx_group(x + i * 16, codes, &sb, xhat + i * 16);
+}
+
+/* The same groups packed like the weights: xq[M, K/8] (low nibble first),  */
+/* scale bytes [M, K/16].  The one scale MLX forms with the sign set        */
+/* (amax = -inf: an all-NaN group) is stored as its magnitude with every    */
+/* code's sign flipped, which dequantises to the same xhat.                 */
+ORC_API void orc_quantize_x(const float *x, int64_t M, int64_t K, uint32_t *xq, uint8_t *s) {
+  uint8_t codes[16], sb;
+  for (int64_t i = 0; i < M * (K / 16); i++) {
+    qx_group(x + i * 16, codes, &sb, NULL);
+    uint8_t flip = (sb & 0x80) ? 0x8 : 0x0;
+    uint32_t w0 = 0, w1 = 0;
+    for (int j = 0; j < 8; j++) w0 |= (uint32_t)((codes[j] ^ flip) & 15) << (4 * j);
+    for (int j = 0; j < 8; j++) w1 |= (uint32_t)((codes[8 + j] ^ flip) & 15) << (4 * j);
+    xq[i * 2] = w0;
+    xq[i * 2 + 1] = w1;
+    s[i] = (uint8_t)(sb & 0x7F);
+  }
+}
+
+/* QQMatmul (quantized.cpp:1322-1360): xhat = fake-quant(x), then the qmm   */
+/* of quantized.cpp:491-533 on xhat.  This is the fp32-accumulated form     */
+/* (T = float); x holds the activation values widened to f32.               */
+ORC_API void orc_qqmm_f32(const float *x, const uint32_t *w, const uint8_t *s, int64_t M,
+                          int64_t N, int64_t K, float *y) {
+  float *xhat = (float *)malloc(sizeof(float) * (size_t)(M * K));
+  if (!xhat) return;
+  orc_quantize_dequantize_x(x, M, K, xhat);
+  orc_qmm_f32(xhat, w, s, M, N, K, y);
+  free(xhat);
+}
+
+/* ------------------------------------------------------------------------ */
 /* Gather QMM (backend/cpu/quantized.cpp:805-844 fp_bs_qmm_dispatch_mode):  */
 /* for pair i, out[i] (M x N) = x[lhs[i]] (M x K) @ W[rhs[i]]^T.  lhs may   */
 /* be NULL, meaning lhs[i] = i (ops.cpp:67-81 indices_or_default after the  */

@@ -10,6 +10,7 @@
 //   detail::FromFP8/ToFP8   backend/cpu/unary_ops.h:120-172
 //   detail::Sigmoid         backend/cpu/unary_ops.h:77-84
 //   to_fp4_e2m1             backend/cpu/quantized.cpp:1064-1091
+//   dequantize_scale<T,16>  backend/cpu/quantized.cpp:49-62
 //   _MLX_BFloat16(float)    types/bf16.h:37-58
 // The gather loop mirrors fp_bs_qmm_dispatch_mode (quantized.cpp:805-844) for
 // row-contiguous operands; the threaded variants only split the output rows
@@ -76,6 +77,50 @@ REF_API void ref_qmm_bf16_mt(const uint16_t* x, const uint32_t* w, const uint8_t
     });
   }
   for (auto& th : pool) th.join();
+}
+
+// QQMatmul::eval_cpu (quantized.cpp:1322-1360) for T = float / bfloat16_t:
+// fp_quantize_dequantize's group loop (quantized.cpp:1093-1129, bits 4,
+// group 16) re-typed over plain pointers -- the reference's own function
+// takes mlx::core::array, whose allocator is not part of this build -- calling
+// the reference's ToFP8, dequantize_scale, to_fp4_e2m1 and FP4_LUT, then the
+// unchanged fp_qmm_t on xhat.
+template <typename T>
+static void ref_fake_quant(const T* w, T* out, size_t w_size) {
+  const int group_size = 16;
+  size_t n_groups = w_size / group_size;
+  for (size_t i = 0; i < n_groups; ++i) {
+    size_t idx = i * group_size;
+    float scale = -std::numeric_limits<float>::infinity();
+    for (int j = 0; j < group_size; ++j) scale = std::max(scale, (float)std::abs((float)w[idx + j]));
+    scale /= 6.0f;
+    scale = mc::dequantize_scale<float, 16>(mc::detail::ToFP8()(scale));
+    for (int j = 0; j < group_size; ++j) {
+      float w_el = scale == 0 ? 0.0f : w[idx + j] / scale;
+      float output = mc::FP4_LUT[mc::to_fp4_e2m1(w_el)];
+      out[idx + j] = static_cast<T>(scale * output);
+    }
+  }
+}
+
+REF_API void ref_fake_quant_f32(const float* x, int M, int K, float* xhat) {
+  ref_fake_quant<float>(x, xhat, (size_t)M * K);
+}
+
+REF_API void ref_qqmm_f32(const float* x, const uint32_t* w, const uint8_t* s, int M, int N,
+                          int K, float* y) {
+  std::vector<float> xhat((size_t)M * K);
+  ref_fake_quant<float>(x, xhat.data(), xhat.size());
+  mc::fp_qmm_t<float, 16, 4>(y, xhat.data(), w, s, M, N, K);
+}
+
+REF_API void ref_qqmm_bf16(const uint16_t* x, const uint32_t* w, const uint8_t* s, int M, int N,
+                           int K, uint16_t* y) {
+  std::vector<mc::bfloat16_t> xhat((size_t)M * K);
+  ref_fake_quant<mc::bfloat16_t>(reinterpret_cast<const mc::bfloat16_t*>(x), xhat.data(),
+                                 xhat.size());
+  mc::fp_qmm_t<mc::bfloat16_t, 16, 4>(reinterpret_cast<mc::bfloat16_t*>(y), xhat.data(), w, s,
+                                      M, N, K);
 }
 
 REF_API float ref_from_fp8(uint8_t b) { return mc::detail::FromFP8{}(b); }

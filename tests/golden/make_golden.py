@@ -9,6 +9,11 @@ quantized.cpp).  Every output array below is produced by reference code:
   sigmoid_*        detail::Sigmoid on a fixed sample    (unary_ops.h:77-84)
   qmm_*            fp_qmm_t<float|bfloat16_t,16,4>      (backend/cpu/quantized.cpp:491-533)
   gather_*         the fp_bs_qmm_dispatch_mode loop     (quantized.cpp:805-844)
+  fp4_enc_*        to_fp4_e2m1 on a fixed sample        (backend/cpu/quantized.cpp:1064-1091)
+  qqmm_*           QQMatmul::eval_cpu's two steps: the fp_quantize_dequantize
+                   group loop (quantized.cpp:1093-1129) over the reference's
+                   ToFP8 / dequantize_scale / to_fp4_e2m1 / FP4_LUT, then
+                   fp_qmm_t<float|bfloat16_t> on xhat (quantized.cpp:1322-1360)
   quant_*          the fp_quantize graph (ops.cpp:4909-4962) composed from the
                    reference's compiled scalar ops: bf16 division
                    (_MLX_BFloat16 operator/, types/bf16.h:71-99), ToFP8,
@@ -127,6 +132,34 @@ def main():
     qb = oracle.bf16_bits_from_f32(qw)
     g["quant_w_bf16"] = qb
     g["quant_wq"], g["quant_sq"] = ref_quantize_bf16(ref, qb)
+
+    # QQMatmul pin: activation fake-quant edge groups and a small product.
+    rng = np.random.default_rng(4)
+    fe = np.concatenate([
+        np.array([0, -0., 0.25, -0.25, 0.2500001, 0.75, 0.7499999, 1.25, 1.2500001, 1.75, 2.5,
+                  2.5000002, 3.5, 3.4999998, 5, 5.0000005, 6, 7, 1e30, np.inf, -np.inf, np.nan],
+                 np.float32),
+        (rng.standard_normal(500) * 3).astype(np.float32)])
+    g["fp4_enc_in"] = fe
+    g["fp4_enc_out"] = np.array([L.ref_to_fp4_e2m1(float(v)) for v in fe], np.uint8)
+    qx = (rng.standard_normal((12, 256)) * rng.choice([1e-6, 1e-3, 1, 30, 1e4], (12, 1))).astype(
+        np.float32)
+    qx[0, :16] = 0.0                                     # all-zero group
+    qx[1, :16] = np.nan                                  # all-NaN group (scale byte 0xFE)
+    qx[2, :16] = [np.nan] * 8 + [1.0] * 8
+    qx[3, :16] = np.inf
+    qx[4, 16:32] = np.array([6, 3, 0.25, -0.25, 0.75, -0.75, 1.25, -1.25, 1.75, 2.5, -3.5, 5,
+                             -5, 0.5, -0.5, 0], np.float32)  # E2M1 midpoints at scale 1
+    g["qqmm_fq_in"] = qx
+    g["qqmm_fq_out"] = ref.fake_quant_x(qx)
+    rng = np.random.default_rng(5)
+    w = oracle.bf16_bits_from_f32((rng.standard_normal((48, 512)) * 0.02).astype(np.float32))
+    wq, sq = port.quantize(w)
+    x = rng.standard_normal((3, 512)).astype(np.float32)
+    xb = oracle.bf16_bits_from_f32(x)
+    g["qqmm_wq"], g["qqmm_sq"], g["qqmm_x_f32"], g["qqmm_x_bf16"] = wq, sq, x, xb
+    g["qqmm_y_f32"] = ref.qqmm_f32(x, wq, sq)
+    g["qqmm_y_bf16"] = ref.qqmm_bf16(xb, wq, sq)
 
     np.savez_compressed(OUT, **g)
     print("wrote", OUT, os.path.getsize(OUT), "bytes")

@@ -171,6 +171,49 @@ def test_gather_matches_per_expert_qmm(orc, E, N, K, rows, experts):
         np.testing.assert_allclose(got[i], want, rtol=2e-3, atol=2e-3)
 
 
+# --- QQMatmul: activation fake-quant (quantized.cpp:1064-1129, 1322-1360) -------
+
+def test_to_fp4_e2m1_matches_reference(orc, golden):
+    got = np.array([orc.port.to_fp4_e2m1(v) for v in golden["fp4_enc_in"]], np.uint8)
+    assert np.array_equal(got, golden["fp4_enc_out"])
+
+
+def test_to_fp4_e2m1_ties_to_even(orc):
+    # RNE on the E2M1 grid with the reference's comparisons: 0.25 -> 0,
+    # 0.75 -> 1.0, 1.25 -> 1.0, 1.75 -> 2.0, 2.5 -> 2.0, 3.5 -> 4.0, 5 -> 4.0.
+    for v, code in [(0.25, 0), (0.75, 2), (1.25, 2), (1.75, 4), (2.5, 4), (3.5, 6), (5.0, 6),
+                    (5.01, 7), (100.0, 7), (-0.75, 10), (float("nan"), 7), (-0.0, 8)]:
+        assert orc.port.to_fp4_e2m1(v) == code, v
+
+
+def test_activation_fake_quant_bit_exact_vs_reference(orc, golden):
+    got = orc.port.fake_quant_x(golden["qqmm_fq_in"])
+    assert np.array_equal(got.view(np.uint32), golden["qqmm_fq_out"].view(np.uint32))
+
+
+def test_activation_codes_dequantize_to_xhat(orc, golden):
+    x = golden["qqmm_fq_in"]
+    xq, s = orc.port.quantize_x(x)
+    assert s.max() <= 0x7E  # UE4M3 magnitudes only (the all-NaN group is re-signed)
+    assert np.array_equal(orc.port.dequantize(xq, s).view(np.uint32),
+                          golden["qqmm_fq_out"].view(np.uint32))
+
+
+def test_qqmm_f32_bit_exact_vs_reference(orc, golden):
+    y = orc.port.qqmm_f32(golden["qqmm_x_f32"], golden["qqmm_wq"], golden["qqmm_sq"])
+    assert np.array_equal(y.view(np.uint32), golden["qqmm_y_f32"].view(np.uint32))
+
+
+def test_qqmm_bf16_path_bit_exact_vs_reference(orc, golden):
+    # T = bfloat16_t: xhat is exact in bf16, then fp_qmm_t with per-op bf16
+    # rounding (the secondary comparison; the tolerance target is the f32 form).
+    x = orc.f32_from_bf16_bits(golden["qqmm_x_bf16"])
+    xhat_bits = orc.bf16_bits_from_f32(orc.port.fake_quant_x(x))
+    assert np.array_equal(orc.f32_from_bf16_bits(xhat_bits), orc.port.fake_quant_x(x))
+    y = orc.port.qmm_bf16(xhat_bits, golden["qqmm_wq"], golden["qqmm_sq"])
+    assert np.array_equal(y, golden["qqmm_y_bf16"])
+
+
 # --- oracle vs the reference kernels on fresh inputs (this container only) ----
 
 def test_port_vs_reference_library_fresh_inputs(orc):
@@ -186,6 +229,11 @@ def test_port_vs_reference_library_fresh_inputs(orc):
     assert np.array_equal(orc.port.qmm_bf16(xb, wq, sq), orc.ref.qmm_bf16(xb, wq, sq))
     for v in rng.standard_normal(5000).astype(np.float32) * 100:
         assert orc.port.e4m3_encode(v) == orc.ref.lib.ref_to_fp8(float(v))
+    xq = (rng.standard_normal((9, 512)) * rng.choice([1e-5, 1, 1e3], (9, 1))).astype(np.float32)
+    assert np.array_equal(orc.port.fake_quant_x(xq).view(np.uint32),
+                          orc.ref.fake_quant_x(xq).view(np.uint32))
+    assert np.array_equal(orc.port.qqmm_f32(x, wq, sq).view(np.uint32),
+                          orc.ref.qqmm_f32(x, wq, sq).view(np.uint32))
 
 
 # --- router / block semantics ----------------------------------------------------
