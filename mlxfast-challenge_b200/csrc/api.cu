@@ -933,6 +933,9 @@ extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64
   }
   if (H % 256 || I % 256 || (Is != 0 && Is != I) || k > 16 || E > 0x7fffffff)
     return fail(NVFP4_ERR_UNSUPPORTED, "[%s] unsupported layer shape.", op);
+  // each consumer thread holds at most 2 x chunks and 4 act chunks of 8 values
+  if (H > 4096 || (k + (Is > 0 ? 1 : 0)) * I > 8192)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layer too wide for the persistent stack.", op);
   const int esz = dtype == NVFP4_F32 ? 4 : 2;
   if (!aligned16(x) || !aligned16(y))
     return fail(NVFP4_ERR_UNSUPPORTED, "[%s] x and y must be 16-byte aligned.", op);

@@ -46,6 +46,8 @@ constexpr int kBatch = 4;                  // gate/up units computed together
 constexpr int kDGroups = kSCons / 4;       // down: groups of 4 warps, each over every kDGroups-th segment
 static_assert(kSCons % 4 == 0 && kSCons >= 8, "down groups are 4 warps (one per chunk of I=512)");
 constexpr int kDAcc = 2;                   // down: accumulator sets per warp
+constexpr int kXChunks = 2;                // x: 8-value chunks per consumer thread (H <= 4096)
+constexpr int kAChunks = 4;                // act: chunks per thread (kk * I <= 8192)
 constexpr int kErrTimeout = 4;
 constexpr int kErrIndex = 2;
 
@@ -357,29 +359,30 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
     void* xout = l == a.L - 1 ? a.y : a.xb[l & 1];
 
     // ---- stage x (one column, f16 x 2^-e) ----
-    // max |x_l|: published by the layer that wrote x_l (atomicMax on the bit
-    // patterns of non-negative floats); layer 0 measures its input here.
-    if (l == 0) {
-      if (threadIdx.x == 0) S.colmax[0] = 0;
-      named_sync(1, nthr);
+    // Each thread keeps its chunks of x in registers; max |x| (over the
+    // values as stored) comes from them, one shared-memory reduction, instead
+    // of a separate global read after the barrier.
+    if (threadIdx.x == 0) S.colmax[0] = 0;
+    named_sync(1, nthr);
+    float xv[kXChunks][8];
+    {
       float m = 0.f;
-      for (int v = threadIdx.x; v < H / 8; v += nthr) {
-        float f[8];
-        load8_cg(xin, a.dtype, (int64_t)v * 8, f);
 #pragma unroll
-        for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(f[i]));
+      for (int c = 0; c < kXChunks; c++) {
+        const int v = threadIdx.x + c * nthr;
+        if (v >= H / 8) continue;
+        load8_cg(xin, a.dtype, (int64_t)v * 8, xv[c]);
+#pragma unroll
+        for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(xv[c][i]));
       }
       warp_atomic_max(&S.colmax[0], m, true);
-      named_sync(1, nthr);
-    } else if (threadIdx.x == 0) {
-      S.colmax[0] = (int)__ldcg(&a.xmax[l]);
     }
     named_sync(1, nthr);
     const float xscale = ldexpf(1.0f, pow2_exponent(__int_as_float(S.colmax[0])));
-    for (int v = threadIdx.x; v < H / 8; v += nthr) {
-      float f[8];
-      load8_cg(xin, a.dtype, (int64_t)v * 8, f);
-      store8_f16(S.xs, v * 8, f, 1.0f / xscale);
+#pragma unroll
+    for (int c = 0; c < kXChunks; c++) {
+      const int v = threadIdx.x + c * nthr;
+      if (v < H / 8) store8_f16(S.xs, v * 8, xv[c], 1.0f / xscale);
     }
     named_sync(1, nthr);
 
@@ -449,10 +452,6 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
         for (int r = 0; r < 4; r++) d[r] = S.red2[(warp * 4 + r) * 32 + lane];
         const float av = silu_ref(d[0] * xscale) * (d[2] * xscale);
         if (t == 0) __stcg(a.act + (int64_t)seg * I + i0 + g, av);
-        // max |act * w_seg| for the down staging (segment weights as there)
-        const float sw = seg < a.k ? S.wts[l * 16 + seg] * ly.scaling : 1.0f;
-        const float am = warp_max(t == 0 ? fabsf(av * sw) : 0.f);
-        if (lane == 0) atomicMax(&a.amax[l], __float_as_uint(am));
       }
       named_sync(1, nthr);
       jg += nb;
@@ -467,28 +466,32 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
       // act columns x (w_j * scaling) (1 for the shared expert), one scale.
       if (threadIdx.x < kk)
         S.segw[threadIdx.x] = threadIdx.x < a.k ? S.wts[l * 16 + threadIdx.x] * ly.scaling : 1.0f;
-      if (threadIdx.x == 0) S.colmax[0] = (int)__ldcg(&a.amax[l]);
+      if (threadIdx.x == 0) S.colmax[0] = 0;
       named_sync(1, nthr);
+      // act of every segment into registers; max |act * w_seg| from them
       const int per = I / 8;
-      const float ascale = ldexpf(1.0f, pow2_exponent(__int_as_float(S.colmax[0])));
-      // all of a thread's loads in flight before the first conversion
-      for (int base = threadIdx.x; base < kk * per; base += 4 * nthr) {
-        float f[4][8];
+      float av[kAChunks][8];
+      {
+        float m = 0.f;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int it = base + i * nthr;
-          if (it < kk * per) {
-            const int sg = it / per, v = it - sg * per;
-            load8_cg(a.act, kF32, (int64_t)sg * I + (int64_t)v * 8, f[i]);
-          }
+        for (int c = 0; c < kAChunks; c++) {
+          const int it = threadIdx.x + c * nthr;
+          if (it >= kk * per) continue;
+          const int sg = it / per, v = it - sg * per;
+          load8_cg(a.act, kF32, (int64_t)sg * I + (int64_t)v * 8, av[c]);
+#pragma unroll
+          for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(av[c][i] * S.segw[sg]));
         }
+        warp_atomic_max(&S.colmax[0], m, true);
+      }
+      named_sync(1, nthr);
+      const float ascale = ldexpf(1.0f, pow2_exponent(__int_as_float(S.colmax[0])));
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const int it = base + i * nthr;
-          if (it < kk * per) {
-            const int sg = it / per, v = it - sg * per;
-            store8_f16(S.xa + (size_t)sg * ldxD, v * 8, f[i], S.segw[sg] / ascale);
-          }
+      for (int c = 0; c < kAChunks; c++) {
+        const int it = threadIdx.x + c * nthr;
+        if (it < kk * per) {
+          const int sg = it / per, v = it - sg * per;
+          store8_f16(S.xa + (size_t)sg * ldxD, v * 8, av[c], S.segw[sg] / ascale);
         }
       }
       named_sync(1, nthr);
@@ -542,17 +545,11 @@ __global__ void __launch_bounds__(kSThreads, 1) moe_decode_stack_kernel(
         if (warp == 0) {
 #pragma unroll
           for (int r = 0; r < 4; r++) d[r] = S.red2[r * 32 + lane];
-          float xm = 0.f;
           if (t == 0) {
             const int64_t h0 = (int64_t)dt * 16;
-            const float v0 = d[0] * ascale, v1 = d[2] * ascale;
-            store_from_f32(xout, a.dtype, h0 + g, v0);
-            store_from_f32(xout, a.dtype, h0 + g + 8, v1);
-            // the next layer's input max, over the values as stored
-            xm = fmaxf(fabsf(round_as(v0, a.dtype)), fabsf(round_as(v1, a.dtype)));
+            store_from_f32(xout, a.dtype, h0 + g, d[0] * ascale);
+            store_from_f32(xout, a.dtype, h0 + g + 8, d[2] * ascale);
           }
-          xm = warp_max(xm);
-          if (lane == 0 && l + 1 < a.L) atomicMax(&a.xmax[l + 1], __float_as_uint(xm));
         }
         named_sync(1, nthr);
       }
