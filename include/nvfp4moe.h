@@ -79,6 +79,13 @@ NVFP4MOE_API int nvfp4_version(void);
  * cp.async.bulk copies into a shared-memory ring (one producer warp, eight
  * consumer warps) instead of per-thread streaming loads.  Same results. */
 #define NVFP4_LAUNCH_BULK_COPY 2
+/* The prefill (T > 8) GEMMs of moe_block_forward run by default on the
+ * block-scaled FP4 tensor cores (tcgen05 kind::mxf4nvf4): activations as a sum
+ * of four NVFP4 terms (relative-L2 ~5e-5 from the W4A16 product, 20x below
+ * bf16 output rounding), weights as stored.  NVFP4_LAUNCH_EXACT_PREFILL
+ * selects the exact path instead (weights dequantised to 16-bit, kind::f16;
+ * ~1.7x slower at T = 512). */
+#define NVFP4_LAUNCH_EXACT_PREFILL 4
 NVFP4MOE_API int nvfp4_set_launch_flags(int flags);
 /* Synchronises the device, returns and clears the latched device status
  * (NVFP4_OK or NVFP4_ERR_DEVICE_INDEX). */

@@ -269,11 +269,14 @@ class launch_flags:
     """Context manager setting the calling thread's C-ABI launch flags
     (nvfp4_set_launch_flags): pdl=True lets the first kernel of each call
     overlap its predecessor; bulk_copy=True selects the bulk-copy fed decode
-    kernels."""
+    kernels; exact_prefill=True runs the prefill GEMMs on 16-bit dequantised
+    weights (kind::f16) instead of the default block-scaled FP4 path
+    (activations as four NVFP4 terms)."""
 
-    def __init__(self, pdl: bool = False, bulk_copy: bool = False):
+    def __init__(self, pdl: bool = False, bulk_copy: bool = False, exact_prefill: bool = False):
         self.flags = (_lib.NVFP4_LAUNCH_PDL if pdl else 0) | (
-            _lib.NVFP4_LAUNCH_BULK_COPY if bulk_copy else 0)
+            _lib.NVFP4_LAUNCH_BULK_COPY if bulk_copy else 0) | (
+            _lib.NVFP4_LAUNCH_EXACT_PREFILL if exact_prefill else 0)
 
     def __enter__(self):
         self.old = lib().nvfp4_set_launch_flags(self.flags)

@@ -21,6 +21,7 @@ NVFP4_ERR_DEVICE_INDEX = 5
 NVFP4_BF16, NVFP4_F16, NVFP4_F32 = 0, 1, 2
 NVFP4_LAUNCH_PDL = 1
 NVFP4_LAUNCH_BULK_COPY = 2
+NVFP4_LAUNCH_EXACT_PREFILL = 4
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64

@@ -19,6 +19,7 @@ thread_local int t_launch_flags = 0;
 
 bool first_pdl() { return (t_launch_flags & NVFP4_LAUNCH_PDL) != 0; }
 bool use_bulk() { return (t_launch_flags & NVFP4_LAUNCH_BULK_COPY) != 0; }
+bool use_fp4_terms() { return (t_launch_flags & NVFP4_LAUNCH_EXACT_PREFILL) == 0; }
 nvfp4_error_handler g_handler = nullptr;
 void* g_handler_data = nullptr;
 
@@ -81,10 +82,12 @@ struct BlockLayout {
   int kk;
   // Prefill (T > 8) buffers: sorted slot maps, tile list, x rows in slot order
   // as pre-scaled f16, f32 act, act as pre-scaled f16 rows, f32 Y.
-  bool prefill;
+  bool prefill, fp4;
   int64_t P, S, max_tiles;
   size_t brow_off, pos_off, tiles_off, ntiles_off, x16_off, xscale_off, act32_off, act16_off,
       ascale_off, y_off;
+  // FP4-terms prefill: term rows of x and of act (codes, scales, factors)
+  size_t xtc_off, xts_off, xtf_off, atc_off, ats_off, atf_off;
 };
 
 // The tensor-core prefill path: T > 8 tokens, K slabs of 256 on both GEMMs,
@@ -113,7 +116,7 @@ BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
   B.total = align_up(B.act_off + (size_t)T * B.kk * B.act_ld * sizeof(float), 256);
   B.prefill = prefill_shape_ok(L, T);
   if (B.prefill) {
-    const int64_t tile = nvfp4::gemm_tile_tokens();
+    const int64_t tile = std::min<int64_t>(nvfp4::gemm_tile_tokens(), nvfp4::kFp4TileTokens);
     B.P = T * L->top_k;
     const bool sh = L->shared_inter > 0;
     B.S = B.P + (sh ? T : 0);
@@ -129,6 +132,18 @@ BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
     B.ascale_off = align_up(B.act16_off + (size_t)B.S * B.act_ld * 2, 256);
     B.y_off = align_up(B.ascale_off + (size_t)B.S * sizeof(float), 256);
     B.total = align_up(B.y_off + (size_t)B.S * L->hidden * sizeof(float), 256);
+    auto k_ok = [](int64_t K) { return K == 512 || K == 1024 || K == 2048; };
+    B.fp4 = k_ok(L->hidden) && k_ok(L->inter);
+    if (B.fp4) {
+      const size_t rows = (size_t)B.S * nvfp4::kFp4Terms;
+      B.xtc_off = B.total;
+      B.xts_off = align_up(B.xtc_off + rows * (L->hidden / 2), 256);
+      B.xtf_off = align_up(B.xts_off + rows * (L->hidden / 16), 256);
+      B.atc_off = align_up(B.xtf_off + rows * sizeof(float), 256);
+      B.ats_off = align_up(B.atc_off + rows * (L->inter / 2), 256);
+      B.atf_off = align_up(B.ats_off + rows * (L->inter / 16), 256);
+      B.total = align_up(B.atf_off + rows * sizeof(float), 256);
+    }
   }
   return B;
 }
@@ -178,7 +193,7 @@ int nvfp4_version(void) { return 1; }
 
 int nvfp4_set_launch_flags(int flags) {
   const int old = t_launch_flags;
-  t_launch_flags = flags & (NVFP4_LAUNCH_PDL | NVFP4_LAUNCH_BULK_COPY);
+  t_launch_flags = flags & (NVFP4_LAUNCH_PDL | NVFP4_LAUNCH_BULK_COPY | NVFP4_LAUNCH_EXACT_PREFILL);
   return old;
 }
 
@@ -200,6 +215,10 @@ int nvfp4_device_status(void) {
   e = nvfp4::read_and_clear_ep_error(&st4);
   if (e != cudaSuccess) return check_cuda(e, "device_status");
   if (st == 0) st = st4;
+  int st6 = 0;
+  e = nvfp4::read_and_clear_fp4_error(&st6);
+  if (e != cudaSuccess) return check_cuda(e, "device_status");
+  if (st == 0) st = st6;
   int st5 = 0;
   e = nvfp4::read_and_clear_qqmm_error(&st5);
   if (e != cudaSuccess) return check_cuda(e, "device_status");
@@ -553,6 +572,138 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
   return down_impl(y, act, B.act_ld, residual, dtype, T, L, inds, wts, stream, /*pdl=*/true);
 }
 
+// The FP4-terms prefill after the sort: x as four NVFP4 term rows per slot,
+// gate/up + SwiGLU and down on the block-scaled tensor cores, act as terms in
+// between, then the same combine.
+static int prefill_fp4_tail(void* y, const void* x, const void* residual, int dtype, int64_t T,
+                            const moe_layer_desc* L, const float* wts, char* ws,
+                            const BlockLayout& B, cudaStream_t s) {
+  const char* op = "moe_block";
+  const int64_t H = L->hidden, I = L->inter, E = L->n_experts, Is = L->shared_inter;
+  const bool sh = Is > 0;
+  int* pos = reinterpret_cast<int*>(ws + B.pos_off);
+  int4* tiles = reinterpret_cast<int4*>(ws + B.tiles_off);
+  int* ntiles = reinterpret_cast<int*>(ws + B.ntiles_off);
+  float* act32 = reinterpret_cast<float*>(ws + B.act32_off);
+  float* Y = reinterpret_cast<float*>(ws + B.y_off);
+  uint8_t* xtc = reinterpret_cast<uint8_t*>(ws + B.xtc_off);
+  uint8_t* xts = reinterpret_cast<uint8_t*>(ws + B.xts_off);
+  float* xtf = reinterpret_cast<float*>(ws + B.xtf_off);
+  uint8_t* atc = reinterpret_cast<uint8_t*>(ws + B.atc_off);
+  uint8_t* ats = reinterpret_cast<uint8_t*>(ws + B.ats_off);
+  float* atf = reinterpret_cast<float*>(ws + B.atf_off);
+  const int64_t trows = B.S * nvfp4::kFp4Terms;
+
+  nvfp4::TermsArgs tx{};
+  tx.src = x;
+  tx.src_dtype = dtype;
+  tx.rows = T;
+  tx.K = H;
+  tx.src_ld = H;
+  tx.dst_map = pos;  // token t feeds slots pos[t * k + j]
+  tx.map_stride = (int)L->top_k;
+  tx.map_count = (int)L->top_k;
+  tx.extra_base = sh ? B.P : -1;  // and its shared-expert slot P + t
+  tx.codes = xtc;
+  tx.scales = xts;
+  tx.fac = xtf;
+  if (int r = check_cuda(nvfp4::launch_rows_to_terms(tx, s), op)) return r;
+
+  auto maps_ok = [](std::initializer_list<cudaError_t> l) {
+    for (cudaError_t e : l)
+      if (e != cudaSuccess) return false;
+    return true;
+  };
+  nvfp4::GemmFp4Args g{};
+  g.mode = 1;
+  g.K = (int)H;
+  g.Mrows = (int)I;
+  g.Mrows_shared = (int)Is;
+  g.shared_group = sh ? (int)E : -1;
+  bool ok = maps_ok({nvfp4::map_codes(&g.mc0, L->gate.w, E * I, H, 64),
+                     nvfp4::map_scales(&g.ms0, L->gate.scales, E * I, H, 64),
+                     nvfp4::map_codes(&g.mc1, L->up.w, E * I, H, 64),
+                     nvfp4::map_scales(&g.ms1, L->up.scales, E * I, H, 64),
+                     nvfp4::map_codes(&g.mb[0], xtc, trows, H, 32),
+                     nvfp4::map_scales(&g.msb[0], xts, trows, H, 32),
+                     nvfp4::map_codes(&g.mb[1], xtc, trows, H, 64),
+                     nvfp4::map_scales(&g.msb[1], xts, trows, H, 64),
+                     nvfp4::map_codes(&g.mb[2], xtc, trows, H, 96),
+                     nvfp4::map_scales(&g.msb[2], xts, trows, H, 96),
+                     nvfp4::map_codes(&g.mb[3], xtc, trows, H, 128),
+                     nvfp4::map_scales(&g.msb[3], xts, trows, H, 128)});
+  if (sh)
+    ok = ok && maps_ok({nvfp4::map_codes(&g.mcs0, L->shared_gate.w, Is, H, 64),
+                        nvfp4::map_scales(&g.mss0, L->shared_gate.scales, Is, H, 64),
+                        nvfp4::map_codes(&g.mcs1, L->shared_up.w, Is, H, 64),
+                        nvfp4::map_scales(&g.mss1, L->shared_up.scales, Is, H, 64)});
+  g.bfac = xtf;
+  g.tiles = tiles;
+  g.ntiles = ntiles;
+  g.max_tiles = (int)B.max_tiles;
+  g.out = act32;
+  g.out_ld = B.act_ld;
+
+  nvfp4::GemmFp4Args d{};
+  d.mode = 2;
+  d.K = (int)I;
+  d.Mrows = (int)H;
+  d.Mrows_shared = (int)H;
+  d.shared_group = sh ? (int)E : -1;
+  ok = ok && maps_ok({nvfp4::map_codes(&d.mc0, L->down.w, E * H, I, 128),
+                      nvfp4::map_scales(&d.ms0, L->down.scales, E * H, I, 128),
+                      nvfp4::map_codes(&d.mb[0], atc, trows, I, 32),
+                      nvfp4::map_scales(&d.msb[0], ats, trows, I, 32),
+                      nvfp4::map_codes(&d.mb[1], atc, trows, I, 64),
+                      nvfp4::map_scales(&d.msb[1], ats, trows, I, 64),
+                      nvfp4::map_codes(&d.mb[2], atc, trows, I, 96),
+                      nvfp4::map_scales(&d.msb[2], ats, trows, I, 96),
+                      nvfp4::map_codes(&d.mb[3], atc, trows, I, 128),
+                      nvfp4::map_scales(&d.msb[3], ats, trows, I, 128)});
+  if (sh)
+    ok = ok && maps_ok({nvfp4::map_codes(&d.mcs0, L->shared_down.w, H, I, 128),
+                        nvfp4::map_scales(&d.mss0, L->shared_down.scales, H, I, 128)});
+  d.bfac = atf;
+  d.tiles = tiles;
+  d.ntiles = ntiles;
+  d.max_tiles = (int)B.max_tiles;
+  d.out = Y;
+  d.out_ld = H;
+  if (!ok) return fail(NVFP4_ERR_CUDA, "[%s] tensor-map encoding failed.", op);
+
+  if (int r = check_cuda(nvfp4::launch_nvfp4_gemm_fp4(g, (int)B.max_tiles, s), op)) return r;
+
+  nvfp4::TermsArgs ta{};
+  ta.src = act32;
+  ta.src_dtype = NVFP4_F32;
+  ta.rows = B.S;
+  ta.K = I;
+  ta.src_ld = B.act_ld;
+  ta.dst_map = nullptr;
+  ta.extra_base = -1;  // identity: slot r
+  ta.codes = atc;
+  ta.scales = ats;
+  ta.fac = atf;
+  if (int r = check_cuda(nvfp4::launch_rows_to_terms(ta, s), op)) return r;
+
+  if (int r = check_cuda(nvfp4::launch_nvfp4_gemm_fp4(d, (int)B.max_tiles, s), op)) return r;
+
+  nvfp4::CombineArgs c{};
+  c.Y = Y;
+  c.pos = pos;
+  c.wts = wts;
+  c.T = (int)T;
+  c.k = (int)L->top_k;
+  c.P = (int)B.P;
+  c.H = (int)H;
+  c.with_shared = sh ? 1 : 0;
+  c.scaling = L->routed_scaling;
+  c.residual = residual;
+  c.y = y;
+  c.dtype = dtype;
+  return check_cuda(nvfp4::launch_moe_combine(c, s, true), op);
+}
+
 // Prefill: sort pairs by expert, gate/up + SwiGLU and down as tcgen05
 // grouped GEMMs over expert-sorted token slots (the shared expert is one more
 // group holding every token), then the weighted per-token combine.  Both GEMMs
@@ -587,7 +738,10 @@ static int prefill_impl(void* y, const void* x, const void* residual, int dtype,
   sa.pos = pos;
   sa.tiles = tiles;
   sa.ntiles = ntiles;
+  const bool fp4 = use_fp4_terms() && B.fp4;
+  sa.tile_tokens = fp4 ? nvfp4::kFp4TileTokens : 0;
   if (int r = check_cuda(nvfp4::launch_moe_sort(sa, s, pdl_first), op)) return r;
+  if (fp4) return prefill_fp4_tail(y, x, residual, dtype, T, L, wts, ws, B, s);
 
   // x rows in slot order (shared-expert slots P.. hold tokens 0..T-1).
   nvfp4::RowsArgs rx{};

@@ -98,6 +98,24 @@ __device__ __forceinline__ uint32_t e4m3_encode(float f) {
   return r | (sign >> 24);
 }
 
+// MLX to_fp4_e2m1: round to the nearest E2M1 magnitude with ties to the even
+// code, saturating at 6; NaN -> +6 (code 7); the sign bit from signbit().
+__device__ __forceinline__ uint32_t fp4_code_mlx(float v) {
+  if (isnan(v)) return 0x7u;
+  const uint32_t sign = signbit(v) ? 0x8u : 0u;
+  const float a = fabsf(v);
+  uint32_t m;
+  if (a > 5.0f) m = 7;
+  else if (a >= 3.5f) m = 6;
+  else if (a > 2.5f) m = 5;
+  else if (a >= 1.75f) m = 4;
+  else if (a > 1.25f) m = 3;
+  else if (a >= 0.75f) m = 2;
+  else if (a > 0.25f) m = 1;
+  else m = 0;
+  return m | sign;
+}
+
 __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
   __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);

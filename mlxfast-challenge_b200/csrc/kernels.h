@@ -188,6 +188,41 @@ struct SortArgs {
   int* pos;    // [P]
   int4* tiles;
   int* ntiles;
+  int tile_tokens;  // tokens per tile (0: the f16 GEMM's 64)
+};
+
+// Activation rows as a sum of kFp4Terms NVFP4 terms (prefill_fp4.cu):
+// term t of a row is its residual after terms 0..t-1, quantised per group of
+// 16 with a UE4M3 scale, under one power-of-two factor per (row, term).
+constexpr int kFp4Terms = 4;
+struct TermsArgs {
+  const void* src;      // [rows, K] (row r at src + r * src_ld elements)
+  int src_dtype;
+  int64_t rows, K, src_ld;
+  // destination slot of source row r: dst_map[r * map_stride + j] for
+  // j < map_count (entries < 0 skipped), plus extra_base + r when
+  // extra_base >= 0; identity when dst_map is null and extra_base < 0
+  const int* dst_map;
+  int map_stride, map_count;
+  int64_t extra_base;
+  uint8_t* codes;   // [slots * 4, K/2]  (term row = slot * 4 + t)
+  uint8_t* scales;  // [slots * 4, K/16]
+  float* fac;       // [slots * 4]: value = fac * dequant(codes, scales)
+};
+
+// Grouped GEMM on the block-scaled tensor cores over slot-ordered term rows.
+struct alignas(64) GemmFp4Args {
+  CUtensorMap mc0, ms0, mc1, ms1;      // routed codes / scales (mc1, ms1: up bank, mode 1)
+  CUtensorMap mcs0, mss0, mcs1, mss1;  // shared-expert codes / scales
+  CUtensorMap mb[4], msb[4];           // term-row codes [S*4, K/2] / scales, boxes of 32 (i+1) rows
+  const float* bfac;                   // [S*4]
+  const int4* tiles;                   // (group, first slot, slots <= 32, 0)
+  const int* ntiles;
+  int max_tiles;                       // capacity of the tile list (shared-memory copy)
+  int mode;          // 1 gate/up + SwiGLU -> act f32, 2 down -> Y f32
+  int K, Mrows, Mrows_shared, shared_group;
+  float* out;        // mode 1: act [S, out_ld]; mode 2: Y [S, out_ld]
+  int64_t out_ld;
 };
 
 struct CombineArgs {
@@ -208,6 +243,11 @@ cudaError_t launch_nvfp4_gemm(const GemmArgs& a, bool f16, int max_tiles, cudaSt
 int gemm_slab_k();
 cudaError_t launch_rows_to_f16(const RowsArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t launch_moe_sort(const SortArgs& a, cudaStream_t stream, bool pdl);
+constexpr int kFp4TileTokens = 32;
+size_t gemm_fp4_smem_bytes(int max_tiles);
+cudaError_t launch_rows_to_terms(const TermsArgs& a, cudaStream_t stream);
+cudaError_t launch_nvfp4_gemm_fp4(const GemmFp4Args& a, int max_tiles, cudaStream_t stream);
+cudaError_t read_and_clear_fp4_error(int* out);
 cudaError_t launch_moe_combine(const CombineArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t read_and_clear_prefill_error(int* out);
 

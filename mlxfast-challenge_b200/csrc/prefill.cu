@@ -618,6 +618,7 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(SortArgs a) {
   pdl_wait();
   pdl_trigger();
   const int E = a.E;
+  const int tb = a.tile_tokens > 0 ? a.tile_tokens : kBN;  // tokens per tile
   const int P = a.P;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
@@ -633,22 +634,22 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(SortArgs a) {
       off[e] = acc;
       toff[e] = tacc;
       acc += cnt[e];
-      tacc += (cnt[e] + kBN - 1) / kBN;
+      tacc += (cnt[e] + tb - 1) / tb;
     }
     toff[E] = tacc;
-    const int tsh = a.with_shared ? (a.T + kBN - 1) / kBN : 0;
+    const int tsh = a.with_shared ? (a.T + tb - 1) / tb : 0;
     *a.ntiles = tacc + tsh;
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     const int n = cnt[e];
-    for (int t = 0; t * kBN < n; t++)
-      a.tiles[toff[e] + t] = make_int4(e, off[e] + t * kBN, min(kBN, n - t * kBN), 0);
+    for (int t = 0; t * tb < n; t++)
+      a.tiles[toff[e] + t] = make_int4(e, off[e] + t * tb, min(tb, n - t * tb), 0);
     cnt[e] = 0;  // reused as the scatter cursor
   }
   if (a.with_shared) {
-    for (int t = threadIdx.x; t * kBN < a.T; t += blockDim.x)
-      a.tiles[toff[E] + t] = make_int4(E, P + t * kBN, min(kBN, a.T - t * kBN), 0);
+    for (int t = threadIdx.x; t * tb < a.T; t += blockDim.x)
+      a.tiles[toff[E] + t] = make_int4(E, P + t * tb, min(tb, a.T - t * tb), 0);
     for (int t = threadIdx.x; t < a.T; t += blockDim.x) a.brow[P + t] = t;
   }
   __syncthreads();

@@ -44,24 +44,6 @@ constexpr long long kDrainBudget = 200000000LL;
 __device__ int g_qqmm_error = 0;
 __device__ __forceinline__ void qflag(int code) { atomicCAS(&g_qqmm_error, 0, code); }
 
-// MLX to_fp4_e2m1: round to the nearest E2M1 magnitude with ties to the even
-// code, saturating at 6; NaN -> +6 (code 7); the sign bit from signbit().
-__device__ __forceinline__ uint32_t fp4_code_mlx(float v) {
-  if (isnan(v)) return 0x7u;
-  const uint32_t sign = signbit(v) ? 0x8u : 0u;
-  const float a = fabsf(v);
-  uint32_t m;
-  if (a > 5.0f) m = 7;
-  else if (a >= 3.5f) m = 6;
-  else if (a > 2.5f) m = 5;
-  else if (a >= 1.75f) m = 4;
-  else if (a > 1.25f) m = 3;
-  else if (a >= 0.75f) m = 2;
-  else if (a > 0.25f) m = 1;
-  else m = 0;
-  return m | sign;
-}
-
 __global__ void qx_quantize_kernel(uint8_t* __restrict__ qx, uint8_t* __restrict__ sx,
                                    const void* __restrict__ x, int dtype, int64_t groups) {
   for (int64_t gi = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; gi < groups;

@@ -2,7 +2,8 @@
 quantized_matmul for M > 8 rows (BASELINE config[0] at M=512) and the
 sorted-expert MoE block for T > 8 tokens (config[3] at T=512), against the
 fp32 oracle on sampled rows / tokens and against the independent decode-path
-kernels on every token."""
+kernels on every token.  The block runs both ways: the default block-scaled
+FP4 path (activations as four NVFP4 terms) and the exact 16-bit path."""
 import importlib
 
 import numpy as np
@@ -79,13 +80,15 @@ def oracle_tokens(orc, raw, x, inds, wts, tokens, residual=None):
                                   scaling=2.5, residual=res)
 
 
+@pytest.mark.parametrize("exact", [False, True])
 @pytest.mark.parametrize("T", [9, 64, 512])
-def test_prefill_block_vs_oracle_and_decode_path(nv, orc, layer, T):
+def test_prefill_block_vs_oracle_and_decode_path(nv, orc, layer, T, exact):
     lag, block, raw = layer
     g = torch.Generator(device=DEV).manual_seed(T)
     x = torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16)
     res = torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16)
-    y, inds, wts = block(x, residual=res, return_routing=True)
+    with nv.launch_flags(exact_prefill=exact):
+        y, inds, wts = block(x, residual=res, return_routing=True)
     nv.device_status()
     assert torch.isfinite(y.float()).all()
     # Oracle on sampled tokens (tokens are independent).
@@ -101,8 +104,9 @@ def test_prefill_block_vs_oracle_and_decode_path(nv, orc, layer, T):
                  max_abs=4e-2, what=f"prefill T={T} vs decode path")
 
 
-def test_prefill_given_routing_with_skew(nv, orc, layer):
-    """Heavily skewed routing: one expert takes every token (tiles > 64 tokens)."""
+@pytest.mark.parametrize("exact", [False, True])
+def test_prefill_given_routing_with_skew(nv, orc, layer, exact):
+    """Heavily skewed routing: one expert takes every token (many tiles per expert)."""
     lag, block, raw = layer
     T = 200
     inds = torch.stack([torch.tensor([5, 9, 17, 33, 64, 100, 200, 255]) for _ in range(T)])
@@ -110,7 +114,23 @@ def test_prefill_given_routing_with_skew(nv, orc, layer):
     wts = torch.softmax(torch.randn(T, 8), dim=-1)
     inds, wts = inds.to(torch.int32).to(DEV), wts.to(DEV)
     x = torch.randn(T, 2048, device=DEV).to(torch.bfloat16)
-    y = block(x, inds=inds, weights=wts)
-    tokens = np.array([0, 63, 64, 127, 128, 199])
+    with nv.launch_flags(exact_prefill=exact):
+        y = block(x, inds=inds, weights=wts)
+    tokens = np.array([0, 31, 32, 63, 64, 127, 128, 199])
     want = oracle_tokens(orc, raw, x, inds, wts, tokens)
     assert_close(y.float().cpu().numpy()[tokens], want, what="skewed routing")
+
+
+def test_prefill_fp4_terms_close_to_exact_path(nv, layer):
+    """The four-term FP4 path against the exact 16-bit path on the same
+    routing: both round to bf16, so they differ by bf16 rounding flips only
+    (relative-L2 well under 1e-3, the terms themselves ~5e-5)."""
+    lag, block, raw = layer
+    g = torch.Generator(device=DEV).manual_seed(4)
+    x = torch.randn(512, 2048, generator=g, device=DEV).to(torch.bfloat16)
+    y0, inds, wts = block(x, return_routing=True)
+    with nv.launch_flags(exact_prefill=True):
+        y1 = block(x, inds=inds.view(torch.int32), weights=wts)
+    nv.device_status()
+    assert_close(y0.float().cpu().numpy(), y1.float().cpu().numpy(), max_abs=4e-2, rel_l2=1e-3,
+                 what="fp4 terms vs exact")
