@@ -107,26 +107,38 @@ def bench_prefill(torch, nv, lag, cfg, dev, steps, warmup, layers, distinct=4, T
         for l in range(layers):
             blocks[l % distinct](x, residual=res, out=y)
 
-    for _ in range(max(warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms_step = e0.elapsed_time(e1) / steps
+    def timed(exact):
+        with nv.launch_flags(exact_prefill=exact):
+            for _ in range(max(warmup, 3)):
+                step()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(steps):
+                step()
+            e1.record()
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    ms_step = timed(False)            # default: block-scaled FP4 GEMMs
+    ms_exact = timed(True)            # exact 16-bit path, for comparison
     us_layer = ms_step * 1e3 / layers
     # Every expert is hit at T=512 (4096 random pairs over 256 experts).
     layer_w = (cfg.n_experts * cfg.routed_bytes_per_expert() + cfg.shared_bytes() +
                cfg.router_bytes())
     layer_b = layer_w + 3 * T * cfg.hidden * 2
+    peak, peak_kind = measured_peak_hbm()
     return {"workload": f"BASELINE config[3] on 1 GPU: sparse block T={T} (router top-8, 256 "
                         f"experts, shared expert, residual), {layers} layers per step "
                         f"({distinct} distinct layers cycled)",
+            "path": "block-scaled FP4 tensor cores (tcgen05 kind::mxf4nvf4), activations as "
+                    "four NVFP4 terms",
             "tok_per_s": T / (ms_step / 1e3), "us_per_layer": us_layer,
             "hbm_gbs_equiv": layer_b / (us_layer / 1e6) / 1e9,
+            "hbm_frac": layer_b / (us_layer / 1e6) / 1e9 / peak,
+            "hbm_peak_gbs": peak, "hbm_peak_source": peak_kind,
+            "us_per_layer_exact_path": ms_exact * 1e3 / layers,
+            "tok_per_s_exact_path": T / (ms_exact / 1e3),
             "bytes_per_layer": layer_b, "steps": steps, "layers_per_step": layers,
             "unit": "tok/s"}
 

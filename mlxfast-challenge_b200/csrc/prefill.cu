@@ -615,11 +615,13 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(SortArgs a) {
   __shared__ int cnt[1024];
   __shared__ int off[1024];
   __shared__ int toff[1025];
+  __shared__ int wsum[32], wtsum[32];
   pdl_wait();
   pdl_trigger();
   const int E = a.E;
   const int tb = a.tile_tokens > 0 ? a.tile_tokens : kBN;  // tokens per tile
   const int P = a.P;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
@@ -628,17 +630,53 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(SortArgs a) {
     else flag(5);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, tacc = 0;
-    for (int e = 0; e < E; e++) {
-      off[e] = acc;
-      toff[e] = tacc;
-      acc += cnt[e];
-      tacc += (cnt[e] + tb - 1) / tb;
+  // Exclusive prefix sums over the experts (E <= 1024 = blockDim.x) of the
+  // pair counts and of the tile counts: warp scans, then a scan of the warp
+  // totals.
+  {
+    const int e = threadIdx.x;
+    const int c = e < E ? cnt[e] : 0;
+    const int tc = (c + tb - 1) / tb;
+    int sc = c, st = tc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int vc = __shfl_up_sync(0xffffffffu, sc, o);
+      const int vt = __shfl_up_sync(0xffffffffu, st, o);
+      if (lane >= o) {
+        sc += vc;
+        st += vt;
+      }
     }
-    toff[E] = tacc;
-    const int tsh = a.with_shared ? (a.T + tb - 1) / tb : 0;
-    *a.ntiles = tacc + tsh;
+    if (lane == 31) {
+      wsum[warp] = sc;
+      wtsum[warp] = st;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      int wc = wsum[lane], wt = wtsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int vc = __shfl_up_sync(0xffffffffu, wc, o);
+        const int vt = __shfl_up_sync(0xffffffffu, wt, o);
+        if (lane >= o) {
+          wc += vc;
+          wt += vt;
+        }
+      }
+      wsum[lane] = wc - wsum[lane];    // exclusive over warps
+      wtsum[lane] = wt - wtsum[lane];
+    }
+    __syncthreads();
+    if (e < E) {
+      off[e] = wsum[warp] + sc - c;
+      toff[e] = wtsum[warp] + st - tc;
+      if (e == E - 1) {
+        const int tacc = toff[e] + tc;
+        toff[E] = tacc;
+        const int tsh = a.with_shared ? (a.T + tb - 1) / tb : 0;
+        *a.ntiles = tacc + tsh;
+      }
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {

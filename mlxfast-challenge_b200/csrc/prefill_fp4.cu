@@ -159,17 +159,19 @@ __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
         m = wmax[t & 1][0];
         for (int w = 1; w < nw; w++) m = fmaxf(m, wmax[t & 1][w]);
       }
-      int ex = 0;
-      float P = 0.f;
-      if (m > 0.f && m < INFINITY) {
-        (void)frexpf(m, &ex);
-        P = ldexpf(1.0f, 11 - ex);  // m * P in [1024, 2048)
-      }
-      fac[t] = P > 0.f ? 1.0f / P : 0.f;
-      const uint32_t b = P > 0.f ? e4m3_ceil(amax * P / 6.0f) : 0u;
+      // P = 2^(10 - floor(log2 m)): m * P in [1024, 2048).  Exponent
+      // arithmetic on normal floats (rows whose max is below 2^-100, zero or
+      // not finite get no terms).
+      const int em = (__float_as_int(m) >> 23) & 0xFF;  // biased exponent of m
+      const bool live = m >= 7.9e-31f && m < INFINITY;
+      const float P = live ? __int_as_float((127 + 10 - (em - 127)) << 23) : 0.f;
+      fac[t] = live ? __int_as_float((127 - 10 + (em - 127)) << 23) : 0.f;  // 1 / P
+      const uint32_t b = live ? e4m3_ceil(amax * P * (1.0f / 6.0f)) : 0u;
       const float s = scale_to_f32(b);
-      const float inv = s > 0.f ? P / s : 0.f;
-      const float back = s > 0.f ? s / P : 0.f;
+      // |v * inv| <= 6 up to rounding (the converter saturates there); the
+      // residual below uses the exact value the code stands for
+      const float inv = s > 0.f ? P * __frcp_rn(s) : 0.f;
+      const float back = s > 0.f ? s * fac[t] : 0.f;
       uint32_t w[2] = {0u, 0u};
 #pragma unroll
       for (int j = 0; j < 16; j += 2) {
