@@ -147,12 +147,17 @@ __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
     uint2 code[kT];
     uint32_t sb[kT];
     float fac[kT];
+    // A row holding NaN or +-inf keeps the reference's non-finite result: its
+    // terms are written with NaN factors (the row max is forced to +inf).
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < 16; j++) bad |= !isfinite(v[j]);
 #pragma unroll
     for (int t = 0; t < kT; t++) {
       float amax = 0.f;
 #pragma unroll
       for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(v[j]));
-      float m = warp_max(amax);
+      float m = warp_max(bad ? INFINITY : amax);
       if (nw > 1) {
         if (lane == 0) wmax[t & 1][warp] = m;
         __syncthreads();
@@ -165,13 +170,14 @@ __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
       const int em = (__float_as_int(m) >> 23) & 0xFF;  // biased exponent of m
       const bool live = m >= 7.9e-31f && m < INFINITY;
       const float P = live ? __int_as_float((127 + 10 - (em - 127)) << 23) : 0.f;
-      fac[t] = live ? __int_as_float((127 - 10 + (em - 127)) << 23) : 0.f;  // 1 / P
+      fac[t] = live ? __int_as_float((127 - 10 + (em - 127)) << 23)  // 1 / P
+                    : (m == INFINITY ? __int_as_float(0x7fc00000) : 0.f);
       const uint32_t b = live ? e4m3_ceil(amax * P * (1.0f / 6.0f)) : 0u;
       const float s = scale_to_f32(b);
       // |v * inv| <= 6 up to rounding (the converter saturates there); the
       // residual below uses the exact value the code stands for
       const float inv = s > 0.f ? P * __frcp_rn(s) : 0.f;
-      const float back = s > 0.f ? s * fac[t] : 0.f;
+      const float back = s > 0.f ? s * fac[t] : 0.f;  // s > 0 only for live rows
       uint32_t w[2] = {0u, 0u};
 #pragma unroll
       for (int j = 0; j < 16; j += 2) {

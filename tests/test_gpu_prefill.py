@@ -134,3 +134,24 @@ def test_prefill_fp4_terms_close_to_exact_path(nv, layer):
     nv.device_status()
     assert_close(y0.float().cpu().numpy(), y1.float().cpu().numpy(), max_abs=4e-2, rel_l2=1e-3,
                  what="fp4 terms vs exact")
+
+
+@pytest.mark.parametrize("exact", [False, True])
+def test_prefill_non_finite_rows_propagate(nv, layer, exact):
+    """A token whose activations hold NaN or inf gives a non-finite output row,
+    as in the reference; the other tokens are unaffected."""
+    lag, block, raw = layer
+    g = torch.Generator(device=DEV).manual_seed(8)
+    x = torch.randn(40, 2048, generator=g, device=DEV).to(torch.bfloat16)
+    y0, inds, wts = block(x, return_routing=True)
+    x[3, 100] = float("nan")
+    x[7, 5] = float("inf")
+    with nv.launch_flags(exact_prefill=exact):
+        y = block(x, inds=inds.view(torch.int32), weights=wts)
+    nv.device_status()
+    bad = ~torch.isfinite(y.float()).all(dim=1)
+    assert bad[3] and bad[7]
+    keep = [i for i in range(40) if i not in (3, 7)]
+    assert torch.isfinite(y[keep].float()).all()
+    assert_close(y[keep].float().cpu().numpy(), y0[keep].float().cpu().numpy(), max_abs=4e-2,
+                 what="finite rows unchanged")
