@@ -26,13 +26,13 @@
 //   (mode 1: 64 gate rows + the same 64 up rows; mode 2: 128 down rows):
 //     TMA warp       per 256-wide K slab: the tile's weight codes + scales and
 //                    its 128 term rows (32 slots x 4 terms) + scales, into a
-//                    5-deep ring (128-byte swizzled K-major);
+//                    4-deep ring (128-byte swizzled K-major);
 //     scale warps    (4) copy each stage's scale bytes into tensor memory in
 //                    the layout the block-scaled MMA reads (scale of row m,
 //                    block j at lanes m % 32 + 32 r, r = 0..3, column m / 32,
 //                    byte j);
 //     MMA thread     4 tcgen05.mma per slab (M=128, N = 4 x slots, K=64) into
-//                    one of two TMEM accumulators;
+//                    one of three TMEM accumulators;
 //     epilogue       (4 warps) accumulator column 4 j + t holds term t of slot
 //                    j: y = sum_t fac * D.  Mode 2 writes Y[slot][row]; mode 1
 //                    passes gate and up values through shared memory (the
@@ -51,7 +51,8 @@ constexpr int kT = kFp4Terms;
 constexpr int kFBM = 128;                  // weight rows per tile (MMA M)
 constexpr int kFTok = kFp4TileTokens;      // slots per tile
 constexpr int kFRows = kT * kFTok;         // term rows per tile = max MMA N (128)
-constexpr int kFStages = 5;
+constexpr int kFStages = 4;
+constexpr int kFBufs = 3;                  // accumulators: the epilogue trails the MMA by up to two tiles
 constexpr int kFA = kFBM * 128;            // weight codes of one slab: 16 KB
 constexpr int kFB = kFRows * 128;          // term-row codes of one slab: 16 KB
 constexpr int kFSA = kFBM * 16;            // weight scales: 2 KB
@@ -63,7 +64,7 @@ constexpr int kWarpTma = 0, kWarpMma = 1, kWarpEpi0 = 6;  // warps 2-5: scale fa
 constexpr int kFAcc = 128;                 // accumulator columns (one buffer)
 constexpr int kFSf = 32;                   // scale columns per stage: 16 A + 16 B
 constexpr int kFTmem = 512;
-static_assert(2 * kFAcc + kFStages * kFSf <= kFTmem, "TMEM budget");
+static_assert(kFBufs * kFAcc + kFStages * kFSf <= kFTmem, "TMEM budget");
 constexpr int kGuPitch = kFTok + 1;        // gate/up exchange rows (bank-conflict free)
 constexpr int kErrTimeout = 4;
 constexpr long long kDrainBudget = 200000000LL;
@@ -259,10 +260,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
   uint64_t* empty = full + kFStages;
   uint64_t* sf_ready = empty + kFStages;
   uint64_t* acc_full = sf_ready + kFStages;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* drain = acc_empty + 2;
+  uint64_t* acc_empty = acc_full + kFBufs;
+  uint64_t* drain = acc_empty + kFBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-  int4* sTiles = reinterpret_cast<int4*>(tmem_slot + 4);  // [a.max_tiles] tile list
+  // [a.max_tiles] tile list, 16-byte aligned for the int4 accesses
+  int4* sTiles = reinterpret_cast<int4*>(
+      (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 15) & ~static_cast<uintptr_t>(15));
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -271,7 +274,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       mbar_init(&empty[i], 1);
       mbar_init(&sf_ready[i], 4);
     }
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < kFBufs; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
     }
@@ -301,7 +304,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tsf = tmem + 2 * kFAcc;  // stage s: tsf + kFSf * s
+  const uint32_t tsf = tmem + kFBufs * kFAcc;  // stage s: tsf + kFSf * s
   const int nslab = a.K / 256;
 
   if (warp == kWarpTma) {
@@ -360,8 +363,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
     for (int u = blockIdx.x; u < ntot && ok; u += gridDim.x) {
       FTile ti;
       if (!f_tile(a, sTiles, u, m_tiles, ti)) continue;
-      const int buf = j & 1;
-      if (j >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((j >> 1) - 1) & 1)) {
+      const int buf = j % kFBufs;
+      if (j >= kFBufs && !mbar_wait_bounded(&acc_empty[buf], ((j / kFBufs) - 1) & 1)) {
         if (el) fflag(kErrTimeout);
         break;
       }
@@ -459,11 +462,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
       const float fcur = fnext;
       un = next_tile(u + gridDim.x, tn);
       fnext = (un < ntot && et < kT * tn.count) ? a.bfac[(int64_t)tn.start * kT + et] : 0.f;
-      const int buf = j & 1;
+      const int buf = j % kFBufs;
       named_sync(2, 128);
       sFac[et] = fcur;
       named_sync(2, 128);
-      const bool got = mbar_wait_bounded(&acc_full[buf], (j >> 1) & 1);
+      const bool got = mbar_wait_bounded(&acc_full[buf], (j / kFBufs) & 1);
       if (!got && lane == 0) fflag(kErrTimeout);
       if (!sync_and(2, 128, got)) break;
       tc_fence_after();
@@ -531,7 +534,7 @@ cudaError_t launch_pdl_f(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStre
 
 size_t gemm_fp4_smem_bytes(int max_tiles) {
   return 1024 + (size_t)kFStages * kFStage + 2 * 64 * kGuPitch * sizeof(float) +
-         kFRows * sizeof(float) + (3 * kFStages + 5) * 8 + 16 + (size_t)max_tiles * 16;
+         kFRows * sizeof(float) + (3 * kFStages + 2 * kFBufs + 1) * 8 + 16 + 16 + (size_t)max_tiles * 16;
 }
 
 cudaError_t launch_rows_to_terms(const TermsArgs& a, cudaStream_t stream) {
