@@ -63,6 +63,16 @@ class ExpertParallelBlock:
     def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
                  routing: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
         ops = self.ops
+        # The shared expert needs neither the routing nor the exchange: it
+        # runs on a side stream, overlapping the all-to-alls (which leave most
+        # SMs idle) and the local experts.
+        side = self._side_stream(x)
+        if side is not None:
+            side.wait_stream(torch.cuda.current_stream(x.device))
+            with torch.cuda.stream(side):
+                shared = ops.shared(x)
+        else:
+            shared = ops.shared(x)
         inds, wts = routing if routing is not None else ops.route(x)
         send_x, send_ids, pos, send_counts = ops.dispatch(x, inds, self.world)
         # Counts travel as int64 on the exchange's device; the row splits are
@@ -74,8 +84,18 @@ class ExpertParallelBlock:
         recv_ids = exchange(send_ids, sc_h, rc_h, self.group)
         y_recv = ops.experts(recv_x, recv_ids)
         y_back = exchange(y_recv, rc_h, sc_h, self.group)
-        shared = ops.shared(x)
+        if side is not None:
+            torch.cuda.current_stream(x.device).wait_stream(side)
+            if shared is not None:
+                shared.record_stream(torch.cuda.current_stream(x.device))
         return ops.combine(y_back, pos, wts, shared, residual)
+
+    def _side_stream(self, x: torch.Tensor):
+        if not x.is_cuda:
+            return None
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=x.device)
+        return self._side
 
 
 class CudaEPOps:
