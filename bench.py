@@ -144,7 +144,7 @@ def bench_prefill(torch, nv, lag, cfg, dev, steps, warmup, layers, distinct=4, T
 
 
 def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers, distinct=2,
-                     T=512):
+                     T=512, form="gather"):
     """config[3] expert-parallel: every rank holds E/world experts, the router
     and the shared expert, and runs the sparse block for its own T tokens; the
     (token, slot) rows cross to their experts' ranks and back by NCCL
@@ -157,11 +157,17 @@ def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers,
         # this rank's expert slice as its own tensors, so the other experts
         # are freed (256/world experts resident per GPU)
         local = {k: v.clone() for k, v in ep.local_slice(raw["routed"], rank, world).items()}
-        ops = ep.CudaEPOps(local, raw["shared"], raw["router_w"], raw["router_b"],
-                           cfg.n_experts, rank, world)
+        if form == "gather":
+            ops = ep.CudaGatherEPOps(local, raw["shared"], raw["router_w"], raw["router_b"],
+                                     cfg.n_experts, rank, world)
+            blk = ep.GatherEPBlock(ops)
+        else:
+            ops = ep.CudaEPOps(local, raw["shared"], raw["router_w"], raw["router_b"],
+                               cfg.n_experts, rank, world)
+            blk = ep.ExpertParallelBlock(ops)
         del raw
         torch.cuda.empty_cache()
-        blocks.append(ep.ExpertParallelBlock(ops))
+        blocks.append(blk)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     x = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
     res = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
@@ -185,10 +191,13 @@ def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers,
     t = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = float(t.item())
+    exchange = ("NCCL all-gather of tokens + routing, per-rank partial sums over its "
+                "experts, NCCL reduce-scatter" if form == "gather" else
+                "NCCL all-to-all dispatch/combine")
     return {"workload": f"BASELINE config[3] expert-parallel over {world} GPUs: sparse block "
                         f"T={T} tokens per GPU (router top-8, {cfg.n_experts // world} experts "
-                        f"per GPU, shared expert, residual), {layers} layers per step, NCCL "
-                        f"all-to-all dispatch/combine", "n_gpus": world,
+                        f"per GPU, shared expert, residual), {layers} layers per step, "
+                        f"{exchange}", "n_gpus": world, "form": form,
             "tok_per_s": world * T / (ms_step / 1e3), "us_per_layer": ms_step * 1e3 / layers,
             "scaling": "weak", "unit": "tok/s", "steps": steps}
 
@@ -523,7 +532,11 @@ def main():
     if world > 1 and args.workload == "all":
         # every rank takes part (the exchange is collective)
         prefill_ep = bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world,
-                                      args.prefill_steps, cfg.num_sparse_layers)
+                                      args.prefill_steps, cfg.num_sparse_layers, form="gather")
+        a2a = bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, args.prefill_steps,
+                               cfg.num_sparse_layers, form="all2all")
+        prefill_ep["all2all_form"] = {"tok_per_s": a2a["tok_per_s"],
+                                      "us_per_layer": a2a["us_per_layer"]}
     if rank == 0 and world == 1 and args.workload == "all":
         del chain
         torch.cuda.empty_cache()

@@ -297,6 +297,32 @@ NVFP4MOE_API int moe_ep_combine(void* y, const void* y_pairs, const int32_t* pos
                                 int dtype, int64_t T, int k, int64_t H, float scaling,
                                 nvfp4_stream stream);
 
+/* Expert parallelism, gather / reduce-scatter form (the alternative to
+ * moe_ep_dispatch / moe_ep_combine): every rank holds all ranks' tokens
+ * (all-gathered with their routing) and computes, for every token, the
+ * contribution of its own experts [expert_base, expert_base + L->n_experts):
+ *   y_partial[t] = routed_scaling * sum_{j: inds[t][j] local} w[t][j] * e_j(x_t)
+ *                  (+ shared(x_t) for t in [shared_row0, shared_row0 + shared_rows))
+ * in f32 (inds are global expert ids; other ids are skipped).  L holds this
+ * rank's routed slice and, when L->shared_inter > 0, the shared expert, which
+ * this rank applies to its own rows only.  x rows are x_ld elements apart.  A
+ * reduce-scatter (sum) of y_partial over the ranks then gives each rank its
+ * tokens' block output; moe_ep_finish adds the residual.  Prefill shapes only (T > 8, the block-scaled FP4 path).  The
+ * reference runs every expert on one device; single-device analogue:
+ * moe_block_forward (Laguna.swift:204-212). */
+NVFP4MOE_API size_t moe_ep_partial_workspace_size(const moe_layer_desc* layer, int64_t T);
+NVFP4MOE_API int moe_ep_partial_forward(float* y_partial, const void* x, int64_t x_ld,
+                                        int dtype, int64_t T, const moe_layer_desc* layer,
+                                        const uint32_t* inds, const float* weights,
+                                        int64_t expert_base, int64_t shared_row0,
+                                        int64_t shared_rows, void* workspace,
+                                        size_t workspace_bytes, nvfp4_stream stream);
+/* y[T, H] = partial (f32) + shared (or NULL) + residual (or NULL), rounded
+ * once to dtype. */
+NVFP4MOE_API int moe_ep_finish(void* y, const float* partial, const void* shared,
+                               const void* residual, int dtype, int64_t T, int64_t H,
+                               nvfp4_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,10 @@ SIGNATURES = {
     "nvfp4_quantized_matmul": (_I, [_P, _P, _I, _P, _P, _I64, _I64, _I64, _P]),
     "nvfp4_quantize_activations": (_I, [_P, _P, _P, _I, _I64, _I64, _P]),
     "nvfp4_qqmm_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64]),
+    "moe_ep_partial_workspace_size": (ctypes.c_size_t, [_P, _I64]),
+    "moe_ep_partial_forward": (_I, [_P, _P, _I64, _I, _I64, _P, _P, _P, _I64, _I64, _I64, _P,
+                                    ctypes.c_size_t, _P]),
+    "moe_ep_finish": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _P]),
     "nvfp4_qqmm": (_I, [_P, _P, _I, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     "nvfp4_gather_qmm": (_I, [_P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                               _I, _P]),

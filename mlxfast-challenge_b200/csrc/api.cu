@@ -577,7 +577,8 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
 // between, then the same combine.
 static int prefill_fp4_tail(void* y, const void* x, const void* residual, int dtype, int64_t T,
                             const moe_layer_desc* L, const float* wts, char* ws,
-                            const BlockLayout& B, cudaStream_t s) {
+                            const BlockLayout& B, cudaStream_t s, int64_t x_ld, int out_dtype,
+                            int64_t sh_row0, int64_t sh_rows) {
   const char* op = "moe_block";
   const int64_t H = L->hidden, I = L->inter, E = L->n_experts, Is = L->shared_inter;
   const bool sh = Is > 0;
@@ -599,11 +600,13 @@ static int prefill_fp4_tail(void* y, const void* x, const void* residual, int dt
   tx.src_dtype = dtype;
   tx.rows = T;
   tx.K = H;
-  tx.src_ld = H;
+  tx.src_ld = x_ld;
   tx.dst_map = pos;  // token t feeds slots pos[t * k + j]
   tx.map_stride = (int)L->top_k;
   tx.map_count = (int)L->top_k;
-  tx.extra_base = sh ? B.P : -1;  // and its shared-expert slot P + t
+  tx.extra_base = sh ? B.P : -1;  // and its shared-expert slot P + (t - sh_row0)
+  tx.extra_lo = sh_row0;
+  tx.extra_hi = sh_row0 + sh_rows;
   tx.codes = xtc;
   tx.scales = xts;
   tx.fac = xtf;
@@ -681,6 +684,7 @@ static int prefill_fp4_tail(void* y, const void* x, const void* residual, int dt
   ta.src_ld = B.act_ld;
   ta.dst_map = nullptr;
   ta.extra_base = -1;  // identity: slot r
+  ta.extra_lo = ta.extra_hi = 0;
   ta.codes = atc;
   ta.scales = ats;
   ta.fac = atf;
@@ -700,7 +704,9 @@ static int prefill_fp4_tail(void* y, const void* x, const void* residual, int dt
   c.scaling = L->routed_scaling;
   c.residual = residual;
   c.y = y;
-  c.dtype = dtype;
+  c.dtype = out_dtype;
+  c.sh_row0 = (int)sh_row0;
+  c.sh_rows = (int)sh_rows;
   return check_cuda(nvfp4::launch_moe_combine(c, s, true), op);
 }
 
@@ -741,7 +747,7 @@ static int prefill_impl(void* y, const void* x, const void* residual, int dtype,
   const bool fp4 = use_fp4_terms() && B.fp4;
   sa.tile_tokens = fp4 ? nvfp4::kFp4TileTokens : 0;
   if (int r = check_cuda(nvfp4::launch_moe_sort(sa, s, pdl_first), op)) return r;
-  if (fp4) return prefill_fp4_tail(y, x, residual, dtype, T, L, wts, ws, B, s);
+  if (fp4) return prefill_fp4_tail(y, x, residual, dtype, T, L, wts, ws, B, s, H, dtype, 0, T);
 
   // x rows in slot order (shared-expert slots P.. hold tokens 0..T-1).
   nvfp4::RowsArgs rx{};
@@ -1033,6 +1039,72 @@ extern "C" int moe_block_forward_noalloc(void* y, const void* x, const void* res
   if (e != cudaSuccess) return check_cuda(e, op);
   return moe_block_forward(y, x, residual, dtype, T, L, inds_in, weights_in, inds_out,
                            weights_out, ws, kNoAllocScratchBytes, stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Expert-parallel block over all ranks' tokens (gather / reduce-scatter form).
+extern "C" {
+
+size_t moe_ep_partial_workspace_size(const moe_layer_desc* L, int64_t T) {
+  if (!L || T <= 0) return 0;
+  return block_layout(L, T).total;
+}
+
+int moe_ep_partial_forward(float* y_partial, const void* x, int64_t x_ld, int dtype, int64_t T,
+                           const moe_layer_desc* L, const uint32_t* inds, const float* weights,
+                           int64_t expert_base, int64_t shared_row0, int64_t shared_rows,
+                           void* workspace, size_t workspace_bytes, nvfp4_stream stream) {
+  const char* op = "moe_ep_partial";
+  if (int r = check_layer(op, L, dtype, T)) return r;
+  if (T == 0) return NVFP4_OK;
+  if (!y_partial || !x || !inds || !weights)
+    return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  if (x_ld < L->hidden || expert_base < 0)
+    return fail(NVFP4_ERR_INVALID, "[%s] invalid x_ld or expert_base.", op);
+  const bool sh = L->shared_inter > 0;
+  if (sh && (shared_row0 < 0 || shared_rows <= 0 || shared_row0 + shared_rows > T))
+    return fail(NVFP4_ERR_INVALID, "[%s] shared rows outside the batch.", op);
+  const BlockLayout B = block_layout(L, T);
+  const int esz = dtype == NVFP4_F32 ? 4 : 2;
+  if (!B.prefill || !B.fp4 || !aligned16(x) || (x_ld * esz) % 16 || !aligned16(y_partial))
+    return fail(NVFP4_ERR_UNSUPPORTED,
+                "[%s] needs T > 8 tokens, Laguna-sized layers and 16-byte aligned rows.", op);
+  if (!workspace || workspace_bytes < B.total)
+    return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, B.total);
+  char* ws = static_cast<char*>(workspace);
+  cudaStream_t s = (cudaStream_t)stream;
+  nvfp4::SortArgs sa{};
+  sa.inds = inds;
+  sa.T = (int)T;
+  sa.k = (int)L->top_k;
+  sa.E = (int)L->n_experts;
+  sa.P = (int)B.P;
+  sa.with_shared = sh ? 1 : 0;
+  sa.sh_row0 = sh ? (int)shared_row0 : 0;
+  sa.sh_rows = sh ? (int)shared_rows : 0;
+  sa.brow = reinterpret_cast<int*>(ws + B.brow_off);
+  sa.pos = reinterpret_cast<int*>(ws + B.pos_off);
+  sa.tiles = reinterpret_cast<int4*>(ws + B.tiles_off);
+  sa.ntiles = reinterpret_cast<int*>(ws + B.ntiles_off);
+  sa.tile_tokens = nvfp4::kFp4TileTokens;
+  sa.e_base = (int)expert_base;
+  sa.skip_foreign = 1;
+  if (int r = check_cuda(nvfp4::launch_moe_sort(sa, s, first_pdl()), op)) return r;
+  return prefill_fp4_tail(y_partial, x, nullptr, dtype, T, L, weights, ws, B, s, x_ld,
+                          NVFP4_F32, sh ? shared_row0 : 0, sh ? shared_rows : 0);
+}
+
+int moe_ep_finish(void* y, const float* partial, const void* shared, const void* residual,
+                  int dtype, int64_t T, int64_t H, nvfp4_stream stream) {
+  if (!valid_dtype(dtype)) return fail(NVFP4_ERR_INVALID, "[moe_ep_finish] invalid dtype.");
+  if (T < 0 || H <= 0) return fail(NVFP4_ERR_INVALID, "[moe_ep_finish] invalid shape.");
+  if (T > 0 && (!y || !partial))
+    return fail(NVFP4_ERR_INVALID, "[moe_ep_finish] null pointer argument.");
+  return check_cuda(nvfp4::launch_ep_finish(y, partial, shared, residual, dtype, T, H,
+                                            (cudaStream_t)stream),
+                    "moe_ep_finish");
 }
 
 }  // extern "C"

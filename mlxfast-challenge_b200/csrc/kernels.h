@@ -179,6 +179,10 @@ struct EpCombineArgs {
 cudaError_t launch_ep_plan(const EpPlanArgs& a, cudaStream_t stream);
 cudaError_t launch_ep_pack(const EpPackArgs& a, cudaStream_t stream);
 cudaError_t launch_ep_combine(const EpCombineArgs& a, cudaStream_t stream);
+// y[T, H] = partial (f32) + shared + residual, rounded once to dtype.
+cudaError_t launch_ep_finish(void* y, const float* partial, const void* shared,
+                             const void* residual, int dtype, int64_t T, int64_t H,
+                             cudaStream_t stream);
 cudaError_t read_and_clear_ep_error(int* out);
 
 struct SortArgs {
@@ -189,6 +193,11 @@ struct SortArgs {
   int4* tiles;
   int* ntiles;
   int tile_tokens;  // tokens per tile (0: the f16 GEMM's 64)
+  // Expert-parallel partial block: ids are global, this rank's experts are
+  // [e_base, e_base + E); other ids are skipped (slot -1) without an error.
+  int e_base, skip_foreign;
+  // shared-expert group over rows [sh_row0, sh_row0 + sh_rows) (sh_rows 0: all T)
+  int sh_row0, sh_rows;
 };
 
 // Activation rows as a sum of kFp4Terms NVFP4 terms (prefill_fp4.cu):
@@ -205,6 +214,7 @@ struct TermsArgs {
   const int* dst_map;
   int map_stride, map_count;
   int64_t extra_base;
+  int64_t extra_lo, extra_hi;  // rows that also feed extra_base + (r - extra_lo)
   uint8_t* codes;   // [slots * 4, K/2]  (term row = slot * 4 + t)
   uint8_t* scales;  // [slots * 4, K/16]
   float* fac;       // [slots * 4]: value = fac * dequant(codes, scales)
@@ -234,6 +244,7 @@ struct CombineArgs {
   const void* residual;
   void* y;
   int dtype;
+  int sh_row0, sh_rows;  // shared-expert rows (sh_rows 0: all T)
 };
 
 size_t gemm_smem_bytes();

@@ -625,9 +625,9 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(SortArgs a) {
   for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
-    const uint32_t e = a.inds[p];
+    const uint32_t e = a.inds[p] - (uint32_t)a.e_base;
     if (e < (uint32_t)E) atomicAdd(&cnt[e], 1);
-    else flag(5);
+    else if (!a.skip_foreign) flag(5);
   }
   __syncthreads();
   // Exclusive prefix sums over the experts (E <= 1024 = blockDim.x) of the
@@ -673,7 +673,8 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(SortArgs a) {
       if (e == E - 1) {
         const int tacc = toff[e] + tc;
         toff[E] = tacc;
-        const int tsh = a.with_shared ? (a.T + tb - 1) / tb : 0;
+        const int shn = a.sh_rows > 0 ? a.sh_rows : a.T;
+        const int tsh = a.with_shared ? (shn + tb - 1) / tb : 0;
         *a.ntiles = tacc + tsh;
       }
     }
@@ -686,13 +687,14 @@ __global__ void __launch_bounds__(1024) moe_sort_kernel(SortArgs a) {
     cnt[e] = 0;  // reused as the scatter cursor
   }
   if (a.with_shared) {
-    for (int t = threadIdx.x; t * tb < a.T; t += blockDim.x)
-      a.tiles[toff[E] + t] = make_int4(E, P + t * tb, min(tb, a.T - t * tb), 0);
-    for (int t = threadIdx.x; t < a.T; t += blockDim.x) a.brow[P + t] = t;
+    const int shn = a.sh_rows > 0 ? a.sh_rows : a.T;
+    for (int t = threadIdx.x; t * tb < shn; t += blockDim.x)
+      a.tiles[toff[E] + t] = make_int4(E, P + t * tb, min(tb, shn - t * tb), 0);
+    for (int t = threadIdx.x; t < shn; t += blockDim.x) a.brow[P + t] = a.sh_row0 + t;
   }
   __syncthreads();
   for (int p = threadIdx.x; p < P; p += blockDim.x) {
-    const uint32_t e = a.inds[p];
+    const uint32_t e = a.inds[p] - (uint32_t)a.e_base;
     if (e >= (uint32_t)E) {
       a.pos[p] = -1;
       continue;
@@ -726,8 +728,9 @@ __global__ void moe_combine_kernel(CombineArgs a) {
     }
 #pragma unroll
     for (int q = 0; q < 8; q++) acc[q] *= a.scaling;
-    if (a.with_shared) {
-      const float4* src = reinterpret_cast<const float4*>(a.Y + (int64_t)(a.P + t) * a.H + h);
+    const int64_t ts = t - a.sh_row0;
+    if (a.with_shared && ts >= 0 && ts < (a.sh_rows > 0 ? a.sh_rows : a.T)) {
+      const float4* src = reinterpret_cast<const float4*>(a.Y + (int64_t)(a.P + ts) * a.H + h);
       const float4 u = src[0], v = src[1];
       acc[0] += u.x; acc[1] += u.y; acc[2] += u.z; acc[3] += u.w;
       acc[4] += v.x; acc[5] += v.y; acc[6] += v.z; acc[7] += v.w;

@@ -141,6 +141,12 @@ __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
   const int64_t cb = K / 2, sbytes = K / 16;  // bytes per term row
   const int grp = 32 * warp + lane;
   for (int64_t r = blockIdx.x; r < a.rows; r += gridDim.x) {
+    const bool extra = a.extra_base >= 0 && r >= a.extra_lo && r < a.extra_hi;
+    if (a.dst_map && !extra) {  // a row no slot reads (expert-parallel: all foreign)
+      bool any = false;
+      for (int d = 0; d < a.map_count; d++) any |= a.dst_map[r * a.map_stride + d] >= 0;
+      if (!any) continue;  // uniform over the CTA
+    }
     float v[16];
     const int64_t e0 = r * a.src_ld + (int64_t)grp * 16;
     load8(a.src, a.src_dtype, e0, *reinterpret_cast<float(*)[8]>(&v[0]));
@@ -202,8 +208,8 @@ __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
         slot = a.dst_map[r * a.map_stride + d];
         if (slot < 0) continue;
       } else {
-        if (a.extra_base < 0) continue;
-        slot = a.extra_base + r;
+        if (!extra) continue;
+        slot = a.extra_base + (r - a.extra_lo);
       }
 #pragma unroll
       for (int t = 0; t < kT; t++) {

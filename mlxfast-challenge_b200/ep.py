@@ -179,3 +179,156 @@ def local_slice(raw_routed: dict, rank: int, world: int) -> dict:
     E = next(iter(raw_routed.values())).shape[0]
     epr = E // world
     return {k: v[rank * epr:(rank + 1) * epr] for k, v in raw_routed.items()}
+
+
+# ---------------------------------------------------------------------------
+# Gather / reduce-scatter form.  Every rank all-gathers all ranks' tokens with
+# their routing (one fixed-size collective), computes for every token the
+# contribution of its own experts (moe_ep_partial_forward: f32 partial sums,
+# foreign experts skipped), and a reduce-scatter sums the partials so each
+# rank receives its own tokens' sum.  The shared expert either joins the
+# partial call as one more group over the rank's own rows (CUDA ops: its GEMM
+# work rides in the same launches) or comes from ops.shared on a side stream;
+# moe_ep_finish adds it, if separate, and the residual.  Sizes are fixed (equal T per rank): no host synchronisation, and
+# the whole call can be captured in a CUDA graph.  Same per-token order of
+# the routed sum as the single-device block within a rank; across ranks the
+# partials add in rank order inside the reduce-scatter.
+
+def gather_rows(t: torch.Tensor, group=None) -> torch.Tensor:
+    """[R, ...] on every rank -> [world * R, ...], rank-major."""
+    world = dist.get_world_size(group)
+    out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype,
+                      device=t.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, t.contiguous(), group=group)
+    else:
+        dist.all_gather(list(out.chunk(world)), t.contiguous(), group=group)
+    return out
+
+
+def reduce_scatter_rows(t: torch.Tensor, group=None) -> torch.Tensor:
+    """[world * R, ...] on every rank -> this rank's [R, ...] block of the sum."""
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    rows = t.shape[0] // world
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((rows,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.reduce_scatter_tensor(out, t.contiguous(), op=dist.ReduceOp.SUM, group=group)
+        return out
+    tmp = t.contiguous().clone()
+    dist.all_reduce(tmp, op=dist.ReduceOp.SUM, group=group)
+    return tmp[rank * rows:(rank + 1) * rows].clone()
+
+
+def pack_tokens(x: torch.Tensor, inds: torch.Tensor, wts: torch.Tensor) -> torch.Tensor:
+    """One byte row per token: x, then the k expert ids (u32), then the k
+    weights (f32) -- 16-byte multiple for Laguna sizes."""
+    T = x.shape[0]
+    xb = x.contiguous().view(torch.uint8).reshape(T, -1)
+    ib = inds.contiguous().to(torch.int32).view(torch.uint8).reshape(T, -1)
+    wb = wts.contiguous().to(torch.float32).view(torch.uint8).reshape(T, -1)
+    return torch.cat([xb, ib, wb], dim=1)
+
+
+def unpack_tokens(rows: torch.Tensor, H: int, k: int, dtype: torch.dtype):
+    esz = torch.empty(0, dtype=dtype).element_size()
+    xb, ib, wb = rows[:, :H * esz], rows[:, H * esz:H * esz + 4 * k], rows[:, H * esz + 4 * k:]
+    return (xb, ib.contiguous().view(torch.int32), wb.contiguous().view(torch.float32))
+
+
+class GatherEPBlock:
+    """One sparse block, expert-parallel over `group` in the gather /
+    reduce-scatter form (see above).  `ops` supplies route, shared, partial
+    and finish."""
+
+    def __init__(self, ops, group=None):
+        self.ops = ops
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self._side = None
+
+    def __call__(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                 routing: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+        ops = self.ops
+        side = None
+        shared = None
+        if getattr(ops, "shared_in_partial", False):
+            pass
+        elif x.is_cuda:
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=x.device)
+            side = self._side
+            side.wait_stream(torch.cuda.current_stream(x.device))
+            with torch.cuda.stream(side):
+                shared = ops.shared(x)
+        else:
+            shared = ops.shared(x)
+        inds, wts = routing if routing is not None else ops.route(x)
+        rows = gather_rows(pack_tokens(x, inds, wts), self.group)
+        T = x.shape[0]
+        part = ops.partial(rows, x.dtype, self.rank * T, T)  # [world * T, H] f32
+        mine = reduce_scatter_rows(part, self.group)  # [T, H] f32
+        if side is not None:
+            torch.cuda.current_stream(x.device).wait_stream(side)
+            if shared is not None:
+                shared.record_stream(torch.cuda.current_stream(x.device))
+        return ops.finish(mine, shared, residual, x.dtype)
+
+
+class CudaGatherEPOps:
+    """Device side of one rank for GatherEPBlock: router, this rank's routed
+    experts and the shared expert (on the rank's own rows) through
+    moe_ep_partial_forward, moe_ep_finish."""
+
+    shared_in_partial = True
+
+    def __init__(self, routed: dict, shared: Optional[dict], router_w: torch.Tensor,
+                 router_b: Optional[torch.Tensor], n_experts: int, rank: int, world: int,
+                 top_k: int = 8, routed_scaling: float = 2.5, norm_topk_prob: bool = True):
+        from . import SparseMoeBlock
+        self.E, self.rank, self.world = n_experts, rank, world
+        self.epr = n_experts // world
+        self.top_k, self.norm = top_k, bool(norm_topk_prob)
+        self.local = SparseMoeBlock(routed, shared, None, None, top_k=top_k,
+                                    routed_scaling=routed_scaling, norm_topk_prob=norm_topk_prob)
+        self.router_w = router_w.contiguous()
+        self.router_b = None if router_b is None else router_b.to(torch.float32).contiguous()
+        self.H = self.local.H
+        self._ws = {}
+
+    def _stream(self, t):
+        return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+    def route(self, x):
+        from . import moe_router_topk
+        return moe_router_topk(x, self.router_w, self.router_b, self.top_k, self.norm)
+
+    def partial(self, rows, dtype, row0, nrows):
+        from . import _dtype_code
+        H, k = self.H, self.top_k
+        xb, ids, wts = unpack_tokens(rows, H, k, dtype)
+        Tt = rows.shape[0]
+        esz = torch.empty(0, dtype=dtype).element_size()
+        nbytes = int(lib().moe_ep_partial_workspace_size(ctypes.byref(self.local.desc), Tt))
+        ws = self._ws.get(Tt)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=rows.device)
+            self._ws[Tt] = ws
+        y = torch.empty(Tt, H, dtype=torch.float32, device=rows.device)
+        probe = torch.empty(0, dtype=dtype, device=rows.device)
+        check(lib().moe_ep_partial_forward(
+            y.data_ptr(), rows.data_ptr(), rows.shape[1] // esz, _dtype_code(probe, "moe_ep"),
+            Tt, ctypes.byref(self.local.desc), ids.data_ptr(), wts.data_ptr(),
+            self.rank * self.epr, row0, nrows, ws.data_ptr(), ws.numel(), self._stream(rows)))
+        return y
+
+    def finish(self, mine, shared, residual, dtype):
+        from . import _dtype_code
+        T, H = mine.shape
+        y = torch.empty(T, H, dtype=dtype, device=mine.device)
+        res = None if residual is None else residual.to(dtype).contiguous()
+        check(lib().moe_ep_finish(y.data_ptr(), mine.data_ptr(),
+                                  None if shared is None else shared.data_ptr(),
+                                  None if res is None else res.data_ptr(),
+                                  _dtype_code(y, "moe_ep_finish"), T, H, self._stream(y)))
+        return y

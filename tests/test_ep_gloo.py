@@ -1,8 +1,10 @@
 """Expert-parallel exchange (mlxfast-challenge_b200/ep.py) on two gloo ranks on
 the CPU.  The device kernels are replaced by CPU ops built on the oracle
 (test-only), so what is checked here is the distributed data flow: counts
-exchange, uneven all-to-all splits, the return path and the combine order.
-Each rank's output must equal the single-process block over all experts."""
+exchange, uneven all-to-all splits, the return path and the combine order
+(all-to-all form); token/routing gather, foreign-expert skipping and the
+reduce-scatter of partial sums (gather form).  Each rank's output must equal
+the single-process block over all experts."""
 import importlib
 import os
 import socket
@@ -125,4 +127,73 @@ def test_ep_exchange_two_gloo_ranks_matches_single_block(orc):
         x, inds, wts, y = out[r]
         want = orc.port.moe_block_f32(x, inds.astype(np.uint32), wts, routed, shared,
                                       scaling=SCALING)
+        assert_close(y, want, what=f"rank {r}")
+
+
+class CpuGatherOps:
+    """Oracle-backed stand-in for CudaGatherEPOps on one rank (test only)."""
+
+    def __init__(self, routed, shared, rank, world):
+        import oracle
+        self.port = oracle.port
+        self.rank = rank
+        self.epr = E // world
+        self.local = {k: v[rank * self.epr:(rank + 1) * self.epr] for k, v in routed.items()}
+        self.shared_b = shared
+
+    def shared(self, x):
+        n = x.shape[0]
+        one = {k: v[None] for k, v in self.shared_b.items()}
+        y = self.port.moe_block_f32(x.numpy(), np.zeros((n, 1), np.uint32),
+                                    np.ones((n, 1), np.float32), one, None, scaling=1.0)
+        return torch.from_numpy(y.astype(np.float32))
+
+    def partial(self, rows, dtype, row0, nrows):
+        ep = importlib.import_module(PKG + ".ep")
+        xb, ids, wts = ep.unpack_tokens(rows, H, K, dtype)
+        x = xb.contiguous().view(dtype).numpy()
+        ids = ids.numpy().astype(np.int64) - self.rank * self.epr
+        local = (ids >= 0) & (ids < self.epr)
+        w = np.where(local, wts.numpy(), 0.0).astype(np.float32)   # foreign pairs weigh 0
+        i = np.where(local, ids, 0).astype(np.uint32)
+        y = self.port.moe_block_f32(x, i, w, self.local, None, scaling=SCALING)
+        return torch.from_numpy(y.astype(np.float32))
+
+    def finish(self, mine, shared, residual, dtype):
+        y = mine + shared
+        return (y if residual is None else y + residual).to(dtype)
+
+
+def worker_gather(rank, world, port, out):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ep = importlib.import_module(PKG + ".ep")
+    routed, shared = make_layer()
+    rng = np.random.default_rng(200 + rank)
+    x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32))
+    inds = torch.from_numpy(np.stack([rng.permutation(E)[:K] for _ in range(T)]))
+    if rank == 0:
+        inds[:, 0] = E - 1  # skew: rank 0's tokens all hit one of rank 1's experts
+    wts = torch.softmax(torch.from_numpy(rng.standard_normal((T, K)).astype(np.float32)), -1)
+    res = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32))
+    block = ep.GatherEPBlock(CpuGatherOps(routed, shared, rank, world))
+    y = block(x, residual=res, routing=(inds, wts))
+    out[rank] = (x.numpy(), inds.numpy(), wts.numpy(), res.numpy(), y.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_ep_gather_two_gloo_ranks_matches_single_block(orc):
+    world = 2
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(worker_gather, args=(world, free_port(), out), nprocs=world, join=True)
+    routed, shared = make_layer()
+    for r in range(world):
+        x, inds, wts, res, y = out[r]
+        want = orc.port.moe_block_f32(x, inds.astype(np.uint32), wts, routed, shared,
+                                      scaling=SCALING, residual=res)
         assert_close(y, want, what=f"rank {r}")

@@ -102,3 +102,52 @@ def test_simulated_ranks_match_single_block(nv, world, T):
         # single-GPU path's f32 expert sums): path-vs-path bound as for prefill
         assert_close(outs[r].float().cpu().numpy(), want.float().cpu().numpy(), max_abs=4e-2,
                      what=f"rank {r} of {world}")
+
+
+@pytest.mark.parametrize("world,T", [(2, 64), (4, 100), (8, 512)])
+def test_gather_form_simulated_ranks_match_single_block(nv, world, T):
+    """GatherEPBlock's steps for `world` ranks in one process: every rank's
+    partial over all gathered tokens (moe_ep_partial_forward, foreign experts
+    skipped), the reduce-scatter as a sum, moe_ep_finish with the shared
+    expert and the residual -- against the single-GPU block."""
+    ep = importlib.import_module(PKG + ".ep")
+    lag = importlib.import_module(PKG + ".laguna")
+    block, raw = lag.random_sparse_layer(nv, seed=37, device=DEV)
+    ops = [ep.CudaGatherEPOps(ep.local_slice(raw["routed"], r, world), raw["shared"],
+                              raw["router_w"], raw["router_b"], 256, r, world)
+           for r in range(world)]
+    g = torch.Generator(device=DEV).manual_seed(world)
+    xs = [torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16) for _ in range(world)]
+    res = [torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16) for _ in range(world)]
+    routings = [ops[r].route(xs[r]) for r in range(world)]
+    rows = torch.cat([ep.pack_tokens(xs[r], *routings[r]) for r in range(world)])
+    partials = [ops[d].partial(rows, torch.bfloat16, d * T, T) for d in range(world)]
+    total = sum(partials)  # the reduce-scatter, all blocks at once
+    torch.cuda.synchronize()
+    nv.device_status()
+    for r in range(world):
+        mine = total[r * T:(r + 1) * T].contiguous()
+        y = ops[r].finish(mine, None, res[r], torch.bfloat16)
+        want = block(xs[r], residual=res[r], inds=routings[r][0].view(torch.int32),
+                     weights=routings[r][1])
+        assert_close(y.float().cpu().numpy(), want.float().cpu().numpy(), max_abs=4e-2,
+                     what=f"gather form, rank {r} of {world}")
+
+
+def test_ep_partial_skips_foreign_experts_without_error(nv):
+    """Ids outside the rank's range contribute nothing and raise no device
+    error; a token with no local pair gets a zero partial."""
+    ep = importlib.import_module(PKG + ".ep")
+    lag = importlib.import_module(PKG + ".laguna")
+    _, raw = lag.random_sparse_layer(nv, seed=5, device=DEV)
+    world, T = 4, 40
+    op1 = ep.CudaGatherEPOps(ep.local_slice(raw["routed"], 1, world), None, raw["router_w"],
+                             raw["router_b"], 256, 1, world)
+    x = torch.randn(T, 2048, device=DEV).to(torch.bfloat16)
+    inds, wts = op1.route(x)
+    inds = inds.clone()
+    inds[:10] = torch.arange(8, dtype=torch.int32, device=DEV).view(inds.dtype)  # experts 0-7: rank 0
+    part = op1.partial(ep.pack_tokens(x, inds, wts), torch.bfloat16, 0, T)
+    nv.device_status()
+    assert torch.count_nonzero(part[:10]) == 0
+    assert torch.isfinite(part).all()
