@@ -86,6 +86,12 @@ NVFP4MOE_API int nvfp4_version(void);
  * selects the exact path instead (weights dequantised to 16-bit, kind::f16;
  * ~1.7x slower at T = 512). */
 #define NVFP4_LAUNCH_EXACT_PREFILL 4
+/* moe_decode_stack_forward runs by default on the block-scaled FP4 tensor
+ * cores where the shape allows (hidden 1024 or 2048, inter 512 / 1024 / 2048,
+ * one gate/up and one down item per SM): activations as four NVFP4 terms as
+ * above.  NVFP4_LAUNCH_EXACT_DECODE selects the mma.sync stack instead (16-bit
+ * activations, exact products). */
+#define NVFP4_LAUNCH_EXACT_DECODE 8
 NVFP4MOE_API int nvfp4_set_launch_flags(int flags);
 /* Synchronises the device, returns and clears the latched device status
  * (NVFP4_OK or NVFP4_ERR_DEVICE_INDEX). */
@@ -261,9 +267,14 @@ NVFP4MOE_API int moe_down_combine(void* y, const float* act, int64_t act_ld,
  * inds[l] / weights[l] are device pointers to [top_k] entries.  The call runs
  * as many CTAs as the GPU has SMs and they wait on one another inside the
  * launch (co-residency is guaranteed by the cooperative launch); do not
- * overlap it with other work that needs whole SMs. */
+ * overlap it with other work that needs whole SMs.  By default (see
+ * NVFP4_LAUNCH_EXACT_DECODE) the products run on the block-scaled FP4 tensor
+ * cores, up to 40 layers per launch (20 with a shared expert);
+ * moe_decode_stack_launches gives the number of launches a call makes under
+ * the calling thread's flags. */
 NVFP4MOE_API size_t moe_decode_stack_workspace_size(const moe_layer_desc* layers,
                                                     int64_t n_layers);
+NVFP4MOE_API int moe_decode_stack_launches(const moe_layer_desc* layers, int64_t n_layers);
 NVFP4MOE_API int moe_decode_stack_forward(void* y, const void* x, int dtype, int64_t n_layers,
                                           const moe_layer_desc* layers,
                                           const uint32_t* const* inds,

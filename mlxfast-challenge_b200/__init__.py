@@ -271,12 +271,16 @@ class launch_flags:
     overlap its predecessor; bulk_copy=True selects the bulk-copy fed decode
     kernels; exact_prefill=True runs the prefill GEMMs on 16-bit dequantised
     weights (kind::f16) instead of the default block-scaled FP4 path
-    (activations as four NVFP4 terms)."""
+    (activations as four NVFP4 terms); exact_decode=True runs the persistent
+    decode stack on the mma.sync engine (16-bit activations) instead of the
+    default block-scaled FP4 stack."""
 
-    def __init__(self, pdl: bool = False, bulk_copy: bool = False, exact_prefill: bool = False):
+    def __init__(self, pdl: bool = False, bulk_copy: bool = False, exact_prefill: bool = False,
+                 exact_decode: bool = False):
         self.flags = (_lib.NVFP4_LAUNCH_PDL if pdl else 0) | (
             _lib.NVFP4_LAUNCH_BULK_COPY if bulk_copy else 0) | (
-            _lib.NVFP4_LAUNCH_EXACT_PREFILL if exact_prefill else 0)
+            _lib.NVFP4_LAUNCH_EXACT_PREFILL if exact_prefill else 0) | (
+            _lib.NVFP4_LAUNCH_EXACT_DECODE if exact_decode else 0)
 
     def __enter__(self):
         self.old = lib().nvfp4_set_launch_flags(self.flags)

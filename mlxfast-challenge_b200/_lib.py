@@ -22,6 +22,7 @@ NVFP4_BF16, NVFP4_F16, NVFP4_F32 = 0, 1, 2
 NVFP4_LAUNCH_PDL = 1
 NVFP4_LAUNCH_BULK_COPY = 2
 NVFP4_LAUNCH_EXACT_PREFILL = 4
+NVFP4_LAUNCH_EXACT_DECODE = 8
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -74,6 +75,7 @@ SIGNATURES = {
     "moe_down_combine": (_I, [_P, _P, _I64, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P,
                               _P]),
     "moe_decode_stack_workspace_size": (_SZ, [ctypes.POINTER(MoeLayerDesc), _I64]),
+    "moe_decode_stack_launches": (_I, [ctypes.POINTER(MoeLayerDesc), _I64]),
     "moe_decode_stack_forward": (_I, [_P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P, _P,
                                       _SZ, _P]),
     "moe_ep_dispatch": (_I, [_P, _P, _P, _P, _P, _I, _P, _I64, _I, _I64, _I64, _I, _P]),

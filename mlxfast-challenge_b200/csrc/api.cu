@@ -8,6 +8,7 @@
 #include <initializer_list>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/nvfp4moe.h"
 #include "kernels.h"
@@ -20,6 +21,7 @@ thread_local int t_launch_flags = 0;
 bool first_pdl() { return (t_launch_flags & NVFP4_LAUNCH_PDL) != 0; }
 bool use_bulk() { return (t_launch_flags & NVFP4_LAUNCH_BULK_COPY) != 0; }
 bool use_fp4_terms() { return (t_launch_flags & NVFP4_LAUNCH_EXACT_PREFILL) == 0; }
+bool use_fp4_decode() { return (t_launch_flags & NVFP4_LAUNCH_EXACT_DECODE) == 0; }
 nvfp4_error_handler g_handler = nullptr;
 void* g_handler_data = nullptr;
 
@@ -193,7 +195,8 @@ int nvfp4_version(void) { return 1; }
 
 int nvfp4_set_launch_flags(int flags) {
   const int old = t_launch_flags;
-  t_launch_flags = flags & (NVFP4_LAUNCH_PDL | NVFP4_LAUNCH_BULK_COPY | NVFP4_LAUNCH_EXACT_PREFILL);
+  t_launch_flags = flags & (NVFP4_LAUNCH_PDL | NVFP4_LAUNCH_BULK_COPY | NVFP4_LAUNCH_EXACT_PREFILL |
+                            NVFP4_LAUNCH_EXACT_DECODE);
   return old;
 }
 
@@ -223,6 +226,10 @@ int nvfp4_device_status(void) {
   e = nvfp4::read_and_clear_qqmm_error(&st5);
   if (e != cudaSuccess) return check_cuda(e, "device_status");
   if (st == 0) st = st5;
+  int st7 = 0;
+  e = nvfp4::read_and_clear_stack_fp4_error(&st7);
+  if (e != cudaSuccess) return check_cuda(e, "device_status");
+  if (st == 0) st = st7;
   if (st != 0)
     return fail(NVFP4_ERR_DEVICE_INDEX,
                 "[gather_qmm] an expert or batch index was out of range (kernel site %d); "
@@ -1113,9 +1120,11 @@ int moe_ep_finish(void* y, const float* partial, const void* shared, const void*
 // Serial decode through a stack of sparse layers in one persistent launch.
 namespace {
 struct StackLayout {
-  size_t act_off, xb0_off, xb1_off, bar_off, total;
+  size_t act_off, xb0_off, xb1_off, bar_off, y32_off, gu_off, total;
 };
 
+// act / xb: the mma.sync stack; y32 / gu: the FP4 stack's f32 partials
+// ([kk][H] per segment, [2][kk][2][I] per K part); bar: grid-barrier counters.
 StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   StackLayout S;
   const int64_t kk = L0->top_k + (L0->shared_inter > 0 ? 1 : 0);
@@ -1123,8 +1132,66 @@ StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   S.xb0_off = align_up((size_t)kk * L0->inter * sizeof(float), 256);
   S.xb1_off = align_up(S.xb0_off + (size_t)L0->hidden * dtype_bytes, 256);
   S.bar_off = align_up(S.xb1_off + (size_t)L0->hidden * dtype_bytes, 256);
-  S.total = align_up(S.bar_off + (2 + 2 * nvfp4::kStackMaxLayers) * sizeof(unsigned), 256);
+  S.y32_off = align_up(S.bar_off + (2 + 2 * nvfp4::kStackMaxLayers) * sizeof(unsigned), 256);
+  S.gu_off = align_up(S.y32_off + (size_t)kk * L0->hidden * sizeof(float), 256);
+  S.total = align_up(S.gu_off + 2 * (size_t)kk * 2 * L0->inter * sizeof(float), 256);
   return S;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return sms;
+}
+
+// Tensor maps of the FP4 stack, cached per calling thread by (stack position,
+// bank pointer, shape, box): a decode step re-issues the same layers, and a map
+// is a pure function of those.
+struct MapKey {
+  const void* p;
+  int64_t rows, K;
+  int box;
+  bool scales;
+  bool operator==(const MapKey& o) const {
+    return p == o.p && rows == o.rows && K == o.K && box == o.box && scales == o.scales;
+  }
+};
+struct MapCacheEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+thread_local std::vector<MapCacheEntry> t_map_cache;
+
+bool cached_map(size_t idx, CUtensorMap* out, const void* p, int64_t rows, int64_t K, int box,
+                bool scales) {
+  if (t_map_cache.size() <= idx) t_map_cache.resize(idx + 1);
+  MapCacheEntry& e = t_map_cache[idx];
+  const MapKey key{p, rows, K, box, scales};
+  if (!e.valid || !(e.key == key)) {
+    e.valid = false;
+    const cudaError_t r = scales ? nvfp4::map_scales(&e.map, p, rows, K, box)
+                                 : nvfp4::map_codes(&e.map, p, rows, K, box);
+    if (r != cudaSuccess) return false;
+    e.key = key;
+    e.valid = true;
+  }
+  *out = e.map;
+  return true;
+}
+
+// Layers per launch of the FP4 stack (the tensor maps ride in the kernel
+// parameters), 0 when the FP4 stack does not take this shape or is switched off.
+int fp4_stack_layers_per_launch(const moe_layer_desc* L0) {
+  if (!use_fp4_decode()) return 0;
+  const int kk = (int)(L0->top_k + (L0->shared_inter > 0 ? 1 : 0));
+  if (L0->shared_inter > 0 && L0->shared_inter != L0->inter) return 0;
+  if (L0->hidden > 4096 || L0->inter > 4096) return 0;
+  if (!nvfp4::decode_stack_fp4_supported((int)L0->hidden, (int)L0->inter, kk, device_sms()))
+    return 0;
+  const int mpl = L0->shared_inter > 0 ? 2 * nvfp4::kFsMapsRouted : nvfp4::kFsMapsRouted;
+  return std::min(nvfp4::kFsMaxLayers, nvfp4::kFsMaxMaps / mpl);
 }
 }  // namespace
 
@@ -1132,6 +1199,12 @@ extern "C" size_t moe_decode_stack_workspace_size(const moe_layer_desc* layers,
                                                   int64_t n_layers) {
   if (!layers || n_layers <= 0) return 0;
   return stack_layout(&layers[0], 4).total;  // sized for the widest dtype
+}
+
+extern "C" int moe_decode_stack_launches(const moe_layer_desc* layers, int64_t n_layers) {
+  if (!layers || n_layers <= 0) return 0;
+  const int per = fp4_stack_layers_per_launch(&layers[0]);
+  return per > 0 ? (int)((n_layers + per - 1) / per) : 1;
 }
 
 extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64_t n_layers,
@@ -1171,6 +1244,70 @@ extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64
   const int kk = (int)(k + (Is > 0 ? 1 : 0));
   if (nvfp4::decode_stack_smem_bytes((int)H, (int)I, kk) > 227 * 1024)
     return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layer too large for the on-chip rings.", op);
+  const int per_launch = fp4_stack_layers_per_launch(L0);
+  if (per_launch > 0) {
+    // Block-scaled FP4 stack: per launch up to per_launch layers, their tensor
+    // maps encoded here.
+    for (int64_t l = 0; l < n_layers; l++) {
+      const moe_layer_desc* Ll = &layers[l];
+      const nvfp4_bank* banks[6] = {&Ll->gate, &Ll->up, &Ll->down,
+                                    &Ll->shared_gate, &Ll->shared_up, &Ll->shared_down};
+      for (int b = 0; b < (Is > 0 ? 6 : 3); b++)
+        if (!banks[b]->w || !banks[b]->scales || !aligned16(banks[b]->w) ||
+            !aligned16(banks[b]->scales))
+          return fail(NVFP4_ERR_UNSUPPORTED, "[%s] banks must be 16-byte aligned.", op);
+      if (!inds[l] || !weights[l])
+        return fail(NVFP4_ERR_INVALID, "[%s] null routing for layer %lld.", op, (long long)l);
+    }
+    char* ws = static_cast<char*>(workspace);
+    cudaStream_t s = (cudaStream_t)stream;
+    static thread_local nvfp4::FsArgs F;
+    const int mpl = Is > 0 ? 2 * nvfp4::kFsMapsRouted : nvfp4::kFsMapsRouted;
+    F.H = (int)H;
+    F.I = (int)I;
+    F.E = (int)E;
+    F.k = (int)k;
+    F.kk = kk;
+    F.nks = nvfp4::decode_stack_fp4_nks((int)I, kk, device_sms());
+    F.mpl = mpl;
+    F.dtype = dtype;
+    F.x0 = x;
+    F.y = y;
+    F.Yp = reinterpret_cast<float*>(ws + S.y32_off);
+    F.GUp = reinterpret_cast<float*>(ws + S.gu_off);
+    F.bar = reinterpret_cast<unsigned*>(ws + S.bar_off);
+    for (int64_t l0 = 0; l0 < n_layers; l0 += per_launch) {
+      const int nl = (int)std::min<int64_t>(per_launch, n_layers - l0);
+      F.L = nl;
+      F.first = l0 == 0;
+      F.last = l0 + nl == n_layers;
+      bool ok = true;
+      for (int li = 0; li < nl; li++) {
+        const moe_layer_desc* Ll = &layers[l0 + li];
+        CUtensorMap* m = &F.maps[li * mpl];
+        const size_t c0 = (size_t)(l0 + li) * 2 * nvfp4::kFsMapsRouted;
+        ok = ok && cached_map(c0 + 0, &m[0], Ll->gate.w, E * I, H, 64, false) &&
+             cached_map(c0 + 1, &m[1], Ll->gate.scales, E * I, H, 64, true) &&
+             cached_map(c0 + 2, &m[2], Ll->up.w, E * I, H, 64, false) &&
+             cached_map(c0 + 3, &m[3], Ll->up.scales, E * I, H, 64, true) &&
+             cached_map(c0 + 4, &m[4], Ll->down.w, E * H, I, 128, false) &&
+             cached_map(c0 + 5, &m[5], Ll->down.scales, E * H, I, 128, true);
+        if (Is > 0)
+          ok = ok && cached_map(c0 + 6, &m[6], Ll->shared_gate.w, Is, H, 64, false) &&
+               cached_map(c0 + 7, &m[7], Ll->shared_gate.scales, Is, H, 64, true) &&
+               cached_map(c0 + 8, &m[8], Ll->shared_up.w, Is, H, 64, false) &&
+               cached_map(c0 + 9, &m[9], Ll->shared_up.scales, Is, H, 64, true) &&
+               cached_map(c0 + 10, &m[10], Ll->shared_down.w, H, I, 128, false) &&
+               cached_map(c0 + 11, &m[11], Ll->shared_down.scales, H, I, 128, true);
+        F.layer[li].inds = inds[l0 + li];
+        F.layer[li].wts = weights[l0 + li];
+        F.layer[li].scaling = Ll->routed_scaling;
+      }
+      if (!ok) return fail(NVFP4_ERR_CUDA, "[%s] tensor-map encoding failed.", op);
+      if (int r = check_cuda(nvfp4::launch_decode_stack_fp4(F, s), op)) return r;
+    }
+    return NVFP4_OK;
+  }
   nvfp4::StackArgs A{};
   A.L = (int)n_layers;
   A.H = (int)H;

@@ -211,11 +211,14 @@ __device__ __forceinline__ void store8_from_f32(void* y, int dtype, int64_t elem
 }
 
 // Power-of-two exponent e with max_abs * 2^-e in [1, 2); 0 for zero / non-finite.
+// Clamped at -100 so that 2^-e stays a finite f32: a row whose largest
+// magnitude is below 2^-100 stages as zeros (its products are below 2^-100 times
+// the weights' norm) instead of overflowing the reciprocal to inf.
 __device__ __forceinline__ int pow2_exponent(float max_abs) {
   if (!(max_abs > 0.0f) || !isfinite(max_abs)) return 0;
   int e;
   frexpf(max_abs, &e);  // max_abs = m * 2^e, m in [0.5, 1)
-  return e - 1;
+  return max(e - 1, -100);
 }
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -1,0 +1,773 @@
+// decode_stack_fp4.cu -- serial decode (T = 1) through a stack of sparse MoE
+// layers on the block-scaled FP4 tensor cores, as ONE persistent cooperative
+// launch (or one per 40 layers).
+//
+// Reference semantics: as decode_stack.cu -- per layer the routed SwitchGLU
+// gate/up -> SwiGLU -> down chain with given routing (VLM/MLXLMCommon/
+// SwitchLayers.swift:532-580) and the Laguna combine y = scaling * sum_j w_j *
+// expert_j(x) + shared(x) (VLM/MLXLLM/Models/Laguna.swift:204-212), the layer
+// loop being the runtime's decode step over its sparse layers
+// (Sources/MLXFastModel/LagunaRuntimeModel.swift:11460 -> :11030 -> :10678);
+// each layer's output rounded to the activation dtype.
+//
+// The products run as tcgen05.mma kind::mxf4nvf4 (M = 128 weight rows, N = 16,
+// K = 64): the weight operand is the checkpoint's E2M1 codes and E4M3 group
+// scales as stored; the activation row is carried, as in prefill_fp4.cu, as
+// four NVFP4 terms (term t = the NVFP4 quantisation of the residual after
+// terms 0..t-1 under a power-of-two factor per term, UE4M3 scales rounded up,
+// codes rounded to nearest even by the hardware converter), B rows 0..3;
+// rows 4..15 are zero.  Sums are f32.
+//
+// Why: at T = 1 the mma.sync stack spends most of each layer on the CUDA
+// cores, converting E2M1 pairs and multiplying group scales into every weight
+// element; here the tensor core consumes codes and scales directly and a layer
+// is two short dependent chains.
+//
+// Work of one layer over G CTAs (CTA c takes item c of each list):
+//   gate/up item (segment, 64-row block b of I, K part p of nks): A = the 64
+//     gate rows of block b and the same 64 up rows over K part p; B = the
+//     x terms of part p.  The part is four runs (one per chain warp), each
+//     decomposed with its own term factors and summed in its own TMEM
+//     accumulator.  Epilogue: sum_run sum_t fac * D_run[:, t]
+//     -> GUp[p][seg][gate|up][i].
+//   down item (segment, 128-row block of H): A = 128 down rows over all of I;
+//     B = the terms of act = silu(sum_p gate) * (sum_p up), four runs as
+//     above.  Epilogue: the same fold * w_seg * scaling (1 for the shared
+//     expert) -> Yp[seg][h]; the next layer's x is sum_seg Yp[seg] in segment
+//     order, rounded to the activation dtype.
+// Every partial has its own slot and is summed in a fixed order: results are
+// the same on every run.  Two grid barriers per layer (after the GUp writes,
+// after the Yp writes); one buffer of each suffices (each is read in the
+// phase after its writes and rewritten only after the next barrier).
+//
+// Roles (320 threads): warp 0 TMA (this CTA's weight slabs of layer l, l+1,
+// ... in consumption order into a 10-stage ring, so the next layer's weights
+// stream while this layer's chain runs), warp 1 MMA issue, warps 2-5 weight
+// scales into tensor memory, warps 6-9 the chain (terms, epilogues, grid
+// barriers).  Every wait is bounded; on expiry error 4 is latched and each
+// role leaves its loop (the copies and MMAs it issued drained) before tensor
+// memory is released.
+#include "common.cuh"
+#include "fp4terms.cuh"
+#include "kernels.h"
+#include "umma.cuh"
+
+namespace nvfp4 {
+namespace {
+
+constexpr int kT = kFp4Terms;
+constexpr int kN = 16;                    // MMA N: term rows 0..3, rows 4..15 zero
+constexpr int kStages = 10;
+constexpr int kA = 128 * 128;             // weight codes of one slab (128 rows x K 256): 16 KB
+constexpr int kSA = 128 * 16;             // their scale bytes: 2 KB
+constexpr int kStage = kA + kSA;          // 18 KB, 1 KB multiple
+static_assert(kStage % 1024 == 0, "stage alignment");
+constexpr int kBSlab = kN * 128;          // term codes of one K slab: 2 KB
+constexpr int kThreads = 320;
+constexpr int kWarpTma = 0, kWarpMma = 1, kWarpChain0 = 6;  // warps 2-5: weight scales
+constexpr int kChain = 128;
+constexpr int kBarChain = 1;              // named barrier of the chain warps
+// accumulators: one per chain warp's K run (16 columns each), gate/up then down
+constexpr uint32_t kAccGU = 0, kAccD = 64, kSfa0 = 128, kSfaCols = 16;
+constexpr uint32_t kSfbx = kSfa0 + kStages * kSfaCols;  // x-term scales, then act-term scales
+constexpr uint32_t kTmemCols = 512;
+constexpr int kErrIndex = 2;
+// A wait that expired latches 1000 * (layer in the launch + 1) + site, site:
+// 41 TMA ring slot, 42 MMA x terms, 43 MMA gate/up stage, 44 MMA act terms,
+// 45 MMA down stage, 46 MMA drain, 47 scale warps stage, 48 chain gate/up
+// accumulator, 49 chain down accumulator, 50 / 51 grid barrier 1 / 2.
+__host__ __device__ constexpr int fs_timeout(int l, int site) { return 1000 * (l + 1) + site; }
+constexpr long long kDrainBudget = 200000000LL;
+
+__device__ int g_fs_error = 0;
+__device__ __forceinline__ void fsflag(int code) { atomicCAS(&g_fs_error, 0, code); }
+
+__device__ __forceinline__ uint32_t elect_one_fs() {
+  uint32_t e;
+  asm volatile("{\n.reg .pred p;\nelect.sync _|p, 0xffffffff;\nselp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(e));
+  return e;
+}
+
+__device__ __forceinline__ bool chain_sync_and(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n"
+      ".reg .pred p, q;\n"
+      "setp.ne.u32 p, %1, 0;\n"
+      "bar.red.and.pred q, %2, %3, p;\n"
+      "selp.u32 %0, 1, 0, q;\n"
+      "}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(kBarChain), "r"(kChain)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ void red_release_add_fs(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_fs(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float round_to(float v, int dtype) {
+  if (dtype == kBF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dtype == kF16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+// Shared-memory carve-up (base 1024-byte aligned); also sizes it on the host.
+struct FsSmem {
+  uint8_t *stage, *bx, *ba, *scx, *sca;
+  float *wmax, *facx, *faca;
+  uint64_t *full, *empty, *sfr, *xready, *aready, *gufull, *dfull, *drain;
+  uint32_t* tslot;
+  int* bar_ok;
+  uint32_t* inds;
+  float* wts;
+};
+
+__host__ __device__ inline size_t fs_carve(int H, int I, int L, uint8_t* base, FsSmem* S) {
+  size_t o = 0;
+  auto take = [&](size_t bytes, size_t align) -> uint8_t* {
+    o = (o + align - 1) / align * align;
+    uint8_t* p = base ? base + o : nullptr;
+    o += bytes;
+    return p;
+  };
+  FsSmem t{};
+  t.stage = take((size_t)kStages * kStage, 1024);
+  t.bx = take((size_t)(H / 256) * kBSlab, 1024);  // bx and ba adjacent (zeroed together)
+  t.ba = take((size_t)(I / 256) * kBSlab, 1024);
+  t.scx = take((size_t)kT * (H / 16), 16);
+  t.sca = take((size_t)kT * (I / 16), 16);
+  t.wmax = reinterpret_cast<float*>(take(8 * 4, 16));
+  t.facx = reinterpret_cast<float*>(take(16 * 4, 16));
+  t.faca = reinterpret_cast<float*>(take(16 * 4, 16));
+  t.full = reinterpret_cast<uint64_t*>(take(kStages * 8, 8));
+  t.empty = reinterpret_cast<uint64_t*>(take(kStages * 8, 8));
+  t.sfr = reinterpret_cast<uint64_t*>(take(kStages * 8, 8));
+  t.xready = reinterpret_cast<uint64_t*>(take(8, 8));
+  t.aready = reinterpret_cast<uint64_t*>(take(8, 8));
+  t.gufull = reinterpret_cast<uint64_t*>(take(8, 8));
+  t.dfull = reinterpret_cast<uint64_t*>(take(8, 8));
+  t.drain = reinterpret_cast<uint64_t*>(take(8, 8));
+  t.tslot = reinterpret_cast<uint32_t*>(take(4, 4));
+  t.bar_ok = reinterpret_cast<int*>(take(4, 4));
+  t.inds = reinterpret_cast<uint32_t*>(take((size_t)L * 16 * 4, 16));
+  t.wts = reinterpret_cast<float*>(take((size_t)L * 16 * 4, 16));
+  if (S) *S = t;
+  return o;
+}
+
+// 128 V values of the activation row (K positions kb .. kb + 128 V) as four
+// NVFP4 terms, in the chain warps: thread ct holds the V values k0 = kb + ct *
+// V .. k0 + V - 1 (a group of 16 spans 16 / V threads), so chain warp w holds
+// the run of 32 V values from kb + 32 V w.  Each run is decomposed on its own
+// (its own power-of-two factor per term: warp shuffles only; the MMAs keep one
+// accumulator per run).  Per term: group max (shuffle), the run's max, the
+// factor, the group's UE4M3 scale, codes by the hardware converter into the B
+// tile (row t, 128-byte swizzle), the residual updated with the values the
+// codes stand for.  Writes the scale bytes sSc[t][group] (groups of the whole
+// row, K / 16 per term) and the factors fac[4 w + t]; ends with a chain
+// barrier.  Follows rows_to_terms_kernel (prefill_fp4.cu) value for value,
+// over the run instead of the row.
+template <int V>
+__device__ __forceinline__ void make_terms(float (&v)[V], int ct, int K, int kb, uint8_t* sB,
+                                           uint8_t* sSc, float* fac) {
+  constexpr int TPG = 16 / V;
+  const int lane = ct & 31, cw = ct >> 5;
+  const int k0 = kb + ct * V;
+  const int grp = k0 / 16;
+  const int byte0 = (k0 & 255) >> 1;
+  const int chunk = byte0 >> 4, within = byte0 & 15;
+  uint8_t* slab = sB + (k0 / 256) * kBSlab;
+  bool bad = false;
+#pragma unroll
+  for (int j = 0; j < V; j++) bad |= !isfinite(v[j]);
+#pragma unroll
+  for (int t = 0; t < kT; t++) {
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; j++) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int o = 1; o < TPG; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float m = warp_max(bad ? INFINITY : amax);
+    const int em = (__float_as_int(m) >> 23) & 0xFF;
+    const bool live = m >= 7.9e-31f && m < INFINITY;
+    const float P = live ? __int_as_float((127 + 10 - (em - 127)) << 23) : 0.f;
+    const float f = live ? __int_as_float((127 - 10 + (em - 127)) << 23)
+                         : (m == INFINITY ? __int_as_float(0x7fc00000) : 0.f);
+    const uint32_t b = live ? e4m3_ceil(amax * P * (1.0f / 6.0f)) : 0u;
+    const float s = scale_to_f32(b);
+    const float inv = s > 0.f ? P * __frcp_rn(s) : 0.f;
+    const float back = s > 0.f ? s * f : 0.f;
+    uint32_t w[(V + 7) / 8] = {};
+#pragma unroll
+    for (int j = 0; j < V; j += 2) {
+      const uint32_t byte = e2m1_pair(v[j] * inv, v[j + 1] * inv);
+      const float2 q = e2m1_pair_value(byte);
+      v[j] -= q.x * back;
+      v[j + 1] -= q.y * back;
+      w[j >> 3] |= byte << (4 * (j & 7));
+    }
+    uint8_t* dst = slab + t * 128 + ((chunk ^ t) << 4) + within;
+    if constexpr (V == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    else if constexpr (V == 8) *reinterpret_cast<uint32_t*>(dst) = w[0];
+    else *reinterpret_cast<uint16_t*>(dst) = (uint16_t)w[0];
+    if (ct % TPG == 0) sSc[t * (K / 16) + grp] = (uint8_t)b;
+    if (lane == 0) fac[4 * cw + t] = f;
+  }
+  named_sync(kBarChain, kChain);
+}
+
+// The term scales into tensor memory in the block-scaled MMA's layout (as the
+// weight scales: row n, block j of K step s at lane n % 32 of every lane
+// quarter, column 4 s + n / 32, byte j), rows 0..3 only.  Each chain warp
+// writes its own lane quarter.
+// Steps step0 .. step0 + nsteps - 1 (nsteps a multiple of 8) of a row of K.
+__device__ __forceinline__ void store_term_scales(const uint8_t* sSc, int K, int step0, int nsteps,
+                                                  uint32_t taddr, int lane) {
+  const int ns = K / 64;  // K steps of the row
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(sSc);  // [t][ns]
+  for (int blk = 0; blk < nsteps / 8; blk++) {
+    uint32_t r[32];
+#pragma unroll
+    for (int cc = 0; cc < 32; cc++)
+      r[cc] = ((cc & 3) == 0 && lane < kT) ? src[lane * ns + step0 + blk * 8 + (cc >> 2)] : 0u;
+    tmem_st32(taddr + 4 * step0 + 32 * blk, r);
+  }
+}
+
+// One accumulator row: sum over the 4 runs r and 4 terms t of fac[4 r + t] *
+// D_r[t] (runs in order, terms in order), D_r at columns 16 r .. 16 r + 3.
+__device__ __forceinline__ float fold_runs(uint32_t taddr, const float* fac) {
+  uint32_t d[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; r++)
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(d[r][0]), "=r"(d[r][1]), "=r"(d[r][2]), "=r"(d[r][3])
+                 : "r"(taddr + 16 * r)
+                 : "memory");
+  tmem_wait_ld();
+  float y = 0.f;
+#pragma unroll
+  for (int r = 0; r < 4; r++)
+#pragma unroll
+    for (int t = 0; t < kT; t++) y += fac[4 * r + t] * __uint_as_float(d[r][t]);
+  return y;
+}
+
+// v[0..V) = sum over the kk segment partials of Yp at k0 .. k0 + V - 1, in
+// segment order; 64 floats of loads in flight per thread per round.
+template <int V>
+__device__ __forceinline__ void load_segment_sum(const float* Yp, int H, int kk, int k0,
+                                                 float (&v)[V]) {
+  constexpr int NF = V / 4;
+  constexpr int SEG = 16 / NF;
+#pragma unroll
+  for (int j = 0; j < V; j++) v[j] = 0.f;
+  for (int s0 = 0; s0 < kk; s0 += SEG) {
+    float4 b[SEG][NF];
+#pragma unroll
+    for (int q = 0; q < SEG; q++)
+#pragma unroll
+      for (int f = 0; f < NF; f++)
+        b[q][f] = s0 + q < kk ? __ldcg(reinterpret_cast<const float4*>(Yp + (size_t)(s0 + q) * H +
+                                                                       k0 + 4 * f))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < SEG; q++)
+#pragma unroll
+      for (int f = 0; f < NF; f++) {
+        v[4 * f] += b[q][f].x;
+        v[4 * f + 1] += b[q][f].y;
+        v[4 * f + 2] += b[q][f].z;
+        v[4 * f + 3] += b[q][f].w;
+      }
+  }
+}
+
+template <int VX, int VA>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_decode_stack_fp4_kernel(const __grid_constant__ FsArgs a) {
+  extern __shared__ __align__(1024) unsigned char fs_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(fs_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int H = a.H, I = a.I;  // H = 128 VX nks, I = 128 VA (checked on the host)
+  FsSmem S;
+  fs_carve(H, I, a.L, base, &S);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int nb = I / 64;
+  const int nGU = a.kk * nb * a.nks;
+  const int nD = a.kk * (H / 128);
+  const bool has_gu = c < nGU, has_d = c < nD;
+  const int gu_seg = has_gu ? c / (nb * a.nks) : 0;
+  const int gu_rem = c - gu_seg * nb * a.nks;
+  const int gu_b = gu_rem / a.nks, gu_p = gu_rem - (gu_rem / a.nks) * a.nks;
+  const int KS = H / 256 / a.nks;  // K slabs of a gate/up item
+  const int d_seg = has_d ? c / (H / 128) : 0;
+  const int d_rb = c - d_seg * (H / 128);
+  const int DS = I / 256;          // K slabs of a down item
+  const uint32_t kSfba = kSfbx + (uint32_t)(H / 16);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; i++) {
+      mbar_init(&S.full[i], 1);
+      mbar_init(&S.empty[i], 1);
+      mbar_init(&S.sfr[i], 4);
+    }
+    mbar_init(S.xready, 4);
+    mbar_init(S.aready, 4);
+    mbar_init(S.gufull, 1);
+    mbar_init(S.dfull, 1);
+    mbar_init(S.drain, 1);
+    fence_barrier_init();
+  }
+  // Routing of the launch's layers into shared memory once.
+  for (int i = threadIdx.x; i < a.L * a.k; i += blockDim.x) {
+    const int l = i / a.k, j = i - l * a.k;
+    S.inds[l * 16 + j] = a.layer[l].inds[j];
+    S.wts[l * 16 + j] = a.layer[l].wts[j];
+  }
+  // Term tiles: rows 4..15 stay zero for the whole launch.
+  {
+    uint4* z = reinterpret_cast<uint4*>(S.bx);
+    const int n = (H / 256 + I / 256) * kBSlab / 16;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    fence_proxy_async();
+  }
+  if (warp == kWarpMma) tmem_alloc(S.tslot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *S.tslot;
+
+  if (warp == kWarpTma) {
+    // ------------------------------ TMA producer ------------------------------
+    const uint32_t el = elect_one_fs();
+    uint32_t g = 0;
+    bool ok = true;
+    auto slot = [&](int& s, int l) -> bool {
+      s = (int)(g % kStages);
+      if (g >= (uint32_t)kStages &&
+          !mbar_wait_bounded(&S.empty[s], ((g / kStages) - 1) & 1)) {
+        if (el) fsflag(fs_timeout(l, 41));
+        return false;
+      }
+      return true;
+    };
+    for (int l = 0; l < a.L && ok; l++) {
+      const CUtensorMap* mp = &a.maps[l * a.mpl];
+      if (has_gu) {
+        const bool sh = gu_seg >= a.k;
+        uint32_t e = 0;
+        if (!sh) {
+          e = S.inds[l * 16 + gu_seg];
+          if (e >= (uint32_t)a.E) {
+            if (el) fsflag(kErrIndex);
+            e = 0;  // the pipeline stays consistent; the output is flagged invalid
+          }
+        }
+        const CUtensorMap* m = sh ? mp + kFsMapsRouted : mp;
+        const int row0 = (sh ? 0 : (int)e * I) + gu_b * 64;
+        for (int sl = 0; sl < KS; sl++, g++) {
+          int s;
+          if (!slot(s, l)) {
+            ok = false;
+            break;
+          }
+          if (el) {
+            uint8_t* st = S.stage + (size_t)s * kStage;
+            const int xk = gu_p * KS + sl;
+            mbar_arrive_expect_tx(&S.full[s], (uint32_t)kStage);
+            tma_load_2d(st, m + 0, xk * 128, row0, &S.full[s]);
+            tma_load_2d(st + kA / 2, m + 2, xk * 128, row0, &S.full[s]);
+            tma_load_2d(st + kA, m + 1, xk * 16, row0, &S.full[s]);
+            tma_load_2d(st + kA + kSA / 2, m + 3, xk * 16, row0, &S.full[s]);
+          }
+          __syncwarp();
+        }
+      }
+      if (has_d && ok) {
+        const bool sh = d_seg >= a.k;
+        uint32_t e = 0;
+        if (!sh) {
+          e = S.inds[l * 16 + d_seg];
+          if (e >= (uint32_t)a.E) {
+            if (el) fsflag(kErrIndex);
+            e = 0;
+          }
+        }
+        const CUtensorMap* m = sh ? mp + kFsMapsRouted : mp;
+        const int row0 = (sh ? 0 : (int)e * H) + d_rb * 128;
+        for (int sl = 0; sl < DS; sl++, g++) {
+          int s;
+          if (!slot(s, l)) {
+            ok = false;
+            break;
+          }
+          if (el) {
+            uint8_t* st = S.stage + (size_t)s * kStage;
+            mbar_arrive_expect_tx(&S.full[s], (uint32_t)kStage);
+            tma_load_2d(st, m + 4, sl * 128, row0, &S.full[s]);
+            tma_load_2d(st + kA, m + 5, sl * 16, row0, &S.full[s]);
+          }
+          __syncwarp();
+        }
+      }
+    }
+    // no copy may still be landing at exit
+    for (uint32_t i = 0; i < (g < (uint32_t)kStages ? g : (uint32_t)kStages); i++) {
+      const uint32_t q = g - 1 - i;
+      mbar_wait_bounded(&S.full[q % kStages], (q / kStages) & 1, kDrainBudget);
+    }
+  } else if (warp == kWarpMma) {
+    // ------------------------------ MMA issuer ------------------------------
+    const uint32_t el = elect_one_fs();
+    const uint32_t idesc = idesc_mxf4nvf4(128, kN);
+    const uint32_t sbx = smem_u32(S.bx), sba = smem_u32(S.ba);
+    uint32_t g = 0, jx = 0, ja = 0;
+    bool ok = true;
+    for (int l = 0; l < a.L && ok; l++) {
+      if (has_gu) {
+        if (!mbar_wait_bounded(S.xready, jx & 1)) {
+          if (el) fsflag(fs_timeout(l, 42));
+          break;
+        }
+        jx++;
+        tc_fence_after();
+        for (int sl = 0; sl < KS; sl++, g++) {
+          const int s = (int)(g % kStages);
+          if (!mbar_wait_bounded(&S.sfr[s], (g / kStages) & 1)) {
+            if (el) fsflag(fs_timeout(l, 43));
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (el) {
+            const uint32_t sa = smem_u32(S.stage + (size_t)s * kStage);
+            const int xk = gu_p * KS + sl;
+            const uint32_t sb = sbx + (uint32_t)(xk * kBSlab);
+            const uint32_t sfa = tmem + kSfa0 + (uint32_t)s * kSfaCols;
+            const uint32_t sfb = tmem + kSfbx + (uint32_t)(16 * xk);
+#pragma unroll
+            for (int k4 = 0; k4 < 4; k4++) {
+              const int ks = 4 * sl + k4;  // K step in the item; run = ks / (VX / 2)
+              umma_mxf4nvf4(tmem + kAccGU + 16 * (ks * 2 / VX), smem_desc_sw128(sa + 32 * k4),
+                            smem_desc_sw128(sb + 32 * k4), idesc, sfa + 4 * k4, sfb + 4 * k4,
+                            ks % (VX / 2) != 0 ? 1u : 0u);
+            }
+            umma_commit(&S.empty[s]);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (el) umma_commit(S.gufull);
+        __syncwarp();
+      }
+      if (has_d) {
+        if (!mbar_wait_bounded(S.aready, ja & 1)) {
+          if (el) fsflag(fs_timeout(l, 44));
+          break;
+        }
+        ja++;
+        tc_fence_after();
+        for (int sl = 0; sl < DS; sl++, g++) {
+          const int s = (int)(g % kStages);
+          if (!mbar_wait_bounded(&S.sfr[s], (g / kStages) & 1)) {
+            if (el) fsflag(fs_timeout(l, 45));
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (el) {
+            const uint32_t sa = smem_u32(S.stage + (size_t)s * kStage);
+            const uint32_t sb = sba + (uint32_t)(sl * kBSlab);
+            const uint32_t sfa = tmem + kSfa0 + (uint32_t)s * kSfaCols;
+            const uint32_t sfb = tmem + kSfba + (uint32_t)(16 * sl);
+#pragma unroll
+            for (int k4 = 0; k4 < 4; k4++) {
+              const int ks = 4 * sl + k4;
+              umma_mxf4nvf4(tmem + kAccD + 16 * (ks * 2 / VA), smem_desc_sw128(sa + 32 * k4),
+                            smem_desc_sw128(sb + 32 * k4), idesc, sfa + 4 * k4, sfb + 4 * k4,
+                            ks % (VA / 2) != 0 ? 1u : 0u);
+            }
+            umma_commit(&S.empty[s]);
+          }
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (el) umma_commit(S.dfull);
+        __syncwarp();
+      }
+    }
+    // every MMA issued has completed before tensor memory is released
+    if (el) umma_commit(S.drain);
+    __syncwarp();
+    if (!mbar_wait_bounded(S.drain, 0, kDrainBudget) && el) fsflag(fs_timeout(-1, 46));
+  } else if (warp < kWarpChain0) {
+    // -------------------- weight scales into tensor memory --------------------
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
+    const int per_layer = (has_gu ? KS : 0) + (has_d ? DS : 0);
+    uint32_t g = 0;
+    bool ok = true;
+    for (int l = 0; l < a.L && ok; l++) {
+      for (int i = 0; i < per_layer; i++, g++) {
+        const int s = (int)(g % kStages);
+        if (!mbar_wait_bounded(&S.full[s], (g / kStages) & 1)) {
+          if (lane == 0) fsflag(fs_timeout(l, 47));
+          ok = false;
+          break;
+        }
+        const uint8_t* sf = S.stage + (size_t)s * kStage + kA;
+        uint32_t ra[16];
+#pragma unroll
+        for (int cq = 0; cq < 4; cq++) {
+          const uint4 va = *reinterpret_cast<const uint4*>(sf + 16 * (lane + 32 * cq));
+          ra[0 + cq] = va.x;
+          ra[4 + cq] = va.y;
+          ra[8 + cq] = va.z;
+          ra[12 + cq] = va.w;
+        }
+        tmem_st16(tmem + lane_base + kSfa0 + (uint32_t)s * kSfaCols, ra);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&S.sfr[s]);
+      }
+    }
+  } else {
+    // ------------------------------ the chain ------------------------------
+    const int ct = threadIdx.x - kWarpChain0 * 32;  // 0..127
+    const int q = warp & 3;                         // TMEM lane quarter
+    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+    const int r = 32 * q + lane;                    // accumulator row = TMEM lane
+    uint32_t jgu = 0, jd = 0;
+    unsigned nb0 = 0, nb1 = 0;
+    // One grid barrier: the chain's global writes and adds, then this CTA's
+    // arrival; thread 0 waits (bounded) for all G CTAs.
+    auto grid_barrier = [&](unsigned* ctr, unsigned& n, int site) -> bool {
+      named_sync(kBarChain, kChain);
+      if (ct == 0) {
+        red_release_add_fs(ctr, 1u);  // orders this CTA's writes (bar.sync above) first
+        const unsigned target = (unsigned)G * (n + 1);
+        bool ok = true;
+        if (ld_acquire_fs(ctr) < target) {
+          const long long start = clock64();
+          while (ld_acquire_fs(ctr) < target) {
+            if (clock64() - start > 2000000000LL) {
+              ok = false;
+              break;
+            }
+            __nanosleep(32);
+          }
+        }
+        *S.bar_ok = ok;
+        if (!ok) fsflag(fs_timeout((int)n, site));
+      }
+      named_sync(kBarChain, kChain);
+      n++;
+      return *S.bar_ok != 0;
+    };
+    for (int l = 0; l < a.L; l++) {
+      bool alive = true;
+
+      // ---- phase A: x terms, gate/up item -> GUp ----
+      if (has_gu) {
+        // only this item's K part of x: its 128 VX values
+        float v[VX];
+        const int kb = gu_p * (H / a.nks);
+        const int k0 = kb + ct * VX;
+        if (l == 0 && a.first) {
+          if constexpr (VX % 8 == 0) {
+#pragma unroll
+            for (int j = 0; j < VX; j += 8)
+              load8(a.x0, a.dtype, k0 + j, *reinterpret_cast<float(*)[8]>(&v[j]));
+          } else {  // VX = 4: the aligned 8 around k0, half of them
+            float f[8];
+            load8(a.x0, a.dtype, k0 & ~7, f);
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[i] = f[(k0 & 4) + i];
+          }
+        } else {
+          // the previous layer's output: its segments' partials in order
+          load_segment_sum<VX>(a.Yp, H, a.kk, k0, v);
+#pragma unroll
+          for (int j = 0; j < VX; j++) v[j] = round_to(v[j], a.dtype);
+        }
+        make_terms<VX>(v, ct, H, kb, S.bx, S.scx, S.facx);
+        store_term_scales(S.scx, H, kb / 64, (H / a.nks) / 64, tmem + lane_base + kSfbx, lane);
+        fence_proxy_async();
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(S.xready);
+        const bool got = mbar_wait_bounded(S.gufull, jgu & 1);
+        jgu++;
+        if (!got && lane == 0) fsflag(fs_timeout(l, 48));
+        alive = chain_sync_and(got);
+        if (alive) {
+          tc_fence_after();
+          const float y = fold_runs(tmem + lane_base + kAccGU, S.facx);
+          tc_fence_before();
+          __stcg(a.GUp + ((size_t)(gu_p * a.kk + gu_seg) * 2 + (r >> 6)) * I + gu_b * 64 + (r & 63),
+                 y);
+        }
+      }
+      if (!alive || !grid_barrier(&a.bar[0], nb0, 50)) break;
+
+      // ---- phase B: act terms, down item -> Yp ----
+      if (has_d) {
+        float v[VA];
+        const int k0 = ct * VA;
+#pragma unroll
+        for (int j = 0; j < VA; j += 4) {
+          float4 gv = make_float4(0.f, 0.f, 0.f, 0.f), uv = gv;
+#pragma unroll
+          for (int p = 0; p < 2; p++) {
+            if (p >= a.nks) break;
+            const float* src = a.GUp + (size_t)(p * a.kk + d_seg) * 2 * I;
+            const float4 g = __ldcg(reinterpret_cast<const float4*>(src + k0 + j));
+            const float4 u = __ldcg(reinterpret_cast<const float4*>(src + I + k0 + j));
+            gv.x += g.x;
+            gv.y += g.y;
+            gv.z += g.z;
+            gv.w += g.w;
+            uv.x += u.x;
+            uv.y += u.y;
+            uv.z += u.z;
+            uv.w += u.w;
+          }
+          v[j] = silu_ref(gv.x) * uv.x;
+          v[j + 1] = silu_ref(gv.y) * uv.y;
+          v[j + 2] = silu_ref(gv.z) * uv.z;
+          v[j + 3] = silu_ref(gv.w) * uv.w;
+        }
+        make_terms<VA>(v, ct, I, 0, S.ba, S.sca, S.faca);
+        store_term_scales(S.sca, I, 0, I / 64, tmem + lane_base + kSfba, lane);
+        fence_proxy_async();
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(S.aready);
+        const bool got = mbar_wait_bounded(S.dfull, jd & 1);
+        jd++;
+        if (!got && lane == 0) fsflag(fs_timeout(l, 49));
+        alive = chain_sync_and(got);
+        if (alive) {
+          tc_fence_after();
+          const float wseg = d_seg < a.k ? S.wts[l * 16 + d_seg] * a.layer[l].scaling : 1.0f;
+          const float y = fold_runs(tmem + lane_base + kAccD, S.faca) * wseg;
+          tc_fence_before();
+          __stcg(a.Yp + (size_t)d_seg * H + d_rb * 128 + r, y);
+        }
+      }
+      if (!alive || !grid_barrier(&a.bar[1], nb1, 51)) break;
+      if (a.last && l == a.L - 1)
+        for (int i = c * kChain + ct; i < H; i += G * kChain) {
+          float y = __ldcg(a.Yp + i);
+          for (int sg = 1; sg < a.kk; sg++) y += __ldcg(a.Yp + (size_t)sg * H + i);
+          store_from_f32(a.y, a.dtype, i, y);
+        }
+    }
+  }
+  __syncthreads();
+  if (warp == kWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int VX>
+const void* pick_va(int va) {
+  switch (va) {
+    case 4: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 4>);
+    case 8: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 8>);
+    case 16: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 16>);
+    default: return nullptr;
+  }
+}
+
+// VX: values of x per chain thread (the K part of a gate/up item / 128).
+const void* pick_kernel(int H, int I, int nks) {
+  switch (H / nks / 128) {
+    case 4: return pick_va<4>(I / 128);
+    case 8: return pick_va<8>(I / 128);
+    case 16: return pick_va<16>(I / 128);
+    default: return nullptr;
+  }
+}
+
+}  // namespace
+
+static_assert(sizeof(FsArgs) <= 32764, "kernel parameters above the 32 KB limit");
+
+int decode_stack_fp4_nks(int I, int kk, int sms) {
+  if (kk * (I / 64) * 2 <= sms) return 2;
+  if (kk * (I / 64) <= sms) return 1;
+  return 0;
+}
+
+size_t decode_stack_fp4_smem_bytes(int H, int I, int L) {
+  return fs_carve(H, I, L, nullptr, nullptr) + 1024;
+}
+
+bool decode_stack_fp4_supported(int H, int I, int kk, int sms) {
+  if (H != 1024 && H != 2048) return false;
+  if (I != 512 && I != 1024 && I != 2048) return false;
+  if (kk < 1 || kk > 16 || kk * (H / 128) > sms) return false;  // one down item per CTA
+  if (decode_stack_fp4_nks(I, kk, sms) == 0) return false;      // one gate/up item per CTA
+  if (kSfbx + (uint32_t)(H / 16 + I / 16) > kTmemCols) return false;
+  return decode_stack_fp4_smem_bytes(H, I, kFsMaxLayers) <= 227 * 1024;
+}
+
+cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
+  const void* kern = a.nks > 0 ? pick_kernel(a.H, a.I, a.nks) : nullptr;
+  if (!kern || a.L < 1 || a.L > kFsMaxLayers || a.L * a.mpl > kFsMaxMaps)
+    return cudaErrorInvalidValue;
+  const size_t smem = decode_stack_fp4_smem_bytes(a.H, a.I, a.L);
+  cudaError_t e = ensure_smem_ptr(kern, smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0;
+  e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  if (decode_stack_fp4_nks(a.I, a.kk, sms) != a.nks || a.kk * (a.H / 128) > sms)
+    return cudaErrorInvalidValue;
+  // Every CTA must be resident (grid barriers): one per SM, cooperative launch.
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+  e = cudaMemsetAsync(a.bar, 0, 2 * sizeof(unsigned), stream);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)sms);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeCooperative;
+  attr.val.cooperative = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  void* args[] = {const_cast<FsArgs*>(&a)};
+  e = cudaLaunchKernelExC(&cfg, kern, args);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+cudaError_t read_and_clear_stack_fp4_error(int* out) {
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_fs_error, sizeof(int));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(g_fs_error, &zero, sizeof(int));
+}
+
+}  // namespace nvfp4

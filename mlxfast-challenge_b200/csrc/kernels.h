@@ -143,6 +143,36 @@ size_t decode_stack_smem_bytes(int H, int I, int kk);
 cudaError_t launch_decode_stack(const StackArgs& a, cudaStream_t stream);
 cudaError_t read_and_clear_stack_error(int* out);
 
+// The same stack on the block-scaled FP4 tensor cores (decode_stack_fp4.cu).
+// Tensor maps travel in the kernel parameters (<= 32 KB): layers of one launch
+// share kFsMaxMaps maps, 6 per layer (12 with a shared expert).
+constexpr int kFsMaxLayers = 40;
+constexpr int kFsMaxMaps = 240;
+constexpr int kFsMapsRouted = 6;  // gate codes, gate scales, up codes, up scales, down codes, down scales
+struct FsLayer {
+  const uint32_t* inds;  // [k] device
+  const float* wts;      // [k] device
+  float scaling;
+};
+struct alignas(64) FsArgs {
+  CUtensorMap maps[kFsMaxMaps];  // layer l: maps[l * mpl + j]; j >= 6: the shared expert's
+  FsLayer layer[kFsMaxLayers];
+  int L;           // layers in this launch
+  int first;       // 1: layer 0 of the stack (input x0 in dtype), else the sum of Yp
+  int last;        // 1: the launch ends the stack (writes y)
+  int H, I, E, k, kk, nks, mpl, dtype;
+  const void* x0;  // [H] stack input (dtype)
+  void* y;         // [H] stack output (dtype)
+  float* Yp;       // [kk][H] the layer's output per segment (f32)
+  float* GUp;      // [nks][kk][2][I] gate / up pre-activations per K part (f32)
+  unsigned* bar;   // [2] grid-barrier counters, zero at launch
+};
+bool decode_stack_fp4_supported(int H, int I, int kk, int sms);
+int decode_stack_fp4_nks(int I, int kk, int sms);
+size_t decode_stack_fp4_smem_bytes(int H, int I, int L);
+cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream);
+cudaError_t read_and_clear_stack_fp4_error(int* out);
+
 // Expert-parallel dispatch / combine (ep.cu).
 struct EpPlanArgs {
   const uint32_t* inds;      // [T, k] global expert ids

@@ -43,6 +43,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "umma.cuh"
+#include "fp4terms.cuh"
 
 namespace nvfp4 {
 namespace {
@@ -100,30 +101,6 @@ __device__ __forceinline__ bool sync_and(int id, int count, bool pred) {
       : "r"((uint32_t)pred), "r"(id), "r"(count)
       : "memory");
   return r != 0;
-}
-
-// Smallest E4M3 magnitude >= v (v >= 0, v <= 448).
-__device__ __forceinline__ uint32_t e4m3_ceil(float v) {
-  uint32_t b = e4m3_encode(v) & 0x7Fu;
-  if (scale_to_f32(b) < v && b < 0x7Eu) b++;
-  return b;
-}
-
-// ---------------------------------------------------------------------------
-// Two values -> one byte of E2M1 codes, rounded to nearest even and saturated
-// at +-6 by the hardware converter (first operand in the high nibble), and the
-// byte back to the two exact values.
-__device__ __forceinline__ uint32_t e2m1_pair(float lo, float hi) {
-  uint32_t r;
-  asm("{\n.reg .b8 t;\ncvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\ncvt.u32.u8 %0, t;\n}"
-      : "=r"(r)
-      : "f"(hi), "f"(lo));
-  return r;
-}
-__device__ __forceinline__ float2 e2m1_pair_value(uint32_t byte) {
-  uint32_t h;
-  asm("{\n.reg .b8 t;\ncvt.u8.u32 t, %1;\ncvt.rn.f16x2.e2m1x2 %0, t;\n}" : "=r"(h) : "r"(byte));
-  return __half22float2(*reinterpret_cast<const __half2*>(&h));
 }
 
 // rows_to_terms: one CTA of K / 512 warps per source row; lane l of warp w

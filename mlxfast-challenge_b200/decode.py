@@ -76,6 +76,7 @@ class MoEDecodeChain:
             self.stack = self._try_stack()
 
     def _stack_call(self, stream_ptr) -> int:
+        self._stack_launches = lib().moe_decode_stack_launches(self._descs, len(self.blocks))
         return lib().moe_decode_stack_forward(
             self.bufs[0].data_ptr(), self.x0.data_ptr(), self._dt, len(self.blocks), self._descs,
             ctypes.cast(self._inds, ctypes.c_void_p), ctypes.cast(self._wts, ctypes.c_void_p),
@@ -84,6 +85,9 @@ class MoEDecodeChain:
     def _try_stack(self) -> bool:
         """Whether the library runs this stack as one launch (shape checks only)."""
         s = torch.cuda.Stream(device=self.device)
+        # after the caller's pending work: the stack's CTAs wait on one another
+        # and must not share the GPU with another persistent stack in flight
+        s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             st = self._stack_call(ctypes.c_void_p(s.cuda_stream))
         s.synchronize()
@@ -119,8 +123,10 @@ class MoEDecodeChain:
         self.out = src
 
     def launches_per_step(self) -> int:
+        """Kernel launches of one step (the stack: as of its last call, whose
+        launch flags choose the FP4 or the mma.sync stack)."""
         if self.stack:
-            return 1
+            return self._stack_launches
         return len(self.blocks) * (3 if self.route else 2)
 
     def capture(self, pdl: bool = True):
@@ -128,6 +134,7 @@ class MoEDecodeChain:
         predecessor drains (programmatic dependent launch): the next layer's
         weights stream in before the previous layer's output is ready."""
         s = self.stream
+        s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             self._launch_step(ctypes.c_void_p(s.cuda_stream))  # warm (sets kernel attributes)
         s.synchronize()
@@ -160,6 +167,7 @@ class MoEDecodeChain:
             self.capture()
         if y_host is None:
             y_host = torch.empty(self.T, self.H, dtype=self.dtype, pin_memory=True)
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self.stream):
             self.x0.copy_(x_host.reshape(self.T, self.H), non_blocking=True)
             self.graph.replay()

@@ -1,10 +1,12 @@
 """GPU parity of the persistent decode stack (moe_decode_stack_forward): the
-whole serial decode over L sparse layers in one cooperative launch.  It runs
-the same GEMV engine and staging as the per-layer bulk-copy kernels but sums
-partial products in another order, so a single layer must be within the
-BASELINE tolerance of the fp32 oracle, an L-layer chain within L times the
-relative-L2 bound of the per-layer chains (every layer rounds its output to
-bf16 in both), and replays are bit-for-bit repeatable."""
+whole serial decode over L sparse layers in one cooperative launch.  Two
+stacks: the default on the block-scaled FP4 tensor cores (activations as four
+NVFP4 terms, tcgen05 kind::mxf4nvf4) and, with the exact_decode launch flag,
+the mma.sync stack (the per-layer kernels' GEMV engine, partial products summed
+in another order).  Either way a single layer must be within the BASELINE
+tolerance of the fp32 oracle, an L-layer chain within L times the relative-L2
+bound of the per-layer chains (every layer rounds its output to bf16 in both),
+and replays are bit-for-bit repeatable."""
 import importlib
 
 import numpy as np
@@ -41,6 +43,17 @@ def seeded_x(seed):
     return torch.randn(1, 2048, generator=g, device=DEV).to(torch.bfloat16)
 
 
+def make_chain(nv, blocks, routing, exact, dtype=torch.bfloat16):
+    """A captured decode chain; exact selects the mma.sync stack."""
+    with nv.launch_flags(exact_decode=exact):
+        return nv.MoEDecodeChain(blocks, routing, T=1, dtype=dtype, device=DEV).capture()
+
+
+@pytest.fixture(params=[False, True], ids=["fp4", "exact"])
+def exact(request):
+    return request.param
+
+
 def layer_by_layer(blocks, routing, x):
     y = x
     for l, b in enumerate(blocks):
@@ -49,9 +62,9 @@ def layer_by_layer(blocks, routing, x):
 
 
 @pytest.mark.parametrize("with_shared,n", [(True, 2), (False, 2), (True, 5)])
-def test_stack_matches_bulk_copy_layer_loop(nv, with_shared, n):
+def test_stack_matches_bulk_copy_layer_loop(nv, with_shared, n, exact):
     blocks, _, routing = layers(nv, n, with_shared=with_shared)
-    chain = nv.MoEDecodeChain(blocks, routing, T=1, device=DEV).capture()
+    chain = make_chain(nv, blocks, routing, exact)
     assert chain.stack and chain.launches_per_step() == 1
     x = seeded_x(n + 10 * with_shared)
     with nv.launch_flags(bulk_copy=True):
@@ -71,9 +84,9 @@ def test_stack_matches_bulk_copy_layer_loop(nv, with_shared, n):
     assert torch.equal(yh, first.cpu())
 
 
-def test_stack_matches_default_kernels_and_oracle(nv, orc):
+def test_stack_matches_default_kernels_and_oracle(nv, orc, exact):
     blocks, raw, routing = layers(nv, 3, n_experts=256, seed=900)
-    chain = nv.MoEDecodeChain(blocks, routing, T=1, device=DEV).capture()
+    chain = make_chain(nv, blocks, routing, exact)
     assert chain.stack
     x = seeded_x(3)
     chain.x0.copy_(x)
@@ -83,7 +96,7 @@ def test_stack_matches_default_kernels_and_oracle(nv, orc):
     assert_close(out.float().cpu().numpy(), want.float().cpu().numpy(), max_abs=float("inf"),
                  rel_l2=chain_tol(3), what="stack vs default")
     # Layer 0 against the fp32 oracle (used experts only).
-    one = nv.MoEDecodeChain(blocks[:1], routing[:1], T=1, device=DEV).capture()
+    one = make_chain(nv, blocks[:1], routing[:1], exact)
     assert one.stack
     one.x0.copy_(x)
     y0 = one.replay()
@@ -103,13 +116,15 @@ def test_stack_matches_default_kernels_and_oracle(nv, orc):
     assert_close(y0.float().cpu().numpy(), o, what="stack layer vs oracle")
 
 
-def test_stack_many_layers(nv):
+def test_stack_many_layers(nv, exact):
     blocks, _, routing = layers(nv, 3, seed=500)
     # 39 layers (the model's sparse count) cycling 3 distinct weight sets.
     stack_blocks = [blocks[l % 3] for l in range(39)]
     stack_routing = [routing[l % 3] for l in range(39)]
-    chain = nv.MoEDecodeChain(stack_blocks, stack_routing, T=1, device=DEV).capture()
+    chain = make_chain(nv, stack_blocks, stack_routing, exact)
     assert chain.stack
+    # with the shared expert the FP4 stack takes 20 layers per launch
+    assert chain.launches_per_step() == (1 if exact else 2)
     x = seeded_x(39)
     chain.x0.copy_(x)
     out = chain.replay()
@@ -120,13 +135,68 @@ def test_stack_many_layers(nv):
                  rel_l2=chain_tol(39), what="39-layer stack")
 
 
-def test_stack_out_of_range_expert_is_reported(nv):
+def test_stack_out_of_range_expert_is_reported(nv, exact):
     blocks, _, routing = layers(nv, 2, seed=700)
     bad = [(routing[0][0].clone(), routing[0][1]), routing[1]]
     bad[0][0][0, 3] = 999  # 32 experts
-    chain = nv.MoEDecodeChain(blocks, bad, T=1, device=DEV).capture()
+    chain = make_chain(nv, blocks, bad, exact)
     assert chain.stack
     chain.replay()
     with pytest.raises(nv.DeviceIndexError):
         nv.device_status()
     nv.device_status()  # the latch was cleared
+
+
+@pytest.mark.parametrize("with_shared,n,launches", [(False, 42, 2), (True, 21, 2), (False, 40, 1)])
+def test_fp4_stack_split_over_launches(nv, with_shared, n, launches):
+    """More layers than one launch's tensor maps hold (40, 20 with a shared
+    expert): the FP4 stack continues in a further launch from the previous
+    one's per-segment partial sums.  Bit-identical to the same layers run as
+    consecutive single-launch stacks.  (A long chain of SwiGLU layers without a
+    residual is quadratic per layer, so it is compared with itself, not with
+    another arithmetic.)"""
+    blocks, _, routing = layers(nv, 3, with_shared=with_shared, seed=1300)
+    sb = [blocks[l % 3] for l in range(n)]
+    sr = [routing[l % 3] for l in range(n)]
+    chain = make_chain(nv, sb, sr, False)
+    assert chain.stack and chain.launches_per_step() == launches
+    per = 20 if with_shared else 40
+    x = seeded_x(n)
+    chain.x0.copy_(x)
+    out = chain.replay().clone()
+    y = x
+    # (no device synchronisation between the chains: each call is ordered
+    # after the caller's stream, so two stacks never share the GPU)
+    for a in range(0, n, per):
+        part = make_chain(nv, sb[a:a + per], sr[a:a + per], False)
+        assert part.launches_per_step() == 1
+        part.x0.copy_(y)
+        y = part.replay().clone()
+    nv.device_status()
+    assert torch.equal(out, y)
+
+
+def test_stacks_tiny_input(nv, exact):
+    """A row below 2^-100 (bf16 subnormals included) gives zeros, not NaN."""
+    blocks, _, routing = layers(nv, 2, seed=1700)
+    chain = make_chain(nv, blocks, routing, exact)
+    chain.x0.copy_((seeded_x(3).float() * 1e-38).to(torch.bfloat16))
+    out = chain.replay()
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    assert float(out.float().abs().max()) < 1e-30
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_fp4_stack_other_dtypes(nv, dtype):
+    blocks, _, routing = layers(nv, 2, with_shared=True, seed=1500)
+    chain = make_chain(nv, blocks, routing, False, dtype=dtype)
+    assert chain.stack
+    x = seeded_x(7).to(dtype)
+    chain.x0.copy_(x)
+    out = chain.replay()
+    torch.cuda.synchronize()
+    want = layer_by_layer(blocks, routing, x)
+    assert out.dtype == dtype
+    assert_close(out.float().cpu().numpy(), want.float().cpu().numpy(), max_abs=float("inf"),
+                 rel_l2=chain_tol(2), what=f"FP4 stack, {dtype}")
