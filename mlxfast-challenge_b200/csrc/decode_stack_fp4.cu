@@ -126,6 +126,8 @@ struct FsSmem {
   uint64_t *full, *empty, *sfr, *xready, *aready, *gufull, *dfull, *drain;
   uint32_t* tslot;
   int* bar_ok;
+  volatile int* hold;  // refills wait (MMA start to the loads after the next barrier)
+  volatile int* cur;   // the layer the chain is in: its stages are never held
   uint32_t* inds;
   float* wts;
 };
@@ -157,6 +159,8 @@ __host__ __device__ inline size_t fs_carve(int H, int I, int L, uint8_t* base, F
   t.drain = reinterpret_cast<uint64_t*>(take(8, 8));
   t.tslot = reinterpret_cast<uint32_t*>(take(4, 4));
   t.bar_ok = reinterpret_cast<int*>(take(4, 4));
+  t.hold = reinterpret_cast<volatile int*>(take(4, 4));
+  t.cur = reinterpret_cast<volatile int*>(take(4, 4));
   t.inds = reinterpret_cast<uint32_t*>(take((size_t)L * 16 * 4, 16));
   t.wts = reinterpret_cast<float*>(take((size_t)L * 16 * 4, 16));
   if (S) *S = t;
@@ -167,14 +171,16 @@ __host__ __device__ inline size_t fs_carve(int H, int I, int L, uint8_t* base, F
 // NVFP4 terms, in the chain warps: thread ct holds the V values k0 = kb + ct *
 // V .. k0 + V - 1 (a group of 16 spans 16 / V threads), so chain warp w holds
 // the run of 32 V values from kb + 32 V w.  Each run is decomposed on its own
-// (its own power-of-two factor per term: warp shuffles only; the MMAs keep one
-// accumulator per run).  Per term: group max (shuffle), the run's max, the
-// factor, the group's UE4M3 scale, codes by the hardware converter into the B
-// tile (row t, 128-byte swizzle), the residual updated with the values the
-// codes stand for.  Writes the scale bytes sSc[t][group] (groups of the whole
+// (its own power-of-two factors: warp shuffles only; the MMAs keep one
+// accumulator per run).  The run's max sets term 0's factor, which places its
+// largest group scale in [171, 352]; term t's factor is 4^-t times that.  Per
+// term: group max (shuffle), the group's UE4M3 scale, codes by the hardware
+// converter into the B tile (row t, 128-byte swizzle), the residual updated
+// with the values the codes stand for.  Writes the scale bytes sSc[t][group] (groups of the whole
 // row, K / 16 per term) and the factors fac[4 w + t]; ends with a chain
-// barrier.  Follows rows_to_terms_kernel (prefill_fp4.cu) value for value,
-// over the run instead of the row.
+// barrier.  Follows rows_to_terms_kernel (prefill_fp4.cu), over the run
+// instead of the row and with the factor progression above instead of one
+// max per term.
 template <int V>
 __device__ __forceinline__ void make_terms(float (&v)[V], int ct, int K, int kb, uint8_t* sB,
                                            uint8_t* sSc, float* fac) {
@@ -188,19 +194,30 @@ __device__ __forceinline__ void make_terms(float (&v)[V], int ct, int K, int kb,
   bool bad = false;
 #pragma unroll
   for (int j = 0; j < V; j++) bad |= !isfinite(v[j]);
+  // The run's factor from its max, once: term t uses P * 4^t.  The largest
+  // term-0 group scale lies in [171, 352]; a term's residual is at most its
+  // group scale (E2M1 spacing 2 at the top, no saturation since scales round
+  // up), so term t + 1's scales stay <= 2/3 of term t's bound (<= 240): no
+  // E4M3 overflow, and 3 mantissa bits at every normal magnitude.
+  float m;
+  {
+    float a0 = 0.f;
 #pragma unroll
-  for (int t = 0; t < kT; t++) {
+    for (int j = 0; j < V; j++) a0 = fmaxf(a0, fabsf(v[j]));
+    m = warp_max(bad ? INFINITY : a0);
+  }
+  const int em = (__float_as_int(m) >> 23) & 0xFF;
+  const bool live = m >= 7.9e-31f && m < INFINITY;
+  float P = live ? __int_as_float((127 + 10 - (em - 127)) << 23) : 0.f;
+  float f = live ? __int_as_float((127 - 10 + (em - 127)) << 23)
+                 : (m == INFINITY ? __int_as_float(0x7fc00000) : 0.f);
+#pragma unroll
+  for (int t = 0; t < kT; t++, P *= 4.0f, f *= 0.25f) {
     float amax = 0.f;
 #pragma unroll
     for (int j = 0; j < V; j++) amax = fmaxf(amax, fabsf(v[j]));
 #pragma unroll
     for (int o = 1; o < TPG; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float m = warp_max(bad ? INFINITY : amax);
-    const int em = (__float_as_int(m) >> 23) & 0xFF;
-    const bool live = m >= 7.9e-31f && m < INFINITY;
-    const float P = live ? __int_as_float((127 + 10 - (em - 127)) << 23) : 0.f;
-    const float f = live ? __int_as_float((127 - 10 + (em - 127)) << 23)
-                         : (m == INFINITY ? __int_as_float(0x7fc00000) : 0.f);
     const uint32_t b = live ? e4m3_ceil(amax * P * (1.0f / 6.0f)) : 0u;
     const float s = scale_to_f32(b);
     const float inv = s > 0.f ? P * __frcp_rn(s) : 0.f;
@@ -326,6 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(S.gufull, 1);
     mbar_init(S.dfull, 1);
     mbar_init(S.drain, 1);
+    *S.hold = 0;
+    *S.cur = 0;
     fence_barrier_init();
   }
   // Routing of the launch's layers into shared memory once.
@@ -359,6 +378,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (el) fsflag(fs_timeout(l, 41));
         return false;
       }
+      // Refills for a later layer than the chain's wait while the chain's
+      // MMAs, epilogue, grid barrier and the L2 loads behind it run (the hold
+      // flag): a refill burst (the stages an MMA batch just released, up to
+      // 72 KB per CTA) issued then queues ahead of the barrier's atomics and
+      // those loads.  They go out while the chain computes terms.  A stage of
+      // the chain's own layer is never held (its MMA may be waiting for it).
+      // Bounded: a missed release only costs time.
+      if (el && *S.hold && l > *S.cur) {
+        const long long h0 = clock64();
+        while (*S.hold && l > *S.cur && clock64() - h0 < 40000) __nanosleep(64);
+      }
+      __syncwarp();
       return true;
     };
     for (int l = 0; l < a.L && ok; l++) {
@@ -578,6 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool alive = true;
 
       // ---- phase A: x terms, gate/up item -> GUp ----
+      if (ct == 0) *S.cur = l;
       if (has_gu) {
         // only this item's K part of x: its 128 VX values
         float v[VX];
@@ -600,12 +632,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < VX; j++) v[j] = round_to(v[j], a.dtype);
         }
+        if (ct == 0) *S.hold = 0;
         make_terms<VX>(v, ct, H, kb, S.bx, S.scx, S.facx);
         store_term_scales(S.scx, H, kb / 64, (H / a.nks) / 64, tmem + lane_base + kSfbx, lane);
         fence_proxy_async();
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
+        if (ct == 0) *S.hold = 1;
         if (lane == 0) mbar_arrive(S.xready);
         const bool got = mbar_wait_bounded(S.gufull, jgu & 1);
         jgu++;
@@ -648,12 +682,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           v[j + 2] = silu_ref(gv.z) * uv.z;
           v[j + 3] = silu_ref(gv.w) * uv.w;
         }
+        if (ct == 0) *S.hold = 0;
         make_terms<VA>(v, ct, I, 0, S.ba, S.sca, S.faca);
         store_term_scales(S.sca, I, 0, I / 64, tmem + lane_base + kSfba, lane);
         fence_proxy_async();
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
+        if (ct == 0) *S.hold = 1;
         if (lane == 0) mbar_arrive(S.aready);
         const bool got = mbar_wait_bounded(S.dfull, jd & 1);
         jd++;
