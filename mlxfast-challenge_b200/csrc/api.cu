@@ -1124,7 +1124,8 @@ struct StackLayout {
 };
 
 // act / xb: the mma.sync stack; y32 / gu: the FP4 stack's f32 partials
-// ([kk][H] per segment, [2][kk][2][I] per K part); bar: grid-barrier counters.
+// ([2][kk][H] per segment, [2][2][kk][2][I] per K part, both by layer parity);
+// bar: grid-barrier / dependency counters.
 StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   StackLayout S;
   const int64_t kk = L0->top_k + (L0->shared_inter > 0 ? 1 : 0);
@@ -1133,8 +1134,8 @@ StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   S.xb1_off = align_up(S.xb0_off + (size_t)L0->hidden * dtype_bytes, 256);
   S.bar_off = align_up(S.xb1_off + (size_t)L0->hidden * dtype_bytes, 256);
   S.y32_off = align_up(S.bar_off + (2 + 2 * nvfp4::kStackMaxLayers) * sizeof(unsigned), 256);
-  S.gu_off = align_up(S.y32_off + (size_t)kk * L0->hidden * sizeof(float), 256);
-  S.total = align_up(S.gu_off + 2 * (size_t)kk * 2 * L0->inter * sizeof(float), 256);
+  S.gu_off = align_up(S.y32_off + 2 * (size_t)kk * L0->hidden * sizeof(float), 256);
+  S.total = align_up(S.gu_off + 4 * (size_t)kk * 2 * L0->inter * sizeof(float), 256);
   return S;
 }
 
@@ -1279,6 +1280,7 @@ extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64
     for (int64_t l0 = 0; l0 < n_layers; l0 += per_launch) {
       const int nl = (int)std::min<int64_t>(per_launch, n_layers - l0);
       F.L = nl;
+      F.l0 = (int)l0;
       F.first = l0 == 0;
       F.last = l0 + nl == n_layers;
       bool ok = true;

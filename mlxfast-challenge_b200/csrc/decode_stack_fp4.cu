@@ -36,9 +36,11 @@
 //     expert) -> Yp[seg][h]; the next layer's x is sum_seg Yp[seg] in segment
 //     order, rounded to the activation dtype.
 // Every partial has its own slot and is summed in a fixed order: results are
-// the same on every run.  Two grid barriers per layer (after the GUp writes,
-// after the Yp writes); one buffer of each suffices (each is read in the
-// phase after its writes and rewritten only after the next barrier).
+// the same on every run.  No grid-wide barrier: a down item waits for the
+// gate/up items of its segment, a gate/up item for the previous layer's down
+// items of its K part (release/acquire counters).  GUp and Yp alternate
+// between two buffers by layer parity: a buffer is rewritten two layers later,
+// after (through those waits) every reader of its previous contents.
 //
 // Roles (320 threads): warp 0 TMA (this CTA's weight slabs of layer l, l+1,
 // ... in consumption order into a 10-stage ring, so the next layer's weights
@@ -75,7 +77,8 @@ constexpr int kErrIndex = 2;
 // A wait that expired latches 1000 * (layer in the launch + 1) + site, site:
 // 41 TMA ring slot, 42 MMA x terms, 43 MMA gate/up stage, 44 MMA act terms,
 // 45 MMA down stage, 46 MMA drain, 47 scale warps stage, 48 chain gate/up
-// accumulator, 49 chain down accumulator, 50 / 51 grid barrier 1 / 2.
+// accumulator, 49 chain down accumulator, 50 a segment's gate/up items, 51 a
+// K part's down items (previous layer), 52 the last layer's down items.
 __host__ __device__ constexpr int fs_timeout(int l, int site) { return 1000 * (l + 1) + site; }
 constexpr long long kDrainBudget = 200000000LL;
 
@@ -218,7 +221,7 @@ __device__ __forceinline__ void make_terms(float (&v)[V], int ct, int K, int kb,
     for (int j = 0; j < V; j++) amax = fmaxf(amax, fabsf(v[j]));
 #pragma unroll
     for (int o = 1; o < TPG; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const uint32_t b = live ? e4m3_ceil(amax * P * (1.0f / 6.0f)) : 0u;
+    const uint32_t b = live ? e4m3_ceil_fast(amax * P * (1.0f / 6.0f)) : 0u;
     const float s = scale_to_f32(b);
     const float inv = s > 0.f ? P * __frcp_rn(s) : 0.f;
     const float back = s > 0.f ? s * f : 0.f;
@@ -579,14 +582,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     const int r = 32 * q + lane;                    // accumulator row = TMEM lane
     uint32_t jgu = 0, jd = 0;
-    unsigned nb0 = 0, nb1 = 0;
-    // One grid barrier: the chain's global writes and adds, then this CTA's
-    // arrival; thread 0 waits (bounded) for all G CTAs.
-    auto grid_barrier = [&](unsigned* ctr, unsigned& n, int site) -> bool {
-      named_sync(kBarChain, kChain);
+    // Dependency counters (zero at launch): cnt1[seg] counts the gate/up items
+    // of segment seg done (nb * nks per layer), cnt2[p] the down items whose
+    // rows lie in K part p done (kk * H / 128 / nks per layer).  Producers:
+    // the chain's writes, a barrier, then one release add.  Consumers: thread 0
+    // polls (acquire, bounded), then a barrier.
+    unsigned* cnt1 = a.bar;
+    unsigned* cnt2 = a.bar + 16;
+    const unsigned per_seg = (unsigned)(nb * a.nks);
+    const int rb_per_part = H / 128 / a.nks;
+    const unsigned per_part = (unsigned)(a.kk * rb_per_part);
+    auto wait_count = [&](const unsigned* ctr, unsigned target, int l, int site) -> bool {
       if (ct == 0) {
-        red_release_add_fs(ctr, 1u);  // orders this CTA's writes (bar.sync above) first
-        const unsigned target = (unsigned)G * (n + 1);
         bool ok = true;
         if (ld_acquire_fs(ctr) < target) {
           const long long start = clock64();
@@ -599,14 +606,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         *S.bar_ok = ok;
-        if (!ok) fsflag(fs_timeout((int)n, site));
+        if (!ok) fsflag(fs_timeout(l, site));
       }
       named_sync(kBarChain, kChain);
-      n++;
       return *S.bar_ok != 0;
     };
-    for (int l = 0; l < a.L; l++) {
-      bool alive = true;
+    auto signal_count = [&](unsigned* ctr) {
+      named_sync(kBarChain, kChain);
+      if (ct == 0) red_release_add_fs(ctr, 1u);  // orders the CTA's writes (bar.sync) first
+    };
+    bool alive = true;
+    for (int l = 0; l < a.L && alive; l++) {
+      const int lg = a.l0 + l;  // index in the stack: buffer parity
+      float* Yout = a.Yp + (size_t)(lg & 1) * a.kk * H;
+      const float* Yin = a.Yp + (size_t)((lg + 1) & 1) * a.kk * H;
+      float* GUb = a.GUp + (size_t)(lg & 1) * 2 * a.kk * 2 * I;
 
       // ---- phase A: x terms, gate/up item -> GUp ----
       if (ct == 0) *S.cur = l;
@@ -627,8 +641,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 4; i++) v[i] = f[(k0 & 4) + i];
           }
         } else {
+          // the previous layer's down items of this part (previous launch: done)
+          if (l > 0 && !wait_count(&cnt2[gu_p], (unsigned)l * per_part, l, 51)) {
+            alive = false;
+            break;
+          }
           // the previous layer's output: its segments' partials in order
-          load_segment_sum<VX>(a.Yp, H, a.kk, k0, v);
+          load_segment_sum<VX>(Yin, H, a.kk, k0, v);
 #pragma unroll
           for (int j = 0; j < VX; j++) v[j] = round_to(v[j], a.dtype);
         }
@@ -645,18 +664,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         jgu++;
         if (!got && lane == 0) fsflag(fs_timeout(l, 48));
         alive = chain_sync_and(got);
-        if (alive) {
-          tc_fence_after();
-          const float y = fold_runs(tmem + lane_base + kAccGU, S.facx);
-          tc_fence_before();
-          __stcg(a.GUp + ((size_t)(gu_p * a.kk + gu_seg) * 2 + (r >> 6)) * I + gu_b * 64 + (r & 63),
-                 y);
-        }
+        if (!alive) break;
+        tc_fence_after();
+        const float y = fold_runs(tmem + lane_base + kAccGU, S.facx);
+        tc_fence_before();
+        __stcg(GUb + ((size_t)(gu_p * a.kk + gu_seg) * 2 + (r >> 6)) * I + gu_b * 64 + (r & 63), y);
+        signal_count(&cnt1[gu_seg]);
       }
-      if (!alive || !grid_barrier(&a.bar[0], nb0, 50)) break;
 
       // ---- phase B: act terms, down item -> Yp ----
       if (has_d) {
+        if (!wait_count(&cnt1[d_seg], (unsigned)(l + 1) * per_seg, l, 50)) {
+          alive = false;
+          break;
+        }
         float v[VA];
         const int k0 = ct * VA;
 #pragma unroll
@@ -665,7 +686,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int p = 0; p < 2; p++) {
             if (p >= a.nks) break;
-            const float* src = a.GUp + (size_t)(p * a.kk + d_seg) * 2 * I;
+            const float* src = GUb + (size_t)(p * a.kk + d_seg) * 2 * I;
             const float4 g = __ldcg(reinterpret_cast<const float4*>(src + k0 + j));
             const float4 u = __ldcg(reinterpret_cast<const float4*>(src + I + k0 + j));
             gv.x += g.x;
@@ -695,21 +716,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         jd++;
         if (!got && lane == 0) fsflag(fs_timeout(l, 49));
         alive = chain_sync_and(got);
-        if (alive) {
-          tc_fence_after();
-          const float wseg = d_seg < a.k ? S.wts[l * 16 + d_seg] * a.layer[l].scaling : 1.0f;
-          const float y = fold_runs(tmem + lane_base + kAccD, S.faca) * wseg;
-          tc_fence_before();
-          __stcg(a.Yp + (size_t)d_seg * H + d_rb * 128 + r, y);
-        }
+        if (!alive) break;
+        tc_fence_after();
+        const float wseg = d_seg < a.k ? S.wts[l * 16 + d_seg] * a.layer[l].scaling : 1.0f;
+        const float y = fold_runs(tmem + lane_base + kAccD, S.faca) * wseg;
+        tc_fence_before();
+        __stcg(Yout + (size_t)d_seg * H + d_rb * 128 + r, y);
+        signal_count(&cnt2[d_rb / rb_per_part]);
       }
-      if (!alive || !grid_barrier(&a.bar[1], nb1, 51)) break;
-      if (a.last && l == a.L - 1)
-        for (int i = c * kChain + ct; i < H; i += G * kChain) {
-          float y = __ldcg(a.Yp + i);
-          for (int sg = 1; sg < a.kk; sg++) y += __ldcg(a.Yp + (size_t)sg * H + i);
-          store_from_f32(a.y, a.dtype, i, y);
-        }
+    }
+    // The stack's output: this CTA's 128-row block of the last layer, once
+    // every down item of its part is done.
+    if (alive && a.last && c < H / 128) {
+      const int lg = a.l0 + a.L - 1;
+      const float* Yl = a.Yp + (size_t)(lg & 1) * a.kk * H;
+      if (wait_count(&cnt2[c / rb_per_part], (unsigned)a.L * per_part, a.L - 1, 52)) {
+        const int i = c * kChain + ct;
+        float y = __ldcg(Yl + i);
+        for (int sg = 1; sg < a.kk; sg++) y += __ldcg(Yl + (size_t)sg * H + i);
+        store_from_f32(a.y, a.dtype, i, y);
+      }
     }
   }
   __syncthreads();
@@ -781,7 +807,7 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
-  e = cudaMemsetAsync(a.bar, 0, 2 * sizeof(unsigned), stream);
+  e = cudaMemsetAsync(a.bar, 0, 32 * sizeof(unsigned), stream);  // dependency counters
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sms);

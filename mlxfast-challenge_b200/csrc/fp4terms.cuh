@@ -17,6 +17,16 @@ __device__ __forceinline__ uint32_t e4m3_ceil(float v) {
   return b;
 }
 
+// The same for 0 <= v <= 448, branch-free above 2^-6: below 2^-6 the
+// subnormal steps k * 2^-9 (k = ceil(v * 2^9), 8 meaning 2^-6); from 2^-6 up the
+// float's mantissa rounded up to 3 bits (a carry moves into the exponent) and
+// the exponent rebased from bias 127 to bias 7; saturated at 0x7E (448).
+__device__ __forceinline__ uint32_t e4m3_ceil_fast(float v) {
+  if (v < 0.015625f) return (uint32_t)ceilf(v * 512.0f);
+  const uint32_t r = ((__float_as_uint(v) + 0xFFFFFu) >> 20) - (120u << 3);
+  return min(r, 0x7Eu);
+}
+
 // Two values -> one byte of E2M1 codes, rounded to nearest even and saturated
 // at +-6 by the hardware converter (first operand in the high nibble), and the
 // byte back to the two exact values.

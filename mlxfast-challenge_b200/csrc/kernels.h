@@ -160,12 +160,13 @@ struct alignas(64) FsArgs {
   int L;           // layers in this launch
   int first;       // 1: layer 0 of the stack (input x0 in dtype), else the sum of Yp
   int last;        // 1: the launch ends the stack (writes y)
+  int l0;          // stack index of this launch's first layer (buffer parity)
   int H, I, E, k, kk, nks, mpl, dtype;
   const void* x0;  // [H] stack input (dtype)
   void* y;         // [H] stack output (dtype)
-  float* Yp;       // [kk][H] the layer's output per segment (f32)
-  float* GUp;      // [nks][kk][2][I] gate / up pre-activations per K part (f32)
-  unsigned* bar;   // [2] grid-barrier counters, zero at launch
+  float* Yp;       // [2][kk][H] a layer's output per segment (f32), by layer parity
+  float* GUp;      // [2][2][kk][2][I] gate / up pre-activations per K part, by parity
+  unsigned* bar;   // [32] dependency counters, zero at launch
 };
 bool decode_stack_fp4_supported(int H, int I, int kk, int sms);
 int decode_stack_fp4_nks(int I, int kk, int sms);
