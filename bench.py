@@ -17,9 +17,10 @@ value   = algorithmic HBM bytes of all ranks' steps / device time (GB/s), the
 e2e     = the same metric through the public API MoEDecodeChain(x_host): per
           step the input is copied from pinned host memory, the layers run and
           the output is read back to the host.
-roofline= the dominant kernel timed alone: moe_decode_stack_kernel, which runs
-          all 39 layers in one persistent launch (or, where the stack does
-          not apply, the per-layer fused gate/up + SwiGLU kernel).
+roofline= the dominant kernel timed alone: the persistent decode stack, which
+          runs all 39 layers in one launch (moe_decode_stack_fp4_kernel on the
+          block-scaled FP4 tensor cores by default; or, where no stack
+          applies, the per-layer fused gate/up + SwiGLU kernel).
 
 --impl reference times the reference's own MLX CPU kernel (fp_qmm_t for bf16
 x, compiled from the reference sources into oracle/_ref) on the same layer,
@@ -336,11 +337,12 @@ def measured_peak_hbm():
         return 6650.0, "fallback"
 
 
-def stack_traffic(layers):
-    """DRAM bytes of one moe_decode_stack_kernel launch over `layers` layers,
-    scaled from the committed ncu capture (taken on fewer layers; the kernel
-    moves the same bytes per layer)."""
-    p = os.path.join(ROOT, "profiles", "moe_decode_stack_traffic.json")
+def stack_traffic(layers, fp4=True):
+    """DRAM bytes of one decode-stack launch over `layers` layers (the FP4 or
+    the mma.sync stack), scaled from the committed ncu capture (taken on fewer
+    layers; the kernel moves the same bytes per layer)."""
+    p = os.path.join(ROOT, "profiles", "moe_decode_stack_fp4_traffic.json" if fp4
+                     else "moe_decode_stack_traffic.json")
     try:
         with open(p) as f:
             d = json.load(f)
@@ -472,9 +474,11 @@ def main():
         torch.cuda.synchronize()
         k_ms = e0.elapsed_time(e1) / reps
         achieved = bytes_step / (k_ms / 1e3) / 1e9
-        tr = stack_traffic(args.layers)
-        roofline = {"bound": "hbm", "kernel": f"moe_decode_stack_kernel ({args.layers} layers, "
-                                              "one persistent launch)",
+        tr = stack_traffic(args.layers, chain.stack_fp4)
+        kname = ("moe_decode_stack_fp4_kernel (tcgen05 kind::mxf4nvf4" if chain.stack_fp4
+                 else "moe_decode_stack_kernel (mma.sync")
+        roofline = {"bound": "hbm", "kernel": f"{kname}, {args.layers} layers, "
+                                              f"{chain.launches_per_step()} persistent launch)",
                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                     "peak_source": peak_src, "traffic": tr,
                     "algorithmic_bytes_per_launch": bytes_step, "us_per_launch": k_ms * 1e3}

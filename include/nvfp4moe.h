@@ -271,10 +271,13 @@ NVFP4MOE_API int moe_down_combine(void* y, const float* act, int64_t act_ld,
  * NVFP4_LAUNCH_EXACT_DECODE) the products run on the block-scaled FP4 tensor
  * cores, up to 40 layers per launch (20 with a shared expert);
  * moe_decode_stack_launches gives the number of launches a call makes under
- * the calling thread's flags. */
+ * the calling thread's flags, moe_decode_stack_uses_fp4 which stack runs. */
 NVFP4MOE_API size_t moe_decode_stack_workspace_size(const moe_layer_desc* layers,
                                                     int64_t n_layers);
 NVFP4MOE_API int moe_decode_stack_launches(const moe_layer_desc* layers, int64_t n_layers);
+/* 1 when a call runs the block-scaled FP4 stack (shape supported and
+ * NVFP4_LAUNCH_EXACT_DECODE clear), 0 for the mma.sync stack. */
+NVFP4MOE_API int moe_decode_stack_uses_fp4(const moe_layer_desc* layers, int64_t n_layers);
 NVFP4MOE_API int moe_decode_stack_forward(void* y, const void* x, int dtype, int64_t n_layers,
                                           const moe_layer_desc* layers,
                                           const uint32_t* const* inds,

@@ -76,6 +76,7 @@ SIGNATURES = {
                               _P]),
     "moe_decode_stack_workspace_size": (_SZ, [ctypes.POINTER(MoeLayerDesc), _I64]),
     "moe_decode_stack_launches": (_I, [ctypes.POINTER(MoeLayerDesc), _I64]),
+    "moe_decode_stack_uses_fp4": (_I, [ctypes.POINTER(MoeLayerDesc), _I64]),
     "moe_decode_stack_forward": (_I, [_P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P, _P,
                                       _SZ, _P]),
     "moe_ep_dispatch": (_I, [_P, _P, _P, _P, _P, _I, _P, _I64, _I, _I64, _I64, _I, _P]),

@@ -1202,6 +1202,11 @@ extern "C" size_t moe_decode_stack_workspace_size(const moe_layer_desc* layers,
   return stack_layout(&layers[0], 4).total;  // sized for the widest dtype
 }
 
+extern "C" int moe_decode_stack_uses_fp4(const moe_layer_desc* layers, int64_t n_layers) {
+  if (!layers || n_layers <= 0) return 0;
+  return fp4_stack_layers_per_launch(&layers[0]) > 0 ? 1 : 0;
+}
+
 extern "C" int moe_decode_stack_launches(const moe_layer_desc* layers, int64_t n_layers) {
   if (!layers || n_layers <= 0) return 0;
   const int per = fp4_stack_layers_per_launch(&layers[0]);

@@ -77,6 +77,7 @@ class MoEDecodeChain:
 
     def _stack_call(self, stream_ptr) -> int:
         self._stack_launches = lib().moe_decode_stack_launches(self._descs, len(self.blocks))
+        self.stack_fp4 = bool(lib().moe_decode_stack_uses_fp4(self._descs, len(self.blocks)))
         return lib().moe_decode_stack_forward(
             self.bufs[0].data_ptr(), self.x0.data_ptr(), self._dt, len(self.blocks), self._descs,
             ctypes.cast(self._inds, ctypes.c_void_p), ctypes.cast(self._wts, ctypes.c_void_p),
