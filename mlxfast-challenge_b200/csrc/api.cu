@@ -1238,19 +1238,20 @@ extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64
   }
   if (H % 256 || I % 256 || (Is != 0 && Is != I) || k > 16 || E > 0x7fffffff)
     return fail(NVFP4_ERR_UNSUPPORTED, "[%s] unsupported layer shape.", op);
-  // each consumer thread holds at most 2 x chunks and 4 act chunks of 8 values
-  if (H > 4096 || (k + (Is > 0 ? 1 : 0)) * I > 8192)
+  const int per_launch = fp4_stack_layers_per_launch(L0);
+  // mma.sync stack: each consumer thread holds at most 2 x chunks and 4 act
+  // chunks of 8 values, and its rings must fit on chip
+  const int kk = (int)(k + (Is > 0 ? 1 : 0));
+  if (per_launch == 0 && (H > 4096 || kk * I > 8192))
     return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layer too wide for the persistent stack.", op);
+  if (per_launch == 0 && nvfp4::decode_stack_smem_bytes((int)H, (int)I, kk) > 227 * 1024)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layer too large for the on-chip rings.", op);
   const int esz = dtype == NVFP4_F32 ? 4 : 2;
   if (!aligned16(x) || !aligned16(y))
     return fail(NVFP4_ERR_UNSUPPORTED, "[%s] x and y must be 16-byte aligned.", op);
   const StackLayout S = stack_layout(L0, esz);
   if (!workspace || workspace_bytes < S.total)
     return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, S.total);
-  const int kk = (int)(k + (Is > 0 ? 1 : 0));
-  if (nvfp4::decode_stack_smem_bytes((int)H, (int)I, kk) > 227 * 1024)
-    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layer too large for the on-chip rings.", op);
-  const int per_launch = fp4_stack_layers_per_launch(L0);
   if (per_launch > 0) {
     // Block-scaled FP4 stack: per launch up to per_launch layers, their tensor
     // maps encoded here.

@@ -200,3 +200,29 @@ def test_fp4_stack_other_dtypes(nv, dtype):
     assert out.dtype == dtype
     assert_close(out.float().cpu().numpy(), want.float().cpu().numpy(), max_abs=float("inf"),
                  rel_l2=chain_tol(2), what=f"FP4 stack, {dtype}")
+
+
+@pytest.mark.parametrize("H,I,with_shared", [(2048, 1024, True), (1024, 512, True),
+                                             (1024, 1024, False)])
+def test_fp4_stack_other_shapes(nv, H, I, with_shared):
+    """Layer shapes other than Laguna's that the FP4 stack takes (one K part of
+    x per gate/up item at I = 1024, a half-width hidden size): the same layers
+    through the per-layer kernels agree within the chain bound."""
+    lag = importlib.import_module(PKG + ".laguna")
+    cfg = lag.LagunaMoEConfig(hidden=H, inter=I, shared_inter=I, n_experts=32)
+    n = 2
+    blocks = [lag.random_sparse_layer(nv, seed=1900 + l, device=DEV, cfg=cfg, n_experts=32,
+                                      with_shared=with_shared)[0] for l in range(n)]
+    routing = [lag.random_routing(1, cfg, seed=2000 + l, device=DEV) for l in range(n)]
+    chain = make_chain(nv, blocks, routing, False)
+    assert chain.stack and chain.stack_fp4
+    g = torch.Generator(device=DEV).manual_seed(H + I)
+    x = torch.randn(1, H, generator=g, device=DEV).to(torch.bfloat16)
+    chain.x0.copy_(x)
+    out = chain.replay().clone()
+    torch.cuda.synchronize()
+    nv.device_status()
+    want = layer_by_layer(blocks, routing, x)
+    assert_close(out.float().cpu().numpy(), want.float().cpu().numpy(), max_abs=float("inf"),
+                 rel_l2=chain_tol(n), what=f"FP4 stack H={H} I={I}")
+    assert float(want.float().abs().max()) > 0
