@@ -33,12 +33,26 @@ constexpr int kRouterPad = 32;  // bf16 elements of padding per staged column
 // of lg[s * stride + e], rounded to the activation dtype as the reference's
 // matmul returns it; sigmoid; bias for choice; top-k by choice (ties to the
 // lower id); weights s / sum(s) when norm.
-__device__ void route_token(const RouterArgs& a, int64_t tok, const float* lg, int64_t stride,
-                            int slices, int lane) {
-  // Lane owns experts lane + 32 j, j < 16 (E <= 512); fully unrolled so the
-  // per-lane arrays stay in registers.
-  constexpr int kPer = 16;
-  float sc[kPer], ch[kPer];
+//
+// Lane owns experts lane + 32 j, j < kPer (E <= 32 kPer), fully unrolled so
+// the per-lane arrays stay in registers.  Each candidate is one 64-bit key:
+// the choice's bits made order-preserving as an unsigned integer, then the
+// complement of the expert id (equal choices: the lower id is the larger
+// key); 0 marks an entry already taken, padding, or a NaN choice (never
+// chosen, as a NaN never compares greater).  A round is a lane-local max, a
+// 5-step shuffle max of the key, and the winner's score from its lane.
+__device__ __forceinline__ uint64_t choice_key(float c, uint32_t e) {
+  if (!(c > -INFINITY)) return 0ull;  // -inf (padding) and NaN
+  const uint32_t b = __float_as_uint(c + 0.0f);  // -0 as +0: equal choices tie by id
+  const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((uint64_t)o << 32) | (uint64_t)(0xFFFFFFFFu - e);
+}
+
+template <int kPer>
+__device__ void route_token_t(const RouterArgs& a, int64_t tok, const float* lg, int64_t stride,
+                              int slices, int lane) {
+  float sc[kPer];
+  uint64_t key[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; j++) {
     const int64_t e = lane + 32 * j;
@@ -48,50 +62,52 @@ __device__ void route_token(const RouterArgs& a, int64_t tok, const float* lg, i
       if (live) l += __ldcg(lg + (int64_t)s * stride + e);
     if (a.dtype == kBF16) l = __bfloat162float(__float2bfloat16_rn(l));
     else if (a.dtype == kF16) l = __half2float(__float2half_rn(l));
-    const float s = sigmoid_ref(l);
-    sc[j] = live ? s : 0.f;
-    ch[j] = live ? s + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
+    const float sg = sigmoid_ref(l);
+    sc[j] = live ? sg : 0.f;
+    key[j] = live ? choice_key(sg + (a.bias ? a.bias[e] : 0.f), (uint32_t)e) : 0ull;
   }
   float wsum = 0.f;
   float wsel = 0.f;
   uint32_t isel = 0;
   for (int r = 0; r < a.k; r++) {
-    // Lane-local best (highest choice, then lowest id = lowest j).
-    float bv = -INFINITY, bs = 0.f;
-    int bj = -1;
+    uint64_t bk = key[0];
+    float bs = sc[0];
 #pragma unroll
-    for (int j = 0; j < kPer; j++)
-      if (ch[j] > bv) {
-        bv = ch[j];
+    for (int j = 1; j < kPer; j++)
+      if (key[j] > bk) {
+        bk = key[j];
         bs = sc[j];
-        bj = j;
       }
-    int bid = bj >= 0 ? lane + 32 * bj : 0x7fffffff;
+    uint64_t wk = bk;
+#pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oid = __shfl_xor_sync(0xffffffffu, bid, o);
-      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
-      if (ov > bv || (ov == bv && oid < bid)) {
-        bv = ov;
-        bid = oid;
-        bs = os;
-      }
+      const uint64_t ok = __shfl_xor_sync(0xffffffffu, wk, o);
+      wk = ok > wk ? ok : wk;
     }
-    if (bid != 0x7fffffff && (bid & 31) == lane) {
+    const uint32_t bid = wk ? 0xFFFFFFFFu - (uint32_t)wk : 0x7fffffffu;
+    const float ws = __shfl_sync(0xffffffffu, bs, (int)(bid & 31));
+    if (wk && (int)(bid & 31) == lane) {
 #pragma unroll
       for (int j = 0; j < kPer; j++)
-        if (j == (bid >> 5)) ch[j] = -INFINITY;
+        if (key[j] == wk) key[j] = 0ull;
     }
-    wsum += bs;
+    const float s = wk ? ws : 0.f;
+    wsum += s;
     if (lane == r) {
-      wsel = bs;
-      isel = (uint32_t)bid;
+      wsel = s;
+      isel = bid;
     }
   }
   if (lane < a.k) {
     a.inds[tok * a.k + lane] = isel;
     a.wts[tok * a.k + lane] = a.norm ? wsel / wsum : wsel;
   }
+}
+
+__device__ void route_token(const RouterArgs& a, int64_t tok, const float* lg, int64_t stride,
+                            int slices, int lane) {
+  if (a.E <= 256) route_token_t<8>(a, tok, lg, stride, slices, lane);
+  else route_token_t<16>(a, tok, lg, stride, slices, lane);
 }
 
 __global__ void __launch_bounds__(kRouterWarps * 32) router_kernel(RouterArgs a) {
