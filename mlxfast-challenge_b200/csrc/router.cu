@@ -39,8 +39,8 @@ constexpr int kRouterPad = 32;  // bf16 elements of padding per staged column
 // the choice's bits made order-preserving as an unsigned integer, then the
 // complement of the expert id (equal choices: the lower id is the larger
 // key); 0 marks an entry already taken, padding, or a NaN choice (never
-// chosen, as a NaN never compares greater).  A round is a lane-local max, a
-// 5-step shuffle max of the key, and the winner's score from its lane.
+// chosen, as a NaN never compares greater).  A round is a lane-local max, the
+// warp max of the key (two redux.sync), and the winner's score from its lane.
 __device__ __forceinline__ uint64_t choice_key(float c, uint32_t e) {
   if (!(c > -INFINITY)) return 0ull;  // -inf (padding) and NaN
   const uint32_t b = __float_as_uint(c + 0.0f);  // -0 as +0: equal choices tie by id
@@ -78,12 +78,12 @@ __device__ void route_token_t(const RouterArgs& a, int64_t tok, const float* lg,
         bk = key[j];
         bs = sc[j];
       }
-    uint64_t wk = bk;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const uint64_t ok = __shfl_xor_sync(0xffffffffu, wk, o);
-      wk = ok > wk ? ok : wk;
-    }
+    // warp max of the 64-bit key: the high words, then the low words among
+    // the lanes holding that high word (redux.sync, one instruction each)
+    const uint32_t hi = (uint32_t)(bk >> 32);
+    const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
+    const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? (uint32_t)bk : 0u);
+    const uint64_t wk = ((uint64_t)mhi << 32) | mlo;
     const uint32_t bid = wk ? 0xFFFFFFFFu - (uint32_t)wk : 0x7fffffffu;
     const float ws = __shfl_sync(0xffffffffu, bs, (int)(bid & 31));
     if (wk && (int)(bid & 31) == lane) {
