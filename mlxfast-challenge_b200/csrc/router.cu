@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(128) router_logits_kernel(RouterArgs a) {
 // 16-byte fragment reads are conflict-free); warp w computes experts
 // 16*(w&1).. x tokens 16*(w>>1).. with mma.sync m16n8k16 bf16 (same K
 // permutation in A and B as above).
-constexpr int kLgStages = 4;
+constexpr int kLgStages = 6;
 constexpr int kLgPitch = 192;                   // bytes per staged row (128 + pad)
 constexpr int kLgTile = 32 * kLgPitch;          // one 32-row operand tile
 __device__ __forceinline__ void cp_async16_lg(void* dst, const void* src, bool valid) {
