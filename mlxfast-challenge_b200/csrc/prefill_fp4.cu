@@ -10,8 +10,9 @@
 //
 // term t being the NVFP4 quantisation (UE4M3 scale per group of 16, E2M1
 // codes rounded to nearest even) of the row's residual after terms 0..t-1,
-// under a power-of-two factor per (row, term) that places the row's largest
-// group scale in [171, 341].  Each term cuts the residual by at least 6x per
+// under a power-of-two factor per (row, term): the row's max places its largest
+// term-0 group scale in [171, 352], term t's factor is 4^-t times that (each
+// term's scales stay in E4M3's normal range).  Each term cuts the residual by at least 6x per
 // group; four terms reproduce the W4A16 product to a relative-L2 of ~5e-5
 // (N(0,1) rows and SwiGLU outputs, measured on the CPU), 100x inside the
 // path's 5e-3 tolerance.  The weight operand is the checkpoint's NVFP4 data as
@@ -104,10 +105,10 @@ __device__ __forceinline__ bool sync_and(int id, int count, bool pred) {
 }
 
 // rows_to_terms: one CTA of K / 512 warps per source row; lane l of warp w
-// owns group 32 w + l (16 consecutive values).  Per term: the row max (warp
-// shuffle + shared memory across the warps), the group's UE4M3 scale (the
-// smallest >= amax * P / 6), codes by the hardware converter, the residual
-// updated with the values the codes stand for.
+// owns group 32 w + l (16 consecutive values).  The row max (warp shuffle +
+// shared memory across the warps) sets the factors; per term: the group's
+// UE4M3 scale (the smallest >= amax * P / 6), codes by the hardware converter,
+// the residual updated with the values the codes stand for.
 __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
   __shared__ float wmax[2][4];
   pdl_wait_f();
@@ -117,6 +118,7 @@ __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
   const int64_t K = a.K;
   const int64_t cb = K / 2, sbytes = K / 16;  // bytes per term row
   const int grp = 32 * warp + lane;
+  int it = 0;  // rows this CTA has decomposed
   for (int64_t r = blockIdx.x; r < a.rows; r += gridDim.x) {
     const bool extra = a.extra_base >= 0 && r >= a.extra_lo && r < a.extra_hi;
     if (a.dst_map && !extra) {  // a row no slot reads (expert-parallel: all foreign)
@@ -136,32 +138,43 @@ __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
     bool bad = false;
 #pragma unroll
     for (int j = 0; j < 16; j++) bad |= !isfinite(v[j]);
+    // The row's max sets term 0's factor P = 2^(10 - floor(log2 m)) (m * P in
+    // [1024, 2048): the largest group scale in [171, 352]); term t uses P * 4^t.
+    // A term's residual is at most its group scale (E2M1 spacing 2 at the top,
+    // no saturation as scales round up), so the next term's scales stay <= 2/3
+    // of this term's bound: no E4M3 overflow, one row max instead of four.
+    float m;
+    {
+      float a0 = 0.f;
 #pragma unroll
-    for (int t = 0; t < kT; t++) {
+      for (int j = 0; j < 16; j++) a0 = fmaxf(a0, fabsf(v[j]));
+      m = warp_max(bad ? INFINITY : a0);
+      if (nw > 1) {  // buffer by row parity: the next row's writes pass one barrier first
+        if (lane == 0) wmax[it & 1][warp] = m;
+        __syncthreads();
+        m = wmax[it & 1][0];
+        for (int w = 1; w < nw; w++) m = fmaxf(m, wmax[it & 1][w]);
+      }
+    }
+    // Exponent arithmetic on normal floats (rows whose max is below 2^-100,
+    // zero or not finite get no terms).
+    const int em = (__float_as_int(m) >> 23) & 0xFF;  // biased exponent of m
+    const bool live = m >= 7.9e-31f && m < INFINITY;
+    float P = live ? __int_as_float((127 + 10 - (em - 127)) << 23) : 0.f;
+    float f = live ? __int_as_float((127 - 10 + (em - 127)) << 23)  // 1 / P
+                   : (m == INFINITY ? __int_as_float(0x7fc00000) : 0.f);
+#pragma unroll
+    for (int t = 0; t < kT; t++, P *= 4.0f, f *= 0.25f) {
       float amax = 0.f;
 #pragma unroll
       for (int j = 0; j < 16; j++) amax = fmaxf(amax, fabsf(v[j]));
-      float m = warp_max(bad ? INFINITY : amax);
-      if (nw > 1) {
-        if (lane == 0) wmax[t & 1][warp] = m;
-        __syncthreads();
-        m = wmax[t & 1][0];
-        for (int w = 1; w < nw; w++) m = fmaxf(m, wmax[t & 1][w]);
-      }
-      // P = 2^(10 - floor(log2 m)): m * P in [1024, 2048).  Exponent
-      // arithmetic on normal floats (rows whose max is below 2^-100, zero or
-      // not finite get no terms).
-      const int em = (__float_as_int(m) >> 23) & 0xFF;  // biased exponent of m
-      const bool live = m >= 7.9e-31f && m < INFINITY;
-      const float P = live ? __int_as_float((127 + 10 - (em - 127)) << 23) : 0.f;
-      fac[t] = live ? __int_as_float((127 - 10 + (em - 127)) << 23)  // 1 / P
-                    : (m == INFINITY ? __int_as_float(0x7fc00000) : 0.f);
-      const uint32_t b = live ? e4m3_ceil(amax * P * (1.0f / 6.0f)) : 0u;
+      fac[t] = f;
+      const uint32_t b = live ? e4m3_ceil_fast(amax * P * (1.0f / 6.0f)) : 0u;
       const float s = scale_to_f32(b);
       // |v * inv| <= 6 up to rounding (the converter saturates there); the
       // residual below uses the exact value the code stands for
       const float inv = s > 0.f ? P * __frcp_rn(s) : 0.f;
-      const float back = s > 0.f ? s * fac[t] : 0.f;  // s > 0 only for live rows
+      const float back = s > 0.f ? s * f : 0.f;  // s > 0 only for live rows
       uint32_t w[2] = {0u, 0u};
 #pragma unroll
       for (int j = 0; j < 16; j += 2) {
@@ -174,6 +187,7 @@ __global__ void __launch_bounds__(128) rows_to_terms_kernel(TermsArgs a) {
       code[t] = make_uint2(w[0], w[1]);
       sb[t] = b;
     }
+    it++;
     // Every destination slot of this row.
     const int nd = a.dst_map ? a.map_count : 0;
     for (int d = -1; d < nd + 1; d++) {
