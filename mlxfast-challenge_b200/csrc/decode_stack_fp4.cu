@@ -45,10 +45,10 @@
 // Roles (320 threads): warp 0 TMA (this CTA's weight slabs of layer l, l+1,
 // ... in consumption order into a 10-stage ring, so the next layer's weights
 // stream while this layer's chain runs), warp 1 MMA issue, warps 2-5 weight
-// scales into tensor memory, warps 6-9 the chain (terms, epilogues, grid
-// barriers).  Every wait is bounded; on expiry error 4 is latched and each
-// role leaves its loop (the copies and MMAs it issued drained) before tensor
-// memory is released.
+// scales into tensor memory, warps 6-9 the chain (terms, epilogues, the
+// dependency counters).  Every wait is bounded; on expiry an error is latched
+// (the site code below) and each role leaves its loop (the copies and MMAs it
+// issued drained) before tensor memory is released.
 #include "common.cuh"
 #include "fp4terms.cuh"
 #include "kernels.h"
@@ -382,9 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         return false;
       }
       // Refills for a later layer than the chain's wait while the chain's
-      // MMAs, epilogue, grid barrier and the L2 loads behind it run (the hold
+      // MMAs, epilogue, dependency wait and the L2 loads behind it run (the hold
       // flag): a refill burst (the stages an MMA batch just released, up to
-      // 72 KB per CTA) issued then queues ahead of the barrier's atomics and
+      // 72 KB per CTA) issued then queues ahead of the counters' atomics and
       // those loads.  They go out while the chain computes terms.  A stage of
       // the chain's own layer is never held (its MMA may be waiting for it).
       // Bounded: a missed release only costs time.
@@ -802,7 +802,8 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   if (decode_stack_fp4_nks(a.I, a.kk, sms) != a.nks || a.kk * (a.H / 128) > sms)
     return cudaErrorInvalidValue;
-  // Every CTA must be resident (grid barriers): one per SM, cooperative launch.
+  // Every CTA must be resident (CTAs wait on one another's counters): one per
+  // SM, cooperative launch.
   int per_sm = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
   if (e != cudaSuccess) return e;
