@@ -226,3 +226,18 @@ def test_fp4_stack_other_shapes(nv, H, I, with_shared):
     assert_close(out.float().cpu().numpy(), want.float().cpu().numpy(), max_abs=float("inf"),
                  rel_l2=chain_tol(n), what=f"FP4 stack H={H} I={I}")
     assert float(want.float().abs().max()) > 0
+
+
+def test_stacks_nonfinite_input(nv, exact):
+    """A non-finite activation gives a non-finite layer output, as the
+    reference's products do (the FP4 stack writes NaN term factors for a run
+    holding one)."""
+    blocks, _, routing = layers(nv, 2, seed=2100)
+    chain = make_chain(nv, blocks, routing, exact)
+    x = seeded_x(11)
+    x[0, 700] = float("inf")
+    chain.x0.copy_(x)
+    out = chain.replay()
+    torch.cuda.synchronize()
+    nv.device_status()
+    assert not bool(torch.isfinite(out.float()).all())
