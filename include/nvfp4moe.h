@@ -49,7 +49,8 @@ enum {
   NVFP4_ERR_UNSUPPORTED = 2,  /* valid for the reference, not provided here */
   NVFP4_ERR_CUDA = 3,         /* CUDA runtime error */
   NVFP4_ERR_WORKSPACE = 4,    /* workspace missing or too small */
-  NVFP4_ERR_DEVICE_INDEX = 5  /* latched by kernels: index out of range */
+  NVFP4_ERR_DEVICE_INDEX = 5,  /* latched by kernels: index out of range */
+  NVFP4_ERR_DEVICE_TIMEOUT = 6 /* latched by kernels: a bounded wait expired */
 };
 
 /* Activation / output dtypes. */
@@ -93,8 +94,11 @@ NVFP4MOE_API int nvfp4_version(void);
  * activations, exact products). */
 #define NVFP4_LAUNCH_EXACT_DECODE 8
 NVFP4MOE_API int nvfp4_set_launch_flags(int flags);
-/* Synchronises the device, returns and clears the latched device status
- * (NVFP4_OK or NVFP4_ERR_DEVICE_INDEX). */
+/* Synchronises the device, returns and clears the latched device status:
+ * NVFP4_OK, NVFP4_ERR_DEVICE_INDEX, or NVFP4_ERR_DEVICE_TIMEOUT when a kernel's
+ * bounded wait (on a copy, a tensor-core commit or another CTA's counter)
+ * gave up -- the kernel then returned early and its outputs are not valid;
+ * the message names the kernel site.  The context stays usable. */
 NVFP4MOE_API int nvfp4_device_status(void);
 
 /* mlx_dequantize (mlx-c ops.h:359; ops.cpp:5120-5241 fp_dequantize), mode
@@ -156,6 +160,14 @@ NVFP4MOE_API int nvfp4_gather_qmm(void* out, const void* x, int dtype, const uin
                                   const uint32_t* rhs_indices, int64_t pairs,
                                   int64_t n_x_batches, int64_t n_experts, int64_t M, int64_t N,
                                   int64_t K, int sorted_indices, nvfp4_stream stream);
+
+/* mlx_fast_rms_norm (mlx-c fast.h:163; mlx/fast.cpp:53-108), as the CPU
+ * evaluates it: y[r] = dtype(dtype(x[r] * rsqrt(mean(x[r]^2) + eps)) * weight),
+ * the mean of f32 squares.  x, y [rows, dims] and weight [dims] (NULL:
+ * weight 1) in dtype; y may alias x.  The norm in front of every Laguna MoE
+ * block (post_attention_layernorm, Laguna.swift:242-246). */
+NVFP4MOE_API int nvfp4_rms_norm(void* y, const void* x, const void* weight, int dtype,
+                                int64_t rows, int64_t dims, float eps, nvfp4_stream stream);
 
 /* LagunaMoEGate (VLM/MLXLLM/Models/Laguna.swift:149-181): logits = x @ G^T
  * (bf16 G [E, H]), sigmoid, + e_score_correction_bias for the choice, top-k
@@ -261,7 +273,7 @@ NVFP4MOE_API int moe_down_combine(void* y, const float* act, int64_t act_ld,
  * persistent cooperative launch that streams the next layers' expert weights
  * while the current layer's dependent chain runs; results equal a loop of
  * moe_gate_up_swiglu + moe_down_combine.  Requirements: every layer has the
- * same hidden / inter / n_experts / top_k (<= 16), shared_inter 0 or equal to
+ * same hidden / inter / n_experts / top_k (<= 16) / shared_inter / routed_scaling, shared_inter 0 or equal to
  * inter, hidden and inter multiples of 256, 16-byte aligned banks,
  * n_layers <= 64; otherwise NVFP4_ERR_UNSUPPORTED (use the per-layer calls).
  * inds[l] / weights[l] are device pointers to [top_k] entries.  The call runs
@@ -283,6 +295,46 @@ NVFP4MOE_API int moe_decode_stack_forward(void* y, const void* x, int dtype, int
                                           const uint32_t* const* inds,
                                           const float* const* weights, void* workspace,
                                           size_t workspace_bytes, nvfp4_stream stream);
+
+/* Serial decode through a stack of sparse MoE layers with the router inside
+ * the launch, T = 1: from h_0 = x, for l = 0 .. n_layers-1
+ *   x_l = RMSNorm(h_l; norm_w[l], norm_eps) when norm_w, else h_l
+ *   (inds_l, w_l) = router_l(x_l)   (LagunaMoEGate, Laguna.swift:149-181)
+ *   h_{l+1} = moe_block(x_l; layers[l], inds_l, w_l) (+ h_l when residual)
+ * and y = h_{n_layers}.  With both, a layer is the reference's decoder layer
+ * without its attention half (Laguna.swift:242-246: h + mlp(
+ * postAttentionLayerNorm(h))); RMSNorm as MLX's fallback (mlx/fast.cpp:90-108):
+ * x = dtype(dtype(h * rsqrt(mean(h^2) + eps)) * w), norm_w[l] a device
+ * pointer to [hidden] weights in dtype.  This is the MoE part of the reference runtime's
+ * decode branch over its sparse layers (Sources/MLXFastModel/
+ * LagunaRuntimeModel.swift:10685-10800 for one layer: router top-k, routed
+ * experts, shared expert, combine), evaluated layer by layer there; it has no
+ * single-operator counterpart.  One persistent cooperative launch per up to 40
+ * layers (20 with a shared expert) on the block-scaled FP4 tensor cores: a
+ * layer's router runs on the device as soon as its input is complete and its
+ * routed experts' weights stream from then on (only the shared expert and the
+ * router weights stream ahead).  Each layer's output is rounded to dtype once:
+ * sum of the experts' contributions, then the residual.  Logits are summed as
+ * 64-bit fixed-point integers (2^-32 units), so the routing and the outputs
+ * are the same bits on every run; a logit beyond 1e9 in magnitude, or not
+ * finite, counts as NaN (never chosen).  inds_out / weights_out: NULL, or
+ * n_layers device pointers (each NULL or [top_k] entries) that receive the
+ * routing used.  Every layer has the same routed_scaling (also required by
+ * moe_decode_stack_forward).  Requirements as moe_decode_stack_forward's FP4 stack (hidden
+ * 1024 or 2048, inter 512 / 1024 / 2048, shared_inter 0 or inter), plus
+ * n_experts <= 256, router_w 16-byte aligned in every layer, one
+ * norm_topk_prob for all layers, NVFP4_LAUNCH_EXACT_DECODE clear; otherwise
+ * NVFP4_ERR_UNSUPPORTED (run moe_block_forward per layer).  Workspace:
+ * moe_decode_stack_workspace_size() bytes.  Co-residency as for
+ * moe_decode_stack_forward.  moe_decode_stack_routed_launches gives the
+ * launches of a call (0: unsupported). */
+NVFP4MOE_API int moe_decode_stack_routed_launches(const moe_layer_desc* layers, int64_t n_layers);
+NVFP4MOE_API int moe_decode_stack_routed_forward(void* y, const void* x, int dtype,
+                                                 int64_t n_layers, const moe_layer_desc* layers,
+                                                 int residual, const void* const* norm_w,
+                                                 float norm_eps, uint32_t* const* inds_out,
+                                                 float* const* weights_out, void* workspace,
+                                                 size_t workspace_bytes, nvfp4_stream stream);
 
 /* Expert parallelism (no reference counterpart: the reference runs every
  * expert on one device; its single-device analogue is SwitchGLU's gatherSort /

@@ -31,12 +31,13 @@ from typing import Optional
 import torch
 
 from . import _lib
-from ._lib import DeviceIndexError, MoeLayerDesc, NvFp4Bank, check, lib
+from ._lib import DeviceIndexError, DeviceTimeoutError, MoeLayerDesc, NvFp4Bank, check, lib
 
 __all__ = [
     "quantize", "dequantize", "quantized_matmul", "gather_qmm", "moe_router_topk", "qqmm",
+    "rms_norm",
     "quantize_activations",
-    "SparseMoeBlock", "MoEDecodeChain", "device_status", "launch_flags", "DeviceIndexError", "library_path",
+    "SparseMoeBlock", "MoEDecodeChain", "device_status", "launch_flags", "DeviceIndexError", "DeviceTimeoutError", "library_path",
 ]
 
 _DT = {torch.bfloat16: _lib.NVFP4_BF16, torch.float16: _lib.NVFP4_F16,
@@ -291,7 +292,8 @@ class launch_flags:
 
 
 def device_status() -> None:
-    """Synchronise and raise DeviceIndexError if a kernel saw an out-of-range index."""
+    """Synchronise; raise DeviceIndexError if a kernel saw an out-of-range index,
+    DeviceTimeoutError if a kernel's bounded wait gave up (the status is cleared)."""
     check(lib().nvfp4_device_status())
 
 
@@ -308,6 +310,30 @@ class _Workspace:
 
 
 _router_ws = _Workspace()
+
+
+def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """mlx.core.fast.rms_norm (mlx/fast.cpp:53-108) over the last axis:
+    dtype(dtype(x * rsqrt(mean(x^2) + eps)) * weight), weight [dims] in x.dtype."""
+    _require_cuda("rms_norm", x, weight, out)
+    if x.dim() < 1:
+        raise ValueError("[rms_norm] Input must have at least 1 dimension but got input with 0 "
+                         "dimensions.")
+    H = x.shape[-1]
+    if weight is not None:
+        if weight.dim() != 1:
+            raise ValueError(f"[rms_norm] (*weight) must have 1 dimension but has "
+                             f"{weight.dim()} dimensions.")
+        if weight.numel() != H:
+            raise ValueError("[rms_norm] (*weight) must have the same size as the last "
+                             f"dimension of x but has {weight.numel()} elements.")
+        weight = weight.to(x.dtype).contiguous()
+    xc = x.contiguous()
+    y = out if out is not None else torch.empty_like(xc)
+    check(lib().nvfp4_rms_norm(_ptr(y), _ptr(xc), _ptr(weight), _dtype_code(xc, "rms_norm"),
+                               xc.numel() // H, H, float(eps), _stream(x.device)))
+    return y
 
 
 def moe_router_topk(x: torch.Tensor, gate_weight: torch.Tensor, bias: Optional[torch.Tensor],

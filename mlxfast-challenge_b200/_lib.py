@@ -17,6 +17,7 @@ NVFP4_ERR_UNSUPPORTED = 2
 NVFP4_ERR_CUDA = 3
 NVFP4_ERR_WORKSPACE = 4
 NVFP4_ERR_DEVICE_INDEX = 5
+NVFP4_ERR_DEVICE_TIMEOUT = 6
 
 NVFP4_BF16, NVFP4_F16, NVFP4_F32 = 0, 1, 2
 NVFP4_LAUNCH_PDL = 1
@@ -67,6 +68,7 @@ SIGNATURES = {
     "moe_router_topk": (_I, [_P, _P, _P, _I, _P, _P, _I64, _I64, _I64, _I, _I, _P, _SZ, _P]),
     "moe_block_workspace_size": (_SZ, [ctypes.POINTER(MoeLayerDesc), _I64]),
     "moe_workspace_init": (_I, [_P, _SZ, _P]),
+    "nvfp4_rms_norm": (_I, [_P, _P, _P, _I, _I64, _I64, ctypes.c_float, _P]),
     "moe_block_forward": (_I, [_P, _P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P, _P,
                                _P, _P, _SZ, _P]),
     "moe_block_forward_noalloc": (_I, [_P, _P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P,
@@ -79,6 +81,9 @@ SIGNATURES = {
     "moe_decode_stack_uses_fp4": (_I, [ctypes.POINTER(MoeLayerDesc), _I64]),
     "moe_decode_stack_forward": (_I, [_P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _P, _P, _P,
                                       _SZ, _P]),
+    "moe_decode_stack_routed_launches": (_I, [ctypes.POINTER(MoeLayerDesc), _I64]),
+    "moe_decode_stack_routed_forward": (_I, [_P, _P, _I, _I64, ctypes.POINTER(MoeLayerDesc), _I,
+                                             _P, ctypes.c_float, _P, _P, _P, _SZ, _P]),
     "moe_ep_dispatch": (_I, [_P, _P, _P, _P, _P, _I, _P, _I64, _I, _I64, _I64, _I, _P]),
     "moe_ep_combine": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I, _I64, ctypes.c_float, _P]),
 }
@@ -106,6 +111,10 @@ class DeviceIndexError(IndexError):
     pass
 
 
+class DeviceTimeoutError(RuntimeError):
+    """A kernel's bounded wait gave up; its outputs are not valid."""
+
+
 def check(status: int) -> None:
     """Raise the Python exception the reference raises for the same failure."""
     if status == NVFP4_OK:
@@ -119,4 +128,6 @@ def check(status: int) -> None:
         raise ValueError(msg)
     if status == NVFP4_ERR_DEVICE_INDEX:
         raise DeviceIndexError(msg)
+    if status == NVFP4_ERR_DEVICE_TIMEOUT:
+        raise DeviceTimeoutError(msg)
     raise RuntimeError(msg)

@@ -230,6 +230,13 @@ int nvfp4_device_status(void) {
   e = nvfp4::read_and_clear_stack_fp4_error(&st7);
   if (e != cudaSuccess) return check_cuda(e, "device_status");
   if (st == 0) st = st7;
+  // 4 and 1000 * (layer + 1) + site: a bounded wait that expired; other codes:
+  // an index out of range
+  if (st == 4 || st >= 1000)
+    return fail(NVFP4_ERR_DEVICE_TIMEOUT,
+                "[device_status] a bounded device wait expired (kernel site %d); the call's "
+                "outputs are not valid.",
+                st);
   if (st != 0)
     return fail(NVFP4_ERR_DEVICE_INDEX,
                 "[gather_qmm] an expert or batch index was out of range (kernel site %d); "
@@ -435,6 +442,27 @@ int nvfp4_quantized_matmul(void* y, const void* x, int dtype, const uint32_t* w,
   // One "pair" whose M rows are the whole activation matrix.
   return nvfp4_gather_qmm(y, x, dtype, w, scales, nullptr, nullptr, 1, 1, 1, M, N, K, 0,
                           stream);
+}
+
+int nvfp4_rms_norm(void* y, const void* x, const void* weight, int dtype, int64_t rows,
+                   int64_t dims, float eps, nvfp4_stream stream) {
+  const char* op = "rms_norm";
+  if (!valid_dtype(dtype))
+    return fail(NVFP4_ERR_INVALID, "[%s] Received unsupported type.", op);
+  if (rows < 0 || dims <= 0)
+    return fail(NVFP4_ERR_INVALID, "[%s] Input must have at least 1 dimension.", op);
+  if (!(eps >= 0.f)) return fail(NVFP4_ERR_INVALID, "[%s] eps must be >= 0.", op);
+  if (rows == 0) return NVFP4_OK;
+  if (!y || !x) return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  nvfp4::NormArgs a{};
+  a.x = x;
+  a.w = weight;
+  a.y = y;
+  a.T = rows;
+  a.H = dims;
+  a.eps = eps;
+  a.dtype = dtype;
+  return check_cuda(nvfp4::launch_rms_norm(a, (cudaStream_t)stream, first_pdl()), op);
 }
 
 size_t moe_router_workspace_size(int64_t T, int64_t H, int64_t E) {
@@ -1120,12 +1148,15 @@ int moe_ep_finish(void* y, const float* partial, const void* shared, const void*
 // Serial decode through a stack of sparse layers in one persistent launch.
 namespace {
 struct StackLayout {
-  size_t act_off, xb0_off, xb1_off, bar_off, y32_off, gu_off, total;
+  size_t act_off, xb0_off, xb1_off, bar_off, y32_off, gu_off, rbar_off, x32_off, total;
 };
 
 // act / xb: the mma.sync stack; y32 / gu: the FP4 stack's f32 partials
 // ([2][kk][H] per segment, [2][2][kk][2][I] per K part, both by layer parity);
-// bar: grid-barrier / dependency counters.
+// bar: grid-barrier / dependency counters; rbar: the routed stack's counters
+// followed by its fixed-point accumulators (3 blocks of fs_acc_block_u64(E)
+// u64), x32 its layer inputs and residual stream ([2][H] + [2][H] f32, by
+// parity).
 StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   StackLayout S;
   const int64_t kk = L0->top_k + (L0->shared_inter > 0 ? 1 : 0);
@@ -1135,7 +1166,11 @@ StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   S.bar_off = align_up(S.xb1_off + (size_t)L0->hidden * dtype_bytes, 256);
   S.y32_off = align_up(S.bar_off + (2 + 2 * nvfp4::kStackMaxLayers) * sizeof(unsigned), 256);
   S.gu_off = align_up(S.y32_off + 2 * (size_t)kk * L0->hidden * sizeof(float), 256);
-  S.total = align_up(S.gu_off + 4 * (size_t)kk * 2 * L0->inter * sizeof(float), 256);
+  S.rbar_off = align_up(S.gu_off + 4 * (size_t)kk * 2 * L0->inter * sizeof(float), 256);
+  S.x32_off = align_up(S.rbar_off + nvfp4::kFsCounters * sizeof(unsigned) +
+                           3 * nvfp4::fs_acc_block_u64((int)L0->n_experts) * sizeof(uint64_t),
+                       256);
+  S.total = align_up(S.x32_off + 4 * (size_t)L0->hidden * sizeof(float), 256);
   return S;
 }
 
@@ -1184,15 +1219,151 @@ bool cached_map(size_t idx, CUtensorMap* out, const void* p, int64_t rows, int64
 
 // Layers per launch of the FP4 stack (the tensor maps ride in the kernel
 // parameters), 0 when the FP4 stack does not take this shape or is switched off.
-int fp4_stack_layers_per_launch(const moe_layer_desc* L0) {
+int fp4_stack_layers_per_launch(const moe_layer_desc* L0, bool routed = false) {
   if (!use_fp4_decode()) return 0;
   const int kk = (int)(L0->top_k + (L0->shared_inter > 0 ? 1 : 0));
   if (L0->shared_inter > 0 && L0->shared_inter != L0->inter) return 0;
   if (L0->hidden > 4096 || L0->inter > 4096) return 0;
-  if (!nvfp4::decode_stack_fp4_supported((int)L0->hidden, (int)L0->inter, kk, device_sms()))
+  if (routed && L0->n_experts > 256) return 0;
+  if (!nvfp4::decode_stack_fp4_supported((int)L0->hidden, (int)L0->inter, kk, device_sms(),
+                                         routed))
     return 0;
   const int mpl = L0->shared_inter > 0 ? 2 * nvfp4::kFsMapsRouted : nvfp4::kFsMapsRouted;
   return std::min(nvfp4::kFsMaxLayers, nvfp4::kFsMaxMaps / mpl);
+}
+
+// Shape checks shared by both stacks: every layer as layer 0.
+int check_stack_layers(const char* op, const moe_layer_desc* layers, int64_t n_layers, int dtype) {
+  if (!layers || n_layers <= 0) return fail(NVFP4_ERR_INVALID, "[%s] no layers.", op);
+  if (n_layers > nvfp4::kStackMaxLayers)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] at most %d layers per call.", op,
+                nvfp4::kStackMaxLayers);
+  for (int64_t l = 0; l < n_layers; l++)
+    if (int r = check_layer(op, &layers[l], dtype, 1)) return r;
+  const moe_layer_desc* L0 = &layers[0];
+  for (int64_t l = 1; l < n_layers; l++) {
+    const moe_layer_desc* Ll = &layers[l];
+    if (Ll->hidden != L0->hidden || Ll->inter != L0->inter || Ll->n_experts != L0->n_experts ||
+        Ll->top_k != L0->top_k || Ll->shared_inter != L0->shared_inter)
+      return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layers must share one shape.", op);
+  }
+  const int64_t H = L0->hidden, I = L0->inter, Is = L0->shared_inter;
+  if (H % 256 || I % 256 || (Is != 0 && Is != I) || L0->top_k > 16 || L0->n_experts > 0x7fffffff)
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] unsupported layer shape.", op);
+  return NVFP4_OK;
+}
+
+// The block-scaled FP4 stack over n_layers layers, per_launch layers per
+// launch.  Given routing: inds / weights [n_layers] device pointers.  Routed:
+// inds_out / wts_out (nullable, entries nullable) receive each layer's routing.
+int run_fp4_stack(const char* op, void* y, const void* x, int dtype, int64_t n_layers,
+                  const moe_layer_desc* layers, const uint32_t* const* inds,
+                  const float* const* weights, bool routed, bool residual,
+                  const void* const* norm_w, float eps, uint32_t* const* inds_out,
+                  float* const* wts_out, int per_launch, const StackLayout& S, char* ws,
+                  cudaStream_t s) {
+  const moe_layer_desc* L0 = &layers[0];
+  const int64_t H = L0->hidden, I = L0->inter, E = L0->n_experts, k = L0->top_k;
+  const int64_t Is = L0->shared_inter;
+  const int kk = (int)(k + (Is > 0 ? 1 : 0));
+  for (int64_t l = 0; l < n_layers; l++) {
+    const moe_layer_desc* Ll = &layers[l];
+    const nvfp4_bank* banks[6] = {&Ll->gate, &Ll->up, &Ll->down,
+                                  &Ll->shared_gate, &Ll->shared_up, &Ll->shared_down};
+    for (int b = 0; b < (Is > 0 ? 6 : 3); b++)
+      if (!banks[b]->w || !banks[b]->scales || !aligned16(banks[b]->w) ||
+          !aligned16(banks[b]->scales))
+        return fail(NVFP4_ERR_UNSUPPORTED, "[%s] banks must be 16-byte aligned.", op);
+    if (Ll->routed_scaling != L0->routed_scaling)
+      return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layers must share routed_scaling.", op);
+    if (routed) {
+      if (!Ll->router_w || !aligned16(Ll->router_w))
+        return fail(NVFP4_ERR_INVALID, "[%s] layer %lld needs a 16-byte aligned router weight.",
+                    op, (long long)l);
+      if (Ll->norm_topk_prob != L0->norm_topk_prob)
+        return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layers must share norm_topk_prob.", op);
+      if (norm_w && !norm_w[l])
+        return fail(NVFP4_ERR_INVALID, "[%s] null norm weight for layer %lld.", op,
+                    (long long)l);
+    } else if (!inds[l] || !weights[l]) {
+      return fail(NVFP4_ERR_INVALID, "[%s] null routing for layer %lld.", op, (long long)l);
+    }
+  }
+  static thread_local nvfp4::FsArgs F;
+  const int mpl = Is > 0 ? 2 * nvfp4::kFsMapsRouted : nvfp4::kFsMapsRouted;
+  F.H = (int)H;
+  F.I = (int)I;
+  F.E = (int)E;
+  F.k = (int)k;
+  F.kk = kk;
+  F.nks = nvfp4::decode_stack_fp4_nks((int)I, kk, device_sms());
+  F.mpl = mpl;
+  F.dtype = dtype;
+  F.routed = routed ? 1 : 0;
+  F.residual = residual ? 1 : 0;
+  F.norm = L0->norm_topk_prob ? 1 : 0;
+  F.has_norm = norm_w ? 1 : 0;
+  F.eps = eps;
+  F.scaling = L0->routed_scaling;
+  F.x0 = x;
+  F.y = y;
+  F.Yp = reinterpret_cast<float*>(ws + S.y32_off);
+  F.GUp = reinterpret_cast<float*>(ws + S.gu_off);
+  if (routed) {
+    F.bar = reinterpret_cast<unsigned*>(ws + S.rbar_off);
+    F.LG = reinterpret_cast<unsigned long long*>(ws + S.rbar_off +
+                                                 nvfp4::kFsCounters * sizeof(unsigned));
+    F.X = reinterpret_cast<float*>(ws + S.x32_off);
+  } else {
+    F.bar = reinterpret_cast<unsigned*>(ws + S.bar_off);
+    F.LG = nullptr;
+    F.X = nullptr;
+  }
+  // routed and given-routing stacks keep separate tensor-map cache entries
+  const size_t cache0 = routed ? (size_t)nvfp4::kStackMaxLayers * 2 * nvfp4::kFsMapsRouted : 0;
+  for (int64_t l0 = 0; l0 < n_layers; l0 += per_launch) {
+    const int nl = (int)std::min<int64_t>(per_launch, n_layers - l0);
+    F.L = nl;
+    F.l0 = (int)l0;
+    F.first = l0 == 0;
+    F.last = l0 + nl == n_layers;
+    bool ok = true;
+    for (int li = 0; li < nl; li++) {
+      const moe_layer_desc* Ll = &layers[l0 + li];
+      CUtensorMap* m = &F.maps[li * mpl];
+      const size_t c0 = cache0 + (size_t)(l0 + li) * 2 * nvfp4::kFsMapsRouted;
+      ok = ok && cached_map(c0 + 0, &m[0], Ll->gate.w, E * I, H, 64, false) &&
+           cached_map(c0 + 1, &m[1], Ll->gate.scales, E * I, H, 64, true) &&
+           cached_map(c0 + 2, &m[2], Ll->up.w, E * I, H, 64, false) &&
+           cached_map(c0 + 3, &m[3], Ll->up.scales, E * I, H, 64, true) &&
+           cached_map(c0 + 4, &m[4], Ll->down.w, E * H, I, 128, false) &&
+           cached_map(c0 + 5, &m[5], Ll->down.scales, E * H, I, 128, true);
+      if (Is > 0)
+        ok = ok && cached_map(c0 + 6, &m[6], Ll->shared_gate.w, Is, H, 64, false) &&
+             cached_map(c0 + 7, &m[7], Ll->shared_gate.scales, Is, H, 64, true) &&
+             cached_map(c0 + 8, &m[8], Ll->shared_up.w, Is, H, 64, false) &&
+             cached_map(c0 + 9, &m[9], Ll->shared_up.scales, Is, H, 64, true) &&
+             cached_map(c0 + 10, &m[10], Ll->shared_down.w, H, I, 128, false) &&
+             cached_map(c0 + 11, &m[11], Ll->shared_down.scales, H, I, 128, true);
+      nvfp4::FsLayer& d = F.layer[li];
+      if (routed) {
+        d.inds = inds_out ? inds_out[l0 + li] : nullptr;
+        d.wts = wts_out ? wts_out[l0 + li] : nullptr;
+        d.router_w = Ll->router_w;
+        d.router_b = Ll->router_bias;
+        d.norm_w = norm_w ? norm_w[l0 + li] : nullptr;
+      } else {
+        d.inds = const_cast<uint32_t*>(inds[l0 + li]);
+        d.wts = const_cast<float*>(weights[l0 + li]);
+        d.router_w = nullptr;
+        d.router_b = nullptr;
+        d.norm_w = nullptr;
+      }
+    }
+    if (!ok) return fail(NVFP4_ERR_CUDA, "[%s] tensor-map encoding failed.", op);
+    if (int r = check_cuda(nvfp4::launch_decode_stack_fp4(F, s), op)) return r;
+  }
+  return NVFP4_OK;
 }
 }  // namespace
 
@@ -1219,25 +1390,12 @@ extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64
                                         void* workspace, size_t workspace_bytes,
                                         nvfp4_stream stream) {
   const char* op = "moe_decode_stack";
-  if (!layers || n_layers <= 0) return fail(NVFP4_ERR_INVALID, "[%s] no layers.", op);
+  if (int r = check_stack_layers(op, layers, n_layers, dtype)) return r;
   if (!y || !x || !inds || !weights)
     return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
-  if (n_layers > nvfp4::kStackMaxLayers)
-    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] at most %d layers per call.", op,
-                nvfp4::kStackMaxLayers);
   const moe_layer_desc* L0 = &layers[0];
-  for (int64_t l = 0; l < n_layers; l++)
-    if (int r = check_layer(op, &layers[l], dtype, 1)) return r;
   const int64_t H = L0->hidden, I = L0->inter, E = L0->n_experts, k = L0->top_k;
   const int64_t Is = L0->shared_inter;
-  for (int64_t l = 1; l < n_layers; l++) {
-    const moe_layer_desc* Ll = &layers[l];
-    if (Ll->hidden != H || Ll->inter != I || Ll->n_experts != E || Ll->top_k != k ||
-        (Ll->shared_inter > 0) != (Is > 0))
-      return fail(NVFP4_ERR_UNSUPPORTED, "[%s] layers must share one shape.", op);
-  }
-  if (H % 256 || I % 256 || (Is != 0 && Is != I) || k > 16 || E > 0x7fffffff)
-    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] unsupported layer shape.", op);
   const int per_launch = fp4_stack_layers_per_launch(L0);
   // mma.sync stack: each consumer thread holds at most 2 x chunks and 4 act
   // chunks of 8 values, and its rings must fit on chip
@@ -1252,70 +1410,10 @@ extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64
   const StackLayout S = stack_layout(L0, esz);
   if (!workspace || workspace_bytes < S.total)
     return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, S.total);
-  if (per_launch > 0) {
-    // Block-scaled FP4 stack: per launch up to per_launch layers, their tensor
-    // maps encoded here.
-    for (int64_t l = 0; l < n_layers; l++) {
-      const moe_layer_desc* Ll = &layers[l];
-      const nvfp4_bank* banks[6] = {&Ll->gate, &Ll->up, &Ll->down,
-                                    &Ll->shared_gate, &Ll->shared_up, &Ll->shared_down};
-      for (int b = 0; b < (Is > 0 ? 6 : 3); b++)
-        if (!banks[b]->w || !banks[b]->scales || !aligned16(banks[b]->w) ||
-            !aligned16(banks[b]->scales))
-          return fail(NVFP4_ERR_UNSUPPORTED, "[%s] banks must be 16-byte aligned.", op);
-      if (!inds[l] || !weights[l])
-        return fail(NVFP4_ERR_INVALID, "[%s] null routing for layer %lld.", op, (long long)l);
-    }
-    char* ws = static_cast<char*>(workspace);
-    cudaStream_t s = (cudaStream_t)stream;
-    static thread_local nvfp4::FsArgs F;
-    const int mpl = Is > 0 ? 2 * nvfp4::kFsMapsRouted : nvfp4::kFsMapsRouted;
-    F.H = (int)H;
-    F.I = (int)I;
-    F.E = (int)E;
-    F.k = (int)k;
-    F.kk = kk;
-    F.nks = nvfp4::decode_stack_fp4_nks((int)I, kk, device_sms());
-    F.mpl = mpl;
-    F.dtype = dtype;
-    F.x0 = x;
-    F.y = y;
-    F.Yp = reinterpret_cast<float*>(ws + S.y32_off);
-    F.GUp = reinterpret_cast<float*>(ws + S.gu_off);
-    F.bar = reinterpret_cast<unsigned*>(ws + S.bar_off);
-    for (int64_t l0 = 0; l0 < n_layers; l0 += per_launch) {
-      const int nl = (int)std::min<int64_t>(per_launch, n_layers - l0);
-      F.L = nl;
-      F.l0 = (int)l0;
-      F.first = l0 == 0;
-      F.last = l0 + nl == n_layers;
-      bool ok = true;
-      for (int li = 0; li < nl; li++) {
-        const moe_layer_desc* Ll = &layers[l0 + li];
-        CUtensorMap* m = &F.maps[li * mpl];
-        const size_t c0 = (size_t)(l0 + li) * 2 * nvfp4::kFsMapsRouted;
-        ok = ok && cached_map(c0 + 0, &m[0], Ll->gate.w, E * I, H, 64, false) &&
-             cached_map(c0 + 1, &m[1], Ll->gate.scales, E * I, H, 64, true) &&
-             cached_map(c0 + 2, &m[2], Ll->up.w, E * I, H, 64, false) &&
-             cached_map(c0 + 3, &m[3], Ll->up.scales, E * I, H, 64, true) &&
-             cached_map(c0 + 4, &m[4], Ll->down.w, E * H, I, 128, false) &&
-             cached_map(c0 + 5, &m[5], Ll->down.scales, E * H, I, 128, true);
-        if (Is > 0)
-          ok = ok && cached_map(c0 + 6, &m[6], Ll->shared_gate.w, Is, H, 64, false) &&
-               cached_map(c0 + 7, &m[7], Ll->shared_gate.scales, Is, H, 64, true) &&
-               cached_map(c0 + 8, &m[8], Ll->shared_up.w, Is, H, 64, false) &&
-               cached_map(c0 + 9, &m[9], Ll->shared_up.scales, Is, H, 64, true) &&
-               cached_map(c0 + 10, &m[10], Ll->shared_down.w, H, I, 128, false) &&
-               cached_map(c0 + 11, &m[11], Ll->shared_down.scales, H, I, 128, true);
-        F.layer[li].inds = inds[l0 + li];
-        F.layer[li].wts = weights[l0 + li];
-        F.layer[li].scaling = Ll->routed_scaling;
-      }
-      if (!ok) return fail(NVFP4_ERR_CUDA, "[%s] tensor-map encoding failed.", op);
-      if (int r = check_cuda(nvfp4::launch_decode_stack_fp4(F, s), op)) return r;
-    }
-    return NVFP4_OK;
-  }
+  if (per_launch > 0)
+    return run_fp4_stack(op, y, x, dtype, n_layers, layers, inds, weights, false, false, nullptr,
+                         0.f, nullptr, nullptr, per_launch, S, static_cast<char*>(workspace),
+                         (cudaStream_t)stream);
   nvfp4::StackArgs A{};
   A.L = (int)n_layers;
   A.H = (int)H;
@@ -1367,6 +1465,42 @@ extern "C" int moe_decode_stack_forward(void* y, const void* x, int dtype, int64
     d.scaling = Ll->routed_scaling;
   }
   return check_cuda(nvfp4::launch_decode_stack(A, (cudaStream_t)stream), op);
+}
+
+// Serial decode with the router inside the stack (the routed FP4 stack).
+extern "C" int moe_decode_stack_routed_launches(const moe_layer_desc* layers, int64_t n_layers) {
+  if (!layers || n_layers <= 0) return 0;
+  const int per = fp4_stack_layers_per_launch(&layers[0], true);
+  return per > 0 ? (int)((n_layers + per - 1) / per) : 0;
+}
+
+extern "C" int moe_decode_stack_routed_forward(void* y, const void* x, int dtype,
+                                               int64_t n_layers, const moe_layer_desc* layers,
+                                               int residual, const void* const* norm_w,
+                                               float norm_eps, uint32_t* const* inds_out,
+                                               float* const* weights_out, void* workspace,
+                                               size_t workspace_bytes, nvfp4_stream stream) {
+  const char* op = "moe_decode_stack_routed";
+  if (int r = check_stack_layers(op, layers, n_layers, dtype)) return r;
+  if (!y || !x) return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
+  const moe_layer_desc* L0 = &layers[0];
+  const int per_launch = fp4_stack_layers_per_launch(L0, true);
+  if (per_launch == 0)
+    return fail(NVFP4_ERR_UNSUPPORTED,
+                "[%s] this layer shape or launch mode has no routed stack (hidden 1024 or 2048, "
+                "inter 512 / 1024 / 2048, at most 256 experts, NVFP4_LAUNCH_EXACT_DECODE "
+                "clear); use moe_block_forward per layer.",
+                op);
+  if (!aligned16(x) || !aligned16(y))
+    return fail(NVFP4_ERR_UNSUPPORTED, "[%s] x and y must be 16-byte aligned.", op);
+  const StackLayout S = stack_layout(L0, dtype == NVFP4_F32 ? 4 : 2);
+  if (!workspace || workspace_bytes < S.total)
+    return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, S.total);
+  if (norm_w && !(norm_eps >= 0.f))
+    return fail(NVFP4_ERR_INVALID, "[%s] norm epsilon must be >= 0.", op);
+  return run_fp4_stack(op, y, x, dtype, n_layers, layers, nullptr, nullptr, true, residual != 0,
+                       norm_w, norm_eps, inds_out, weights_out, per_launch, S,
+                       static_cast<char*>(workspace), (cudaStream_t)stream);
 }
 
 // ---------------------------------------------------------------------------

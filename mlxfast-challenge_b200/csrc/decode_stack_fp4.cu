@@ -42,9 +42,32 @@
 // between two buffers by layer parity: a buffer is rewritten two layers later,
 // after (through those waits) every reader of its previous contents.
 //
+// Routed stack (ROUTED, BASELINE config[2] at one sequence): the router runs
+// inside the launch, per layer -- the Laguna gate (Laguna.swift:149-181) on
+// the layer's input, then the experts it picks -- with, optionally, the
+// decoder layer's residual stream and RMSNorm around the block
+// (Laguna.swift:242-246: h_{l+1} = h_l + block_l(RMSNorm_l(h_l))).  Only the
+// shared expert's weights can stream ahead of the chain; a routed expert's
+// slabs go out the moment its layer's top-k is known.  The layer's output
+// reduction, the norm and the router's logits are the reducers' step:
+// reducer j (CTA j < H / 32) waits for the down items of its 32 rows, sums
+// their segment partials in segment order (+ the residual h_l), rounds to
+// the activation dtype -- h_{l+1} for those rows -- and, with the norm, adds
+// the rows' squares into the layer's sum-of-squares accumulator, waits for
+// all reducers and forms x = dtype(dtype(h * rsqrt(mean + eps)) * w), the
+// reference's RMSNorm fallback (mlx/fast.cpp:90-108); then it adds
+// x[rows] . G[e, rows] for every expert e into the expert's accumulator.
+// Sums are 64-bit fixed-point integers (2^-32 units for logits, 2^-24 for
+// squares): integer sums do not depend on the order of the adds, so every
+// run gives the same bits.  Each CTA then reads the E sums, rounds each logit
+// to the activation dtype as the reference's bf16 matmul does, and selects
+// the top-k itself (topk.cuh).  The reducers' router rows are prefetched two
+// layers ahead with cp.async.
+//
 // Roles (320 threads): warp 0 TMA (this CTA's weight slabs of layer l, l+1,
-// ... in consumption order into a 10-stage ring, so the next layer's weights
-// stream while this layer's chain runs), warp 1 MMA issue, warps 2-5 weight
+// ... in consumption order into a 10-stage ring -- 8 in the routed stack, one
+// layer's slabs and two more -- so the next layer's weights stream while this
+// layer's chain runs), warp 1 MMA issue, warps 2-5 weight
 // scales into tensor memory, warps 6-9 the chain (terms, epilogues, the
 // dependency counters).  Every wait is bounded; on expiry an error is latched
 // (the site code below) and each role leaves its loop (the copies and MMAs it
@@ -52,6 +75,7 @@
 #include "common.cuh"
 #include "fp4terms.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 #include "umma.cuh"
 
 namespace nvfp4 {
@@ -59,7 +83,8 @@ namespace {
 
 constexpr int kT = kFp4Terms;
 constexpr int kN = 16;                    // MMA N: term rows 0..3, rows 4..15 zero
-constexpr int kStages = 10;
+constexpr int kStages = 10;               // ring stages (8 in the routed stack)
+constexpr int stages(bool routed) { return routed ? 8 : kStages; }
 constexpr int kA = 128 * 128;             // weight codes of one slab (128 rows x K 256): 16 KB
 constexpr int kSA = 128 * 16;             // their scale bytes: 2 KB
 constexpr int kStage = kA + kSA;          // 18 KB, 1 KB multiple
@@ -78,7 +103,10 @@ constexpr int kErrIndex = 2;
 // 41 TMA ring slot, 42 MMA x terms, 43 MMA gate/up stage, 44 MMA act terms,
 // 45 MMA down stage, 46 MMA drain, 47 scale warps stage, 48 chain gate/up
 // accumulator, 49 chain down accumulator, 50 a segment's gate/up items, 51 a
-// K part's down items (previous layer), 52 the last layer's down items.
+// K part's down items (previous layer), 52 the last layer's down items; routed
+// stack: 53 the layer's router reducers, 54 a row block's down items (the
+// reducer), 55 the TMA warp waiting for the layer's routing, 56 the reducers'
+// sums of squares (the norm).
 __host__ __device__ constexpr int fs_timeout(int l, int site) { return 1000 * (l + 1) + site; }
 constexpr long long kDrainBudget = 200000000LL;
 
@@ -133,9 +161,14 @@ struct FsSmem {
   volatile int* cur;   // the layer the chain is in: its stages are never held
   uint32_t* inds;
   float* wts;
+  uint8_t* rsl;          // routed: [2][E <= 256][32] bf16, a reducer's router rows
+  float* xs;             // routed: [32] the reducer's rows of x_{l+1}
+  volatile int* rlayer;  // routed: layers whose routing is in inds / wts
 };
 
-__host__ __device__ inline size_t fs_carve(int H, int I, int L, uint8_t* base, FsSmem* S) {
+__host__ __device__ inline size_t fs_carve(int H, int I, int L, bool routed, uint8_t* base,
+                                           FsSmem* S) {
+  const int ns = stages(routed);
   size_t o = 0;
   auto take = [&](size_t bytes, size_t align) -> uint8_t* {
     o = (o + align - 1) / align * align;
@@ -144,7 +177,7 @@ __host__ __device__ inline size_t fs_carve(int H, int I, int L, uint8_t* base, F
     return p;
   };
   FsSmem t{};
-  t.stage = take((size_t)kStages * kStage, 1024);
+  t.stage = take((size_t)ns * kStage, 1024);
   t.bx = take((size_t)(H / 256) * kBSlab, 1024);  // bx and ba adjacent (zeroed together)
   t.ba = take((size_t)(I / 256) * kBSlab, 1024);
   t.scx = take((size_t)kT * (H / 16), 16);
@@ -152,9 +185,9 @@ __host__ __device__ inline size_t fs_carve(int H, int I, int L, uint8_t* base, F
   t.wmax = reinterpret_cast<float*>(take(8 * 4, 16));
   t.facx = reinterpret_cast<float*>(take(16 * 4, 16));
   t.faca = reinterpret_cast<float*>(take(16 * 4, 16));
-  t.full = reinterpret_cast<uint64_t*>(take(kStages * 8, 8));
-  t.empty = reinterpret_cast<uint64_t*>(take(kStages * 8, 8));
-  t.sfr = reinterpret_cast<uint64_t*>(take(kStages * 8, 8));
+  t.full = reinterpret_cast<uint64_t*>(take(ns * 8, 8));
+  t.empty = reinterpret_cast<uint64_t*>(take(ns * 8, 8));
+  t.sfr = reinterpret_cast<uint64_t*>(take(ns * 8, 8));
   t.xready = reinterpret_cast<uint64_t*>(take(8, 8));
   t.aready = reinterpret_cast<uint64_t*>(take(8, 8));
   t.gufull = reinterpret_cast<uint64_t*>(take(8, 8));
@@ -166,6 +199,11 @@ __host__ __device__ inline size_t fs_carve(int H, int I, int L, uint8_t* base, F
   t.cur = reinterpret_cast<volatile int*>(take(4, 4));
   t.inds = reinterpret_cast<uint32_t*>(take((size_t)L * 16 * 4, 16));
   t.wts = reinterpret_cast<float*>(take((size_t)L * 16 * 4, 16));
+  if (routed) {
+    t.rsl = take((size_t)2 * 256 * kFsRedRows * 2, 128);
+    t.xs = reinterpret_cast<float*>(take(kFsRedRows * 4, 16));
+    t.rlayer = reinterpret_cast<volatile int*>(take(4, 4));
+  }
   if (S) *S = t;
   return o;
 }
@@ -311,15 +349,128 @@ __device__ __forceinline__ void load_segment_sum(const float* Yp, int H, int kk,
   }
 }
 
-template <int VX, int VA>
+// ---- routed stack: router rows, logit partials, routing ----
+
+__device__ __forceinline__ void cp_async16_fs(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_fs() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// every group but the most recent one has landed
+__device__ __forceinline__ void cp_async_wait_prev_fs() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+
+// Reducer rows [r0, r0 + 32) of every expert's router row of layer j into
+// rsl[j & 1] ([e][32] bf16, 64 bytes per expert), by the 128 chain threads;
+// one cp.async group per call (empty when j is past the launch).
+__device__ __forceinline__ void issue_router_rows(const FsArgs& a, const FsSmem& S, int j, int r0,
+                                                  int ct) {
+  if (j < a.L) {
+    const uint16_t* G = a.layer[j].router_w;
+    uint8_t* dst = S.rsl + (size_t)(j & 1) * (256 * kFsRedRows * 2);
+    for (int i = ct; i < a.E * 4; i += kChain) {
+      const int e = i >> 2, q = i & 3;
+      cp_async16_fs(dst + e * 64 + q * 16, G + (size_t)e * a.H + r0 + q * 8);
+    }
+  }
+  cp_async_commit_fs();
+}
+
+// Layer j's accumulator block (fs_acc_block_u64): expert e's logit line at
+// e * kFsLgStride, the sum-of-squares line after the E of them.
+__device__ __forceinline__ unsigned long long* acc_block(const FsArgs& a, int j) {
+  return a.LG + (size_t)(j % 3) * fs_acc_block_u64(a.E);
+}
+
+// Fixed-point partials: one 128-byte line per sum, u64 slot 0 the sum in
+// units of 2^-32 (logits) or 2^-24 (squares), two's complement; slot 1 a count
+// of partials that were not finite or too large for the format (the sum is
+// then NaN).
+__device__ __forceinline__ void add_fixed_partial(unsigned long long* line, float p,
+                                                  float unit_inv, float limit) {
+  if (fabsf(p) < limit) {
+    const long long q = __float2ll_rn(p * unit_inv);
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(line),
+                 "l"((unsigned long long)q)
+                 : "memory");
+  } else {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(line + 1) : "memory");
+  }
+}
+__device__ __forceinline__ float read_fixed_sum(const unsigned long long* line, float unit) {
+  const ulonglong2 q = __ldcg(reinterpret_cast<const ulonglong2*>(line));
+  return q.y ? __int_as_float(0x7fc00000) : __ll2float_rn((long long)q.x) * unit;
+}
+constexpr float kLogitUnitInv = 4294967296.0f, kLogitUnit = 2.3283064365386963e-10f;  // 2^32
+constexpr float kSqUnitInv = 16777216.0f, kSqUnit = 5.9604644775390625e-08f;          // 2^24
+
+// The reducer's share of layer j's logits: for experts ct and ct + 128,
+// sum over its 32 rows r (in order) of xs[r] * G_j[e, r0 + r], into LG[j % 3].
+__device__ __forceinline__ void router_partials(const FsArgs& a, const FsSmem& S, int j, int ct) {
+  const uint8_t* sl = S.rsl + (size_t)(j & 1) * (256 * kFsRedRows * 2);
+  unsigned long long* lg = acc_block(a, j);
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int e = ct + 128 * h;
+    if (e >= a.E) break;
+    const uint4* g = reinterpret_cast<const uint4*>(sl + e * 64);
+    float p = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint4 w = g[q];
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
+        p += S.xs[8 * q + 2 * i] * f.x;
+        p += S.xs[8 * q + 2 * i + 1] * f.y;
+      }
+    }
+    add_fixed_partial(lg + (size_t)e * kFsLgStride, p, kLogitUnitInv, 1.0e9f);
+  }
+}
+
+// Layer l's routing from LG[l % 3], on one warp: logit = sum * 2^-32 rounded
+// to the activation dtype (NaN when a partial was not representable), then
+// the router's selection.  Lanes < k write slot lane into inds / wts (shared
+// memory) and, from CTA 0, into the layer's routing outputs.
+__device__ __forceinline__ void route_layer(const FsArgs& a, const FsSmem& S, int l, int lane,
+                                            bool write_out) {
+  const unsigned long long* lg = acc_block(a, l);
+  float logit[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int e = lane + 32 * j;
+    logit[j] = e < a.E ? round_to_dtype(read_fixed_sum(lg + (size_t)e * kFsLgStride, kLogitUnit),
+                                        a.dtype)
+                       : 0.f;
+  }
+  uint32_t isel;
+  float wsel;
+  topk_select<8>(logit, a.layer[l].router_b, a.E, a.k, a.norm != 0, lane, isel, wsel);
+  if (lane < a.k) {
+    S.inds[l * 16 + lane] = isel;
+    S.wts[l * 16 + lane] = wsel;
+    if (write_out) {
+      if (a.layer[l].inds) a.layer[l].inds[lane] = isel;
+      if (a.layer[l].wts) a.layer[l].wts[lane] = wsel;
+    }
+  }
+}
+
+template <int VX, int VA, bool ROUTED>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_decode_stack_fp4_kernel(const __grid_constant__ FsArgs a) {
+  constexpr int NS = stages(ROUTED);
   extern __shared__ __align__(1024) unsigned char fs_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(fs_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int H = a.H, I = a.I;  // H = 128 VX nks, I = 128 VA (checked on the host)
   FsSmem S;
-  fs_carve(H, I, a.L, base, &S);
+  fs_carve(H, I, a.L, ROUTED, base, &S);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, c = blockIdx.x;
   const int nb = I / 64;
@@ -336,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t kSfba = kSfbx + (uint32_t)(H / 16);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; i++) {
+    for (int i = 0; i < NS; i++) {
       mbar_init(&S.full[i], 1);
       mbar_init(&S.empty[i], 1);
       mbar_init(&S.sfr[i], 4);
@@ -348,14 +499,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(S.drain, 1);
     *S.hold = 0;
     *S.cur = 0;
+    if (ROUTED) *S.rlayer = 0;
     fence_barrier_init();
   }
-  // Routing of the launch's layers into shared memory once.
-  for (int i = threadIdx.x; i < a.L * a.k; i += blockDim.x) {
-    const int l = i / a.k, j = i - l * a.k;
-    S.inds[l * 16 + j] = a.layer[l].inds[j];
-    S.wts[l * 16 + j] = a.layer[l].wts[j];
-  }
+  // Given routing: the launch's layers into shared memory once.
+  if (!ROUTED)
+    for (int i = threadIdx.x; i < a.L * a.k; i += blockDim.x) {
+      const int l = i / a.k, j = i - l * a.k;
+      S.inds[l * 16 + j] = a.layer[l].inds[j];
+      S.wts[l * 16 + j] = a.layer[l].wts[j];
+    }
   // Term tiles: rows 4..15 stay zero for the whole launch.
   {
     uint4* z = reinterpret_cast<uint4*>(S.bx);
@@ -375,9 +528,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t g = 0;
     bool ok = true;
     auto slot = [&](int& s, int l) -> bool {
-      s = (int)(g % kStages);
-      if (g >= (uint32_t)kStages &&
-          !mbar_wait_bounded(&S.empty[s], ((g / kStages) - 1) & 1)) {
+      s = (int)(g % NS);
+      if (g >= (uint32_t)NS &&
+          !mbar_wait_bounded(&S.empty[s], ((g / NS) - 1) & 1)) {
         if (el) fsflag(fs_timeout(l, 41));
         return false;
       }
@@ -395,12 +548,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       return true;
     };
+    // Routed stack: a routed segment's slabs of layer l wait for its routing.
+    auto routing_known = [&](int l) -> bool {
+      if (!ROUTED) return true;
+      if (el && *S.rlayer <= l) {
+        const long long t0 = clock64();
+        while (*S.rlayer <= l) {
+          if (clock64() - t0 > 2000000000LL) {
+            fsflag(fs_timeout(l, 55));
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      __syncwarp();
+      __threadfence_block();  // the routing written before the flag
+      return *S.rlayer > l;
+    };
     for (int l = 0; l < a.L && ok; l++) {
       const CUtensorMap* mp = &a.maps[l * a.mpl];
       if (has_gu) {
         const bool sh = gu_seg >= a.k;
         uint32_t e = 0;
         if (!sh) {
+          if (!routing_known(l)) {
+            ok = false;
+            break;
+          }
           e = S.inds[l * 16 + gu_seg];
           if (e >= (uint32_t)a.E) {
             if (el) fsflag(kErrIndex);
@@ -431,6 +605,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool sh = d_seg >= a.k;
         uint32_t e = 0;
         if (!sh) {
+          if (!routing_known(l)) {
+            ok = false;
+            break;
+          }
           e = S.inds[l * 16 + d_seg];
           if (e >= (uint32_t)a.E) {
             if (el) fsflag(kErrIndex);
@@ -456,9 +634,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     // no copy may still be landing at exit
-    for (uint32_t i = 0; i < (g < (uint32_t)kStages ? g : (uint32_t)kStages); i++) {
+    for (uint32_t i = 0; i < (g < (uint32_t)NS ? g : (uint32_t)NS); i++) {
       const uint32_t q = g - 1 - i;
-      mbar_wait_bounded(&S.full[q % kStages], (q / kStages) & 1, kDrainBudget);
+      mbar_wait_bounded(&S.full[q % NS], (q / NS) & 1, kDrainBudget);
     }
   } else if (warp == kWarpMma) {
     // ------------------------------ MMA issuer ------------------------------
@@ -476,8 +654,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         jx++;
         tc_fence_after();
         for (int sl = 0; sl < KS; sl++, g++) {
-          const int s = (int)(g % kStages);
-          if (!mbar_wait_bounded(&S.sfr[s], (g / kStages) & 1)) {
+          const int s = (int)(g % NS);
+          if (!mbar_wait_bounded(&S.sfr[s], (g / NS) & 1)) {
             if (el) fsflag(fs_timeout(l, 43));
             ok = false;
             break;
@@ -512,8 +690,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ja++;
         tc_fence_after();
         for (int sl = 0; sl < DS; sl++, g++) {
-          const int s = (int)(g % kStages);
-          if (!mbar_wait_bounded(&S.sfr[s], (g / kStages) & 1)) {
+          const int s = (int)(g % NS);
+          if (!mbar_wait_bounded(&S.sfr[s], (g / NS) & 1)) {
             if (el) fsflag(fs_timeout(l, 45));
             ok = false;
             break;
@@ -552,8 +730,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int l = 0; l < a.L && ok; l++) {
       for (int i = 0; i < per_layer; i++, g++) {
-        const int s = (int)(g % kStages);
-        if (!mbar_wait_bounded(&S.full[s], (g / kStages) & 1)) {
+        const int s = (int)(g % NS);
+        if (!mbar_wait_bounded(&S.full[s], (g / NS) & 1)) {
           if (lane == 0) fsflag(fs_timeout(l, 47));
           ok = false;
           break;
@@ -583,12 +761,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = 32 * q + lane;                    // accumulator row = TMEM lane
     uint32_t jgu = 0, jd = 0;
     // Dependency counters (zero at launch): cnt1[seg] counts the gate/up items
-    // of segment seg done (nb * nks per layer), cnt2[p] the down items whose
-    // rows lie in K part p done (kk * H / 128 / nks per layer).  Producers:
-    // the chain's writes, a barrier, then one release add.  Consumers: thread 0
-    // polls (acquire, bounded), then a barrier.
+    // of segment seg done (nb * nks per layer); cnt2[p] the down items whose
+    // rows lie in K part p done (kk * H / 128 / nks per layer) -- in the
+    // routed stack cnt2[rb] the down items of 128-row block rb (kk per layer)
+    // and rcnt the reducers done (nR per layer, the launch's prologue first).
+    // Producers: the chain's writes, a barrier, then one release add.
+    // Consumers: thread 0 polls (acquire, bounded), then a barrier.
     unsigned* cnt1 = a.bar;
     unsigned* cnt2 = a.bar + 16;
+    unsigned* rcnt = a.bar + 32;
+    unsigned* rcnt1 = a.bar + 33;
     const unsigned per_seg = (unsigned)(nb * a.nks);
     const int rb_per_part = H / 128 / a.nks;
     const unsigned per_part = (unsigned)(a.kk * rb_per_part);
@@ -615,21 +797,99 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_sync(kBarChain, kChain);
       if (ct == 0) red_release_add_fs(ctr, 1u);  // orders the CTA's writes (bar.sync) first
     };
+    // Routed stack, reducer c (c < nR): rows [red_r0, red_r0 + 32), one per
+    // thread ct < 32 (the chain's first warp).
+    const int nR = H / kFsRedRows;
+    const bool is_red = ROUTED && c < nR;
+    const int red_r0 = c * kFsRedRows;
+    float hrow = 0.f;  // reducer thread ct < 32: h_j at its row (the residual)
+    // Layer j's input x_j from h_j (hrow), its logit partials, and the release.
+    // With the norm: the rows' squares into layer j's sum-of-squares line, a
+    // wait for every reducer's, then x = dtype(dtype(h * r) * w) with
+    // r = 1 / sqrt(sum / H + eps).  Then x_j into X and S.xs, the partials of
+    // x_j[rows] . G_j[e, rows] (router rows of layer j landed: issued two
+    // layers ago), the accumulator block of layer j + 1 zeroed (this reducer's
+    // experts c, c + nR, ..., and reducer 0 the squares line: their previous
+    // contents, layer j - 2's, were read before any item of layer j - 2 and
+    // in the norm step of layer j - 2, all of which precede the releases of
+    // layer j - 1 that this reducer has waited for), the router rows of layer
+    // j + 2 into the freed buffer, and the release.
+    auto route_rows = [&](int j) -> bool {
+      const int row = red_r0 + ct;
+      float xv = hrow;
+      if (a.has_norm) {
+        unsigned long long* sq = acc_block(a, j) + (size_t)a.E * kFsLgStride;
+        if (ct < 32) {
+          const float s2 = warp_sum(hrow * hrow);
+          if (ct == 0) add_fixed_partial(sq, s2, kSqUnitInv, 1.0e10f);
+        }
+        signal_count(rcnt1);
+        if (!wait_count(rcnt1, (unsigned)(j + 1) * nR, j, 56)) return false;
+        if (ct < 32) {
+          const float r = 1.0f / sqrtf(read_fixed_sum(sq, kSqUnit) / (float)H + a.eps);
+          const float w = load_as_f32(a.layer[j].norm_w, a.dtype, row);
+          xv = round_to(round_to(hrow * r, a.dtype) * w, a.dtype);
+        }
+      }
+      if (ct < 32) {
+        __stcg(a.X + (size_t)((a.l0 + j) & 1) * H + row, xv);
+        S.xs[ct] = xv;
+      }
+      cp_async_wait_prev_fs();
+      named_sync(kBarChain, kChain);
+      router_partials(a, S, j, ct);
+      unsigned long long* z = acc_block(a, j + 1);
+      for (int i = ct; i < 2 * ((a.E + nR - 1) / nR); i += kChain) {
+        const int e = c + nR * (i >> 1);
+        if (e < a.E) z[(size_t)e * kFsLgStride + (i & 1)] = 0ull;
+      }
+      if (c == 0 && ct < 2) z[(size_t)a.E * kFsLgStride + ct] = 0ull;
+      named_sync(kBarChain, kChain);
+      issue_router_rows(a, S, j + 2, red_r0, ct);
+      signal_count(rcnt);
+      return true;
+    };
     bool alive = true;
+    if (is_red) {
+      // prologue: layer 0's input and logits from this launch's h_0
+      issue_router_rows(a, S, 0, red_r0, ct);
+      issue_router_rows(a, S, 1, red_r0, ct);
+      if (ct < kFsRedRows) {
+        const int row = red_r0 + ct;
+        hrow = a.first ? load_as_f32(a.x0, a.dtype, row)
+                       : __ldcg(a.X + (size_t)(2 + (a.l0 & 1)) * H + row);
+      }
+      alive = route_rows(0);
+    }
     for (int l = 0; l < a.L && alive; l++) {
       const int lg = a.l0 + l;  // index in the stack: buffer parity
       float* Yout = a.Yp + (size_t)(lg & 1) * a.kk * H;
       const float* Yin = a.Yp + (size_t)((lg + 1) & 1) * a.kk * H;
       float* GUb = a.GUp + (size_t)(lg & 1) * 2 * a.kk * 2 * I;
+      if (ct == 0) *S.cur = l;
+
+      // ---- routed stack: this layer's routing, once its reducers are done ----
+      if (ROUTED && (has_gu || has_d)) {
+        if (!wait_count(rcnt, (unsigned)(l + 1) * nR, l, 53)) {
+          alive = false;
+          break;
+        }
+        if (ct < 32) {
+          route_layer(a, S, l, lane, c == 0);
+          __threadfence_block();
+          __syncwarp();
+          if (lane == 0) *S.rlayer = l + 1;  // the TMA warp may issue the routed slabs
+        }
+        named_sync(kBarChain, kChain);
+      }
 
       // ---- phase A: x terms, gate/up item -> GUp ----
-      if (ct == 0) *S.cur = l;
       if (has_gu) {
         // only this item's K part of x: its 128 VX values
         float v[VX];
         const int kb = gu_p * (H / a.nks);
         const int k0 = kb + ct * VX;
-        if (l == 0 && a.first) {
+        if (l == 0 && a.first && !ROUTED) {
           if constexpr (VX % 8 == 0) {
 #pragma unroll
             for (int j = 0; j < VX; j += 8)
@@ -639,6 +899,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             load8(a.x0, a.dtype, k0 & ~7, f);
 #pragma unroll
             for (int i = 0; i < 4; i++) v[i] = f[(k0 & 4) + i];
+          }
+        } else if (ROUTED) {
+          // the reducers' x_l (rounded), complete once the routing is
+          const float* Xl = a.X + (size_t)(lg & 1) * H + k0;
+#pragma unroll
+          for (int j = 0; j < VX; j += 4) {
+            const float4 f = __ldcg(reinterpret_cast<const float4*>(Xl + j));
+            v[j] = f.x;
+            v[j + 1] = f.y;
+            v[j + 2] = f.z;
+            v[j + 3] = f.w;
           }
         } else {
           // the previous layer's down items of this part (previous launch: done)
@@ -718,16 +989,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         alive = chain_sync_and(got);
         if (!alive) break;
         tc_fence_after();
-        const float wseg = d_seg < a.k ? S.wts[l * 16 + d_seg] * a.layer[l].scaling : 1.0f;
+        const float wseg = d_seg < a.k ? S.wts[l * 16 + d_seg] * a.scaling : 1.0f;
         const float y = fold_runs(tmem + lane_base + kAccD, S.faca) * wseg;
         tc_fence_before();
         __stcg(Yout + (size_t)d_seg * H + d_rb * 128 + r, y);
-        signal_count(&cnt2[d_rb / rb_per_part]);
+        signal_count(ROUTED ? &cnt2[d_rb] : &cnt2[d_rb / rb_per_part]);
+      }
+
+      // ---- routed stack, reducer: h_{l+1} for its rows, then layer l+1's input ----
+      if (is_red) {
+        if (!wait_count(&cnt2[red_r0 / 128], (unsigned)(l + 1) * a.kk, l, 54)) {
+          alive = false;
+          break;
+        }
+        if (ct < kFsRedRows) {
+          const int row = red_r0 + ct;
+          float part[16];
+#pragma unroll
+          for (int sg = 0; sg < 16; sg++)
+            part[sg] = sg < a.kk ? __ldcg(Yout + (size_t)sg * H + row) : 0.f;
+          float v = 0.f;
+#pragma unroll
+          for (int sg = 0; sg < 16; sg++)
+            if (sg < a.kk) v += part[sg];
+          if (a.residual) v += hrow;
+          hrow = round_to(v, a.dtype);
+          if (l == a.L - 1) {
+            if (a.last) store_from_f32(a.y, a.dtype, row, hrow);
+            else __stcg(a.X + (size_t)(2 + ((lg + 1) & 1)) * H + row, hrow);  // next launch's h_0
+          }
+        }
+        if (l + 1 < a.L && !route_rows(l + 1)) {
+          alive = false;
+          break;
+        }
       }
     }
-    // The stack's output: this CTA's 128-row block of the last layer, once
-    // every down item of its part is done.
-    if (alive && a.last && c < H / 128) {
+    // Given routing: the stack's output, this CTA's 128-row block of the last
+    // layer, once every down item of its part is done.
+    if (!ROUTED && alive && a.last && c < H / 128) {
       const int lg = a.l0 + a.L - 1;
       const float* Yl = a.Yp + (size_t)(lg & 1) * a.kk * H;
       if (wait_count(&cnt2[c / rb_per_part], (unsigned)a.L * per_part, a.L - 1, 52)) {
@@ -745,22 +1045,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int VX>
+template <int VX, bool R>
 const void* pick_va(int va) {
   switch (va) {
-    case 4: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 4>);
-    case 8: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 8>);
-    case 16: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 16>);
+    case 4: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 4, R>);
+    case 8: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 8, R>);
+    case 16: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 16, R>);
     default: return nullptr;
   }
 }
 
 // VX: values of x per chain thread (the K part of a gate/up item / 128).
+template <bool R>
 const void* pick_kernel(int H, int I, int nks) {
   switch (H / nks / 128) {
-    case 4: return pick_va<4>(I / 128);
-    case 8: return pick_va<8>(I / 128);
-    case 16: return pick_va<16>(I / 128);
+    case 4: return pick_va<4, R>(I / 128);
+    case 8: return pick_va<8, R>(I / 128);
+    case 16: return pick_va<16, R>(I / 128);
     default: return nullptr;
   }
 }
@@ -775,24 +1076,28 @@ int decode_stack_fp4_nks(int I, int kk, int sms) {
   return 0;
 }
 
-size_t decode_stack_fp4_smem_bytes(int H, int I, int L) {
-  return fs_carve(H, I, L, nullptr, nullptr) + 1024;
+size_t decode_stack_fp4_smem_bytes(int H, int I, int L, bool routed) {
+  return fs_carve(H, I, L, routed, nullptr, nullptr) + 1024;
 }
 
-bool decode_stack_fp4_supported(int H, int I, int kk, int sms) {
+bool decode_stack_fp4_supported(int H, int I, int kk, int sms, bool routed) {
   if (H != 1024 && H != 2048) return false;
   if (I != 512 && I != 1024 && I != 2048) return false;
   if (kk < 1 || kk > 16 || kk * (H / 128) > sms) return false;  // one down item per CTA
   if (decode_stack_fp4_nks(I, kk, sms) == 0) return false;      // one gate/up item per CTA
+  if (routed && H / kFsRedRows > sms) return false;             // one reducer per CTA
   if (kSfbx + (uint32_t)(H / 16 + I / 16) > kTmemCols) return false;
-  return decode_stack_fp4_smem_bytes(H, I, kFsMaxLayers) <= 227 * 1024;
+  return decode_stack_fp4_smem_bytes(H, I, kFsMaxLayers, routed) <= 227 * 1024;
 }
 
 cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
-  const void* kern = a.nks > 0 ? pick_kernel(a.H, a.I, a.nks) : nullptr;
+  const void* kern = a.nks <= 0 ? nullptr
+                     : a.routed ? pick_kernel<true>(a.H, a.I, a.nks)
+                                : pick_kernel<false>(a.H, a.I, a.nks);
   if (!kern || a.L < 1 || a.L > kFsMaxLayers || a.L * a.mpl > kFsMaxMaps)
     return cudaErrorInvalidValue;
-  const size_t smem = decode_stack_fp4_smem_bytes(a.H, a.I, a.L);
+  if (a.routed && (a.E < 1 || a.E > 256)) return cudaErrorInvalidValue;
+  const size_t smem = decode_stack_fp4_smem_bytes(a.H, a.I, a.L, a.routed != 0);
   cudaError_t e = ensure_smem_ptr(kern, smem);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 0;
@@ -800,7 +1105,8 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  if (decode_stack_fp4_nks(a.I, a.kk, sms) != a.nks || a.kk * (a.H / 128) > sms)
+  if (decode_stack_fp4_nks(a.I, a.kk, sms) != a.nks || a.kk * (a.H / 128) > sms ||
+      (a.routed && a.H / kFsRedRows > sms))
     return cudaErrorInvalidValue;
   // Every CTA must be resident (CTAs wait on one another's counters): one per
   // SM, cooperative launch.
@@ -808,7 +1114,13 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
-  e = cudaMemsetAsync(a.bar, 0, 32 * sizeof(unsigned), stream);  // dependency counters
+  // dependency counters, and (routed) the first layer's logit accumulators
+  const size_t zero = kFsCounters * sizeof(unsigned) +
+                      (a.routed ? fs_acc_block_u64(a.E) * sizeof(unsigned long long) : 0);
+  if (a.routed && reinterpret_cast<const char*>(a.LG) !=
+                      reinterpret_cast<const char*>(a.bar) + kFsCounters * sizeof(unsigned))
+    return cudaErrorInvalidValue;
+  e = cudaMemsetAsync(a.bar, 0, zero, stream);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sms);

@@ -150,29 +150,63 @@ constexpr int kFsMaxLayers = 40;
 constexpr int kFsMaxMaps = 240;
 constexpr int kFsMapsRouted = 6;  // gate codes, gate scales, up codes, up scales, down codes, down scales
 struct FsLayer {
-  const uint32_t* inds;  // [k] device
-  const float* wts;      // [k] device
-  float scaling;
+  // Given routing: inds / wts [k] read.  Routed stack: where the layer's
+  // routing is written (both nullable).
+  uint32_t* inds;
+  float* wts;
+  const uint16_t* router_w;  // routed stack: bf16 [E, H]
+  const float* router_b;     // routed stack: f32 [E] or null
+  const void* norm_w;        // routed stack with the norm: RMSNorm weight [H] (dtype)
 };
+// Routed stack: the reducers of a layer.  Reducer j (CTA j, j < H / kFsRedRows)
+// sums the segment partials of rows [j * kFsRedRows, (j + 1) * kFsRedRows) and
+// adds their share of every expert's router logit.
+constexpr int kFsRedRows = 32;
+constexpr int kFsLgStride = 16;  // u64 per accumulator (one 128-byte line)
+constexpr int kFsCounters = 64;  // cnt1[16] gate/up per segment, cnt2[16], rcnt, rcnt1
+// Routed stack accumulators, one block per layer index mod 3: E expert logit
+// lines, then one line for the sum of squares of the layer's input (the norm).
+__host__ __device__ constexpr size_t fs_acc_block_u64(int E) {
+  return (size_t)(E + 1) * kFsLgStride;
+}
 struct alignas(64) FsArgs {
   CUtensorMap maps[kFsMaxMaps];  // layer l: maps[l * mpl + j]; j >= 6: the shared expert's
   FsLayer layer[kFsMaxLayers];
   int L;           // layers in this launch
-  int first;       // 1: layer 0 of the stack (input x0 in dtype), else the sum of Yp
+  int first;       // 1: layer 0 of the stack (input x0 in dtype), else the previous launch's
   int last;        // 1: the launch ends the stack (writes y)
   int l0;          // stack index of this launch's first layer (buffer parity)
   int H, I, E, k, kk, nks, mpl, dtype;
-  const void* x0;  // [H] stack input (dtype)
+  int routed;      // 1: routing computed per layer on the device (the routed stack)
+  int residual;    // routed stack: h_{l+1} = h_l + block_l(x_l) (else block_l(x_l))
+  int norm;        // routed stack: norm_topk_prob
+  int has_norm;    // routed stack: x_l = RMSNorm(h_l; layer[l].norm_w, eps) (else x_l = h_l)
+  float eps;       // the norm's epsilon
+  float scaling;   // routed_scaling of every layer
+  const void* x0;  // [H] stack input h_0 (dtype)
   void* y;         // [H] stack output (dtype)
   float* Yp;       // [2][kk][H] a layer's output per segment (f32), by layer parity
   float* GUp;      // [2][2][kk][2][I] gate / up pre-activations per K part, by parity
-  unsigned* bar;   // [32] dependency counters, zero at launch
+  float* X;        // routed stack: [2][H] x_l (rounded to dtype), then [2][H] h_l, by parity
+  unsigned long long* LG;  // routed stack: [3][fs_acc_block_u64(E)] fixed-point sums
+  unsigned* bar;   // [kFsCounters] dependency counters, zero at launch (LG block 0 too)
 };
-bool decode_stack_fp4_supported(int H, int I, int kk, int sms);
+bool decode_stack_fp4_supported(int H, int I, int kk, int sms, bool routed = false);
 int decode_stack_fp4_nks(int I, int kk, int sms);
-size_t decode_stack_fp4_smem_bytes(int H, int I, int L);
+size_t decode_stack_fp4_smem_bytes(int H, int I, int L, bool routed = false);
 cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream);
 cudaError_t read_and_clear_stack_fp4_error(int* out);
+
+// RMSNorm of T rows of H (norm.cu).
+struct NormArgs {
+  const void* x;  // [T, H] dtype
+  const void* w;  // [H] dtype, or null (weight 1)
+  void* y;        // [T, H] dtype
+  int64_t T, H;
+  float eps;
+  int dtype;
+};
+cudaError_t launch_rms_norm(const NormArgs& a, cudaStream_t stream, bool pdl);
 
 // Expert-parallel dispatch / combine (ep.cu).
 struct EpPlanArgs {

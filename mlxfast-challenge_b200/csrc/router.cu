@@ -22,6 +22,7 @@
 // so the result is deterministic.
 #include "common.cuh"
 #include "kernels.h"
+#include "topk.cuh"
 
 namespace nvfp4 {
 namespace {
@@ -31,28 +32,13 @@ constexpr int kRouterPad = 32;  // bf16 elements of padding per staged column
 
 // Route one token (called by a whole warp): logit(e) = sum over `slices`
 // of lg[s * stride + e], rounded to the activation dtype as the reference's
-// matmul returns it; sigmoid; bias for choice; top-k by choice (ties to the
-// lower id); weights s / sum(s) when norm.
-//
-// Lane owns experts lane + 32 j, j < kPer (E <= 32 kPer), fully unrolled so
-// the per-lane arrays stay in registers.  Each candidate is one 64-bit key:
-// the choice's bits made order-preserving as an unsigned integer, then the
-// complement of the expert id (equal choices: the lower id is the larger
-// key); 0 marks an entry already taken, padding, or a NaN choice (never
-// chosen, as a NaN never compares greater).  A round is a lane-local max, the
-// warp max of the key (two redux.sync), and the winner's score from its lane.
-__device__ __forceinline__ uint64_t choice_key(float c, uint32_t e) {
-  if (!(c > -INFINITY)) return 0ull;  // -inf (padding) and NaN
-  const uint32_t b = __float_as_uint(c + 0.0f);  // -0 as +0: equal choices tie by id
-  const uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return ((uint64_t)o << 32) | (uint64_t)(0xFFFFFFFFu - e);
-}
-
+// matmul returns it, then the selection of topk.cuh.  Lane owns experts
+// lane + 32 j, j < kPer (E <= 32 kPer), fully unrolled so the per-lane arrays
+// stay in registers.
 template <int kPer>
 __device__ void route_token_t(const RouterArgs& a, int64_t tok, const float* lg, int64_t stride,
                               int slices, int lane) {
-  float sc[kPer];
-  uint64_t key[kPer];
+  float lgt[kPer];
 #pragma unroll
   for (int j = 0; j < kPer; j++) {
     const int64_t e = lane + 32 * j;
@@ -60,47 +46,14 @@ __device__ void route_token_t(const RouterArgs& a, int64_t tok, const float* lg,
     float l = live ? __ldcg(lg + e) : 0.f;
     for (int s = 1; s < slices; s++)
       if (live) l += __ldcg(lg + (int64_t)s * stride + e);
-    if (a.dtype == kBF16) l = __bfloat162float(__float2bfloat16_rn(l));
-    else if (a.dtype == kF16) l = __half2float(__float2half_rn(l));
-    const float sg = sigmoid_ref(l);
-    sc[j] = live ? sg : 0.f;
-    key[j] = live ? choice_key(sg + (a.bias ? a.bias[e] : 0.f), (uint32_t)e) : 0ull;
+    lgt[j] = round_to_dtype(l, a.dtype);
   }
-  float wsum = 0.f;
-  float wsel = 0.f;
-  uint32_t isel = 0;
-  for (int r = 0; r < a.k; r++) {
-    uint64_t bk = key[0];
-    float bs = sc[0];
-#pragma unroll
-    for (int j = 1; j < kPer; j++)
-      if (key[j] > bk) {
-        bk = key[j];
-        bs = sc[j];
-      }
-    // warp max of the 64-bit key: the high words, then the low words among
-    // the lanes holding that high word (redux.sync, one instruction each)
-    const uint32_t hi = (uint32_t)(bk >> 32);
-    const uint32_t mhi = __reduce_max_sync(0xffffffffu, hi);
-    const uint32_t mlo = __reduce_max_sync(0xffffffffu, hi == mhi ? (uint32_t)bk : 0u);
-    const uint64_t wk = ((uint64_t)mhi << 32) | mlo;
-    const uint32_t bid = wk ? 0xFFFFFFFFu - (uint32_t)wk : 0x7fffffffu;
-    const float ws = __shfl_sync(0xffffffffu, bs, (int)(bid & 31));
-    if (wk && (int)(bid & 31) == lane) {
-#pragma unroll
-      for (int j = 0; j < kPer; j++)
-        if (key[j] == wk) key[j] = 0ull;
-    }
-    const float s = wk ? ws : 0.f;
-    wsum += s;
-    if (lane == r) {
-      wsel = s;
-      isel = bid;
-    }
-  }
+  uint32_t isel;
+  float wsel;
+  topk_select<kPer>(lgt, a.bias, (int)a.E, a.k, a.norm != 0, lane, isel, wsel);
   if (lane < a.k) {
     a.inds[tok * a.k + lane] = isel;
-    a.wts[tok * a.k + lane] = a.norm ? wsel / wsum : wsel;
+    a.wts[tok * a.k + lane] = wsel;
   }
 }
 

@@ -8,15 +8,27 @@ kernel and the fused down+combine kernel (C ABI moe_gate_up_swiglu /
 moe_down_combine), the output of layer l feeding layer l+1.  A step replays
 the graph, so launch overhead is paid once per step instead of per kernel.
 
-With given routing and uniform layer shapes (the Laguna case) the step is
-instead ONE persistent launch over all layers (C ABI moe_decode_stack_forward),
-which streams the next layers' expert weights while the current layer's
-dependent chain runs; stack=False keeps the per-layer kernels.
+With uniform layer shapes (the Laguna case) and one sequence (T = 1) the step
+is instead ONE persistent launch over all layers: with given routing
+moe_decode_stack_forward, which streams the next layers'
+expert weights while the current layer's dependent chain runs; with
+route=True (config[2]) moe_decode_stack_routed_forward, which runs each
+layer's router inside the launch and streams a routed expert's weights from
+the moment its layer's top-k is known.  stack=False keeps the per-layer
+kernels (moe_gate_up_swiglu + moe_down_combine, or moe_block_forward with the
+router when route=True), which also serve T > 1 and other shapes.
+
+residual=True makes each layer h_{l+1} = h_l + block_l(x_l), the block output
+summed into the residual stream, and norms (one RMSNorm weight per layer, in
+the activation dtype) makes the block input x_l = RMSNorm(h_l) (else h_l):
+with both, each layer is the decoder layer's MoE half, h + mlp(
+postAttentionLayerNorm(h)) (Laguna.swift:242-246), without the attention
+half.  Routed decode with norms and residual is the realistic serial step: the
+norm keeps every layer's input at unit scale, as in the model.
 
 MoEDecodeChain(blocks, routing)(x_host) is the end-to-end call: it copies the
 step's input from pinned host memory, replays the graph and copies the result
-back.  Routing is given per layer; with route=True each
-layer runs the router first (config[2]).
+back.  With route=True, self.routing[l] holds layer l's routing after a step.
 """
 from __future__ import annotations
 
@@ -32,16 +44,21 @@ class MoEDecodeChain:
     def __init__(self, blocks: Sequence, routing: Optional[Sequence[Tuple[torch.Tensor,
                                                                            torch.Tensor]]],
                  T: int = 1, dtype=torch.bfloat16, route: bool = False, device="cuda:0",
-                 stack: bool = True):
+                 stack: bool = True, residual: bool = False,
+                 norms: Optional[Sequence[torch.Tensor]] = None, eps: float = 1e-6):
         self.blocks = list(blocks)
         self.T = T
         self.dtype = dtype
         self.route = route
+        self.residual = residual
+        self.norms = None if norms is None else [w.to(dtype).contiguous() for w in norms]
+        self.eps = float(eps)
         self.device = torch.device(device)
         H = self.blocks[0].H
         self.H = H
         self.x0 = torch.zeros(T, H, dtype=dtype, device=self.device)
         self.bufs = [torch.zeros(T, H, dtype=dtype, device=self.device) for _ in range(2)]
+        self.xn = torch.zeros(T, H, dtype=dtype, device=self.device)  # a layer's normed input
         self.routing = []
         for l, b in enumerate(self.blocks):
             if route:
@@ -63,23 +80,39 @@ class MoEDecodeChain:
         self.out = None
         from . import _dtype_code
         self._dt = _dtype_code(self.x0, "decode")
-        # One persistent launch for the whole stack when the library accepts it.
+        # One persistent launch for the whole stack when the library accepts it
+        # (the given-routing stack has no residual form).
         self.stack = False
-        if stack and not route and T == 1 and len(self.blocks) <= 64:
+        self.stack_fp4 = False
+        if stack and T == 1 and len(self.blocks) <= 64 and (
+                route or (not residual and self.norms is None)):
             from ._lib import MoeLayerDesc
             n = len(self.blocks)
             self._descs = (MoeLayerDesc * n)(*[b.desc for b in self.blocks])
             self._inds = (ctypes.c_void_p * n)(*[r[0].data_ptr() for r in self.routing])
             self._wts = (ctypes.c_void_p * n)(*[r[1].data_ptr() for r in self.routing])
+            self._norm_ptrs = None if self.norms is None else (ctypes.c_void_p * n)(
+                *[w.data_ptr() for w in self.norms])
             sb = lib().moe_decode_stack_workspace_size(self._descs, n)
             self._stack_ws = torch.zeros(max(sb, 256), dtype=torch.uint8, device=self.device)
             self.stack = self._try_stack()
 
     def _stack_call(self, stream_ptr) -> int:
-        self._stack_launches = lib().moe_decode_stack_launches(self._descs, len(self.blocks))
-        self.stack_fp4 = bool(lib().moe_decode_stack_uses_fp4(self._descs, len(self.blocks)))
+        n = len(self.blocks)
+        if self.route:
+            self._stack_launches = lib().moe_decode_stack_routed_launches(self._descs, n)
+            self.stack_fp4 = self._stack_launches > 0
+            norms = (None if self._norm_ptrs is None
+                     else ctypes.cast(self._norm_ptrs, ctypes.c_void_p))
+            return lib().moe_decode_stack_routed_forward(
+                self.bufs[0].data_ptr(), self.x0.data_ptr(), self._dt, n, self._descs,
+                int(self.residual), norms, self.eps, ctypes.cast(self._inds, ctypes.c_void_p),
+                ctypes.cast(self._wts, ctypes.c_void_p), self._stack_ws.data_ptr(),
+                self._stack_ws.numel(), stream_ptr)
+        self._stack_launches = lib().moe_decode_stack_launches(self._descs, n)
+        self.stack_fp4 = bool(lib().moe_decode_stack_uses_fp4(self._descs, n))
         return lib().moe_decode_stack_forward(
-            self.bufs[0].data_ptr(), self.x0.data_ptr(), self._dt, len(self.blocks), self._descs,
+            self.bufs[0].data_ptr(), self.x0.data_ptr(), self._dt, n, self._descs,
             ctypes.cast(self._inds, ctypes.c_void_p), ctypes.cast(self._wts, ctypes.c_void_p),
             self._stack_ws.data_ptr(), self._stack_ws.numel(), stream_ptr)
 
@@ -105,19 +138,26 @@ class MoEDecodeChain:
         for l, b in enumerate(self.blocks):
             dst = self.bufs[l % 2]
             inds, wts = self.routing[l]
+            res = src.data_ptr() if self.residual else None
+            inp = src
+            if self.norms is not None:
+                check(L.nvfp4_rms_norm(self.xn.data_ptr(), src.data_ptr(),
+                                       self.norms[l].data_ptr(), self._dt, self.T, self.H,
+                                       self.eps, stream_ptr))
+                inp = self.xn
             if self.route:
                 # Router + gate/up + down in one call: the library knows the
                 # gate/up kernel must read the fresh routing after its wait.
-                check(L.moe_block_forward(dst.data_ptr(), src.data_ptr(), None, self._dt, self.T,
+                check(L.moe_block_forward(dst.data_ptr(), inp.data_ptr(), res, self._dt, self.T,
                                           ctypes.byref(b.desc), None, None, inds.data_ptr(),
                                           wts.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
                                           stream_ptr))
                 src = dst
                 continue
-            check(L.moe_gate_up_swiglu(self.act.data_ptr(), self.act_ld, src.data_ptr(),
+            check(L.moe_gate_up_swiglu(self.act.data_ptr(), self.act_ld, inp.data_ptr(),
                                        self._dt, self.T, ctypes.byref(b.desc), inds.data_ptr(),
                                        stream_ptr))
-            check(L.moe_down_combine(dst.data_ptr(), self.act.data_ptr(), self.act_ld, None,
+            check(L.moe_down_combine(dst.data_ptr(), self.act.data_ptr(), self.act_ld, res,
                                      self._dt, self.T, ctypes.byref(b.desc), inds.data_ptr(),
                                      wts.data_ptr(), stream_ptr))
             src = dst
@@ -128,7 +168,7 @@ class MoEDecodeChain:
         launch flags choose the FP4 or the mma.sync stack)."""
         if self.stack:
             return self._stack_launches
-        return len(self.blocks) * (3 if self.route else 2)
+        return len(self.blocks) * ((3 if self.route else 2) + (1 if self.norms else 0))
 
     def capture(self, pdl: bool = True):
         """Capture one step.  With pdl, every kernel may start while its

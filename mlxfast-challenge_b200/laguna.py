@@ -3,8 +3,8 @@
 Geometry from the reference's fixtures/poolside_laguna_xs_2_1_nvfp4_config.json
 (hidden_size :61, moe_intermediate_size :153, moe_routed_scaling_factor :154,
 norm_topk_prob :155, num_experts :199, num_experts_per_tok :200,
-num_hidden_layers :201, quantization :204-213, shared_expert_intermediate_size
-:233).  Layer 0 is dense BF16; layers 1..39 carry the sparse MoE block.
+num_hidden_layers :201, quantization :204-213, rms_norm_eps :214,
+shared_expert_intermediate_size :233).  Layer 0 is dense BF16; layers 1..39 carry the sparse MoE block.
 
 The real checkpoint is not available, so layers are random-init: bf16 weights
 ~ N(0, std) quantized to NVFP4 by this library's quantizer (bit-identical to
@@ -31,6 +31,7 @@ class LagunaMoEConfig:
     norm_topk_prob: bool = True
     num_layers: int = 40
     num_sparse_layers: int = 39
+    rms_norm_eps: float = 1e-6
 
     def routed_bytes_per_expert(self) -> int:
         """Packed codes + scales of one expert's gate, up and down projections."""
@@ -86,10 +87,13 @@ def random_sparse_layer(nv, seed: int, device="cuda:0", cfg: LagunaMoEConfig = L
         shared["down_w"], shared["down_s"] = _quantized_bank(nv, (H, Is), std, gen, device)
     router_w = (torch.randn(E, H, generator=gen, device=device) * std).to(torch.bfloat16)
     router_b = torch.randn(E, generator=gen, device=device) * bias_std
+    # the decoder layer's post_attention_layernorm weight in front of the block
+    norm_w = (1.0 + 0.1 * torch.randn(H, generator=gen, device=device)).to(torch.bfloat16)
     block = nv.SparseMoeBlock(routed, shared, router_w, router_b, top_k=cfg.top_k,
                               routed_scaling=cfg.routed_scaling,
                               norm_topk_prob=cfg.norm_topk_prob)
-    return block, dict(routed=routed, shared=shared, router_w=router_w, router_b=router_b)
+    return block, dict(routed=routed, shared=shared, router_w=router_w, router_b=router_b,
+                       norm_w=norm_w)
 
 
 def random_routing(T: int, cfg: LagunaMoEConfig, seed: int, device="cuda:0"):

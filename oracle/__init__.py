@@ -54,6 +54,7 @@ class _Port:
         L.orc_gather_qmm_f32.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]
         L.orc_gather_qmm_bf16.argtypes = [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _P]
         L.orc_router_topk.argtypes = [_P, _P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P]
+        L.orc_rms_norm_bf16.argtypes = [_P, _P, _I64, _I64, _F, _P]
         L.orc_moe_block_f32.argtypes = ([_P, _P, _P, _I64, _I64, _I64, _I, _F] + [_P] * 6 +
                                         [_I64] + [_P] * 6 + [_P, _P])
         L.orc_to_fp4_e2m1.restype = ctypes.c_uint8
@@ -177,6 +178,15 @@ class _Port:
         self.lib.orc_router_topk(_ptr(x), _ptr(G), _ptr(b), T, H, E, k, int(norm),
                                  int(round_logits), _ptr(inds), _ptr(wts), _ptr(logits))
         return inds, wts, logits
+
+    def rms_norm_bf16(self, x_bits, w_bits, eps):
+        """RMSNorm of bf16 rows (bit patterns) with bf16 weights -> bf16 bits."""
+        x = np.ascontiguousarray(x_bits, np.uint16)
+        H = x.shape[-1]
+        w = None if w_bits is None else np.ascontiguousarray(w_bits, np.uint16)
+        y = np.empty_like(x)
+        self.lib.orc_rms_norm_bf16(_ptr(x), _ptr(w), x.size // H, H, float(eps), _ptr(y))
+        return y
 
     def moe_block_f32(self, x, inds, wts, routed, shared=None, scaling=2.5, residual=None):
         """routed / shared: dicts with gate_w, gate_s, up_w, up_s, down_w, down_s."""

@@ -340,6 +340,32 @@ ORC_API float orc_sigmoid(float x) {
 static inline float silu(float g) { return g * orc_sigmoid(g); }
 
 /* ------------------------------------------------------------------------ */
+/* RMSNorm (mlx/fast.cpp:90-108, the fallback graph the CPU evaluates):      */
+/*   x32 = f32(x); x32 *= rsqrt(mean(x32^2) + eps); x = bf16(x32);          */
+/*   y = bf16(x * w)   (x, w bf16 bits [T, H] / [H], w NULL = 1).           */
+/* MLX sums the squares in f32 in its reduction's order; this restatement   */
+/* sums in double and rounds the mean to f32 once (the two agree to an ulp  */
+/* of the mean).  rsqrt is 1 / sqrt in f32.                                  */
+/* ------------------------------------------------------------------------ */
+ORC_API void orc_rms_norm_bf16(const uint16_t *x, const uint16_t *w, int64_t T, int64_t H,
+                               float eps, uint16_t *y) {
+  for (int64_t t = 0; t < T; t++) {
+    double ss = 0.0;
+    for (int64_t h = 0; h < H; h++) {
+      const double v = orc_bf16_to_f32(x[t * H + h]);
+      ss += v * v;
+    }
+    const float mean = (float)(ss / (double)H);
+    const float r = 1.0f / sqrtf(mean + eps);
+    for (int64_t h = 0; h < H; h++) {
+      const float v = bfr(orc_bf16_to_f32(x[t * H + h]) * r);
+      const float g = w ? orc_bf16_to_f32(w[h]) : 1.0f;
+      y[t * H + h] = orc_bf16_from_f32(v * g);
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Router (VLM/MLXLLM/Models/Laguna.swift:165-180 LagunaMoEGate):           */
 /*   logits = x @ G^T  (bf16 matmul: f32 accumulation, result rounded to    */
 /*            bf16 when round_logits is set, as MLX does for bf16 inputs),  */

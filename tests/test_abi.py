@@ -122,3 +122,25 @@ def test_decode_stack_rejects_unsupported_shapes(nv):
                                     ctypes.cast(ptrs, ctypes.c_void_p),
                                     ctypes.cast(ptrs, ctypes.c_void_p), None, 0, None)
     assert st == nv._lib.NVFP4_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("field,value", [("shared_inter", 256), ("inter", 1024),
+                                         ("n_experts", 128), ("top_k", 4)])
+def test_stacks_reject_layers_of_another_shape(nv, field, value):
+    """Every layer of a decode stack must have layer 0's shape, the shared
+    expert's width included (its tensor maps and work split come from layer
+    0): a later layer that differs is refused on the host."""
+    L = nv._lib.lib()
+    D = nv._lib.MoeLayerDesc
+    a = D()
+    a.hidden, a.inter, a.n_experts, a.top_k, a.shared_inter = 2048, 512, 256, 8, 512
+    a.routed_scaling, a.norm_topk_prob = 2.5, 1
+    b = D.from_buffer_copy(a)
+    setattr(b, field, value)
+    descs = (D * 2)(a, b)
+    assert L.moe_decode_stack_forward(None, None, 0, 2, descs, None, None, None, 0,
+                                      None) == nv._lib.NVFP4_ERR_UNSUPPORTED
+    assert "share one shape" in _last(L)
+    assert L.moe_decode_stack_routed_forward(None, None, 0, 2, descs, 1, None, 1e-6, None, None,
+                                             None, 0, None) == nv._lib.NVFP4_ERR_UNSUPPORTED
+    assert "[moe_decode_stack_routed]" in _last(L)
