@@ -1,32 +1,43 @@
 #!/usr/bin/env python
 """Benchmark of the NVFP4 MoE decode hot path (Laguna XS 2.1 sparse layers).
 
-Workload (the configuration the metric is quoted on): one
-routed-MoE expert layer at decode, T=1 -- 256 experts, top-8 with given
-distinct uniform expert picks and softmax(N(0,1)) routing weights, SwiGLU
-gate/up [512, 2048] and down [2048, 512] NVFP4 group-16, weights quantized
-from bf16 N(0, 0.02), x bf16 N(0, 1).  A "step" runs that layer for each of
-the model's 39 sparse layers back to back (distinct weights per layer, the
-output of one layer is the input of the next), i.e. the routed-MoE work of
-one decode token.  One step streams 39 x 14.16 MB = 552 MB of expert weights,
-far more than the 126 MB L2, so no timed iteration is served from L2.
+Headline workload (BASELINE config[2] at one sequence, the Laguna decode the
+metric is quoted on): the full sparse block at decode, T=1 -- RMSNorm, the
+BF16 router [256, 2048] top-8 computed on the device, 256 routed NVFP4
+experts (SwiGLU gate/up [512, 2048], down [2048, 512], group 16), the NVFP4
+shared expert, summed into the bf16 residual stream -- for each of the
+model's 39 sparse layers in turn: h_{l+1} = h_l + block_l(RMSNorm_l(h_l)),
+the decoder layers' MoE halves without the attention halves.  The routing of
+layer l+1 depends on layer l's output, so no routed expert's weights can be
+fetched before its layer's router has run.  Weights are random-init (bf16
+N(0, 0.02) quantized with the reference's nvfp4 quantizer, router N(0, 0.02),
+norm weights 1 + N(0, 0.1)); the input h_0 is bf16 N(0, 1).  One step streams
+39 x ~17 MB of weights, far more than the 126 MB L2, so no timed iteration is
+served from L2.
 
-value   = algorithmic HBM bytes of all ranks' steps / device time (GB/s), the
-          device time measured with CUDA events around K graph replays, max
-          over ranks.
+value   = algorithmic HBM bytes of all ranks' steps / device time (GB/s): per
+          layer the router, the shared expert, the distinct routed experts the
+          router chose (counted from its outputs), the norm weight and the
+          activations; device time with CUDA events around K CUDA-graph
+          replays, max over ranks.
 e2e     = the same metric through the public API MoEDecodeChain(x_host): per
           step the input is copied from pinned host memory, the layers run and
           the output is read back to the host.
-roofline= the dominant kernel timed alone: the persistent decode stack, which
-          runs all 39 layers in one launch (moe_decode_stack_fp4_kernel on the
-          block-scaled FP4 tensor cores by default; or, where no stack
-          applies, the per-layer fused gate/up + SwiGLU kernel).
+roofline= the dominant kernel timed alone: the routed persistent decode stack
+          (moe_decode_stack_fp4_kernel, routed form), which is the whole step.
 
 --impl reference times the reference's own MLX CPU kernel (fp_qmm_t for bf16
-x, compiled from the reference sources into oracle/_ref) on the same layer,
-with all host threads, one sparse layer per step.
+x, compiled from the reference sources into oracle/_ref) for the same layer
+(8 routed experts and the shared expert; the router and norm, which MLX
+evaluates with its generic ops, through the CPU restatement), with all host
+threads, one sparse layer per step.
 
 Also reported on the same line (rank 0, N=1 runs):
+decode_given_routing = BASELINE config[1]: the routed experts only, routing
+          given for all 39 layers before the step (the persistent stack
+          streams later layers' experts ahead).
+decode_b8 = config[2] at 8 sequences (T=8) through the per-layer kernels
+          (RMSNorm, router, fused gate/up and down + combine per layer).
 prefill = BASELINE config[3] on one GPU: the full sparse block (BF16 router
           top-8, 256 routed experts, shared expert, residual) at T=512 tokens,
           39 sparse layers per step (4 distinct random-init layers cycled, 452 MB
@@ -39,11 +50,11 @@ dense   = BASELINE config[0]: quantized_matmul x[M, 2048] @ W[4096, 2048]^T,
 
 prefill_ep (N > 1 only) = config[3] expert-parallel: each GPU holds 256/N
           experts (+ router and shared expert) and its own 512 tokens; pair
-          rows go to their experts' GPU and back by NCCL all-to-all; total
-          tok/s over all GPUs, device time max over ranks.
+          rows go to their experts' GPU and back by NCCL; total tok/s over all
+          GPUs, device time max over ranks.
 
---workload prefill|dense prints only that measurement (used by the committed
-ncu profiling commands).
+--workload prefill|dense|decode prints only that measurement (used by the
+committed ncu profiling commands).
 
 Multi-GPU: serial decode does not shard (replicas only): each rank runs its own
 chain; value is the aggregate.
@@ -66,7 +77,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "moe_decode_hbm_gbs"
 UNIT = "GB/s"
-L2_NOTE = "inputs larger than L2 (552 MB of expert weights per step vs 126 MB L2)"
+L2_NOTE = "inputs larger than L2 (~660 MB of weights per step vs 126 MB L2)"
 
 
 def parse():
@@ -87,11 +98,6 @@ def layer_bytes(cfg, k, T=1):
     """Algorithmic bytes of one config[1] layer: the k selected experts' packed
     codes + scales (gate, up, down) plus bf16 x in and y out."""
     return k * cfg.routed_bytes_per_expert() + 2 * T * cfg.hidden * 2
-
-
-def gateup_bytes(cfg, k, T=1):
-    per_row = cfg.hidden // 2 + cfg.hidden // 16
-    return k * 2 * cfg.inter * per_row + T * cfg.hidden * 2 + T * k * cfg.inter * 2
 
 
 # ----------------------------------------------------------------------------- prefill / dense
@@ -238,56 +244,76 @@ def bench_dense(torch, nv, dev, reps=50, copies=32):
 
 
 # ----------------------------------------------------------------------------- CPU
-def cpu_reference_gbs(seconds, threads, cfg, steps=None, warmup=0):
-    """The reference's MLX CPU kernel (oracle/_ref) on one config[1] layer per step."""
-    import numpy as np
+class _CpuLayer:
+    """One config[2] sparse layer (one sequence) for the CPU arms: 8 routed
+    experts and the shared expert as packed NVFP4 banks quantized from bf16
+    N(0, 0.02) by the reference's quantizer (the CPU restatement, bit-identical
+    to it), a bf16 router and norm weight; x bf16 N(0, 1)."""
+
+    def __init__(self, cfg, seed=0):
+        import numpy as np
+        import oracle
+        self.np, self.orc = np, oracle
+        rng = np.random.default_rng(seed)
+        H, I, k = cfg.hidden, cfg.inter, cfg.top_k
+        bits = lambda *shape: oracle.bf16_bits_from_f32(
+            (rng.standard_normal(shape) * 0.02).astype(np.float32))
+        q = lambda *shape: oracle.port.quantize(bits(*shape))
+        self.experts = [(q(I, H), q(I, H), q(H, I)) for _ in range(k + 1)]  # k routed + shared
+        self.G = bits(cfg.n_experts, H)
+        self.bias = (rng.standard_normal(cfg.n_experts) * 1e-3).astype(np.float32)
+        self.norm_w = oracle.bf16_bits_from_f32(
+            (1 + 0.1 * rng.standard_normal(H)).astype(np.float32))
+        self.h = oracle.bf16_bits_from_f32(rng.standard_normal((1, H)).astype(np.float32))
+        self.k = k
+        self.bytes = (cfg.router_bytes() + cfg.shared_bytes() + k * cfg.routed_bytes_per_expert()
+                      + 2 * H * 2 + H * 2)
+
+    def run(self, impl, kind, threads):
+        """The layer as MLX evaluates it for bf16 on the CPU: norm, router,
+        then each expert's gate / up / down through fp_qmm_t<bfloat16_t> (the
+        reference's own kernel when kind == "reference"), SwiGLU and the
+        weighted sum in bf16 steps, plus the residual."""
+        np, orc = self.np, self.orc
+        x = orc.port.rms_norm_bf16(self.h, self.norm_w, 1e-6)
+        _, w, _ = orc.port.router_topk(x, self.G, self.bias, self.k)
+        if kind == "reference":
+            mm = lambda a, wq: impl.qmm_bf16(a, wq[0], wq[1], threads=threads)
+        else:
+            mm = lambda a, wq: orc.bf16_bits_from_f32(
+                impl.qmm_f32(orc.f32_from_bf16_bits(a), wq[0], wq[1]))
+        acc = np.zeros(self.h.shape[-1], np.float32)
+        for j, (g, u, d) in enumerate(self.experts):
+            gf = orc.f32_from_bf16_bits(mm(x, g))
+            uf = orc.f32_from_bf16_bits(mm(x, u))
+            a = orc.bf16_bits_from_f32(gf / (1 + np.exp(-gf)) * uf)
+            y = orc.f32_from_bf16_bits(mm(a, d))[0]
+            acc += (2.5 * w[0][j] if j < self.k else 1.0) * y
+        return acc + orc.f32_from_bf16_bits(self.h)[0]
+
+
+def cpu_reference_gbs(seconds, threads, cfg, steps=None, warmup=0, layer=None):
+    """The reference's MLX CPU kernel (oracle/_ref) on one config[2] layer per step."""
     import oracle
     impl = oracle.ref if oracle.ref is not None else oracle.port
     kind = "reference" if oracle.ref is not None else "port"
-    rng = np.random.default_rng(0)
-    k, H, I = cfg.top_k, cfg.hidden, cfg.inter
-    # Codes/scales of the 8 selected experts (values do not change CPU timing).
-    gw = rng.integers(0, 2**32, (k, I, H // 8), dtype=np.uint64).astype(np.uint32)
-    gs = rng.integers(0x20, 0x48, (k, I, H // 16)).astype(np.uint8)
-    uw, us = gw[::-1].copy(), gs[::-1].copy()
-    dw = rng.integers(0, 2**32, (k, H, I // 8), dtype=np.uint64).astype(np.uint32)
-    ds = rng.integers(0x20, 0x48, (k, H, I // 16)).astype(np.uint8)
-    x = oracle.bf16_bits_from_f32(rng.standard_normal((1, H)).astype(np.float32))
-    wts = np.full(k, 1.0 / k, np.float32)
-
-    def one_layer():
-        acc = np.zeros(H, np.float32)
-        for j in range(k):
-            if kind == "reference":
-                g = impl.qmm_bf16(x, gw[j], gs[j], threads=threads)
-                u = impl.qmm_bf16(x, uw[j], us[j], threads=threads)
-            else:
-                g = oracle.bf16_bits_from_f32(impl.qmm_f32(oracle.f32_from_bf16_bits(x), gw[j], gs[j]))
-                u = oracle.bf16_bits_from_f32(impl.qmm_f32(oracle.f32_from_bf16_bits(x), uw[j], us[j]))
-            gf, uf = oracle.f32_from_bf16_bits(g), oracle.f32_from_bf16_bits(u)
-            a = oracle.bf16_bits_from_f32(gf / (1 + np.exp(-gf)) * uf)
-            if kind == "reference":
-                d = impl.qmm_bf16(a, dw[j], ds[j], threads=threads)
-            else:
-                d = oracle.bf16_bits_from_f32(impl.qmm_f32(oracle.f32_from_bf16_bits(a), dw[j], ds[j]))
-            acc += wts[j] * oracle.f32_from_bf16_bits(d)[0]
-        return acc * 2.5
-
+    layer = layer or _CpuLayer(cfg)
     for _ in range(warmup):
-        one_layer()
+        layer.run(impl, kind, threads)
     t0 = time.perf_counter()
     n = 0
     while True:
-        one_layer()
+        layer.run(impl, kind, threads)
         n += 1
         el = time.perf_counter() - t0
         if (steps is not None and n >= steps) or (steps is None and el >= seconds):
             break
-    b = layer_bytes(cfg, k)
-    return dict(value=b * n / el / 1e9, unit=UNIT, cores=threads, kind=kind,
-                sample=f"{n} config[1] layers (8 experts x gate/up/down, T=1), bf16 x through "
-                       f"the reference fp_qmm_t<bfloat16_t,16,4> split over {threads} threads; "
-                       f"{el:.2f} s"), n, el
+    what = ("the reference fp_qmm_t<bfloat16_t,16,4>" if kind == "reference"
+            else "the CPU restatement of fp_qmm_t")
+    return dict(value=layer.bytes * n / el / 1e9, unit=UNIT, cores=threads, kind=kind,
+                sample=f"{n} config[2] layers (norm, router, 8 routed experts + shared expert "
+                       f"x gate/up/down, T=1), bf16 x through {what} split over {threads} "
+                       f"thread(s); {el:.2f} s"), n, el
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -337,28 +363,100 @@ def measured_peak_hbm():
         return 6650.0, "fallback"
 
 
-def stack_traffic(layers, fp4=True):
-    """DRAM bytes of one decode-stack launch over `layers` layers (the FP4 or
-    the mma.sync stack), scaled from the committed ncu capture (taken on fewer
+def stack_traffic(layers, kind="routed", launches=1):
+    """DRAM bytes per launch of a decode stack over `layers` layers in
+    `launches` launches (kind: "routed", "fp4" given routing, or "exact", the
+    mma.sync stack), scaled from the committed ncu capture (taken on fewer
     layers; the kernel moves the same bytes per layer)."""
-    p = os.path.join(ROOT, "profiles", "moe_decode_stack_fp4_traffic.json" if fp4
-                     else "moe_decode_stack_traffic.json")
+    name = {"routed": "moe_decode_stack_routed_traffic.json",
+            "fp4": "moe_decode_stack_fp4_traffic.json",
+            "exact": "moe_decode_stack_traffic.json"}[kind]
     try:
-        with open(p) as f:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
             d = json.load(f)
-        return d["dram_bytes_per_layer"] * layers
+        return d["dram_bytes_per_layer"] * layers / launches
     except Exception:
         return None
 
 
-def ncu_traffic():
-    """dram bytes per launch of the gate/up kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "moe_gateup_decode_traffic.json")
-    try:
-        with open(p) as f:
-            return json.load(f).get("dram_bytes_per_launch")
-    except Exception:
-        return None
+# ----------------------------------------------------------------------------- decode
+def time_replays(torch, chain, steps):
+    """Device ms per step over `steps` replays of the chain's graph (CUDA events
+    on its stream)."""
+    s = chain.stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(steps):
+            chain.graph.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def distinct_experts(chain):
+    """Distinct routed experts per layer of the chain's last step."""
+    return [int(len(set(r[0].view(torch_int32()).flatten().tolist()))) for r in chain.routing]
+
+
+def torch_int32():
+    import torch
+    return torch.int32
+
+
+def step_bytes(cfg, U, T):
+    """Algorithmic bytes of one step: per layer the router, the shared expert,
+    the distinct routed experts U[l] (packed codes + scales of gate, up and
+    down), the norm weight, and the activations in (h) and out (h_next)."""
+    per_act = 2 * T * cfg.hidden * 2
+    return sum(cfg.router_bytes() + cfg.shared_bytes() + u * cfg.routed_bytes_per_expert() +
+               cfg.hidden * 2 + per_act for u in U)
+
+
+def bench_given_routing(torch, nv, lag, cfg, dev, made, steps, warmup):
+    """config[1]: the routed experts only (no shared expert, no router), the
+    routing of all layers given before the step (k distinct uniform experts,
+    softmax(N(0,1)) weights), 39 layers chained through the persistent stack."""
+    blocks = [nv.SparseMoeBlock(m[1]["routed"], None, top_k=cfg.top_k,
+                                routed_scaling=cfg.routed_scaling) for m in made]
+    routing = [lag.random_routing(1, cfg, seed=5000 + l, device=dev) for l in range(len(made))]
+    chain = nv.MoEDecodeChain(blocks, routing, T=1, device=dev).capture()
+    chain.x0.copy_(torch.randn(1, cfg.hidden, device=dev).to(torch.bfloat16))
+    for _ in range(max(warmup, 3)):
+        chain.replay()
+    torch.cuda.synchronize()
+    ms = time_replays(torch, chain, steps)
+    b = len(made) * layer_bytes(cfg, cfg.top_k)
+    out = {"workload": "BASELINE config[1]: routed experts only, routing given for all "
+                       f"{len(made)} layers before the step (the stack streams later layers' "
+                       "experts ahead)",
+           "value": b / (ms / 1e3) / 1e9, "unit": UNIT, "us_per_layer": ms * 1e3 / len(made),
+           "kernel": "moe_decode_stack_fp4_kernel (given routing)" if chain.stack_fp4
+           else "moe_decode_stack_kernel (mma.sync)", "bytes_per_step": b}
+    del chain
+    return out
+
+
+def bench_decode_b8(torch, nv, cfg, dev, blocks, norms, steps, warmup, T=8):
+    """config[2] at T sequences: per layer RMSNorm, router, fused gate/up +
+    SwiGLU and down + combine + residual (the per-layer kernels in one CUDA
+    graph); bytes from the distinct experts the router chose."""
+    chain = nv.MoEDecodeChain(blocks, None, T=T, route=True, residual=True, norms=norms,
+                              device=dev, stack=False).capture()
+    chain.x0.copy_(torch.randn(T, cfg.hidden, device=dev).to(torch.bfloat16))
+    for _ in range(max(warmup, 3)):
+        chain.replay()
+    torch.cuda.synchronize()
+    ms = time_replays(torch, chain, steps)
+    U = distinct_experts(chain)
+    b = step_bytes(cfg, U, T)
+    out = {"workload": f"BASELINE config[2] at {T} sequences: the same layers, T={T}, per-layer "
+                       "kernels (rms_norm, router, gate/up + SwiGLU, down + combine + residual)",
+           "value": b / (ms / 1e3) / 1e9, "unit": UNIT, "us_per_layer": ms * 1e3 / len(blocks),
+           "tok_per_s_moe_only": T * 1e3 / ms, "mean_distinct_experts": sum(U) / len(U),
+           "bytes_per_step": b, "launches_per_step": chain.launches_per_step()}
+    del chain
+    return out
 
 
 # ----------------------------------------------------------------------------- main
@@ -379,8 +477,10 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / n * 1e3,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": "BASELINE config[1]: routed MoE layer decode T=1, "
-                                       "256 experts top-8, H=2048 I=512, one layer per step",
+                "config": {"workload": "BASELINE config[2] at one sequence: Laguna sparse "
+                                       "block at decode T=1 (RMSNorm, router top-8, 8 of 256 "
+                                       "routed experts, shared expert, residual), H=2048 "
+                                       "I=512, one layer per step",
                            "l2": "CPU"},
                 "impl": "reference", "cpu_baseline": cb,
                 "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -408,16 +508,16 @@ def main():
             dist.destroy_process_group()
         return
 
-    # Setup: L random-init sparse layers (routed banks only: config[1]).
-    blocks, routing = [], []
-    for l in range(args.layers):
-        blk, _ = lag.random_sparse_layer(nv, seed=1000 + l, device=dev, with_shared=False)
-        blocks.append(blk)
-        routing.append(lag.random_routing(1, cfg, seed=5000 + l, device=dev))
-    chain = nv.MoEDecodeChain(blocks, routing, T=1, device=dev).capture()
+    # Setup: L random-init sparse layers (config[2]: router, routed experts,
+    # shared expert, the decoder layer's norm weight).
+    made = [lag.random_sparse_layer(nv, seed=1000 + l, device=dev) for l in range(args.layers)]
+    blocks = [m[0] for m in made]
+    norms = [m[1]["norm_w"] for m in made]
     g = torch.Generator(device=dev).manual_seed(7 + rank)
-    chain.x0.copy_(torch.randn(1, cfg.hidden, generator=g, device=dev).to(torch.bfloat16))
-    bytes_step = args.layers * layer_bytes(cfg, cfg.top_k)
+    x0 = torch.randn(1, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+    chain = nv.MoEDecodeChain(blocks, None, T=1, route=True, residual=True, norms=norms,
+                              device=dev).capture()
+    chain.x0.copy_(x0)
     s = chain.stream
 
     # Warm-up, then K timed replays bracketed by barrier + synchronize.
@@ -433,86 +533,54 @@ def main():
     if rank == 0:
         sampler.start()
         time.sleep(0.3)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(s):
-        ev0.record(s)
-        for _ in range(args.steps):
-            chain.graph.replay()
-        ev1.record(s)
+    ms = time_replays(torch, chain, args.steps)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     clocks = sampler.stop() if rank == 0 else None
-    ms = ev0.elapsed_time(ev1)
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world * args.steps * bytes_step / (ms_max / 1e3) / 1e9
+    # The step's algorithmic bytes from the routing it used (the same every
+    # replay: the input and the weights do not change).
+    U = distinct_experts(chain)
+    bytes_step = step_bytes(cfg, U, T=1)
+    value = world * bytes_step / (ms_max / 1e3) / 1e9
 
-    # Dominant kernel alone.  With the persistent stack (one launch per step)
-    # that kernel is the whole step: time moe_decode_stack_forward calls alone
-    # (its tiny counter reset included); otherwise the L gate/up launches in
-    # one graph.
+    # Dominant kernel alone: the routed stack is the whole step (its launches,
+    # with their counter resets).
     import ctypes
-    L = nv._lib.lib()
     peak, peak_kind = measured_peak_hbm()
     peak_src = (f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6650 GB/s")
-    if chain.stack:
-        reps = max(20, args.steps // 4)
-        with torch.cuda.stream(s):
-            sp = ctypes.c_void_p(s.cuda_stream)
-            for _ in range(3):
-                nv._lib.check(chain._stack_call(sp))
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(s)
-            for _ in range(reps):
-                nv._lib.check(chain._stack_call(sp))
-            e1.record(s)
-        torch.cuda.synchronize()
-        k_ms = e0.elapsed_time(e1) / reps
-        achieved = bytes_step / (k_ms / 1e3) / 1e9
-        tr = stack_traffic(args.layers, chain.stack_fp4)
-        kname = ("moe_decode_stack_fp4_kernel (tcgen05 kind::mxf4nvf4" if chain.stack_fp4
-                 else "moe_decode_stack_kernel (mma.sync")
-        roofline = {"bound": "hbm", "kernel": f"{kname}, {args.layers} layers, "
-                                              f"{chain.launches_per_step()} persistent launch)",
-                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                    "peak_source": peak_src, "traffic": tr,
-                    "algorithmic_bytes_per_launch": bytes_step, "us_per_launch": k_ms * 1e3}
-        gu = None
-    else:
-        gu = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(gu, stream=s):
-                sp = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-                for l, b in enumerate(blocks):
-                    inds, _ = chain.routing[l]
-                    nv._lib.check(L.moe_gate_up_swiglu(chain.act.data_ptr(), chain.act_ld,
-                                                       chain.x0.data_ptr(), 0, 1,
-                                                       ctypes.byref(b.desc), inds.data_ptr(), sp))
-            for _ in range(5):
-                gu.replay()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            reps = max(20, args.steps // 4)
-            e0.record(s)
-            for _ in range(reps):
-                gu.replay()
-            e1.record(s)
-        torch.cuda.synchronize()
-        gu_ms = e0.elapsed_time(e1) / (reps * args.layers)
-        gu_bytes = gateup_bytes(cfg, cfg.top_k)
-        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
-        roofline = {"bound": "hbm", "kernel": "moe_gateup_kernel (fused gate/up + SwiGLU)",
-                    "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                    "peak_source": peak_src, "traffic": ncu_traffic(),
-                    "algorithmic_bytes_per_launch": gu_bytes, "us_per_launch": gu_ms * 1e3}
+    reps = max(20, args.steps // 4)
+    with torch.cuda.stream(s):
+        sp = ctypes.c_void_p(s.cuda_stream)
+        for _ in range(3):
+            nv._lib.check(chain._stack_call(sp))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            nv._lib.check(chain._stack_call(sp))
+        e1.record(s)
+    torch.cuda.synchronize()
+    k_ms = e0.elapsed_time(e1) / reps
+    achieved = bytes_step / (k_ms / 1e3) / 1e9
+    tr = stack_traffic(args.layers, "routed", chain.launches_per_step())
+    roofline = {"bound": "hbm",
+                "kernel": f"moe_decode_stack_fp4_kernel, routed form (tcgen05 kind::mxf4nvf4; "
+                          f"norm, router, experts, residual on the device), {args.layers} layers, "
+                          f"{chain.launches_per_step()} persistent launches",
+                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "peak_source": peak_src, "traffic": tr,
+                "algorithmic_bytes_per_launch": bytes_step / chain.launches_per_step(),
+                "algorithmic_bytes_per_step": bytes_step, "us_per_step": k_ms * 1e3,
+                "us_per_layer": k_ms * 1e3 / args.layers}
 
     # End to end through the public API: pinned host x in, host y out, every step.
-    xh = torch.randn(1, cfg.hidden, generator=torch.Generator().manual_seed(3)).to(
-        torch.bfloat16).pin_memory()
+    xh = x0.cpu().pin_memory()
     yh = torch.empty(1, cfg.hidden, dtype=torch.bfloat16).pin_memory()
     for _ in range(3):
         chain(xh, yh)
@@ -527,12 +595,19 @@ def main():
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_val = world * e2e_steps * bytes_step / float(te.item()) / 1e9
-
     launches = args.steps * chain.launches_per_step()
+    del chain
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu, _, _ = cpu_reference_gbs(args.cpu_seconds, os.cpu_count() or 1, cfg)
-    prefill = dense = prefill_ep = None
+        threads = os.cpu_count() or 1
+        layer = _CpuLayer(cfg)
+        cpu, _, _ = cpu_reference_gbs(args.cpu_seconds, threads, cfg, layer=layer)
+        one, _, _ = cpu_reference_gbs(max(2.0, args.cpu_seconds / 3), 1, cfg, layer=layer)
+        cpu["one_thread"] = {"value": one["value"], "unit": UNIT, "cores": 1,
+                             "sample": one["sample"],
+                             "note": "MLX runs its CPU stream on one thread"}
+    given = b8 = prefill = dense = prefill_ep = None
     if world > 1 and args.workload == "all":
         # every rank takes part (the exchange is collective)
         prefill_ep = bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world,
@@ -542,7 +617,10 @@ def main():
         prefill_ep["all2all_form"] = {"tok_per_s": a2a["tok_per_s"],
                                       "us_per_layer": a2a["us_per_layer"]}
     if rank == 0 and world == 1 and args.workload == "all":
-        del chain
+        given = bench_given_routing(torch, nv, lag, cfg, dev, made, args.steps, args.warmup)
+        b8 = bench_decode_b8(torch, nv, cfg, dev, blocks, norms, max(10, args.steps // 4),
+                             args.warmup)
+        del made, blocks, norms
         torch.cuda.empty_cache()
         prefill = bench_prefill(torch, nv, lag, cfg, dev, args.prefill_steps, 3,
                                 cfg.num_sparse_layers)
@@ -551,16 +629,21 @@ def main():
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE config[1]: routed MoE layer decode T=1 (256 experts, "
-                                   "top-8, H=2048, I=512, NVFP4 g16) x 39 sparse layers per step",
+            "config": {"workload": "BASELINE config[2] at one sequence: Laguna sparse block at "
+                                   "decode T=1 (RMSNorm, BF16 router top-8 on the device, 256 "
+                                   "NVFP4 g16 routed experts, NVFP4 shared expert, residual), "
+                                   "H=2048, I=512, x 39 sparse layers per step, each layer's "
+                                   "input the previous layer's output",
                        "layers_per_step": args.layers, "bytes_per_step": bytes_step,
+                       "distinct_experts_per_layer": U,
                        "l2": L2_NOTE, "parallelism": f"replicas{world}",
-                       "weights": "nvfp4 e2m1/e4m3-g16", "activations": "bf16",
-                       "accumulate": "f32"},
-            "tok_per_s_moe_only": world * args.steps / (ms_max / 1e3),
+                       "weights": "nvfp4 e2m1/e4m3-g16 (router, norm: bf16)",
+                       "activations": "bf16", "accumulate": "f32"},
+            "tok_per_s_moe_only": world * 1e3 / ms_max,
+            "us_per_layer": ms_max * 1e3 / args.layers,
             "gpu_launches": launches,
             "clocks": clocks,
             "roofline": roofline,
@@ -568,13 +651,13 @@ def main():
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": cfg.hidden * 2,
                     "d2h_bytes_per_step": cfg.hidden * 2,
                     "api": "MoEDecodeChain.__call__ (pinned host x -> device -> host y)"},
+            "decode_given_routing": given,
+            "decode_b8": b8,
             "prefill": prefill,
             "prefill_ep": prefill_ep,
             "dense": dense,
         }
         print(json.dumps(line), flush=True)
-    if prefill is None:
-        del chain
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

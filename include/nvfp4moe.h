@@ -315,14 +315,15 @@ NVFP4MOE_API int moe_decode_stack_forward(void* y, const void* x, int dtype, int
  * routed experts' weights stream from then on (only the shared expert and the
  * router weights stream ahead).  Each layer's output is rounded to dtype once:
  * sum of the experts' contributions, then the residual.  Logits are summed as
- * 64-bit fixed-point integers (2^-32 units), so the routing and the outputs
- * are the same bits on every run; a logit beyond 1e9 in magnitude, or not
- * finite, counts as NaN (never chosen).  inds_out / weights_out: NULL, or
+ * 64-bit fixed-point integers (2^-28 units) and the norm's squares in a fixed
+ * order, so the routing and the outputs are the same bits on every run; a
+ * logit partial (32 rows) beyond 8192 in magnitude, or not finite, makes the
+ * logit NaN (never chosen).  inds_out / weights_out: NULL, or
  * n_layers device pointers (each NULL or [top_k] entries) that receive the
  * routing used.  Every layer has the same routed_scaling (also required by
  * moe_decode_stack_forward).  Requirements as moe_decode_stack_forward's FP4 stack (hidden
  * 1024 or 2048, inter 512 / 1024 / 2048, shared_inter 0 or inter), plus
- * n_experts <= 256, router_w 16-byte aligned in every layer, one
+ * n_experts <= 256, top_k <= 8, dtype bf16 or f16, router_w 16-byte aligned in every layer, one
  * norm_topk_prob for all layers, NVFP4_LAUNCH_EXACT_DECODE clear; otherwise
  * NVFP4_ERR_UNSUPPORTED (run moe_block_forward per layer).  Workspace:
  * moe_decode_stack_workspace_size() bytes.  Co-residency as for

@@ -1154,9 +1154,8 @@ struct StackLayout {
 // act / xb: the mma.sync stack; y32 / gu: the FP4 stack's f32 partials
 // ([2][kk][H] per segment, [2][2][kk][2][I] per K part, both by layer parity);
 // bar: grid-barrier / dependency counters; rbar: the routed stack's counters
-// followed by its fixed-point accumulators (3 blocks of fs_acc_block_u64(E)
-// u64), x32 its layer inputs and residual stream ([2][H] + [2][H] f32, by
-// parity).
+// followed by its exchange area (fs_xchg_u64 words, zeroed at each launch),
+// x32 its residual stream at launch boundaries ([2][H] f32, by parity).
 StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   StackLayout S;
   const int64_t kk = L0->top_k + (L0->shared_inter > 0 ? 1 : 0);
@@ -1168,9 +1167,10 @@ StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   S.gu_off = align_up(S.y32_off + 2 * (size_t)kk * L0->hidden * sizeof(float), 256);
   S.rbar_off = align_up(S.gu_off + 4 * (size_t)kk * 2 * L0->inter * sizeof(float), 256);
   S.x32_off = align_up(S.rbar_off + nvfp4::kFsCounters * sizeof(unsigned) +
-                           3 * nvfp4::fs_acc_block_u64((int)L0->n_experts) * sizeof(uint64_t),
+                           nvfp4::fs_xchg_u64((int)L0->hidden, (int)L0->n_experts,
+                                              nvfp4::kFsMaxLayers) * sizeof(uint64_t),
                        256);
-  S.total = align_up(S.x32_off + 4 * (size_t)L0->hidden * sizeof(float), 256);
+  S.total = align_up(S.x32_off + 2 * (size_t)L0->hidden * sizeof(float), 256);
   return S;
 }
 
@@ -1224,7 +1224,9 @@ int fp4_stack_layers_per_launch(const moe_layer_desc* L0, bool routed = false) {
   const int kk = (int)(L0->top_k + (L0->shared_inter > 0 ? 1 : 0));
   if (L0->shared_inter > 0 && L0->shared_inter != L0->inter) return 0;
   if (L0->hidden > 4096 || L0->inter > 4096) return 0;
-  if (routed && L0->n_experts > 256) return 0;
+  if (routed && (L0->n_experts > 256 || L0->top_k > 8 ||
+                 L0->hidden / nvfp4::kFsRedRows > nvfp4::kFsMaxReducers))
+    return 0;
   if (!nvfp4::decode_stack_fp4_supported((int)L0->hidden, (int)L0->inter, kk, device_sms(),
                                          routed))
     return 0;
@@ -1311,13 +1313,13 @@ int run_fp4_stack(const char* op, void* y, const void* x, int dtype, int64_t n_l
   F.GUp = reinterpret_cast<float*>(ws + S.gu_off);
   if (routed) {
     F.bar = reinterpret_cast<unsigned*>(ws + S.rbar_off);
-    F.LG = reinterpret_cast<unsigned long long*>(ws + S.rbar_off +
+    F.XG = reinterpret_cast<unsigned long long*>(ws + S.rbar_off +
                                                  nvfp4::kFsCounters * sizeof(unsigned));
-    F.X = reinterpret_cast<float*>(ws + S.x32_off);
+    F.Hres = reinterpret_cast<float*>(ws + S.x32_off);
   } else {
     F.bar = reinterpret_cast<unsigned*>(ws + S.bar_off);
-    F.LG = nullptr;
-    F.X = nullptr;
+    F.XG = nullptr;
+    F.Hres = nullptr;
   }
   // routed and given-routing stacks keep separate tensor-map cache entries
   const size_t cache0 = routed ? (size_t)nvfp4::kStackMaxLayers * 2 * nvfp4::kFsMapsRouted : 0;
@@ -1485,11 +1487,11 @@ extern "C" int moe_decode_stack_routed_forward(void* y, const void* x, int dtype
   if (!y || !x) return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
   const moe_layer_desc* L0 = &layers[0];
   const int per_launch = fp4_stack_layers_per_launch(L0, true);
-  if (per_launch == 0)
+  if (per_launch == 0 || dtype == NVFP4_F32)
     return fail(NVFP4_ERR_UNSUPPORTED,
-                "[%s] this layer shape or launch mode has no routed stack (hidden 1024 or 2048, "
-                "inter 512 / 1024 / 2048, at most 256 experts, NVFP4_LAUNCH_EXACT_DECODE "
-                "clear); use moe_block_forward per layer.",
+                "[%s] this layer shape, dtype or launch mode has no routed stack (bf16 or f16, "
+                "hidden 1024 or 2048, inter 512 / 1024 / 2048, at most 256 experts, top_k <= 8, "
+                "NVFP4_LAUNCH_EXACT_DECODE clear); use moe_block_forward per layer.",
                 op);
   if (!aligned16(x) || !aligned16(y))
     return fail(NVFP4_ERR_UNSUPPORTED, "[%s] x and y must be 16-byte aligned.", op);

@@ -379,39 +379,85 @@ __device__ __forceinline__ void issue_router_rows(const FsArgs& a, const FsSmem&
   cp_async_commit_fs();
 }
 
-// Layer j's accumulator block (fs_acc_block_u64): expert e's logit line at
-// e * kFsLgStride, the sum-of-squares line after the E of them.
-__device__ __forceinline__ unsigned long long* acc_block(const FsArgs& a, int j) {
-  return a.LG + (size_t)(j % 3) * fs_acc_block_u64(a.E);
+// ---- routed stack: the exchange area (zeroed at launch; values carry their
+// own completion, so no release / acquire pair sits in the routing chain) ----
+struct Xchg {
+  unsigned long long* rt;   // [kFsMaxLayers][8]: layer l's routing, slot j tagged l + 1
+  unsigned long long* xin;  // [2][H / 2]: the layer inputs, two values per word, tagged
+  unsigned long long* sq;   // [kFsMaxLayers][kFsMaxReducers]: sums of squares, tagged
+  unsigned long long* lg;   // [L][E][kFsLgStride]: counted logit sums
+};
+__device__ __forceinline__ Xchg xchg(const FsArgs& a) {
+  Xchg x;
+  x.rt = a.XG;
+  x.xin = x.rt + (size_t)kFsMaxLayers * 8;
+  x.sq = x.xin + (size_t)a.H;
+  x.lg = x.sq + (size_t)kFsMaxLayers * kFsMaxReducers;
+  return x;
 }
 
-// Fixed-point partials: one 128-byte line per sum, u64 slot 0 the sum in
-// units of 2^-32 (logits) or 2^-24 (squares), two's complement; slot 1 a count
-// of partials that were not finite or too large for the format (the sum is
-// then NaN).
-__device__ __forceinline__ void add_fixed_partial(unsigned long long* line, float p,
-                                                  float unit_inv, float limit) {
-  if (fabsf(p) < limit) {
-    const long long q = __float2ll_rn(p * unit_inv);
-    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(line),
-                 "l"((unsigned long long)q)
-                 : "memory");
-  } else {
-    asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;" ::"l"(line + 1) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// A tagged word: bits 63..48 the tag (a layer of the launch + 1, never 0 after
+// the launch's zeroing), bits 31..0 the payload.  One 8-byte store, so a
+// reader sees the payload whole once it sees the tag.
+__device__ __forceinline__ unsigned long long tagged(uint32_t tag, uint32_t payload) {
+  return ((unsigned long long)tag << 48) | payload;
+}
+__device__ __forceinline__ uint32_t tag_of(unsigned long long w) { return (uint32_t)(w >> 48); }
+
+// Counted logit partials: each reducer adds (q << 16) + (bad << 8) + 1 with q
+// its partial in 2^-28 units; bits 7..0 count the adds (complete at nR), bits
+// 15..8 the partials that were not finite or beyond 2^13 in magnitude (the
+// logit is then NaN), bits 63..16 the sum of q (|sum| < 2^47 for nR <= 64).
+// Integer sums do not depend on the order of the adds.
+constexpr float kLogitUnitInv = 268435456.0f, kLogitUnit = 3.7252902984619141e-09f;  // 2^28
+__device__ __forceinline__ void add_counted_logit(unsigned long long* line, float p) {
+  const bool ok = fabsf(p) < 8192.0f;
+  const long long q = ok ? __float2ll_rn(p * kLogitUnitInv) : 0ll;
+  const unsigned long long v = ((unsigned long long)q << 16) + (ok ? 1ull : 0x101ull);
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(line), "l"(v) : "memory");
+}
+__device__ __forceinline__ float decode_counted_logit(unsigned long long v) {
+  if ((v >> 8) & 0xFF) return __int_as_float(0x7fc00000);
+  return __ll2float_rn((long long)v >> 16) * kLogitUnit;
+}
+
+// Bounded poll by a whole warp: every lane's `n` words (in its registers
+// after the call) until done(word) holds for all of them across the warp.
+template <int N, typename Done>
+__device__ __forceinline__ bool poll_words(const unsigned long long* const (&p)[N],
+                                           unsigned long long (&w)[N], Done done) {
+  const long long t0 = clock64();
+  for (;;) {
+    bool mine = true;
+#pragma unroll
+    for (int i = 0; i < N; i++) {
+      if (p[i]) {
+        w[i] = ld_relaxed_u64(p[i]);
+        mine &= done(w[i]);
+      }
+    }
+    if (__all_sync(0xffffffffu, mine)) return true;
+    if (__any_sync(0xffffffffu, clock64() - t0 > 2000000000LL)) return false;  // warp-uniform
+    __nanosleep(20);
   }
 }
-__device__ __forceinline__ float read_fixed_sum(const unsigned long long* line, float unit) {
-  const ulonglong2 q = __ldcg(reinterpret_cast<const ulonglong2*>(line));
-  return q.y ? __int_as_float(0x7fc00000) : __ll2float_rn((long long)q.x) * unit;
-}
-constexpr float kLogitUnitInv = 4294967296.0f, kLogitUnit = 2.3283064365386963e-10f;  // 2^32
-constexpr float kSqUnitInv = 16777216.0f, kSqUnit = 5.9604644775390625e-08f;          // 2^24
 
 // The reducer's share of layer j's logits: for experts ct and ct + 128,
-// sum over its 32 rows r (in order) of xs[r] * G_j[e, r0 + r], into LG[j % 3].
-__device__ __forceinline__ void router_partials(const FsArgs& a, const FsSmem& S, int j, int ct) {
+// sum over its 32 rows r (in order) of xs[r] * G_j[e, r0 + r], added to the
+// experts' counted sums.
+__device__ __forceinline__ void router_partials(const FsArgs& a, const FsSmem& S, const Xchg& X,
+                                                int j, int ct) {
   const uint8_t* sl = S.rsl + (size_t)(j & 1) * (256 * kFsRedRows * 2);
-  unsigned long long* lg = acc_block(a, j);
+  unsigned long long* lg = X.lg + (size_t)j * a.E * kFsLgStride;
 #pragma unroll
   for (int h = 0; h < 2; h++) {
     const int e = ct + 128 * h;
@@ -429,36 +475,66 @@ __device__ __forceinline__ void router_partials(const FsArgs& a, const FsSmem& S
         p += S.xs[8 * q + 2 * i + 1] * f.y;
       }
     }
-    add_fixed_partial(lg + (size_t)e * kFsLgStride, p, kLogitUnitInv, 1.0e9f);
+    add_counted_logit(lg + (size_t)e * kFsLgStride, p);
   }
 }
 
-// Layer l's routing from LG[l % 3], on one warp: logit = sum * 2^-32 rounded
-// to the activation dtype (NaN when a partial was not representable), then
-// the router's selection.  Lanes < k write slot lane into inds / wts (shared
-// memory) and, from CTA 0, into the layer's routing outputs.
-__device__ __forceinline__ void route_layer(const FsArgs& a, const FsSmem& S, int l, int lane,
-                                            bool write_out) {
-  const unsigned long long* lg = acc_block(a, l);
-  float logit[8];
+// Layer l's router biases of the lane's experts (lane + 32 j), loaded before
+// the layer's logits are complete.
+__device__ __forceinline__ void load_router_bias(const FsArgs& a, int l, int lane,
+                                                 float (&bias)[8]) {
+  const float* b = a.layer[l].router_b;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int e = lane + 32 * j;
-    logit[j] = e < a.E ? round_to_dtype(read_fixed_sum(lg + (size_t)e * kFsLgStride, kLogitUnit),
-                                        a.dtype)
-                       : 0.f;
+    bias[j] = (b && e < a.E) ? __ldg(b + e) : 0.f;
   }
-  uint32_t isel;
-  float wsel;
-  topk_select<8>(logit, a.layer[l].router_b, a.E, a.k, a.norm != 0, lane, isel, wsel);
+}
+
+// The router CTA, one warp: waits until all nR reducers have added to each of
+// the E logit sums of layer l, rounds each logit to the activation dtype as
+// the reference's bf16 matmul returns it, selects (topk_merge), and publishes
+// slot j (lane j < k) as tagged (expert id << 32 | weight bits) words of
+// layer l's routing line, and into the layer's routing outputs.
+__device__ __forceinline__ bool route_and_publish(const FsArgs& a, const Xchg& X, int l,
+                                                  int lane, int nR, const float (&bias)[8],
+                                                  uint32_t& isel, float& wsel) {
+  const unsigned long long* lg = X.lg + (size_t)l * a.E * kFsLgStride;
+  const unsigned long long* p[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int e = lane + 32 * j;
+    p[j] = e < a.E ? lg + (size_t)e * kFsLgStride : nullptr;
+  }
+  unsigned long long w[8];
+  const bool ok = poll_words<8>(p, w, [&](unsigned long long v) { return (int)(v & 0xFF) == nR; });
+  float score[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++)
+    score[j] = sigmoid_ref(p[j] ? round_to_dtype(decode_counted_logit(w[j]), a.dtype) : 0.f);
+  topk_merge<8, 8>(score, bias, a.E, a.k, a.norm != 0, lane, isel, wsel);
   if (lane < a.k) {
-    S.inds[l * 16 + lane] = isel;
-    S.wts[l * 16 + lane] = wsel;
-    if (write_out) {
-      if (a.layer[l].inds) a.layer[l].inds[lane] = isel;
-      if (a.layer[l].wts) a.layer[l].wts[lane] = wsel;
-    }
+    const uint32_t id16 = isel < 0xFFFFu ? isel : 0xFFFFu;
+    st_relaxed_u64(X.rt + (size_t)l * 8 + lane,
+                   tagged((uint32_t)(l + 1), 0u) | ((unsigned long long)id16 << 32) |
+                       __float_as_uint(wsel));
+    if (a.layer[l].inds) a.layer[l].inds[lane] = isel;
+    if (a.layer[l].wts) a.layer[l].wts[lane] = wsel;
   }
+  return ok;
+}
+
+// Any other CTA, one warp: layer l's routing from its routing line.
+__device__ __forceinline__ bool read_routing(const FsArgs& a, const Xchg& X, int l, int lane,
+                                             uint32_t& isel, float& wsel) {
+  const unsigned long long* p[1] = {lane < a.k ? X.rt + (size_t)l * 8 + lane : nullptr};
+  unsigned long long w[1] = {0};
+  const uint32_t tag = (uint32_t)(l + 1);
+  const bool ok = poll_words<1>(p, w, [&](unsigned long long v) { return tag_of(v) == tag; });
+  const uint32_t id16 = (uint32_t)(w[0] >> 32) & 0xFFFFu;
+  isel = id16 == 0xFFFFu ? 0x7fffffffu : id16;
+  wsel = __uint_as_float((uint32_t)w[0]);
+  return ok;
 }
 
 template <int VX, int VA, bool ROUTED>
@@ -763,14 +839,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Dependency counters (zero at launch): cnt1[seg] counts the gate/up items
     // of segment seg done (nb * nks per layer); cnt2[p] the down items whose
     // rows lie in K part p done (kk * H / 128 / nks per layer) -- in the
-    // routed stack cnt2[rb] the down items of 128-row block rb (kk per layer)
-    // and rcnt the reducers done (nR per layer, the launch's prologue first).
+    // routed stack cnt2[rb] the down items of 128-row block rb (kk per layer).
     // Producers: the chain's writes, a barrier, then one release add.
     // Consumers: thread 0 polls (acquire, bounded), then a barrier.
     unsigned* cnt1 = a.bar;
     unsigned* cnt2 = a.bar + 16;
-    unsigned* rcnt = a.bar + 32;
-    unsigned* rcnt1 = a.bar + 33;
     const unsigned per_seg = (unsigned)(nb * a.nks);
     const int rb_per_part = H / 128 / a.nks;
     const unsigned per_part = (unsigned)(a.kk * rb_per_part);
@@ -798,56 +871,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ct == 0) red_release_add_fs(ctr, 1u);  // orders the CTA's writes (bar.sync) first
     };
     // Routed stack, reducer c (c < nR): rows [red_r0, red_r0 + 32), one per
-    // thread ct < 32 (the chain's first warp).
+    // thread ct < 32 (the chain's first warp); the router: the last CTA.
     const int nR = H / kFsRedRows;
     const bool is_red = ROUTED && c < nR;
+    const bool is_router = ROUTED && c == G - 1;
     const int red_r0 = c * kFsRedRows;
+    const Xchg XC = ROUTED ? xchg(a) : Xchg{};
     float hrow = 0.f;  // reducer thread ct < 32: h_j at its row (the residual)
-    // Layer j's input x_j from h_j (hrow), its logit partials, and the release.
-    // With the norm: the rows' squares into layer j's sum-of-squares line, a
-    // wait for every reducer's, then x = dtype(dtype(h * r) * w) with
-    // r = 1 / sqrt(sum / H + eps).  Then x_j into X and S.xs, the partials of
-    // x_j[rows] . G_j[e, rows] (router rows of layer j landed: issued two
-    // layers ago), the accumulator block of layer j + 1 zeroed (this reducer's
-    // experts c, c + nR, ..., and reducer 0 the squares line: their previous
-    // contents, layer j - 2's, were read before any item of layer j - 2 and
-    // in the norm step of layer j - 2, all of which precede the releases of
-    // layer j - 1 that this reducer has waited for), the router rows of layer
-    // j + 2 into the freed buffer, and the release.
+    // Layer j's input x_j from h_j (hrow) and its logit partials.  With the
+    // norm: the rows' sum of squares as this reducer's tagged word of layer j,
+    // every reducer's word (polled), their sum in reducer order -- the same
+    // bits on every reducer -- and x = dtype(dtype(h * r) * w) with
+    // r = 1 / sqrt(sum / H + eps).  Then x_j as tagged words (two values each)
+    // and into S.xs, the counted partials of x_j[rows] . G_j[e, rows] (router
+    // rows of layer j landed: issued two layers ago), and the router rows of
+    // layer j + 2 into the freed buffer.
     auto route_rows = [&](int j) -> bool {
       const int row = red_r0 + ct;
+      const uint32_t tag = (uint32_t)(j + 1);
       float xv = hrow;
-      if (a.has_norm) {
-        unsigned long long* sq = acc_block(a, j) + (size_t)a.E * kFsLgStride;
-        if (ct < 32) {
-          const float s2 = warp_sum(hrow * hrow);
-          if (ct == 0) add_fixed_partial(sq, s2, kSqUnitInv, 1.0e10f);
-        }
-        signal_count(rcnt1);
-        if (!wait_count(rcnt1, (unsigned)(j + 1) * nR, j, 56)) return false;
-        if (ct < 32) {
-          const float r = 1.0f / sqrtf(read_fixed_sum(sq, kSqUnit) / (float)H + a.eps);
-          const float w = load_as_f32(a.layer[j].norm_w, a.dtype, row);
-          xv = round_to(round_to(hrow * r, a.dtype) * w, a.dtype);
-        }
+      bool ok = true;
+      if (a.has_norm && ct < 32) {
+        const float w = load_as_f32(a.layer[j].norm_w, a.dtype, row);
+        const float s2 = warp_sum(hrow * hrow);
+        unsigned long long* sq = XC.sq + (size_t)j * kFsMaxReducers;
+        if (ct == 0) st_relaxed_u64(sq + c, tagged(tag, __float_as_uint(s2)));
+        const unsigned long long* p[2] = {lane < nR ? sq + lane : nullptr,
+                                          lane + 32 < nR ? sq + lane + 32 : nullptr};
+        unsigned long long wv[2] = {0ull, 0ull};
+        ok = poll_words<2>(p, wv, [&](unsigned long long v) { return tag_of(v) == tag; });
+        if (!ok && ct == 0) fsflag(fs_timeout(j, 56));
+        const float tot = warp_sum((p[0] ? __uint_as_float((uint32_t)wv[0]) : 0.f) +
+                                   (p[1] ? __uint_as_float((uint32_t)wv[1]) : 0.f));
+        const float r = 1.0f / sqrtf(tot / (float)H + a.eps);
+        xv = round_to(round_to(hrow * r, a.dtype) * w, a.dtype);
       }
       if (ct < 32) {
-        __stcg(a.X + (size_t)((a.l0 + j) & 1) * H + row, xv);
+        const uint32_t bits = a.dtype == kBF16 ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(xv))
+                                               : (uint32_t)__half_as_ushort(__float2half_rn(xv));
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, bits, 1);
+        if ((ct & 1) == 0)
+          st_relaxed_u64(XC.xin + (size_t)((a.l0 + j) & 1) * (H / 2) + (row >> 1),
+                         tagged(tag, (hi << 16) | bits));
         S.xs[ct] = xv;
       }
+      ok = chain_sync_and(ok);
       cp_async_wait_prev_fs();
       named_sync(kBarChain, kChain);
-      router_partials(a, S, j, ct);
-      unsigned long long* z = acc_block(a, j + 1);
-      for (int i = ct; i < 2 * ((a.E + nR - 1) / nR); i += kChain) {
-        const int e = c + nR * (i >> 1);
-        if (e < a.E) z[(size_t)e * kFsLgStride + (i & 1)] = 0ull;
-      }
-      if (c == 0 && ct < 2) z[(size_t)a.E * kFsLgStride + ct] = 0ull;
-      named_sync(kBarChain, kChain);
+      router_partials(a, S, XC, j, ct);
+      named_sync(kBarChain, kChain);  // every read of rsl[j & 1] done
       issue_router_rows(a, S, j + 2, red_r0, ct);
-      signal_count(rcnt);
-      return true;
+      return ok;
     };
     bool alive = true;
     if (is_red) {
@@ -857,7 +931,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ct < kFsRedRows) {
         const int row = red_r0 + ct;
         hrow = a.first ? load_as_f32(a.x0, a.dtype, row)
-                       : __ldcg(a.X + (size_t)(2 + (a.l0 & 1)) * H + row);
+                       : __ldcg(a.Hres + (size_t)(a.l0 & 1) * H + row);
       }
       alive = route_rows(0);
     }
@@ -868,19 +942,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* GUb = a.GUp + (size_t)(lg & 1) * 2 * a.kk * 2 * I;
       if (ct == 0) *S.cur = l;
 
-      // ---- routed stack: this layer's routing, once its reducers are done ----
-      if (ROUTED && (has_gu || has_d)) {
-        if (!wait_count(rcnt, (unsigned)(l + 1) * nR, l, 53)) {
+      // ---- routed stack: this layer's routing (the router CTA computes and
+      // publishes it; the others read its routing line) ----
+      if (ROUTED && (has_gu || has_d || is_router)) {
+        if (ct < 32) {
+          uint32_t isel;
+          float wsel;
+          bool got;
+          if (is_router) {
+            float bias[8];
+            load_router_bias(a, l, lane, bias);
+            got = route_and_publish(a, XC, l, lane, nR, bias, isel, wsel);
+          } else {
+            got = read_routing(a, XC, l, lane, isel, wsel);
+          }
+          if (!got && lane == 0) fsflag(fs_timeout(l, 53));
+          if (lane < a.k) {
+            S.inds[l * 16 + lane] = isel;
+            S.wts[l * 16 + lane] = wsel;
+          }
+          __threadfence_block();
+          __syncwarp();
+          // the TMA warp may issue the routed slabs (on a failed poll too: ids out
+          // of range are replaced and flagged there, and the chain stops below)
+          if (lane == 0) *S.rlayer = l + 1;
+          if (lane == 0) *S.bar_ok = got;
+        }
+        named_sync(kBarChain, kChain);
+        if (!*S.bar_ok) {
           alive = false;
           break;
         }
-        if (ct < 32) {
-          route_layer(a, S, l, lane, c == 0);
-          __threadfence_block();
-          __syncwarp();
-          if (lane == 0) *S.rlayer = l + 1;  // the TMA warp may issue the routed slabs
-        }
-        named_sync(kBarChain, kChain);
       }
 
       // ---- phase A: x terms, gate/up item -> GUp ----
@@ -901,15 +993,40 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 4; i++) v[i] = f[(k0 & 4) + i];
           }
         } else if (ROUTED) {
-          // the reducers' x_l (rounded), complete once the routing is
-          const float* Xl = a.X + (size_t)(lg & 1) * H + k0;
+          // the reducers' x_l: tagged words of two values, polled until every
+          // word of this thread carries layer l's tag
+          const unsigned long long* xw = XC.xin + (size_t)(lg & 1) * (H / 2) + (k0 >> 1);
+          const uint32_t tag = (uint32_t)(l + 1);
+          unsigned long long w[VX / 2];
+          const long long t0 = clock64();
+          bool ok = true;
+          for (;;) {
+            bool done = true;
 #pragma unroll
-          for (int j = 0; j < VX; j += 4) {
-            const float4 f = __ldcg(reinterpret_cast<const float4*>(Xl + j));
-            v[j] = f.x;
-            v[j + 1] = f.y;
-            v[j + 2] = f.z;
-            v[j + 3] = f.w;
+            for (int i = 0; i < VX / 2; i += 2) {
+              const ulonglong2 q = __ldcg(reinterpret_cast<const ulonglong2*>(xw + i));
+              w[i] = q.x;
+              w[i + 1] = q.y;
+              done &= tag_of(q.x) == tag && tag_of(q.y) == tag;
+            }
+            if (done) break;
+            if (clock64() - t0 > 2000000000LL) {
+              ok = false;
+              break;
+            }
+            __nanosleep(20);
+          }
+          if (!ok) fsflag(fs_timeout(l, 57));
+#pragma unroll
+          for (int i = 0; i < VX / 2; i++) {
+            const uint32_t lo = (uint32_t)w[i] & 0xFFFFu, hi = ((uint32_t)w[i] >> 16) & 0xFFFFu;
+            if (a.dtype == kBF16) {
+              v[2 * i] = __bfloat162float(__ushort_as_bfloat16((unsigned short)lo));
+              v[2 * i + 1] = __bfloat162float(__ushort_as_bfloat16((unsigned short)hi));
+            } else {
+              v[2 * i] = __half2float(__ushort_as_half((unsigned short)lo));
+              v[2 * i + 1] = __half2float(__ushort_as_half((unsigned short)hi));
+            }
           }
         } else {
           // the previous layer's down items of this part (previous launch: done)
@@ -1016,7 +1133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           hrow = round_to(v, a.dtype);
           if (l == a.L - 1) {
             if (a.last) store_from_f32(a.y, a.dtype, row, hrow);
-            else __stcg(a.X + (size_t)(2 + ((lg + 1) & 1)) * H + row, hrow);  // next launch's h_0
+            else __stcg(a.Hres + (size_t)((lg + 1) & 1) * H + row, hrow);  // next launch's h_0
           }
         }
         if (l + 1 < a.L && !route_rows(l + 1)) {
@@ -1096,7 +1213,9 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
                                 : pick_kernel<false>(a.H, a.I, a.nks);
   if (!kern || a.L < 1 || a.L > kFsMaxLayers || a.L * a.mpl > kFsMaxMaps)
     return cudaErrorInvalidValue;
-  if (a.routed && (a.E < 1 || a.E > 256)) return cudaErrorInvalidValue;
+  if (a.routed && (a.E < 1 || a.E > 256 || a.k > 8 || a.dtype == kF32 ||
+                   a.H / kFsRedRows > kFsMaxReducers))
+    return cudaErrorInvalidValue;
   const size_t smem = decode_stack_fp4_smem_bytes(a.H, a.I, a.L, a.routed != 0);
   cudaError_t e = ensure_smem_ptr(kern, smem);
   if (e != cudaSuccess) return e;
@@ -1114,10 +1233,10 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
   if (e != cudaSuccess) return e;
   if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
-  // dependency counters, and (routed) the first layer's logit accumulators
+  // dependency counters, and (routed) the exchange area behind them
   const size_t zero = kFsCounters * sizeof(unsigned) +
-                      (a.routed ? fs_acc_block_u64(a.E) * sizeof(unsigned long long) : 0);
-  if (a.routed && reinterpret_cast<const char*>(a.LG) !=
+                      (a.routed ? fs_xchg_u64(a.H, a.E, a.L) * sizeof(unsigned long long) : 0);
+  if (a.routed && reinterpret_cast<const char*>(a.XG) !=
                       reinterpret_cast<const char*>(a.bar) + kFsCounters * sizeof(unsigned))
     return cudaErrorInvalidValue;
   e = cudaMemsetAsync(a.bar, 0, zero, stream);

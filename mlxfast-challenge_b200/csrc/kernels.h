@@ -162,12 +162,18 @@ struct FsLayer {
 // sums the segment partials of rows [j * kFsRedRows, (j + 1) * kFsRedRows) and
 // adds their share of every expert's router logit.
 constexpr int kFsRedRows = 32;
-constexpr int kFsLgStride = 16;  // u64 per accumulator (one 128-byte line)
-constexpr int kFsCounters = 64;  // cnt1[16] gate/up per segment, cnt2[16], rcnt, rcnt1
-// Routed stack accumulators, one block per layer index mod 3: E expert logit
-// lines, then one line for the sum of squares of the layer's input (the norm).
-__host__ __device__ constexpr size_t fs_acc_block_u64(int E) {
-  return (size_t)(E + 1) * kFsLgStride;
+constexpr int kFsLgStride = 16;  // u64 per logit accumulator (one 128-byte line)
+constexpr int kFsCounters = 64;  // cnt1[16] gate/up items per segment, cnt2[16] down items
+constexpr int kFsMaxReducers = 64;
+// Routed stack exchange area, zeroed at every launch (its values carry their
+// own completion: counts or layer tags), laid out after the counters:
+//   routing lines  [kFsMaxLayers][8] u64
+//   layer inputs   [2][H / 2] u64 (by stack-layer parity)
+//   squares        [kFsMaxLayers][kFsMaxReducers] u64
+//   logits         [L][E][kFsLgStride] u64
+__host__ __device__ constexpr size_t fs_xchg_u64(int H, int E, int L) {
+  return (size_t)kFsMaxLayers * 8 + (size_t)H + (size_t)kFsMaxLayers * kFsMaxReducers +
+         (size_t)L * E * kFsLgStride;
 }
 struct alignas(64) FsArgs {
   CUtensorMap maps[kFsMaxMaps];  // layer l: maps[l * mpl + j]; j >= 6: the shared expert's
@@ -187,9 +193,9 @@ struct alignas(64) FsArgs {
   void* y;         // [H] stack output (dtype)
   float* Yp;       // [2][kk][H] a layer's output per segment (f32), by layer parity
   float* GUp;      // [2][2][kk][2][I] gate / up pre-activations per K part, by parity
-  float* X;        // routed stack: [2][H] x_l (rounded to dtype), then [2][H] h_l, by parity
-  unsigned long long* LG;  // routed stack: [3][fs_acc_block_u64(E)] fixed-point sums
-  unsigned* bar;   // [kFsCounters] dependency counters, zero at launch (LG block 0 too)
+  float* Hres;     // routed stack: [2][H] h at a launch boundary (the next launch's h_0)
+  unsigned long long* XG;  // routed stack: the exchange area (fs_xchg_u64), after bar
+  unsigned* bar;   // [kFsCounters] dependency counters; zeroed at launch with XG
 };
 bool decode_stack_fp4_supported(int H, int I, int kk, int sms, bool routed = false);
 int decode_stack_fp4_nks(int I, int kk, int sms);

@@ -32,7 +32,8 @@ constexpr int kRouterPad = 32;  // bf16 elements of padding per staged column
 
 // Route one token (called by a whole warp): logit(e) = sum over `slices`
 // of lg[s * stride + e], rounded to the activation dtype as the reference's
-// matmul returns it, then the selection of topk.cuh.  Lane owns experts
+// matmul returns it, then the selection of topk.cuh (sort and merge for
+// k <= 16, rounds of warp maxima beyond).  Lane owns experts
 // lane + 32 j, j < kPer (E <= 32 kPer), fully unrolled so the per-lane arrays
 // stay in registers.
 template <int kPer>
@@ -50,7 +51,19 @@ __device__ void route_token_t(const RouterArgs& a, int64_t tok, const float* lg,
   }
   uint32_t isel;
   float wsel;
-  topk_select<kPer>(lgt, a.bias, (int)a.E, a.k, a.norm != 0, lane, isel, wsel);
+  if (a.k <= 16) {
+    float sc[kPer], bs[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; j++) {
+      const int64_t e = lane + 32 * j;
+      sc[j] = sigmoid_ref(lgt[j]);
+      bs[j] = (a.bias && e < a.E) ? a.bias[e] : 0.f;
+    }
+    if (a.k <= 8) topk_merge<kPer, 8>(sc, bs, (int)a.E, a.k, a.norm != 0, lane, isel, wsel);
+    else topk_merge<kPer, 16>(sc, bs, (int)a.E, a.k, a.norm != 0, lane, isel, wsel);
+  } else {
+    topk_select<kPer>(lgt, a.bias, (int)a.E, a.k, a.norm != 0, lane, isel, wsel);
+  }
   if (lane < a.k) {
     a.inds[tok * a.k + lane] = isel;
     a.wts[tok * a.k + lane] = wsel;

@@ -78,6 +78,99 @@ __device__ __forceinline__ void topk_select(const float (&logit)[kPer], const fl
   if (norm) wsel = wsel / wsum;
 }
 
+// The same selection by sorting and merging, for k <= K (K = 8 or 16), in a
+// fixed number of steps instead of k dependent rounds of warp reductions: each
+// lane sorts its kPer keys (a bitonic network in registers) and keeps its top
+// K; five butterfly levels (lane xor 1, 2, 4, 8, 16) each merge the lane's
+// list with its partner's (max of the list and the reversed partner list is
+// bitonic and holds the top K of both; a half-cleaner cascade sorts it), so
+// every lane ends with the warp's top K in descending key order -- the order,
+// ties and NaN handling of topk_select.  score / bias: the lane's sigmoid
+// scores and biases (bias 0 where there is none).  The weight sum runs over
+// slots 0..k-1 in order, as topk_select's.
+template <int N>
+__device__ __forceinline__ void sort_keys_desc(uint64_t (&v)[N]) {
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1)
+#pragma unroll
+    for (int stride = size / 2; stride > 0; stride >>= 1)
+#pragma unroll
+      for (int i = 0; i < N; i++) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const uint64_t a = v[i], b = v[j];
+          const bool sw = desc ? (b > a) : (b < a);
+          v[i] = sw ? b : a;
+          v[j] = sw ? a : b;
+        }
+      }
+}
+
+template <int kPer, int K>
+__device__ __forceinline__ void topk_merge(const float (&score)[kPer], const float (&bias)[kPer],
+                                           int E, int k, bool norm, int lane, uint32_t& isel,
+                                           float& wsel) {
+  constexpr int NS = kPer > K ? kPer : K;
+  uint64_t v[NS];
+#pragma unroll
+  for (int j = 0; j < NS; j++) {
+    const int e = lane + 32 * j;
+    v[j] = (j < kPer && e < E) ? choice_key(score[j < kPer ? j : 0] + bias[j < kPer ? j : 0],
+                                            (uint32_t)e)
+                               : 0ull;
+  }
+  sort_keys_desc<NS>(v);
+  uint64_t t[K];
+#pragma unroll
+  for (int i = 0; i < K; i++) t[i] = v[i];
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    uint64_t p[K];
+#pragma unroll
+    for (int i = 0; i < K; i++) {
+      const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)t[i], o);
+      const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(t[i] >> 32), o);
+      p[i] = ((uint64_t)hi << 32) | lo;
+    }
+#pragma unroll
+    for (int i = 0; i < K; i++) t[i] = t[i] > p[K - 1 - i] ? t[i] : p[K - 1 - i];
+#pragma unroll
+    for (int stride = K / 2; stride > 0; stride >>= 1)
+#pragma unroll
+      for (int i = 0; i < K; i++) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint64_t a = t[i], b = t[j];
+          t[i] = b > a ? b : a;
+          t[j] = b > a ? a : b;
+        }
+      }
+  }
+  // slot r = t[r]; its score from the expert's lane (id % 32, entry id / 32)
+  float wsum = 0.f;
+  wsel = 0.f;
+  isel = 0;
+#pragma unroll
+  for (int r = 0; r < K; r++) {
+    if (r >= k) break;
+    const uint64_t key = t[r];
+    const uint32_t id = key ? 0xFFFFFFFFu - (uint32_t)key : 0x7fffffffu;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; j++) {
+      const float sj = __shfl_sync(0xffffffffu, score[j], (int)(id & 31));
+      if (key && (int)(id >> 5) == j) s = sj;
+    }
+    wsum += s;
+    if (lane == r) {
+      wsel = s;
+      isel = id;
+    }
+  }
+  if (norm) wsel = wsel / wsum;
+}
+
 __device__ __forceinline__ float round_to_dtype(float v, int dtype) {
   if (dtype == kBF16) return __bfloat162float(__float2bfloat16_rn(v));
   if (dtype == kF16) return __half2float(__float2half_rn(v));

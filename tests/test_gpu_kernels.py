@@ -221,6 +221,27 @@ def check_routing(orc, x, G, bias, inds, wts, k):
                                        atol=1e-6)
 
 
+@pytest.mark.parametrize("T,E,k", [(1, 256, 8), (4, 256, 8), (19, 256, 8), (3, 64, 4),
+                                   (2, 256, 12), (2, 512, 8), (2, 128, 20)])
+def test_router_exact_ties_and_nan(nv, orc, T, E, k):
+    """Exact ties and NaN choices: zero inputs make every logit 0, so the
+    choice is 0.5 + bias with many equal biases; the reference's argPartition
+    leaves ties unspecified, this library (and the oracle) take the lower
+    expert id, and a NaN choice is never taken.  The selection must be the
+    oracle's bit for bit (ids in slot order and weights), for the sort-and-
+    merge selection (k <= 16) and the rounds of warp maxima (k > 16)."""
+    H = 2048
+    G = rand_bf16((E, H), 0.02, seed=7)
+    x = torch.zeros(T, H, dtype=torch.bfloat16, device=DEV)
+    bias = (torch.arange(E, device=DEV) % 5).float() * 1e-3
+    bias[9] = float("nan")  # would tie with the winners; must be skipped
+    inds, wts = nv.moe_router_topk(x, G, bias, k)
+    oi, ow, _ = orc.port.router_topk(bf16_np_bits(x), bf16_np_bits(G), bias.cpu().numpy(), k)
+    assert np.array_equal(u32_np(inds).reshape(oi.shape), oi)
+    assert np.array_equal(wts.cpu().numpy().reshape(ow.shape), ow)
+    assert 9 not in set(oi.ravel().tolist())
+
+
 @pytest.mark.parametrize("T", [1, 3, 8, 19])
 def test_router_vs_oracle(nv, orc, T):
     E, H, k = 256, 2048, 8
