@@ -93,6 +93,15 @@ NVFP4MOE_API int nvfp4_version(void);
  * above.  NVFP4_LAUNCH_EXACT_DECODE selects the mma.sync stack instead (16-bit
  * activations, exact products). */
 #define NVFP4_LAUNCH_EXACT_DECODE 8
+/* Test only (no counterpart in the reference): the block-scaled FP4 decode
+ * stacks (moe_decode_stack_forward, moe_decode_stack_routed_forward) give
+ * every bounded wait ~1 ms instead of ~1 s and withhold one release (the
+ * last layer's segment-0 gate/up items never signal), so the waits behind it
+ * run out: the launch returns, nvfp4_device_status() reports
+ * NVFP4_ERR_DEVICE_TIMEOUT with the site 1000 * (layer + 1) + 50..52 / 54,
+ * and the outputs are not valid.  The context stays usable.  It exercises
+ * the error path of the bounded waits without faulting or hanging a GPU. */
+#define NVFP4_LAUNCH_TEST_EXPIRE 16
 NVFP4MOE_API int nvfp4_set_launch_flags(int flags);
 /* Synchronises the device, returns and clears the latched device status:
  * NVFP4_OK, NVFP4_ERR_DEVICE_INDEX, or NVFP4_ERR_DEVICE_TIMEOUT when a kernel's

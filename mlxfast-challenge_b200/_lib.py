@@ -24,6 +24,7 @@ NVFP4_LAUNCH_PDL = 1
 NVFP4_LAUNCH_BULK_COPY = 2
 NVFP4_LAUNCH_EXACT_PREFILL = 4
 NVFP4_LAUNCH_EXACT_DECODE = 8
+NVFP4_LAUNCH_TEST_EXPIRE = 16
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64

@@ -196,7 +196,7 @@ int nvfp4_version(void) { return 1; }
 int nvfp4_set_launch_flags(int flags) {
   const int old = t_launch_flags;
   t_launch_flags = flags & (NVFP4_LAUNCH_PDL | NVFP4_LAUNCH_BULK_COPY | NVFP4_LAUNCH_EXACT_PREFILL |
-                            NVFP4_LAUNCH_EXACT_DECODE);
+                            NVFP4_LAUNCH_EXACT_DECODE | NVFP4_LAUNCH_TEST_EXPIRE);
   return old;
 }
 
@@ -1307,6 +1307,10 @@ int run_fp4_stack(const char* op, void* y, const void* x, int dtype, int64_t n_l
   F.has_norm = norm_w ? 1 : 0;
   F.eps = eps;
   F.scaling = L0->routed_scaling;
+  // a bounded wait gives up after ~1 s (2e9 cycles); the test flag shortens
+  // it to ~1 ms and withholds one release, so the waits behind it expire
+  F.test_skip_release = (t_launch_flags & NVFP4_LAUNCH_TEST_EXPIRE) ? 1 : 0;
+  F.budget = F.test_skip_release ? 2000000LL : 2000000000LL;
   F.x0 = x;
   F.y = y;
   F.Yp = reinterpret_cast<float*>(ws + S.y32_off);

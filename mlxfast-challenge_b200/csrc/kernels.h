@@ -189,6 +189,8 @@ struct alignas(64) FsArgs {
   int has_norm;    // routed stack: x_l = RMSNorm(h_l; layer[l].norm_w, eps) (else x_l = h_l)
   float eps;       // the norm's epsilon
   float scaling;   // routed_scaling of every layer
+  int test_skip_release;  // test only: the last layer's segment-0 gate/up items skip a release
+  long long budget;       // cycles a bounded wait may take before it gives up
   const void* x0;  // [H] stack input h_0 (dtype)
   void* y;         // [H] stack output (dtype)
   float* Yp;       // [2][kk][H] a layer's output per segment (f32), by layer parity

@@ -74,3 +74,30 @@ REL_L2 = 5e-3
 def assert_close(got, want, max_abs=MAX_ABS, rel_l2=REL_L2, what=""):
     ma, rl = close_report(got, want)
     assert ma <= max_abs and rl <= rel_l2, f"{what}: max_abs={ma:.3e} rel_l2={rl:.3e}"
+
+
+def check_routing(orc, x_bits, G_bits, bias, inds, wts, k):
+    """GPU routing [T, k] against the oracle router (Laguna.swift:165-180) on the
+    same x (bf16 bits [T, H]).  The GPU sums the logits in another order than
+    the oracle, so a logit may round to the neighbouring bf16 value: an expert
+    may differ from the oracle's set only where its choice lies within one
+    such rounding step (sigmoid' <= 1/4 times the bf16 spacing of the logit,
+    2^-7 |logit|) of the k-th choice, and the weights of an equal set agree
+    to that step.  Returns (oracle inds, oracle weights)."""
+    b = np.asarray(bias, np.float32)
+    oi, ow, logits = orc.port.router_topk(x_bits, G_bits, b, k)
+    gi = np.asarray(inds).reshape(oi.shape)
+    gw = np.asarray(wts).reshape(ow.shape)
+    s = 1.0 / (1.0 + np.exp(-logits.astype(np.float64)))
+    choice = s + b
+    step = 0.25 * 2.0 ** -7 * np.maximum(np.abs(logits), 1e-3)
+    for t in range(oi.shape[0]):
+        kth = np.sort(choice[t])[::-1][k - 1]
+        diff = set(gi[t].tolist()) ^ set(oi[t].tolist())
+        for e in diff:
+            assert abs(choice[t, e] - kth) <= step[t, e] + 1e-6, (t, e, choice[t, e], kth)
+        if not diff:
+            order = {e: j for j, e in enumerate(oi[t])}
+            np.testing.assert_allclose(gw[t], ow[t][[order[e] for e in gi[t]]], rtol=1e-2,
+                                       atol=1e-6)
+    return oi, ow

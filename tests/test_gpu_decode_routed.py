@@ -24,7 +24,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import PKG, assert_close
+from conftest import PKG, assert_close, check_routing
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -76,20 +76,9 @@ def routed_stack(nv, blocks, x, residual=True, norms=None):
 
 def check_layer_routing(orc, x_bits, raw, inds, wts, k):
     """GPU routing vs the oracle router on the same x (one token, bf16 bits)."""
-    oi, ow, logits = orc.port.router_topk(x_bits, bf16_bits(raw["router_w"]),
-                                          raw["router_b"].cpu().numpy(), k)
     gi, gw = u32_np(inds), wts.cpu().numpy()
-    s = 1.0 / (1.0 + np.exp(-logits[0].astype(np.float64)))
-    choice = s + raw["router_b"].cpu().numpy()
-    # one bf16 rounding step of a logit moves its choice by at most
-    # sigmoid' * ulp <= 0.25 * 2^-7 * |logit|
-    step = 0.25 * 2.0 ** -7 * np.maximum(np.abs(logits[0]), 1e-3)
-    kth = np.sort(choice)[::-1][k - 1]
-    for e in set(gi.tolist()) ^ set(oi[0].tolist()):
-        assert abs(choice[e] - kth) <= step[e] + 1e-6, (e, choice[e], kth)
-    if set(gi.tolist()) == set(oi[0].tolist()):
-        order = {e: j for j, e in enumerate(oi[0])}
-        np.testing.assert_allclose(gw, ow[0][[order[e] for e in gi]], rtol=1e-2, atol=1e-6)
+    check_routing(orc, x_bits, bf16_bits(raw["router_w"]), raw["router_b"].cpu().numpy(),
+                  gi.reshape(1, k), gw.reshape(1, k), k)
     return gi, gw
 
 

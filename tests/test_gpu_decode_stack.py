@@ -116,9 +116,37 @@ def test_stack_matches_default_kernels_and_oracle(nv, orc, exact):
     assert_close(y0.float().cpu().numpy(), o, what="stack layer vs oracle")
 
 
-def test_stack_many_layers(nv, exact):
-    blocks, _, routing = layers(nv, 3, seed=500)
-    # 39 layers (the model's sparse count) cycling 3 distinct weight sets.
+def oracle_layer(orc, raw, inds, wts, x):
+    """The fp32 oracle block on x (float32 [1, H]) with the given routing (used
+    experts only)."""
+    inds = inds.cpu().numpy().astype(np.int64).reshape(1, -1)
+    used = np.unique(inds)
+    remap = {e: i for i, e in enumerate(used)}
+    ids = torch.from_numpy(used).to(DEV)
+    routed = {k: (u32_np(v.view(torch.int32)[ids]) if v.dtype == torch.uint32 else
+                  v[ids].cpu().numpy()) for k, v in raw["routed"].items()}
+    shared = None if raw["shared"] is None else {
+        k: (u32_np(v) if v.dtype == torch.uint32 else v.cpu().numpy())
+        for k, v in raw["shared"].items()}
+    ci = np.vectorize(remap.get)(inds).astype(np.uint32)
+    return orc.port.moe_block_f32(x, ci, wts.float().cpu().numpy().reshape(1, -1), routed,
+                                  shared, scaling=2.5)
+
+
+def test_stack_many_layers(nv, orc, exact):
+    """39 layers (the model's sparse count, 3 distinct weight sets cycled),
+    every layer checked against the fp32 oracle at the BASELINE bound: a stack
+    of n layers returns x_n, and each launch computes a layer the same way
+    whatever follows it, so the prefixes n = 1 .. 39 give every layer's input
+    (bit-identical to the full stack's: the 39-layer prefix equals the full
+    run).  Without a norm between the blocks the activations shrink layer by
+    layer (the block is quadratic in its input) until, a few layers in, the
+    SwiGLU activations fall below ~1e-30, where the stack stages a row as
+    zeros (its term factors are clamped there): layers whose oracle output is
+    below 1e-20 are checked for absolute agreement only.  The routed
+    stack's test runs the same depth with RMSNorm and a live residual
+    stream."""
+    blocks, raw, routing = layers(nv, 3, seed=500)
     stack_blocks = [blocks[l % 3] for l in range(39)]
     stack_routing = [routing[l % 3] for l in range(39)]
     chain = make_chain(nv, stack_blocks, stack_routing, exact)
@@ -127,12 +155,29 @@ def test_stack_many_layers(nv, exact):
     assert chain.launches_per_step() == (1 if exact else 2)
     x = seeded_x(39)
     chain.x0.copy_(x)
-    out = chain.replay()
+    full = chain.replay().clone()
     torch.cuda.synchronize()
-    with nv.launch_flags(bulk_copy=True):
-        want = layer_by_layer(stack_blocks, stack_routing, x)
-    assert_close(out.float().cpu().numpy(), want.float().cpu().numpy(), max_abs=float("inf"),
-                 rel_l2=chain_tol(39), what="39-layer stack")
+    xs = [x]
+    for n in range(1, 40):
+        c = make_chain(nv, stack_blocks[:n], stack_routing[:n], exact)
+        c.x0.copy_(x)
+        xs.append(c.replay().clone())
+        torch.cuda.synchronize()
+    assert torch.equal(xs[39], full)
+    live = 0
+    for l in range(39):
+        xl = xs[l].float().cpu().numpy()
+        if l < 2:
+            assert np.abs(xl).max() > 1e-3  # live activations in the first layers
+        want = oracle_layer(orc, raw[l % 3], *stack_routing[l], xl)
+        if np.abs(want).max() > 1e-20:
+            assert_close(xs[l + 1].float().cpu().numpy(), want, what=f"layer {l}")
+            live += 1
+        else:
+            assert_close(xs[l + 1].float().cpu().numpy(), want, rel_l2=float("inf"),
+                         what=f"layer {l} (decayed)")
+    assert live >= 3
+    nv.device_status()
 
 
 def test_stack_out_of_range_expert_is_reported(nv, exact):
@@ -239,5 +284,7 @@ def test_stacks_nonfinite_input(nv, exact):
     chain.x0.copy_(x)
     out = chain.replay()
     torch.cuda.synchronize()
-    nv.device_status()
-    assert not bool(torch.isfinite(out.float()).all())
+    nv.device_status()  # raises on an expired bounded wait (or an index error)
+    # inf in the token's x reaches every expert's gate/up sums, so every
+    # activation and every output element is non-finite
+    assert not bool(torch.isfinite(out.float()).any())

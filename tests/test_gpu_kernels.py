@@ -9,6 +9,7 @@ import pytest
 import torch
 
 from conftest import assert_close, close_report
+from conftest import check_routing as check_routing_bits
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -203,22 +204,8 @@ def test_empty_inputs(nv):
 # --- router -----------------------------------------------------------------------------
 
 def check_routing(orc, x, G, bias, inds, wts, k):
-    oi, ow, logits = orc.port.router_topk(bf16_np_bits(x), bf16_np_bits(G),
-                                          bias.cpu().numpy(), k)
-    gi = u32_np(inds).reshape(oi.shape)
-    gw = wts.cpu().numpy().reshape(ow.shape)
-    s = 1.0 / (1.0 + np.exp(-logits.astype(np.float64)))
-    choice = s + bias.cpu().numpy()
-    for t in range(oi.shape[0]):
-        if set(gi[t]) != set(oi[t]):
-            # Only a near-tie at the k-th place may differ.
-            kth = np.sort(choice[t])[::-1][k - 1]
-            for e in set(gi[t]) ^ set(oi[t]):
-                assert abs(choice[t, e] - kth) < 2e-6
-        else:
-            order = {e: j for j, e in enumerate(oi[t])}
-            np.testing.assert_allclose(gw[t], ow[t][[order[e] for e in gi[t]]], rtol=1e-5,
-                                       atol=1e-6)
+    return check_routing_bits(orc, bf16_np_bits(x), bf16_np_bits(G), bias.cpu().numpy(),
+                              u32_np(inds), wts.cpu().numpy(), k)
 
 
 @pytest.mark.parametrize("T,E,k", [(1, 256, 8), (4, 256, 8), (19, 256, 8), (3, 64, 4),
@@ -242,8 +229,11 @@ def test_router_exact_ties_and_nan(nv, orc, T, E, k):
     assert 9 not in set(oi.ravel().tolist())
 
 
-@pytest.mark.parametrize("T", [1, 3, 8, 19])
+@pytest.mark.parametrize("T", [1, 3, 8, 19, 512])
 def test_router_vs_oracle(nv, orc, T):
+    """Decode (T <= 8: mma.sync partial logits, last CTA routes) and prefill
+    (T > 8: shared-memory tiled logits GEMM, one warp per token) routers;
+    T = 512 is BASELINE config[3]'s prompt."""
     E, H, k = 256, 2048, 8
     G = rand_bf16((E, H), 0.02, seed=100 + T)
     x = rand_bf16((T, H), 1.0, seed=200 + T)

@@ -73,3 +73,24 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(nv, layer):
     x = torch.zeros(64, 2048, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="static scratch"):
         _noalloc(nv, block, x)
+
+
+def test_noalloc_at_its_documented_limit(nv):
+    """The documented limit at Laguna XS 2.1 sizes: T = 8 tokens with all 256
+    experts (the router's partial logits are then the largest user of the
+    scratch), the shared expert and a residual, twice in a row; T = 9 is
+    refused."""
+    lag = importlib.import_module(PKG + ".laguna")
+    block, raw = lag.random_sparse_layer(nv, seed=8765, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(88)
+    x = torch.randn(8, 2048, generator=g, device=DEV).to(torch.bfloat16)
+    res = torch.randn(8, 2048, generator=g, device=DEV).to(torch.bfloat16)
+    want, winds, _ = block(x, residual=res, return_routing=True)
+    for _ in range(2):
+        got, inds, _ = _noalloc(nv, block, x, residual=res)
+        torch.cuda.synchronize()
+        assert torch.equal(inds.view(torch.uint32), winds)
+        assert_close(got.float().cpu().numpy(), want.float().cpu().numpy(),
+                     what="noalloc T=8 E=256")
+    with pytest.raises(ValueError, match="static scratch"):
+        _noalloc(nv, block, torch.zeros(9, 2048, device=DEV, dtype=torch.bfloat16))
