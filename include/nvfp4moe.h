@@ -76,11 +76,13 @@ NVFP4MOE_API int nvfp4_version(void);
  * Later kernels inside one call always overlap their predecessor.  Returns
  * the previous flags. */
 #define NVFP4_LAUNCH_PDL 1
-/* NVFP4_LAUNCH_BULK_COPY selects, for T <= 8, the decode kernels fed by
- * cp.async.bulk copies into a shared-memory ring (one producer warp, eight
- * consumer warps) instead of per-thread streaming loads.  Same results. */
+/* NVFP4_LAUNCH_BULK_COPY selects, for the GEMV engine (moe_gate_up_swiglu /
+ * moe_down_combine at T <= 8, moe_block_forward at T = 1), the decode kernels
+ * fed by cp.async.bulk copies into a shared-memory ring (one producer warp,
+ * eight consumer warps) instead of per-thread streaming loads.  Same results. */
 #define NVFP4_LAUNCH_BULK_COPY 2
-/* The prefill (T > 8) GEMMs of moe_block_forward run by default on the
+/* The grouped GEMMs of moe_block_forward (T >= 2: expert sort, each distinct
+ * expert streamed once) run by default on the
  * block-scaled FP4 tensor cores (tcgen05 kind::mxf4nvf4): activations as a sum
  * of four NVFP4 terms (relative-L2 ~5e-5 from the W4A16 product, 20x below
  * bf16 output rounding), weights as stored.  NVFP4_LAUNCH_EXACT_PREFILL
@@ -225,7 +227,9 @@ NVFP4MOE_API int moe_workspace_init(void* workspace, size_t bytes, nvfp4_stream 
  * x, y, residual [T, H] in `dtype`.  When inds_in is NULL the router runs
  * first (router_w required); otherwise inds_in [T, k] / weights_in [T, k]
  * are used as given.  inds_out / weights_out (nullable) receive the routing
- * that was used. */
+ * that was used.  T = 1 runs the GEMV engine; T >= 2 (Laguna-shaped layers:
+ * hidden and inter multiples of 256) the expert sort and grouped tensor-core
+ * GEMMs, which stream each distinct expert once for all its tokens. */
 NVFP4MOE_API int moe_block_forward(void* y, const void* x, const void* residual, int dtype,
                                    int64_t T, const moe_layer_desc* layer,
                                    const uint32_t* inds_in, const float* weights_in,
@@ -383,7 +387,7 @@ NVFP4MOE_API int moe_ep_combine(void* y, const void* y_pairs, const int32_t* pos
  * rank's routed slice and, when L->shared_inter > 0, the shared expert, which
  * this rank applies to its own rows only.  x rows are x_ld elements apart.  A
  * reduce-scatter (sum) of y_partial over the ranks then gives each rank its
- * tokens' block output; moe_ep_finish adds the residual.  Prefill shapes only (T > 8, the block-scaled FP4 path).  The
+ * tokens' block output; moe_ep_finish adds the residual.  T >= 2 (the grouped block-scaled FP4 path).  The
  * reference runs every expert on one device; single-device analogue:
  * moe_block_forward (Laguna.swift:204-212). */
 NVFP4MOE_API size_t moe_ep_partial_workspace_size(const moe_layer_desc* layer, int64_t T);

@@ -92,12 +92,18 @@ struct BlockLayout {
   size_t xtc_off, xts_off, xtf_off, atc_off, ats_off, atf_off;
 };
 
-// The tensor-core prefill path: T > 8 tokens, K slabs of 256 on both GEMMs,
-// a shared expert (if any) as wide as a routed one (one K for the down GEMM),
-// and 16-byte aligned banks (TMA tensor-map bases).
-bool prefill_shape_ok(const moe_layer_desc* L, int64_t T) {
+// The tensor-core grouped path (expert sort, grouped GEMMs): at least
+// min_tokens tokens, K slabs of 256 on both GEMMs, a shared expert (if any) as
+// wide as a routed one (one K for the down GEMM), and 16-byte aligned banks
+// (TMA tensor-map bases).  moe_block_forward takes it from T = 2: each
+// distinct expert's weights then stream once for all the tokens that chose it
+// (the GEMV engine streams them once per token and slot); measured per
+// Laguna layer with norm and router, T = 2 / 4 / 8: 53 / 59 / 90 us against
+// 55 / 78 / 140 us.  T = 1 keeps the GEMV engine.
+constexpr int64_t kGroupedMinTokens = 2;
+bool prefill_shape_ok(const moe_layer_desc* L, int64_t T, int64_t min_tokens = kGroupedMinTokens) {
   const int64_t slab = nvfp4::gemm_slab_k();
-  bool ok = T > 8 && L->hidden % slab == 0 && L->inter % slab == 0 &&
+  bool ok = T >= min_tokens && L->hidden % slab == 0 && L->inter % slab == 0 &&
             (L->shared_inter == 0 || L->shared_inter == L->inter) && L->n_experts <= 1024 &&
             (int64_t)L->n_experts * std::max(L->hidden, L->inter) < (1ll << 31);
   const nvfp4_bank* banks[6] = {&L->gate, &L->up, &L->down,
@@ -107,7 +113,8 @@ bool prefill_shape_ok(const moe_layer_desc* L, int64_t T) {
   return ok;
 }
 
-BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
+BlockLayout block_layout(const moe_layer_desc* L, int64_t T,
+                         int64_t grouped_min_tokens = kGroupedMinTokens) {
   BlockLayout B;
   B.router = router_layout(T, L->hidden, L->n_experts);
   B.kk = (int)L->top_k + (L->shared_inter > 0 ? 1 : 0);
@@ -116,7 +123,7 @@ BlockLayout block_layout(const moe_layer_desc* L, int64_t T) {
   B.wts_off = align_up(B.inds_off + (size_t)T * L->top_k * sizeof(uint32_t), 256);
   B.act_off = align_up(B.wts_off + (size_t)T * L->top_k * sizeof(float), 256);
   B.total = align_up(B.act_off + (size_t)T * B.kk * B.act_ld * sizeof(float), 256);
-  B.prefill = prefill_shape_ok(L, T);
+  B.prefill = prefill_shape_ok(L, T, grouped_min_tokens);
   if (B.prefill) {
     const int64_t tile = std::min<int64_t>(nvfp4::gemm_tile_tokens(), nvfp4::kFp4TileTokens);
     B.P = T * L->top_k;
@@ -534,11 +541,31 @@ static int down_impl(void* y, const float* act, int64_t act_ld, const void* resi
                      int64_t T, const moe_layer_desc* L, const uint32_t* inds,
                      const float* weights, nvfp4_stream stream, bool pdl);
 
+// moe_block_forward with the grouped path from grouped_min_tokens tokens on
+// (the no-alloc entry keeps the GEMV engine up to T = 8, whose workspace fits
+// its static scratch).
+static int block_forward_impl(const char* op, void* y, const void* x, const void* residual,
+                              int dtype, int64_t T, const moe_layer_desc* L,
+                              const uint32_t* inds_in, const float* weights_in,
+                              uint32_t* inds_out, float* weights_out, void* workspace,
+                              size_t workspace_bytes, nvfp4_stream stream,
+                              int64_t grouped_min_tokens);
+
 int moe_block_forward(void* y, const void* x, const void* residual, int dtype, int64_t T,
                       const moe_layer_desc* L, const uint32_t* inds_in, const float* weights_in,
                       uint32_t* inds_out, float* weights_out, void* workspace,
                       size_t workspace_bytes, nvfp4_stream stream) {
-  const char* op = "moe_block";
+  return block_forward_impl("moe_block", y, x, residual, dtype, T, L, inds_in, weights_in,
+                            inds_out, weights_out, workspace, workspace_bytes, stream,
+                            kGroupedMinTokens);
+}
+
+static int block_forward_impl(const char* op, void* y, const void* x, const void* residual,
+                              int dtype, int64_t T, const moe_layer_desc* L,
+                              const uint32_t* inds_in, const float* weights_in,
+                              uint32_t* inds_out, float* weights_out, void* workspace,
+                              size_t workspace_bytes, nvfp4_stream stream,
+                              int64_t grouped_min_tokens) {
   if (int r = check_layer(op, L, dtype, T)) return r;
   const int64_t H = L->hidden, E = L->n_experts;
   const int k = (int)L->top_k;
@@ -548,7 +575,7 @@ int moe_block_forward(void* y, const void* x, const void* residual, int dtype, i
     return fail(NVFP4_ERR_INVALID, "[%s] either inds_in or router_w is required.", op);
   if (inds_in && !weights_in)
     return fail(NVFP4_ERR_INVALID, "[%s] weights_in is required with inds_in.", op);
-  const BlockLayout B = block_layout(L, T);
+  const BlockLayout B = block_layout(L, T, grouped_min_tokens);
   if (!workspace || workspace_bytes < B.total)
     return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, B.total);
   char* ws = static_cast<char*>(workspace);
@@ -1030,6 +1057,10 @@ static int down_impl(void* y, const float* act, int64_t act_ld, const void* resi
 // sizes (E = 256, H = 2048, top-8 + shared expert of 512).
 static constexpr size_t kNoAllocScratchBytes = 256 * 1024;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+// The no-alloc block runs the GEMV engine up to T = 8 (its workspace fits the
+// scratch at Laguna sizes) and the grouped path beyond, where the scratch
+// rejects Laguna-sized layers.
+constexpr int64_t kNoAllocGroupedMinTokens = 9;
 
 static int noalloc_scratch(void** out) {
   static void* addr[64] = {};
@@ -1058,7 +1089,7 @@ extern "C" int moe_block_forward_noalloc(void* y, const void* x, const void* res
   const char* op = "moe_block_noalloc";
   if (int r = check_layer(op, L, dtype, T)) return r;
   if (T == 0) return NVFP4_OK;
-  const BlockLayout B = block_layout(L, T);
+  const BlockLayout B = block_layout(L, T, kNoAllocGroupedMinTokens);
   if (B.total > kNoAllocScratchBytes)
     return fail(NVFP4_ERR_WORKSPACE,
                 "[%s] T=%lld needs %zu bytes of scratch but the static scratch holds %zu "
@@ -1072,8 +1103,9 @@ extern "C" int moe_block_forward_noalloc(void* y, const void* x, const void* res
   cudaError_t e = cudaMemsetAsync(static_cast<char*>(ws) + B.router.counters_off, 0, counters,
                                   (cudaStream_t)stream);
   if (e != cudaSuccess) return check_cuda(e, op);
-  return moe_block_forward(y, x, residual, dtype, T, L, inds_in, weights_in, inds_out,
-                           weights_out, ws, kNoAllocScratchBytes, stream);
+  return block_forward_impl(op, y, x, residual, dtype, T, L, inds_in, weights_in, inds_out,
+                            weights_out, ws, kNoAllocScratchBytes, stream,
+                            kNoAllocGroupedMinTokens);
 }
 
 }  // extern "C"

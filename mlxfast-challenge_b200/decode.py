@@ -15,8 +15,9 @@ expert weights while the current layer's dependent chain runs; with
 route=True (config[2]) moe_decode_stack_routed_forward, which runs each
 layer's router inside the launch and streams a routed expert's weights from
 the moment its layer's top-k is known.  stack=False keeps the per-layer
-kernels (moe_gate_up_swiglu + moe_down_combine, or moe_block_forward with the
-router when route=True), which also serve T > 1 and other shapes.
+kernels (moe_block_forward per layer: with the router when route=True, the
+GEMV engine at T = 1 and the grouped GEMMs from T = 2), which also serve
+T > 1 and other shapes.
 
 residual=True makes each layer h_{l+1} = h_l + block_l(x_l), the block output
 summed into the residual stream, and norms (one RMSNorm weight per layer, in
@@ -70,9 +71,6 @@ class MoEDecodeChain:
                 self.routing.append((i.to(torch.int32).view(torch.uint32).reshape(T, b.top_k)
                                      .contiguous(), w.to(torch.float32).reshape(T, b.top_k)
                                      .contiguous()))
-        kk = max(b.top_k + (1 if b.Is else 0) for b in self.blocks)
-        self.act_ld = max(max(b.I, b.Is) for b in self.blocks)
-        self.act = torch.empty(T * kk * self.act_ld, dtype=torch.float32, device=self.device)
         nbytes = max(b.workspace_bytes(T) for b in self.blocks)
         self.ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
         self.stream = torch.cuda.Stream(device=self.device)
@@ -154,12 +152,12 @@ class MoEDecodeChain:
                                           stream_ptr))
                 src = dst
                 continue
-            check(L.moe_gate_up_swiglu(self.act.data_ptr(), self.act_ld, inp.data_ptr(),
-                                       self._dt, self.T, ctypes.byref(b.desc), inds.data_ptr(),
-                                       stream_ptr))
-            check(L.moe_down_combine(dst.data_ptr(), self.act.data_ptr(), self.act_ld, res,
-                                     self._dt, self.T, ctypes.byref(b.desc), inds.data_ptr(),
-                                     wts.data_ptr(), stream_ptr))
+            # given routing: the block with it (the GEMV engine at T = 1, the
+            # grouped GEMMs from T = 2, as SparseMoeBlock runs it)
+            check(L.moe_block_forward(dst.data_ptr(), inp.data_ptr(), res, self._dt, self.T,
+                                      ctypes.byref(b.desc), inds.data_ptr(), wts.data_ptr(),
+                                      None, None, self.ws.data_ptr(), self.ws.numel(),
+                                      stream_ptr))
             src = dst
         self.out = src
 
@@ -168,7 +166,12 @@ class MoEDecodeChain:
         launch flags choose the FP4 or the mma.sync stack)."""
         if self.stack:
             return self._stack_launches
-        return len(self.blocks) * ((3 if self.route else 2) + (1 if self.norms else 0))
+        # per layer: the norm, the router (one kernel for T <= 8, logits + top-k
+        # beyond), then the GEMV pair (T = 1) or the sort, two term passes, two
+        # grouped GEMMs and the combine (T >= 2)
+        router = 0 if not self.route else (1 if self.T <= 8 else 2)
+        block = 2 if self.T == 1 else 6
+        return len(self.blocks) * ((1 if self.norms else 0) + router + block)
 
     def capture(self, pdl: bool = True):
         """Capture one step.  With pdl, every kernel may start while its
