@@ -234,8 +234,10 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // SiLU exactly as the reference composes it: g * sigmoid(g) with
 // sigmoid(x) = x < 0 ? 1/(1+e^|x|) : 1 - 1/(1+e^|x|)  (backend/cpu/unary_ops.h:77-84).
+// 1/(1+e^|x|) is the correctly rounded reciprocal (the same bits as the IEEE
+// division 1.0f / y, without its general-operand path).
 __device__ __forceinline__ float sigmoid_ref(float x) {
-  const float y = 1.0f / (1.0f + expf(fabsf(x)));
+  const float y = __frcp_rn(1.0f + expf(fabsf(x)));
   return x < 0.0f ? y : 1.0f - y;
 }
 __device__ __forceinline__ float silu_ref(float g) { return g * sigmoid_ref(g); }

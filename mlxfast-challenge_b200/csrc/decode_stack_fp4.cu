@@ -401,8 +401,13 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// Publishing a tagged word: an atomic exchange, performed at L2 at once (a
+// relaxed store could wait in the writing SM; measured: the reducers' sums of
+// squares were seen 1.8 us later with plain stores, the layer 1.9 us longer).
+__device__ __forceinline__ void publish_u64(unsigned long long* p, unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.relaxed.gpu.global.exch.b64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v)
+               : "memory");
 }
 
 // A tagged word: bits 63..48 the tag (a layer of the launch + 1, never 0 after
@@ -480,50 +485,77 @@ __device__ __forceinline__ void router_partials(const FsArgs& a, const FsSmem& S
   }
 }
 
-// Layer l's router biases of the lane's experts (lane + 32 j), loaded before
-// the layer's logits are complete.
-__device__ __forceinline__ void load_router_bias(const FsArgs& a, int l, int lane,
-                                                 float (&bias)[8]) {
-  const float* b = a.layer[l].router_b;
-#pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const int e = lane + 32 * j;
-    bias[j] = (b && e < a.E) ? __ldg(b + e) : 0.f;
-  }
-}
-
-// The router CTA, one warp: waits until all nR reducers have added to each of
-// the E logit sums of layer l, rounds each logit to the activation dtype as
-// the reference's bf16 matmul returns it, selects (topk_merge), and publishes
-// slot j (lane j < k) as tagged (expert id << 32 | weight bits) words of
-// layer l's routing line, and into the layer's routing outputs.
-__device__ __forceinline__ bool route_and_publish(const FsArgs& a, const Xchg& X, int l,
-                                                  int lane, int nR, const float (&bias)[8],
+// The router CTA (no reducer: its router-row buffer holds the scores and the
+// warps' lists), all four chain warps: warp w waits until all nR reducers have
+// added to the logit sums of experts 64 w + lane and 64 w + 32 + lane, rounds
+// each logit to the activation dtype as the reference's bf16 matmul returns
+// it, scores it, and merges its warp's top 8 (topk.cuh: merge_levels); warp 0
+// merges the four lists and publishes slot j (lane j < k) as tagged
+// (expert id << 32 | weight bits) words of layer l's routing line, and into
+// the layer's routing outputs.  Lanes of warp 0 end with their slot.
+__device__ __forceinline__ bool route_and_publish(const FsArgs& a, const FsSmem& S,
+                                                  const Xchg& X, int l, int ct, int nR,
                                                   uint32_t& isel, float& wsel) {
+  const int w = ct >> 5, lane = ct & 31;
+  float* scores = reinterpret_cast<float*>(S.rsl);                 // [E <= 256]
+  uint64_t* lists = reinterpret_cast<uint64_t*>(S.rsl + 256 * 4);  // [4][8]
   const unsigned long long* lg = X.lg + (size_t)l * a.E * kFsLgStride;
-  const unsigned long long* p[8];
+  const float* b = a.layer[l].router_b;
+  const int e[2] = {64 * w + lane, 64 * w + 32 + lane};
+  float bias[2];
+  const unsigned long long* p[2];
 #pragma unroll
-  for (int j = 0; j < 8; j++) {
-    const int e = lane + 32 * j;
-    p[j] = e < a.E ? lg + (size_t)e * kFsLgStride : nullptr;
+  for (int i = 0; i < 2; i++) {
+    bias[i] = (b && e[i] < a.E) ? __ldg(b + e[i]) : 0.f;
+    p[i] = e[i] < a.E ? lg + (size_t)e[i] * kFsLgStride : nullptr;
   }
-  unsigned long long w[8];
+  unsigned long long wv[2] = {0ull, 0ull};
   const bool ok =
-      poll_words<8>(p, w, a.budget, [&](unsigned long long v) { return (int)(v & 0xFF) == nR; });
-  float score[8];
+      poll_words<2>(p, wv, a.budget, [&](unsigned long long v) { return (int)(v & 0xFF) == nR; });
+  uint64_t t[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) t[i] = 0ull;
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    if (p[i]) {
+      const float sc = sigmoid_ref(round_to_dtype(decode_counted_logit(wv[i]), a.dtype));
+      scores[e[i]] = sc;
+      t[i] = choice_key(sc + bias[i], (uint32_t)e[i]);
+    }
+  }
+  if (t[1] > t[0]) {
+    const uint64_t x = t[0];
+    t[0] = t[1];
+    t[1] = x;
+  }
+  merge_levels<8>(t, 1, 32);
 #pragma unroll
   for (int j = 0; j < 8; j++)
-    score[j] = sigmoid_ref(p[j] ? round_to_dtype(decode_counted_logit(w[j]), a.dtype) : 0.f);
-  topk_merge<8, 8>(score, bias, a.E, a.k, a.norm != 0, lane, isel, wsel);
-  if (lane < a.k) {
-    const uint32_t id16 = isel < 0xFFFFu ? isel : 0xFFFFu;
-    st_relaxed_u64(X.rt + (size_t)l * 8 + lane,
-                   tagged((uint32_t)(l + 1), 0u) | ((unsigned long long)id16 << 32) |
-                       __float_as_uint(wsel));
-    if (a.layer[l].inds) a.layer[l].inds[lane] = isel;
-    if (a.layer[l].wts) a.layer[l].wts[lane] = wsel;
+    if (lane == j) lists[w * 8 + j] = t[j];
+  const bool all_ok = chain_sync_and(ok);  // scores and lists visible to warp 0
+  if (w == 0) {
+    uint64_t u[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) u[j] = lane < 4 ? lists[lane * 8 + j] : 0ull;
+    merge_levels<8>(u, 1, 4);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {  // lane 0's list (lanes 0-3 hold the top 8) to every lane
+      const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)u[j], 0);
+      const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(u[j] >> 32), 0);
+      u[j] = ((uint64_t)hi << 32) | lo;
+    }
+    slots_from_keys<8>(u, scores, a.k, a.norm != 0, lane, isel, wsel);
+    if (lane < a.k) {
+      const uint32_t id16 = isel < 0xFFFFu ? isel : 0xFFFFu;
+      publish_u64(X.rt + (size_t)l * 8 + lane, tagged((uint32_t)(l + 1), 0u) |
+                                                   ((unsigned long long)id16 << 32) |
+                                                   __float_as_uint(wsel));
+      if (a.layer[l].inds) a.layer[l].inds[lane] = isel;
+      if (a.layer[l].wts) a.layer[l].wts[lane] = wsel;
+    }
   }
-  return ok;
+  named_sync(kBarChain, kChain);  // the scratch is free again
+  return all_ok;
 }
 
 // Any other CTA, one warp: layer l's routing from its routing line.
@@ -898,7 +930,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float w = load_as_f32(a.layer[j].norm_w, a.dtype, row);
         const float s2 = warp_sum(hrow * hrow);
         unsigned long long* sq = XC.sq + (size_t)j * kFsMaxReducers;
-        if (ct == 0) st_relaxed_u64(sq + c, tagged(tag, __float_as_uint(s2)));
+        if (ct == 0) publish_u64(sq + c, tagged(tag, __float_as_uint(s2)));
         const unsigned long long* p[2] = {lane < nR ? sq + lane : nullptr,
                                           lane + 32 < nR ? sq + lane + 32 : nullptr};
         unsigned long long wv[2] = {0ull, 0ull};
@@ -914,7 +946,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                : (uint32_t)__half_as_ushort(__float2half_rn(xv));
         const uint32_t hi = __shfl_down_sync(0xffffffffu, bits, 1);
         if ((ct & 1) == 0)
-          st_relaxed_u64(XC.xin + (size_t)((a.l0 + j) & 1) * (H / 2) + (row >> 1),
+          publish_u64(XC.xin + (size_t)((a.l0 + j) & 1) * (H / 2) + (row >> 1),
                          tagged(tag, (hi << 16) | bits));
         S.xs[ct] = xv;
       }
@@ -948,17 +980,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- routed stack: this layer's routing (the router CTA computes and
       // publishes it; the others read its routing line) ----
       if (ROUTED && (has_gu || has_d || is_router)) {
+        uint32_t isel = 0;
+        float wsel = 0.f;
+        bool got = true;
+        if (is_router) got = route_and_publish(a, S, XC, l, ct, nR, isel, wsel);
+        else if (ct < 32) got = read_routing(a, XC, l, lane, isel, wsel);
         if (ct < 32) {
-          uint32_t isel;
-          float wsel;
-          bool got;
-          if (is_router) {
-            float bias[8];
-            load_router_bias(a, l, lane, bias);
-            got = route_and_publish(a, XC, l, lane, nR, bias, isel, wsel);
-          } else {
-            got = read_routing(a, XC, l, lane, isel, wsel);
-          }
           if (!got && lane == 0) fsflag(fs_timeout(l, 53));
           if (lane < a.k) {
             S.inds[l * 16 + lane] = isel;
@@ -1211,7 +1238,7 @@ bool decode_stack_fp4_supported(int H, int I, int kk, int sms, bool routed) {
   if (I != 512 && I != 1024 && I != 2048) return false;
   if (kk < 1 || kk > 16 || kk * (H / 128) > sms) return false;  // one down item per CTA
   if (decode_stack_fp4_nks(I, kk, sms) == 0) return false;      // one gate/up item per CTA
-  if (routed && H / kFsRedRows > sms) return false;             // one reducer per CTA
+  if (routed && H / kFsRedRows > sms - 1) return false;  // one reducer per CTA, the router apart
   if (kSfbx + (uint32_t)(H / 16 + I / 16) > kTmemCols) return false;
   return decode_stack_fp4_smem_bytes(H, I, kFsMaxLayers, routed) <= 227 * 1024;
 }
@@ -1234,7 +1261,7 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   if (decode_stack_fp4_nks(a.I, a.kk, sms) != a.nks || a.kk * (a.H / 128) > sms ||
-      (a.routed && a.H / kFsRedRows > sms))
+      (a.routed && a.H / kFsRedRows > sms - 1))
     return cudaErrorInvalidValue;
   // Every CTA must be resident (CTAs wait on one another's counters): one per
   // SM, cooperative launch.

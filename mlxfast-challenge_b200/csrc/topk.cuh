@@ -107,25 +107,13 @@ __device__ __forceinline__ void sort_keys_desc(uint64_t (&v)[N]) {
       }
 }
 
-template <int kPer, int K>
-__device__ __forceinline__ void topk_merge(const float (&score)[kPer], const float (&bias)[kPer],
-                                           int E, int k, bool norm, int lane, uint32_t& isel,
-                                           float& wsel) {
-  constexpr int NS = kPer > K ? kPer : K;
-  uint64_t v[NS];
-#pragma unroll
-  for (int j = 0; j < NS; j++) {
-    const int e = lane + 32 * j;
-    v[j] = (j < kPer && e < E) ? choice_key(score[j < kPer ? j : 0] + bias[j < kPer ? j : 0],
-                                            (uint32_t)e)
-                               : 0ull;
-  }
-  sort_keys_desc<NS>(v);
-  uint64_t t[K];
-#pragma unroll
-  for (int i = 0; i < K; i++) t[i] = v[i];
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
+// Butterfly levels lane xor o, o = o_first, 2 o_first, .. < o_end, on
+// descending lists of K keys (the max of the list and the reversed partner
+// list is bitonic and holds the top K of both; a half-cleaner cascade sorts
+// it): afterwards lanes that differ only in those bits hold the same list.
+template <int K>
+__device__ __forceinline__ void merge_levels(uint64_t (&t)[K], int o_first, int o_end) {
+  for (int o = o_first; o < o_end; o <<= 1) {
     uint64_t p[K];
 #pragma unroll
     for (int i = 0; i < K; i++) {
@@ -147,7 +135,14 @@ __device__ __forceinline__ void topk_merge(const float (&score)[kPer], const flo
         }
       }
   }
-  // slot r = t[r]; its score from the expert's lane (id % 32, entry id / 32)
+}
+
+// Slots 0 .. k-1 of a sorted key list (the same on every lane): lane r < k
+// gets slot r's expert id and weight (its score from scores[id], shared
+// memory; weights / their sum in slot order when norm).
+template <int K>
+__device__ __forceinline__ void slots_from_keys(const uint64_t (&t)[K], const float* scores, int k,
+                                                bool norm, int lane, uint32_t& isel, float& wsel) {
   float wsum = 0.f;
   wsel = 0.f;
   isel = 0;
@@ -156,11 +151,59 @@ __device__ __forceinline__ void topk_merge(const float (&score)[kPer], const flo
     if (r >= k) break;
     const uint64_t key = t[r];
     const uint32_t id = key ? 0xFFFFFFFFu - (uint32_t)key : 0x7fffffffu;
-    float s = 0.f;
+    const float s = key ? scores[id] : 0.f;
+    wsum += s;
+    if (lane == r) {
+      wsel = s;
+      isel = id;
+    }
+  }
+  if (norm) wsel = wsel / wsum;
+}
+
+template <int kPer, int K>
+__device__ __forceinline__ void topk_merge(const float (&score)[kPer], const float (&bias)[kPer],
+                                           int E, int k, bool norm, int lane, uint32_t& isel,
+                                           float& wsel, float* scratch = nullptr) {
+  constexpr int NS = kPer > K ? kPer : K;
+  uint64_t v[NS];
 #pragma unroll
-    for (int j = 0; j < kPer; j++) {
-      const float sj = __shfl_sync(0xffffffffu, score[j], (int)(id & 31));
-      if (key && (int)(id >> 5) == j) s = sj;
+  for (int j = 0; j < NS; j++) {
+    const int e = lane + 32 * j;
+    v[j] = (j < kPer && e < E) ? choice_key(score[j < kPer ? j : 0] + bias[j < kPer ? j : 0],
+                                            (uint32_t)e)
+                               : 0ull;
+  }
+  sort_keys_desc<NS>(v);
+  uint64_t t[K];
+#pragma unroll
+  for (int i = 0; i < K; i++) t[i] = v[i];
+  merge_levels<K>(t, 1, 32);
+  // slot r = t[r]; its score from the expert's lane (id % 32, entry id / 32):
+  // through `scratch` (32 kPer floats of this warp's shared memory) when
+  // given, else by shuffles
+  float wsum = 0.f;
+  wsel = 0.f;
+  isel = 0;
+  if (scratch) {
+#pragma unroll
+    for (int j = 0; j < kPer; j++) scratch[lane + 32 * j] = score[j];
+    __syncwarp();
+  }
+#pragma unroll
+  for (int r = 0; r < K; r++) {
+    if (r >= k) break;
+    const uint64_t key = t[r];
+    const uint32_t id = key ? 0xFFFFFFFFu - (uint32_t)key : 0x7fffffffu;
+    float s = 0.f;
+    if (scratch) {
+      s = key ? scratch[id] : 0.f;
+    } else {
+#pragma unroll
+      for (int j = 0; j < kPer; j++) {
+        const float sj = __shfl_sync(0xffffffffu, score[j], (int)(id & 31));
+        if (key && (int)(id >> 5) == j) s = sj;
+      }
     }
     wsum += s;
     if (lane == r) {
@@ -168,6 +211,7 @@ __device__ __forceinline__ void topk_merge(const float (&score)[kPer], const flo
       isel = id;
     }
   }
+  if (scratch) __syncwarp();  // the scratch may be reused after the call
   if (norm) wsel = wsel / wsum;
 }
 
