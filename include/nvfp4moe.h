@@ -100,8 +100,9 @@ NVFP4MOE_API int nvfp4_version(void);
  * every bounded wait ~1 ms instead of ~1 s and withhold one release (the
  * last layer's segment-0 gate/up items never signal), so the waits behind it
  * run out: the launch returns, nvfp4_device_status() reports
- * NVFP4_ERR_DEVICE_TIMEOUT with the site 1000 * (layer + 1) + 50..52 / 54,
- * and the outputs are not valid.  The context stays usable.  It exercises
+ * NVFP4_ERR_DEVICE_TIMEOUT with the site 1000 * (last layer + 1) + 40..59
+ * (whichever wait behind the withheld release gave up first: a counter wait
+ * 50..54 or a tensor-core wait 41..49), and the outputs are not valid.  The context stays usable.  It exercises
  * the error path of the bounded waits without faulting or hanging a GPU. */
 #define NVFP4_LAUNCH_TEST_EXPIRE 16
 NVFP4MOE_API int nvfp4_set_launch_flags(int flags);

@@ -52,17 +52,19 @@
 // reduction, the norm and the router's logits are the reducers' step:
 // reducer j (CTA j < H / 32) waits for the down items of its 32 rows, sums
 // their segment partials in segment order (+ the residual h_l), rounds to
-// the activation dtype -- h_{l+1} for those rows -- and, with the norm, adds
-// the rows' squares into the layer's sum-of-squares accumulator, waits for
-// all reducers and forms x = dtype(dtype(h * rsqrt(mean + eps)) * w), the
-// reference's RMSNorm fallback (mlx/fast.cpp:90-108); then it adds
-// x[rows] . G[e, rows] for every expert e into the expert's accumulator.
-// Sums are 64-bit fixed-point integers (2^-32 units for logits, 2^-24 for
-// squares): integer sums do not depend on the order of the adds, so every
-// run gives the same bits.  Each CTA then reads the E sums, rounds each logit
-// to the activation dtype as the reference's bf16 matmul does, and selects
-// the top-k itself (topk.cuh).  The reducers' router rows are prefetched two
-// layers ahead with cp.async.
+// the activation dtype -- h_{l+1} for those rows -- and, with the norm,
+// publishes the rows' f32 sum of squares as its tagged word of the layer,
+// reads every reducer's word and sums them in reducer order (the same bits on
+// every reducer), and forms x = dtype(dtype(h * rsqrt(mean + eps)) * w), the
+// reference's RMSNorm fallback (mlx/fast.cpp:90-108); x goes out as tagged
+// words (the gate/up items' input); then it adds x[rows] . G[e, rows] for
+// every expert e into the expert's counted logit sum (64-bit fixed point,
+// 2^-28 units, with an add count: integer sums do not depend on the order of
+// the adds, so every run gives the same bits).  The router CTA (the last
+// one) waits for the counts, rounds each logit to the activation dtype as the
+// reference's bf16 matmul does, selects the top-k (topk.cuh) and publishes the
+// layer's routing line; every CTA with an item of the layer reads it.  The
+// reducers' router rows are prefetched two layers ahead with cp.async.
 //
 // Roles (320 threads): warp 0 TMA (this CTA's weight slabs of layer l, l+1,
 // ... in consumption order into a 10-stage ring -- 8 in the routed stack, one
