@@ -108,7 +108,7 @@ constexpr int kErrIndex = 2;
 // K part's down items (previous layer), 52 the last layer's down items; routed
 // stack: 53 the layer's router reducers, 54 a row block's down items (the
 // reducer), 55 the TMA warp waiting for the layer's routing, 56 the reducers'
-// sums of squares (the norm).
+// sums of squares (the norm), 57 a gate/up item's tagged inputs.
 __host__ __device__ constexpr int fs_timeout(int l, int site) { return 1000 * (l + 1) + site; }
 constexpr long long kDrainBudget = 200000000LL;
 
@@ -466,12 +466,12 @@ __device__ __forceinline__ void router_partials(const FsArgs& a, const FsSmem& S
                                                 int j, int ct) {
   const uint8_t* sl = S.rsl + (size_t)(j & 1) * (256 * kFsRedRows * 2);
   unsigned long long* lg = X.lg + (size_t)j * a.E * kFsLgStride;
+  float p[2] = {0.f, 0.f};
 #pragma unroll
   for (int h = 0; h < 2; h++) {
     const int e = ct + 128 * h;
     if (e >= a.E) break;
     const uint4* g = reinterpret_cast<const uint4*>(sl + e * 64);
-    float p = 0.f;
 #pragma unroll
     for (int q = 0; q < 4; q++) {
       const uint4 w = g[q];
@@ -479,28 +479,38 @@ __device__ __forceinline__ void router_partials(const FsArgs& a, const FsSmem& S
 #pragma unroll
       for (int i = 0; i < 4; i++) {
         const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
-        p += S.xs[8 * q + 2 * i] * f.x;
-        p += S.xs[8 * q + 2 * i + 1] * f.y;
+        p[h] += S.xs[8 * q + 2 * i] * f.x;
+        p[h] += S.xs[8 * q + 2 * i + 1] * f.y;
       }
     }
-    add_counted_logit(lg + (size_t)e * kFsLgStride, p);
   }
+  // both adds back to back: every expert's sum completes at about the same time
+#pragma unroll
+  for (int h = 0; h < 2; h++)
+    if (ct + 128 * h < a.E) add_counted_logit(lg + (size_t)(ct + 128 * h) * kFsLgStride, p[h]);
 }
 
-// The router CTA (no reducer: its router-row buffer holds the scores and the
-// warps' lists), all four chain warps: warp w waits until all nR reducers have
-// added to the logit sums of experts 64 w + lane and 64 w + 32 + lane, rounds
-// each logit to the activation dtype as the reference's bf16 matmul returns
-// it, scores it, and merges its warp's top 8 (topk.cuh: merge_levels); warp 0
-// merges the four lists and publishes slot j (lane j < k) as tagged
-// (expert id << 32 | weight bits) words of layer l's routing line, and into
-// the layer's routing outputs.  Lanes of warp 0 end with their slot.
+// The router CTA (no reducer: its router-row buffer is the scratch), all four
+// chain warps: warp w waits until all nR reducers have added to the logit
+// sums of experts 64 w + lane and 64 w + 32 + lane, rounds each logit to the
+// activation dtype as the reference's bf16 matmul returns it, scores it, and
+// ranks its two keys among the warp's 64 (the number of larger keys: keys are
+// distinct apart from 0, topk.cuh); keys of rank < k form the warp's sorted
+// list.  Warp 0 ranks the 32 list entries the same way, which gives the top k
+// in slot order, and publishes slot j (lane j < k) as tagged (expert id << 32
+// | weight bits) words of layer l's routing line, and into the layer's routing
+// outputs; weights / their sum in slot order.  Counting compares shared-memory
+// words instead of exchanging keys between lanes: no dependent chain of warp
+// shuffles.  Lanes of warp 0 end with their slot.
 __device__ __forceinline__ bool route_and_publish(const FsArgs& a, const FsSmem& S,
                                                   const Xchg& X, int l, int ct, int nR,
                                                   uint32_t& isel, float& wsel) {
   const int w = ct >> 5, lane = ct & 31;
-  float* scores = reinterpret_cast<float*>(S.rsl);                 // [E <= 256]
-  uint64_t* lists = reinterpret_cast<uint64_t*>(S.rsl + 256 * 4);  // [4][8]
+  uint64_t* wkeys = reinterpret_cast<uint64_t*>(S.rsl) + w * 64;        // [4][64]
+  uint64_t* lists = reinterpret_cast<uint64_t*>(S.rsl + 2048);           // [4][8]
+  float* lscore = reinterpret_cast<float*>(S.rsl + 2048 + 256);          // [4][8]
+  uint64_t* skey = reinterpret_cast<uint64_t*>(S.rsl + 2048 + 384);      // [8] slots
+  float* sscore = reinterpret_cast<float*>(S.rsl + 2048 + 384 + 64);     // [8]
   const unsigned long long* lg = X.lg + (size_t)l * a.E * kFsLgStride;
   const float* b = a.layer[l].router_b;
   const int e[2] = {64 * w + lane, 64 * w + 32 + lane};
@@ -511,42 +521,89 @@ __device__ __forceinline__ bool route_and_publish(const FsArgs& a, const FsSmem&
     bias[i] = (b && e[i] < a.E) ? __ldg(b + e[i]) : 0.f;
     p[i] = e[i] < a.E ? lg + (size_t)e[i] * kFsLgStride : nullptr;
   }
+  if (lane < 8) {  // empty list entries and slots: no expert, score 0
+    lists[w * 8 + lane] = 0ull;
+    lscore[w * 8 + lane] = 0.f;
+    if (w == 0) {
+      skey[lane] = 0ull;
+      sscore[lane] = 0.f;
+    }
+  }
   unsigned long long wv[2] = {0ull, 0ull};
   const bool ok =
       poll_words<2>(p, wv, a.budget, [&](unsigned long long v) { return (int)(v & 0xFF) == nR; });
-  uint64_t t[8];
-#pragma unroll
-  for (int i = 0; i < 8; i++) t[i] = 0ull;
+  uint64_t t[2];
+  float sc[2];
 #pragma unroll
   for (int i = 0; i < 2; i++) {
+    sc[i] = 0.f;
+    t[i] = 0ull;
     if (p[i]) {
-      const float sc = sigmoid_ref(round_to_dtype(decode_counted_logit(wv[i]), a.dtype));
-      scores[e[i]] = sc;
-      t[i] = choice_key(sc + bias[i], (uint32_t)e[i]);
+      sc[i] = sigmoid_ref(round_to_dtype(decode_counted_logit(wv[i]), a.dtype));
+      t[i] = choice_key(sc[i] + bias[i], (uint32_t)e[i]);
     }
   }
-  if (t[1] > t[0]) {
-    const uint64_t x = t[0];
-    t[0] = t[1];
-    t[1] = x;
-  }
-  merge_levels<8>(t, 1, 32);
+  wkeys[lane] = t[0];
+  wkeys[32 + lane] = t[1];
+  __syncwarp();
+  int rc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // four counts per key: short add chains
+  const ulonglong2* wk = reinterpret_cast<const ulonglong2*>(wkeys);
 #pragma unroll
-  for (int j = 0; j < 8; j++)
-    if (lane == j) lists[w * 8 + j] = t[j];
-  const bool all_ok = chain_sync_and(ok);  // scores and lists visible to warp 0
+  for (int j = 0; j < 32; j += 2) {
+    const ulonglong2 q0 = wk[j], q1 = wk[j + 1];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+      rc[i][0] += (int)(q0.x > t[i]);
+      rc[i][1] += (int)(q0.y > t[i]);
+      rc[i][2] += (int)(q1.x > t[i]);
+      rc[i][3] += (int)(q1.y > t[i]);
+    }
+  }
+  const int r0 = (rc[0][0] + rc[0][1]) + (rc[0][2] + rc[0][3]);
+  const int r1 = (rc[1][0] + rc[1][1]) + (rc[1][2] + rc[1][3]);
+  // a key of 0 (no expert) ranks after every real key; its entry stays empty
+  if (t[0] && r0 < a.k) {
+    lists[w * 8 + r0] = t[0];
+    lscore[w * 8 + r0] = sc[0];
+  }
+  if (t[1] && r1 < a.k) {
+    lists[w * 8 + r1] = t[1];
+    lscore[w * 8 + r1] = sc[1];
+  }
+  const bool all_ok = chain_sync_and(ok);  // the lists visible to warp 0
   if (w == 0) {
-    uint64_t u[8];
+    const uint64_t u = lists[lane];
+    const float us = lscore[lane];
+    const ulonglong2* lk = reinterpret_cast<const ulonglong2*>(lists);
+    int rq[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int j = 0; j < 8; j++) u[j] = lane < 4 ? lists[lane * 8 + j] : 0ull;
-    merge_levels<8>(u, 1, 4);
-#pragma unroll
-    for (int j = 0; j < 8; j++) {  // lane 0's list (lanes 0-3 hold the top 8) to every lane
-      const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)u[j], 0);
-      const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(u[j] >> 32), 0);
-      u[j] = ((uint64_t)hi << 32) | lo;
+    for (int j = 0; j < 16; j += 2) {
+      const ulonglong2 q0 = lk[j], q1 = lk[j + 1];
+      rq[0] += (int)(q0.x > u);
+      rq[1] += (int)(q0.y > u);
+      rq[2] += (int)(q1.x > u);
+      rq[3] += (int)(q1.y > u);
     }
-    slots_from_keys<8>(u, scores, a.k, a.norm != 0, lane, isel, wsel);
+    const int r = (rq[0] + rq[1]) + (rq[2] + rq[3]);
+    if (u && r < a.k) {
+      skey[r] = u;
+      sscore[r] = us;
+    }
+    __syncwarp();
+    // slot scores for every lane (two vector loads), summed in slot order
+    const float4 s0 = reinterpret_cast<const float4*>(sscore)[0];
+    const float4 s1 = reinterpret_cast<const float4*>(sscore)[1];
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    float wsum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) wsum += j < a.k ? sv[j] : 0.f;
+    const uint64_t key = lane < 8 ? skey[lane] : 0ull;
+    isel = key ? 0xFFFFFFFFu - (uint32_t)key : 0x7fffffffu;
+    wsel = lane < 8 ? sv[0] : 0.f;
+#pragma unroll
+    for (int j = 1; j < 8; j++)
+      if (lane == j) wsel = sv[j];
+    if (a.norm) wsel = wsel / wsum;
     if (lane < a.k) {
       const uint32_t id16 = isel < 0xFFFFu ? isel : 0xFFFFu;
       publish_u64(X.rt + (size_t)l * 8 + lane, tagged((uint32_t)(l + 1), 0u) |
@@ -980,8 +1037,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ct == 0) *S.cur = l;
 
       // ---- routed stack: this layer's routing (the router CTA computes and
-      // publishes it; the others read its routing line) ----
-      if (ROUTED && (has_gu || has_d || is_router)) {
+      // publishes it; the others read its routing line).  A gate/up CTA takes
+      // it after its x terms (x does not depend on the routing and is
+      // published before the logits), the others here. ----
+      auto take_routing = [&]() -> bool {
         uint32_t isel = 0;
         float wsel = 0.f;
         bool got = true;
@@ -1001,10 +1060,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) *S.bar_ok = got;
         }
         named_sync(kBarChain, kChain);
-        if (!*S.bar_ok) {
-          alive = false;
-          break;
-        }
+        return *S.bar_ok != 0;
+      };
+      if (ROUTED && !has_gu && (has_d || is_router) && !take_routing()) {
+        alive = false;
+        break;
       }
 
       // ---- phase A: x terms, gate/up item -> GUp ----
@@ -1080,6 +1140,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (ct == 0) *S.hold = 1;
         if (lane == 0) mbar_arrive(S.xready);
+        if (ROUTED && !take_routing()) {
+          alive = false;
+          break;
+        }
         const bool got = mbar_wait_bounded(S.gufull, jgu & 1, a.budget);
         jgu++;
         if (!got && lane == 0) fsflag(fs_timeout(l, 48));
