@@ -151,7 +151,7 @@ def bench_prefill(torch, nv, lag, cfg, dev, steps, warmup, layers, distinct=4, T
 
 
 def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers, distinct=2,
-                     T=512, form="gather"):
+                     T=512, form="gather", partial_dtype=None, check=False):
     """config[3] expert-parallel: every rank holds E/world experts, the router
     and the shared expert, and runs the sparse block for its own T tokens; the
     (token, slot) rows cross to their experts' ranks and back by NCCL
@@ -159,14 +159,19 @@ def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers,
     over ranks."""
     ep = importlib.import_module("mlxfast-challenge_b200.ep")
     blocks = []
+    full0 = None  # rank 0 with check: the whole layer 0 on one GPU, the reference path
     for l in range(distinct):
-        _, raw = lag.random_sparse_layer(nv, seed=3000 + l, device=dev)
+        full, raw = lag.random_sparse_layer(nv, seed=3000 + l, device=dev)
+        if check and rank == 0 and l == 0:
+            full0 = full
+        del full
         # this rank's expert slice as its own tensors, so the other experts
         # are freed (256/world experts resident per GPU)
         local = {k: v.clone() for k, v in ep.local_slice(raw["routed"], rank, world).items()}
         if form == "gather":
             ops = ep.CudaGatherEPOps(local, raw["shared"], raw["router_w"], raw["router_b"],
-                                     cfg.n_experts, rank, world)
+                                     cfg.n_experts, rank, world,
+                                     partial_dtype=partial_dtype or torch.bfloat16)
             blk = ep.GatherEPBlock(ops)
         else:
             ops = ep.CudaEPOps(local, raw["shared"], raw["router_w"], raw["router_b"],
@@ -178,6 +183,21 @@ def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers,
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     x = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
     res = torch.randn(T, cfg.hidden, generator=g, device=dev).to(torch.bfloat16)
+    checked = None
+    if check:
+        # every rank takes part; rank 0 compares its tokens' output with the
+        # single-GPU block on the same tokens (same router, all 256 experts)
+        y_ep = blocks[0](x, residual=res)
+        if rank == 0:
+            want = full0(x, residual=res)
+            d = (y_ep.float() - want.float())
+            checked = {"vs": "single-GPU SparseMoeBlock (all 256 experts) on rank 0's tokens",
+                       "rel_l2": float(d.norm() / want.float().norm()),
+                       "max_abs": float(d.abs().max()), "tolerance_rel_l2": 1e-2}
+            checked["ok"] = bool(checked["rel_l2"] <= 1e-2)
+        full0 = None
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
 
     def step():
         for l in range(layers):
@@ -201,12 +221,17 @@ def bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, steps, layers,
     exchange = ("NCCL all-gather of tokens + routing, per-rank partial sums over its "
                 "experts, NCCL reduce-scatter" if form == "gather" else
                 "NCCL all-to-all dispatch/combine")
-    return {"workload": f"BASELINE config[3] expert-parallel over {world} GPUs: sparse block "
-                        f"T={T} tokens per GPU (router top-8, {cfg.n_experts // world} experts "
-                        f"per GPU, shared expert, residual), {layers} layers per step, "
-                        f"{exchange}", "n_gpus": world, "form": form,
-            "tok_per_s": world * T / (ms_step / 1e3), "us_per_layer": ms_step * 1e3 / layers,
-            "scaling": "weak", "unit": "tok/s", "steps": steps}
+    out = {"workload": f"BASELINE config[3] expert-parallel over {world} GPUs: sparse block "
+                       f"T={T} tokens per GPU (router top-8, {cfg.n_experts // world} experts "
+                       f"per GPU, shared expert, residual), {layers} layers per step, "
+                       f"{exchange}", "n_gpus": world, "form": form,
+           "tok_per_s": world * T / (ms_step / 1e3), "us_per_layer": ms_step * 1e3 / layers,
+           "scaling": "weak", "unit": "tok/s", "steps": steps}
+    if form == "gather":
+        out["partials"] = str(partial_dtype or torch.bfloat16).replace("torch.", "")
+    if checked is not None:
+        out["check"] = checked
+    return out
 
 
 def blocked_scales(torch, s):
@@ -689,7 +714,13 @@ def main():
     if world > 1 and args.workload == "all":
         # every rank takes part (the exchange is collective)
         prefill_ep = bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world,
-                                      args.prefill_steps, cfg.num_sparse_layers, form="gather")
+                                      args.prefill_steps, cfg.num_sparse_layers, form="gather",
+                                      partial_dtype=torch.bfloat16, check=True)
+        f32 = bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, args.prefill_steps,
+                               cfg.num_sparse_layers, form="gather",
+                               partial_dtype=torch.float32)
+        prefill_ep["f32_partials"] = {"tok_per_s": f32["tok_per_s"],
+                                      "us_per_layer": f32["us_per_layer"]}
         a2a = bench_prefill_ep(torch, dist, nv, lag, cfg, dev, rank, world, args.prefill_steps,
                                cfg.num_sparse_layers, form="all2all")
         prefill_ep["all2all_form"] = {"tok_per_s": a2a["tok_per_s"],

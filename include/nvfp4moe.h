@@ -398,11 +398,26 @@ NVFP4MOE_API int moe_ep_partial_forward(float* y_partial, const void* x, int64_t
                                         int64_t expert_base, int64_t shared_row0,
                                         int64_t shared_rows, void* workspace,
                                         size_t workspace_bytes, nvfp4_stream stream);
+/* The same with the partials written in partial_dtype: NVFP4_F32 (as
+ * moe_ep_partial_forward) or NVFP4_BF16, which halves the reduce-scatter's
+ * bytes; each rank's partial is then rounded to bf16 once before the sum
+ * (the block output is bf16 anyway). */
+NVFP4MOE_API int moe_ep_partial_forward_typed(void* y_partial, int partial_dtype, const void* x,
+                                              int64_t x_ld, int dtype, int64_t T,
+                                              const moe_layer_desc* layer, const uint32_t* inds,
+                                              const float* weights, int64_t expert_base,
+                                              int64_t shared_row0, int64_t shared_rows,
+                                              void* workspace, size_t workspace_bytes,
+                                              nvfp4_stream stream);
 /* y[T, H] = partial (f32) + shared (or NULL) + residual (or NULL), rounded
  * once to dtype. */
 NVFP4MOE_API int moe_ep_finish(void* y, const float* partial, const void* shared,
                                const void* residual, int dtype, int64_t T, int64_t H,
                                nvfp4_stream stream);
+/* The same with the partial sums in partial_dtype (f32, bf16 or f16). */
+NVFP4MOE_API int moe_ep_finish_typed(void* y, const void* partial, int partial_dtype,
+                                     const void* shared, const void* residual, int dtype,
+                                     int64_t T, int64_t H, nvfp4_stream stream);
 
 #ifdef __cplusplus
 }

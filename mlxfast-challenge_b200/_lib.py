@@ -62,6 +62,9 @@ SIGNATURES = {
     "moe_ep_partial_forward": (_I, [_P, _P, _I64, _I, _I64, _P, _P, _P, _I64, _I64, _I64, _P,
                                     ctypes.c_size_t, _P]),
     "moe_ep_finish": (_I, [_P, _P, _P, _P, _I, _I64, _I64, _P]),
+    "moe_ep_partial_forward_typed": (_I, [_P, _I, _P, _I64, _I, _I64, _P, _P, _P, _I64, _I64,
+                                          _I64, _P, ctypes.c_size_t, _P]),
+    "moe_ep_finish_typed": (_I, [_P, _P, _I, _P, _P, _I, _I64, _I64, _P]),
     "nvfp4_qqmm": (_I, [_P, _P, _I, _P, _P, _I64, _I64, _I64, _P, ctypes.c_size_t, _P]),
     "nvfp4_gather_qmm": (_I, [_P, _P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
                               _I, _P]),

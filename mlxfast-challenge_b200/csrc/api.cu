@@ -1123,8 +1123,20 @@ int moe_ep_partial_forward(float* y_partial, const void* x, int64_t x_ld, int dt
                            const moe_layer_desc* L, const uint32_t* inds, const float* weights,
                            int64_t expert_base, int64_t shared_row0, int64_t shared_rows,
                            void* workspace, size_t workspace_bytes, nvfp4_stream stream) {
+  return moe_ep_partial_forward_typed(y_partial, NVFP4_F32, x, x_ld, dtype, T, L, inds, weights,
+                                      expert_base, shared_row0, shared_rows, workspace,
+                                      workspace_bytes, stream);
+}
+
+int moe_ep_partial_forward_typed(void* y_partial, int partial_dtype, const void* x, int64_t x_ld,
+                                 int dtype, int64_t T, const moe_layer_desc* L,
+                                 const uint32_t* inds, const float* weights, int64_t expert_base,
+                                 int64_t shared_row0, int64_t shared_rows, void* workspace,
+                                 size_t workspace_bytes, nvfp4_stream stream) {
   const char* op = "moe_ep_partial";
   if (int r = check_layer(op, L, dtype, T)) return r;
+  if (partial_dtype != NVFP4_F32 && partial_dtype != NVFP4_BF16)
+    return fail(NVFP4_ERR_INVALID, "[%s] partials are f32 or bf16.", op);
   if (T == 0) return NVFP4_OK;
   if (!y_partial || !x || !inds || !weights)
     return fail(NVFP4_ERR_INVALID, "[%s] null pointer argument.", op);
@@ -1160,16 +1172,23 @@ int moe_ep_partial_forward(float* y_partial, const void* x, int64_t x_ld, int dt
   sa.skip_foreign = 1;
   if (int r = check_cuda(nvfp4::launch_moe_sort(sa, s, first_pdl()), op)) return r;
   return prefill_fp4_tail(y_partial, x, nullptr, dtype, T, L, weights, ws, B, s, x_ld,
-                          NVFP4_F32, sh ? shared_row0 : 0, sh ? shared_rows : 0);
+                          partial_dtype, sh ? shared_row0 : 0, sh ? shared_rows : 0);
 }
 
 int moe_ep_finish(void* y, const float* partial, const void* shared, const void* residual,
                   int dtype, int64_t T, int64_t H, nvfp4_stream stream) {
-  if (!valid_dtype(dtype)) return fail(NVFP4_ERR_INVALID, "[moe_ep_finish] invalid dtype.");
+  return moe_ep_finish_typed(y, partial, NVFP4_F32, shared, residual, dtype, T, H, stream);
+}
+
+int moe_ep_finish_typed(void* y, const void* partial, int partial_dtype, const void* shared,
+                        const void* residual, int dtype, int64_t T, int64_t H,
+                        nvfp4_stream stream) {
+  if (!valid_dtype(dtype) || !valid_dtype(partial_dtype))
+    return fail(NVFP4_ERR_INVALID, "[moe_ep_finish] invalid dtype.");
   if (T < 0 || H <= 0) return fail(NVFP4_ERR_INVALID, "[moe_ep_finish] invalid shape.");
   if (T > 0 && (!y || !partial))
     return fail(NVFP4_ERR_INVALID, "[moe_ep_finish] null pointer argument.");
-  return check_cuda(nvfp4::launch_ep_finish(y, partial, shared, residual, dtype, T, H,
+  return check_cuda(nvfp4::launch_ep_finish(y, partial, partial_dtype, shared, residual, dtype, T, H,
                                             (cudaStream_t)stream),
                     "moe_ep_finish");
 }

@@ -139,11 +139,12 @@ __global__ void moe_ep_combine_kernel(EpCombineArgs a) {
   }
 }
 
-__global__ void moe_ep_finish_kernel(void* y, const float* partial, const void* shared,
-                                     const void* residual, int dtype, int64_t total) {
+__global__ void moe_ep_finish_kernel(void* y, const void* partial, int partial_dtype,
+                                     const void* shared, const void* residual, int dtype,
+                                     int64_t total) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    float acc = partial[i];
+    float acc = load_as_f32(partial, partial_dtype, i);
     if (shared) acc += load_as_f32(shared, dtype, i);
     if (residual) acc += load_as_f32(residual, dtype, i);
     store_from_f32(y, dtype, i, acc);
@@ -152,14 +153,15 @@ __global__ void moe_ep_finish_kernel(void* y, const float* partial, const void* 
 
 }  // namespace
 
-cudaError_t launch_ep_finish(void* y, const float* partial, const void* shared,
+cudaError_t launch_ep_finish(void* y, const void* partial, int partial_dtype, const void* shared,
                              const void* residual, int dtype, int64_t T, int64_t H,
                              cudaStream_t stream) {
   const int64_t total = T * H;
   if (total == 0) return cudaSuccess;
   const int threads = 256;
   const int blocks = (int)std::min<int64_t>((total + threads - 1) / threads, 148 * 8);
-  moe_ep_finish_kernel<<<blocks, threads, 0, stream>>>(y, partial, shared, residual, dtype, total);
+  moe_ep_finish_kernel<<<blocks, threads, 0, stream>>>(y, partial, partial_dtype, shared, residual,
+                                                       dtype, total);
   return cudaGetLastError();
 }
 

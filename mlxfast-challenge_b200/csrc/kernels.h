@@ -253,7 +253,7 @@ cudaError_t launch_ep_plan(const EpPlanArgs& a, cudaStream_t stream);
 cudaError_t launch_ep_pack(const EpPackArgs& a, cudaStream_t stream);
 cudaError_t launch_ep_combine(const EpCombineArgs& a, cudaStream_t stream);
 // y[T, H] = partial (f32) + shared + residual, rounded once to dtype.
-cudaError_t launch_ep_finish(void* y, const float* partial, const void* shared,
+cudaError_t launch_ep_finish(void* y, const void* partial, int partial_dtype, const void* shared,
                              const void* residual, int dtype, int64_t T, int64_t H,
                              cudaStream_t stream);
 cudaError_t read_and_clear_ep_error(int* out);

@@ -266,8 +266,8 @@ class GatherEPBlock:
         inds, wts = routing if routing is not None else ops.route(x)
         rows = gather_rows(pack_tokens(x, inds, wts), self.group)
         T = x.shape[0]
-        part = ops.partial(rows, x.dtype, self.rank * T, T)  # [world * T, H] f32
-        mine = reduce_scatter_rows(part, self.group)  # [T, H] f32
+        part = ops.partial(rows, x.dtype, self.rank * T, T)  # [world * T, H]
+        mine = reduce_scatter_rows(part, self.group)  # [T, H], the partials' dtype
         if side is not None:
             torch.cuda.current_stream(x.device).wait_stream(side)
             if shared is not None:
@@ -278,14 +278,20 @@ class GatherEPBlock:
 class CudaGatherEPOps:
     """Device side of one rank for GatherEPBlock: router, this rank's routed
     experts and the shared expert (on the rank's own rows) through
-    moe_ep_partial_forward, moe_ep_finish."""
+    moe_ep_partial_forward_typed, moe_ep_finish_typed.  partial_dtype: the
+    partial sums' type on the wire -- torch.float32, or torch.bfloat16 (half
+    the reduce-scatter bytes; each rank's partial rounded once to bf16)."""
 
     shared_in_partial = True
 
     def __init__(self, routed: dict, shared: Optional[dict], router_w: torch.Tensor,
                  router_b: Optional[torch.Tensor], n_experts: int, rank: int, world: int,
-                 top_k: int = 8, routed_scaling: float = 2.5, norm_topk_prob: bool = True):
+                 top_k: int = 8, routed_scaling: float = 2.5, norm_topk_prob: bool = True,
+                 partial_dtype: torch.dtype = torch.float32):
         from . import SparseMoeBlock
+        if partial_dtype not in (torch.float32, torch.bfloat16):
+            raise ValueError("[moe_ep] partials are float32 or bfloat16")
+        self.partial_dtype = partial_dtype
         self.E, self.rank, self.world = n_experts, rank, world
         self.epr = n_experts // world
         self.top_k, self.norm = top_k, bool(norm_topk_prob)
@@ -314,10 +320,11 @@ class CudaGatherEPOps:
         if ws is None or ws.numel() < nbytes:
             ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=rows.device)
             self._ws[Tt] = ws
-        y = torch.empty(Tt, H, dtype=torch.float32, device=rows.device)
+        y = torch.empty(Tt, H, dtype=self.partial_dtype, device=rows.device)
         probe = torch.empty(0, dtype=dtype, device=rows.device)
-        check(lib().moe_ep_partial_forward(
-            y.data_ptr(), rows.data_ptr(), rows.shape[1] // esz, _dtype_code(probe, "moe_ep"),
+        check(lib().moe_ep_partial_forward_typed(
+            y.data_ptr(), _dtype_code(y, "moe_ep"), rows.data_ptr(), rows.shape[1] // esz,
+            _dtype_code(probe, "moe_ep"),
             Tt, ctypes.byref(self.local.desc), ids.data_ptr(), wts.data_ptr(),
             self.rank * self.epr, row0, nrows, ws.data_ptr(), ws.numel(), self._stream(rows)))
         return y
@@ -327,8 +334,9 @@ class CudaGatherEPOps:
         T, H = mine.shape
         y = torch.empty(T, H, dtype=dtype, device=mine.device)
         res = None if residual is None else residual.to(dtype).contiguous()
-        check(lib().moe_ep_finish(y.data_ptr(), mine.data_ptr(),
-                                  None if shared is None else shared.data_ptr(),
-                                  None if res is None else res.data_ptr(),
-                                  _dtype_code(y, "moe_ep_finish"), T, H, self._stream(y)))
+        check(lib().moe_ep_finish_typed(y.data_ptr(), mine.data_ptr(),
+                                        _dtype_code(mine, "moe_ep_finish"),
+                                        None if shared is None else shared.data_ptr(),
+                                        None if res is None else res.data_ptr(),
+                                        _dtype_code(y, "moe_ep_finish"), T, H, self._stream(y)))
         return y

@@ -104,17 +104,21 @@ def test_simulated_ranks_match_single_block(nv, world, T):
                      what=f"rank {r} of {world}")
 
 
-@pytest.mark.parametrize("world,T", [(2, 64), (4, 100), (8, 512)])
-def test_gather_form_simulated_ranks_match_single_block(nv, world, T):
+@pytest.mark.parametrize("world,T,pdt", [(2, 64, torch.float32), (4, 100, torch.float32),
+                                         (8, 512, torch.float32), (2, 64, torch.bfloat16),
+                                         (8, 512, torch.bfloat16)])
+def test_gather_form_simulated_ranks_match_single_block(nv, world, T, pdt):
     """GatherEPBlock's steps for `world` ranks in one process: every rank's
-    partial over all gathered tokens (moe_ep_partial_forward, foreign experts
-    skipped), the reduce-scatter as a sum, moe_ep_finish with the shared
-    expert and the residual -- against the single-GPU block."""
+    partial over all gathered tokens (moe_ep_partial_forward_typed, foreign
+    experts skipped; f32 or bf16 partials), the reduce-scatter as a sum in the
+    partials' dtype, moe_ep_finish_typed with the shared expert and the
+    residual -- against the single-GPU block."""
     ep = importlib.import_module(PKG + ".ep")
     lag = importlib.import_module(PKG + ".laguna")
     block, raw = lag.random_sparse_layer(nv, seed=37, device=DEV)
     ops = [ep.CudaGatherEPOps(ep.local_slice(raw["routed"], r, world), raw["shared"],
-                              raw["router_w"], raw["router_b"], 256, r, world)
+                              raw["router_w"], raw["router_b"], 256, r, world,
+                              partial_dtype=pdt)
            for r in range(world)]
     g = torch.Generator(device=DEV).manual_seed(world)
     xs = [torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16) for _ in range(world)]
@@ -122,7 +126,8 @@ def test_gather_form_simulated_ranks_match_single_block(nv, world, T):
     routings = [ops[r].route(xs[r]) for r in range(world)]
     rows = torch.cat([ep.pack_tokens(xs[r], *routings[r]) for r in range(world)])
     partials = [ops[d].partial(rows, torch.bfloat16, d * T, T) for d in range(world)]
-    total = sum(partials)  # the reduce-scatter, all blocks at once
+    assert all(p.dtype == pdt for p in partials)
+    total = sum(partials)  # the reduce-scatter, all blocks at once (bf16: rounded per add)
     torch.cuda.synchronize()
     nv.device_status()
     for r in range(world):
