@@ -1203,7 +1203,8 @@ struct StackLayout {
 };
 
 // act / xb: the mma.sync stack; y32 / gu: the FP4 stack's f32 partials
-// ([2][kk][H] per segment, [2][2][kk][2][I] per K part, both by layer parity);
+// (per segment -- and, routed, per I block -- and [2][2][kk][2][I] per K part,
+// both by layer parity);
 // bar: grid-barrier / dependency counters; rbar: the routed stack's counters
 // followed by its exchange area (fs_xchg_u64 words, zeroed at each launch),
 // x32 its residual stream at launch boundaries ([2][H] f32, by parity).
@@ -1215,7 +1216,10 @@ StackLayout stack_layout(const moe_layer_desc* L0, int dtype_bytes) {
   S.xb1_off = align_up(S.xb0_off + (size_t)L0->hidden * dtype_bytes, 256);
   S.bar_off = align_up(S.xb1_off + (size_t)L0->hidden * dtype_bytes, 256);
   S.y32_off = align_up(S.bar_off + (2 + 2 * nvfp4::kStackMaxLayers) * sizeof(unsigned), 256);
-  S.gu_off = align_up(S.y32_off + 2 * (size_t)kk * L0->hidden * sizeof(float), 256);
+  // segment partials: [2][kk][H] for the given-routing stack, [2][kk][I / 64][H]
+  // (per I block of a CTA pair) for the routed one
+  S.gu_off = align_up(S.y32_off + 2 * (size_t)kk * (L0->inter / 64) * L0->hidden * sizeof(float),
+                      256);
   S.rbar_off = align_up(S.gu_off + 4 * (size_t)kk * 2 * L0->inter * sizeof(float), 256);
   S.x32_off = align_up(S.rbar_off + nvfp4::kFsCounters * sizeof(unsigned) +
                            nvfp4::fs_xchg_u64((int)L0->hidden, (int)L0->n_experts,
@@ -1239,9 +1243,9 @@ struct MapKey {
   const void* p;
   int64_t rows, K;
   int box;
-  bool scales;
+  int kind;
   bool operator==(const MapKey& o) const {
-    return p == o.p && rows == o.rows && K == o.K && box == o.box && scales == o.scales;
+    return p == o.p && rows == o.rows && K == o.K && box == o.box && kind == o.kind;
   }
 };
 struct MapCacheEntry {
@@ -1251,15 +1255,18 @@ struct MapCacheEntry {
 };
 thread_local std::vector<MapCacheEntry> t_map_cache;
 
+// kind 0: codes in 128-byte rows (K 256 per box), 1: scale bytes, 2: codes in
+// 32-byte rows (K 64 per box, the routed stack's down tiles).
 bool cached_map(size_t idx, CUtensorMap* out, const void* p, int64_t rows, int64_t K, int box,
-                bool scales) {
+                int kind) {
   if (t_map_cache.size() <= idx) t_map_cache.resize(idx + 1);
   MapCacheEntry& e = t_map_cache[idx];
-  const MapKey key{p, rows, K, box, scales};
+  const MapKey key{p, rows, K, box, kind};
   if (!e.valid || !(e.key == key)) {
     e.valid = false;
-    const cudaError_t r = scales ? nvfp4::map_scales(&e.map, p, rows, K, box)
-                                 : nvfp4::map_codes(&e.map, p, rows, K, box);
+    const cudaError_t r = kind == 1   ? nvfp4::map_scales(&e.map, p, rows, K, box)
+                          : kind == 2 ? nvfp4::map_codes_k64(&e.map, p, rows, K, box)
+                                      : nvfp4::map_codes(&e.map, p, rows, K, box);
     if (r != cudaSuccess) return false;
     e.key = key;
     e.valid = true;
@@ -1389,19 +1396,21 @@ int run_fp4_stack(const char* op, void* y, const void* x, int dtype, int64_t n_l
       const moe_layer_desc* Ll = &layers[l0 + li];
       CUtensorMap* m = &F.maps[li * mpl];
       const size_t c0 = cache0 + (size_t)(l0 + li) * 2 * nvfp4::kFsMapsRouted;
-      ok = ok && cached_map(c0 + 0, &m[0], Ll->gate.w, E * I, H, 64, false) &&
-           cached_map(c0 + 1, &m[1], Ll->gate.scales, E * I, H, 64, true) &&
-           cached_map(c0 + 2, &m[2], Ll->up.w, E * I, H, 64, false) &&
-           cached_map(c0 + 3, &m[3], Ll->up.scales, E * I, H, 64, true) &&
-           cached_map(c0 + 4, &m[4], Ll->down.w, E * H, I, 128, false) &&
-           cached_map(c0 + 5, &m[5], Ll->down.scales, E * H, I, 128, true);
+      // the routed stack's down tiles are K = 64 steps (its CTA pairs' I blocks)
+      const int dk = routed ? 2 : 0;
+      ok = ok && cached_map(c0 + 0, &m[0], Ll->gate.w, E * I, H, 64, 0) &&
+           cached_map(c0 + 1, &m[1], Ll->gate.scales, E * I, H, 64, 1) &&
+           cached_map(c0 + 2, &m[2], Ll->up.w, E * I, H, 64, 0) &&
+           cached_map(c0 + 3, &m[3], Ll->up.scales, E * I, H, 64, 1) &&
+           cached_map(c0 + 4, &m[4], Ll->down.w, E * H, I, 128, dk) &&
+           cached_map(c0 + 5, &m[5], Ll->down.scales, E * H, I, 128, 1);
       if (Is > 0)
-        ok = ok && cached_map(c0 + 6, &m[6], Ll->shared_gate.w, Is, H, 64, false) &&
-             cached_map(c0 + 7, &m[7], Ll->shared_gate.scales, Is, H, 64, true) &&
-             cached_map(c0 + 8, &m[8], Ll->shared_up.w, Is, H, 64, false) &&
-             cached_map(c0 + 9, &m[9], Ll->shared_up.scales, Is, H, 64, true) &&
-             cached_map(c0 + 10, &m[10], Ll->shared_down.w, H, I, 128, false) &&
-             cached_map(c0 + 11, &m[11], Ll->shared_down.scales, H, I, 128, true);
+        ok = ok && cached_map(c0 + 6, &m[6], Ll->shared_gate.w, Is, H, 64, 0) &&
+             cached_map(c0 + 7, &m[7], Ll->shared_gate.scales, Is, H, 64, 1) &&
+             cached_map(c0 + 8, &m[8], Ll->shared_up.w, Is, H, 64, 0) &&
+             cached_map(c0 + 9, &m[9], Ll->shared_up.scales, Is, H, 64, 1) &&
+             cached_map(c0 + 10, &m[10], Ll->shared_down.w, H, I, 128, dk) &&
+             cached_map(c0 + 11, &m[11], Ll->shared_down.scales, H, I, 128, 1);
       nvfp4::FsLayer& d = F.layer[li];
       if (routed) {
         d.inds = inds_out ? inds_out[l0 + li] : nullptr;

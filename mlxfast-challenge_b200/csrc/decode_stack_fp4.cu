@@ -86,7 +86,7 @@ namespace {
 constexpr int kT = kFp4Terms;
 constexpr int kN = 16;                    // MMA N: term rows 0..3, rows 4..15 zero
 constexpr int kStages = 10;               // ring stages (8 in the routed stack)
-constexpr int stages(bool routed) { return routed ? 8 : kStages; }
+__host__ __device__ constexpr int stages(bool routed) { return routed ? 8 : kStages; }
 constexpr int kA = 128 * 128;             // weight codes of one slab (128 rows x K 256): 16 KB
 constexpr int kSA = 128 * 16;             // their scale bytes: 2 KB
 constexpr int kStage = kA + kSA;          // 18 KB, 1 KB multiple
@@ -96,10 +96,22 @@ constexpr int kThreads = 320;
 constexpr int kWarpTma = 0, kWarpMma = 1, kWarpChain0 = 6;  // warps 2-5: weight scales
 constexpr int kChain = 128;
 constexpr int kBarChain = 1;              // named barrier of the chain warps
-// accumulators: one per chain warp's K run (16 columns each), gate/up then down
-constexpr uint32_t kAccGU = 0, kAccD = 64, kSfa0 = 128, kSfaCols = 16;
-constexpr uint32_t kSfbx = kSfa0 + kStages * kSfaCols;  // x-term scales, then act-term scales
+// Tensor memory: gate/up accumulators (one per chain warp's K run, 16 columns
+// each), down accumulators (given routing: one per run; routed stack: one per
+// 128-row tile, up to 8), the weight scales of each ring stage, the x-term
+// scales, the act-term scales.
+constexpr uint32_t kAccGU = 0, kAccD = 64, kSfaCols = 16;
+__host__ __device__ constexpr uint32_t sfa0_of(bool routed) { return routed ? 192u : 128u; }
+__host__ __device__ constexpr uint32_t sfbx_of(bool routed) {
+  return sfa0_of(routed) + (uint32_t)stages(routed) * kSfaCols;
+}
 constexpr uint32_t kTmemCols = 512;
+// Routed stack down stage: up to 3 row tiles of 128 rows x K 64 (an I block):
+// codes 4 KB each (32-byte rows, 32-byte swizzle) at 4 KB * j, then their
+// scale bytes (16 per row, the four K steps around the block) at 12 KB + 2 KB * j.
+constexpr int kRTileCodes = 128 * 32, kRTileScales = 128 * 16, kRTilesPerStage = 3;
+constexpr int kRScales0 = kRTilesPerStage * kRTileCodes;
+static_assert(kRScales0 + kRTilesPerStage * kRTileScales <= kStage, "routed down stage");
 constexpr int kErrIndex = 2;
 // A wait that expired latches 1000 * (layer in the launch + 1) + site, site:
 // 41 TMA ring slot, 42 MMA x terms, 43 MMA gate/up stage, 44 MMA act terms,
@@ -108,7 +120,8 @@ constexpr int kErrIndex = 2;
 // K part's down items (previous layer), 52 the last layer's down items; routed
 // stack: 53 the layer's router reducers, 54 a row block's down items (the
 // reducer), 55 the TMA warp waiting for the layer's routing, 56 the reducers'
-// sums of squares (the norm), 57 a gate/up item's tagged inputs.
+// sums of squares (the norm), 57 a gate/up item's tagged inputs; the routed
+// stack's pairs: 50 the partner's gate/up partials.
 __host__ __device__ constexpr int fs_timeout(int l, int site) { return 1000 * (l + 1) + site; }
 constexpr long long kDrainBudget = 200000000LL;
 
@@ -165,6 +178,9 @@ struct FsSmem {
   float* wts;
   uint8_t* rsl;          // routed: [2][E <= 256][32] bf16, a reducer's router rows
   float* xs;             // routed: [32] the reducer's rows of x_{l+1}
+  float* gux;            // routed: [2][128] the pair's gate/up partials (K part 0, 1)
+  float* red;            // routed: [4][32] the reducer's quarter sums
+  uint64_t* guready;     // routed: the partner's partials have landed in gux
   volatile int* rlayer;  // routed: layers whose routing is in inds / wts
 };
 
@@ -204,6 +220,9 @@ __host__ __device__ inline size_t fs_carve(int H, int I, int L, bool routed, uin
   if (routed) {
     t.rsl = take((size_t)2 * 256 * kFsRedRows * 2, 128);
     t.xs = reinterpret_cast<float*>(take(kFsRedRows * 4, 16));
+    t.gux = reinterpret_cast<float*>(take(2 * 128 * 4, 16));
+    t.red = reinterpret_cast<float*>(take(4 * 32 * 4, 16));
+    t.guready = reinterpret_cast<uint64_t*>(take(8, 8));
     t.rlayer = reinterpret_cast<volatile int*>(take(4, 4));
   }
   if (S) *S = t;
@@ -227,9 +246,11 @@ __host__ __device__ inline size_t fs_carve(int H, int I, int L, bool routed, uin
 template <int V>
 __device__ __forceinline__ void make_terms(float (&v)[V], int ct, int K, int kb, uint8_t* sB,
                                            uint8_t* sSc, float* fac) {
+  static_assert(V == 2 || V == 4 || V == 8 || V == 16, "values per thread");
   constexpr int TPG = 16 / V;
   const int lane = ct & 31, cw = ct >> 5;
   const int k0 = kb + ct * V;
+  const bool in = k0 < K;  // threads past the row (all zeros) store nothing
   const int grp = k0 / 16;
   const int byte0 = (k0 & 255) >> 1;
   const int chunk = byte0 >> 4, within = byte0 & 15;
@@ -275,10 +296,13 @@ __device__ __forceinline__ void make_terms(float (&v)[V], int ct, int K, int kb,
       w[j >> 3] |= byte << (4 * (j & 7));
     }
     uint8_t* dst = slab + t * 128 + ((chunk ^ t) << 4) + within;
-    if constexpr (V == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
-    else if constexpr (V == 8) *reinterpret_cast<uint32_t*>(dst) = w[0];
-    else *reinterpret_cast<uint16_t*>(dst) = (uint16_t)w[0];
-    if (ct % TPG == 0) sSc[t * (K / 16) + grp] = (uint8_t)b;
+    if (in) {
+      if constexpr (V == 16) *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+      else if constexpr (V == 8) *reinterpret_cast<uint32_t*>(dst) = w[0];
+      else if constexpr (V == 4) *reinterpret_cast<uint16_t*>(dst) = (uint16_t)w[0];
+      else *dst = (uint8_t)w[0];  // V = 2: one byte per thread
+      if (ct % TPG == 0) sSc[t * (K / 16) + grp] = (uint8_t)b;
+    }
     if (lane == 0) fac[4 * cw + t] = f;
   }
   named_sync(kBarChain, kChain);
@@ -349,6 +373,49 @@ __device__ __forceinline__ void load_segment_sum(const float* Yp, int H, int kk,
         v[4 * f + 3] += b[q][f].w;
       }
   }
+}
+
+// ---- routed stack: CTA pairs (clusters of 2) ----
+// The partner CTA's shared-memory address of this CTA's smem address a.
+__device__ __forceinline__ uint32_t peer_smem(uint32_t a, uint32_t peer) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(peer));
+  return r;
+}
+__device__ __forceinline__ void st_peer_f32(uint32_t a, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+// One arrival on a barrier in the partner's shared memory, ordering this
+// thread's earlier stores to the partner first.
+__device__ __forceinline__ void mbar_arrive_peer(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n"
+      ".reg .pred p;\n"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      "selp.u32 %0, 1, 0, p;\n"
+      "}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity,
+                                                          long long budget) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait_cluster(bar, parity))
+    if (clock64() - start > budget) return false;
+  return true;
+}
+// Every thread of both CTAs of the pair.
+__device__ __forceinline__ void cluster_sync_fs() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
 }
 
 // ---- routed stack: router rows, logit partials, routing ----
@@ -641,19 +708,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int H = a.H, I = a.I;  // H = 128 VX nks, I = 128 VA (checked on the host)
   FsSmem S;
   fs_carve(H, I, a.L, ROUTED, base, &S);
+  constexpr uint32_t kSfa0 = sfa0_of(ROUTED), kSfbx = sfbx_of(ROUTED);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, c = blockIdx.x;
   const int nb = I / 64;
   const int nGU = a.kk * nb * a.nks;
   const int nD = a.kk * (H / 128);
-  const bool has_gu = c < nGU, has_d = c < nD;
+  const bool has_gu = c < nGU;
   const int gu_seg = has_gu ? c / (nb * a.nks) : 0;
   const int gu_rem = c - gu_seg * nb * a.nks;
   const int gu_b = gu_rem / a.nks, gu_p = gu_rem - (gu_rem / a.nks) * a.nks;
   const int KS = H / 256 / a.nks;  // K slabs of a gate/up item
-  const int d_seg = has_d ? c / (H / 128) : 0;
+  // Given routing: down item (segment, 128-row block d_rb) over all of I.
+  // Routed stack: the CTA pair (cluster of 2) of one (segment, I block gu_b)
+  // computes gate/up over its two K halves, exchanges the partials through
+  // distributed shared memory, and each CTA computes the down projection of
+  // the block's 64 act values for its half of H (DT tiles of 128 rows x K 64).
+  const bool has_d = ROUTED ? has_gu : c < nD;
+  const int d_seg = ROUTED ? gu_seg : (has_d ? c / (H / 128) : 0);
   const int d_rb = c - d_seg * (H / 128);
-  const int DS = I / 256;          // K slabs of a down item
+  const int DT = H / 256;
+  const int DS = ROUTED ? (DT + kRTilesPerStage - 1) / kRTilesPerStage : I / 256;
   const uint32_t kSfba = kSfbx + (uint32_t)(H / 16);
 
   if (threadIdx.x == 0) {
@@ -667,6 +742,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(S.gufull, 1);
     mbar_init(S.dfull, 1);
     mbar_init(S.drain, 1);
+    if (ROUTED) mbar_init(S.guready, kChain);  // the partner's chain threads, one arrival each
     *S.hold = 0;
     *S.cur = 0;
     if (ROUTED) *S.rlayer = 0;
@@ -690,6 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if constexpr (ROUTED) cluster_sync_fs();  // the partner's barriers exist before any arrival
   const uint32_t tmem = *S.tslot;
 
   if (warp == kWarpTma) {
@@ -786,20 +863,46 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         const CUtensorMap* m = sh ? mp + kFsMapsRouted : mp;
-        const int row0 = (sh ? 0 : (int)e * H) + d_rb * 128;
-        for (int sl = 0; sl < DS; sl++, g++) {
-          int s;
-          if (!slot(s, l)) {
-            ok = false;
-            break;
+        if (ROUTED) {
+          // this CTA's half of H, K = the pair's I block: row tiles of 128 x 64
+          // codes (32-byte rows), their scale bytes with the block's neighbours
+          const int row0 = (sh ? 0 : (int)e * H) + gu_p * (H / 2);
+          for (int sl = 0; sl < DS; sl++, g++) {
+            int s;
+            if (!slot(s, l)) {
+              ok = false;
+              break;
+            }
+            if (el) {
+              uint8_t* st = S.stage + (size_t)s * kStage;
+              const int t0 = sl * kRTilesPerStage;
+              const int nt = DT - t0 < kRTilesPerStage ? DT - t0 : kRTilesPerStage;
+              mbar_arrive_expect_tx(&S.full[s], (uint32_t)(nt * (kRTileCodes + kRTileScales)));
+              for (int j = 0; j < nt; j++) {
+                const int rr = row0 + (t0 + j) * 128;
+                tma_load_2d(st + j * kRTileCodes, m + 4, gu_b * 32, rr, &S.full[s]);
+                tma_load_2d(st + kRScales0 + j * kRTileScales, m + 5, (gu_b / 4) * 16, rr,
+                            &S.full[s]);
+              }
+            }
+            __syncwarp();
           }
-          if (el) {
-            uint8_t* st = S.stage + (size_t)s * kStage;
-            mbar_arrive_expect_tx(&S.full[s], (uint32_t)kStage);
-            tma_load_2d(st, m + 4, sl * 128, row0, &S.full[s]);
-            tma_load_2d(st + kA, m + 5, sl * 16, row0, &S.full[s]);
+        } else {
+          const int row0 = (sh ? 0 : (int)e * H) + d_rb * 128;
+          for (int sl = 0; sl < DS; sl++, g++) {
+            int s;
+            if (!slot(s, l)) {
+              ok = false;
+              break;
+            }
+            if (el) {
+              uint8_t* st = S.stage + (size_t)s * kStage;
+              mbar_arrive_expect_tx(&S.full[s], (uint32_t)kStage);
+              tma_load_2d(st, m + 4, sl * 128, row0, &S.full[s]);
+              tma_load_2d(st + kA, m + 5, sl * 16, row0, &S.full[s]);
+            }
+            __syncwarp();
           }
-          __syncwarp();
         }
       }
     }
@@ -867,6 +970,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if (ROUTED) {
+            // one K = 64 step per 128-row tile: tile t into accumulator t
+            if (el) {
+              const uint32_t sa = smem_u32(S.stage + (size_t)s * kStage);
+              const int t0 = sl * kRTilesPerStage;
+              const int nt = DT - t0 < kRTilesPerStage ? DT - t0 : kRTilesPerStage;
+              for (int j = 0; j < nt; j++)
+                umma_mxf4nvf4(tmem + kAccD + 16 * (uint32_t)(t0 + j),
+                              smem_desc_sw32(sa + (uint32_t)(j * kRTileCodes)),
+                              smem_desc_sw128(sba), idesc,
+                              tmem + kSfa0 + (uint32_t)s * kSfaCols + 4u * (uint32_t)j,
+                              tmem + kSfba, 0u);
+              umma_commit(&S.empty[s]);
+            }
+            __syncwarp();
+            continue;
+          }
           if (el) {
             const uint32_t sa = smem_u32(S.stage + (size_t)s * kStage);
             const uint32_t sb = sba + (uint32_t)(sl * kBSlab);
@@ -906,17 +1026,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        const uint8_t* sf = S.stage + (size_t)s * kStage + kA;
-        uint32_t ra[16];
+        if (ROUTED && i >= KS) {
+          // routed down stage: per tile, the I block's K step (4 scale bytes)
+          // of each row, columns 4 j .. 4 j + 3 of the stage's scale columns
+          const int t0 = (i - KS) * kRTilesPerStage;
+          const int nt = DT - t0 < kRTilesPerStage ? DT - t0 : kRTilesPerStage;
+          const uint8_t* sf = S.stage + (size_t)s * kStage + kRScales0 + 4 * (gu_b & 3);
+          for (int j = 0; j < nt; j++) {
+            uint32_t ra[4];
 #pragma unroll
-        for (int cq = 0; cq < 4; cq++) {
-          const uint4 va = *reinterpret_cast<const uint4*>(sf + 16 * (lane + 32 * cq));
-          ra[0 + cq] = va.x;
-          ra[4 + cq] = va.y;
-          ra[8 + cq] = va.z;
-          ra[12 + cq] = va.w;
+            for (int cq = 0; cq < 4; cq++)
+              ra[cq] = *reinterpret_cast<const uint32_t*>(sf + j * kRTileScales +
+                                                          16 * (lane + 32 * cq));
+            tmem_st4(tmem + lane_base + kSfa0 + (uint32_t)s * kSfaCols + 4u * (uint32_t)j, ra);
+          }
+        } else {
+          const uint8_t* sf = S.stage + (size_t)s * kStage + kA;
+          uint32_t ra[16];
+#pragma unroll
+          for (int cq = 0; cq < 4; cq++) {
+            const uint4 va = *reinterpret_cast<const uint4*>(sf + 16 * (lane + 32 * cq));
+            ra[0 + cq] = va.x;
+            ra[4 + cq] = va.y;
+            ra[8 + cq] = va.z;
+            ra[12 + cq] = va.w;
+          }
+          tmem_st16(tmem + lane_base + kSfa0 + (uint32_t)s * kSfaCols, ra);
         }
-        tmem_st16(tmem + lane_base + kSfa0 + (uint32_t)s * kSfaCols, ra);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -929,7 +1065,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;                         // TMEM lane quarter
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     const int r = 32 * q + lane;                    // accumulator row = TMEM lane
-    uint32_t jgu = 0, jd = 0;
+    uint32_t jgu = 0, jd = 0, jpair = 0;
     // Dependency counters (zero at launch): cnt1[seg] counts the gate/up items
     // of segment seg done (nb * nks per layer); cnt2[p] the down items whose
     // rows lie in K part p done (kk * H / 128 / nks per layer) -- in the
@@ -1031,7 +1167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int l = 0; l < a.L && alive; l++) {
       const int lg = a.l0 + l;  // index in the stack: buffer parity
-      float* Yout = a.Yp + (size_t)(lg & 1) * a.kk * H;
+      float* Yout = a.Yp + (size_t)(lg & 1) * a.kk * (ROUTED ? nb : 1) * H;
       const float* Yin = a.Yp + (size_t)((lg + 1) & 1) * a.kk * H;
       float* GUb = a.GUp + (size_t)(lg & 1) * 2 * a.kk * 2 * I;
       if (ct == 0) *S.cur = l;
@@ -1152,18 +1288,88 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float y = fold_runs(tmem + lane_base + kAccGU, S.facx);
         tc_fence_before();
-        __stcg(GUb + ((size_t)(gu_p * a.kk + gu_seg) * 2 + (r >> 6)) * I + gu_b * 64 + (r & 63), y);
-        if (a.test_skip_release && l == a.L - 1 && gu_seg == 0) {
+        if (ROUTED) {
+          // the pair exchange: this K part's partial of accumulator row r into
+          // gux[gu_p][r] of both CTAs, then one arrival on the partner's barrier
+          // (test-only NVFP4_LAUNCH_TEST_EXPIRE: the last layer's segment 0
+          // never sends, so the partner's wait runs out and reports its site)
+          S.gux[gu_p * 128 + r] = y;
+          if (!(a.test_skip_release && l == a.L - 1 && gu_seg == 0)) {
+            const uint32_t peer = (uint32_t)(gu_p ^ 1);
+            st_peer_f32(peer_smem(smem_u32(&S.gux[gu_p * 128 + r]), peer), y);
+            mbar_arrive_peer(peer_smem(smem_u32(S.guready), peer));
+          }
+        } else if (a.test_skip_release && l == a.L - 1 && gu_seg == 0) {
+          __stcg(GUb + ((size_t)(gu_p * a.kk + gu_seg) * 2 + (r >> 6)) * I + gu_b * 64 + (r & 63), y);
           // test-only (NVFP4_LAUNCH_TEST_EXPIRE): this release is never made,
           // so the waits behind it run out and report their site
           named_sync(kBarChain, kChain);
         } else {
+          __stcg(GUb + ((size_t)(gu_p * a.kk + gu_seg) * 2 + (r >> 6)) * I + gu_b * 64 + (r & 63), y);
           signal_count(&cnt1[gu_seg]);
         }
       }
 
       // ---- phase B: act terms, down item -> Yp ----
-      if (has_d) {
+      if (has_d && ROUTED) {
+        // the partner's partials of this layer (one arrival per chain thread);
+        // the barrier below also publishes this CTA's own rows of gux
+        const bool gotp = mbar_wait_cluster_bounded(S.guready, jpair & 1, a.budget);
+        jpair++;
+        if (!gotp && ct == 0) fsflag(fs_timeout(l, 50));
+        alive = chain_sync_and(gotp);
+        if (!alive) break;
+        // the block's 64 act values, two per thread of the first warp (the
+        // other warps hold zeros and store nothing): silu(gate) * up, the K
+        // parts summed in order
+        float v2[2] = {0.f, 0.f};
+        if (ct < 32) {
+#pragma unroll
+          for (int j = 0; j < 2; j++) {
+            const int i = 2 * ct + j;
+            v2[j] = silu_ref(S.gux[i] + S.gux[128 + i]) * (S.gux[64 + i] + S.gux[192 + i]);
+          }
+        }
+        if (ct == 0) *S.hold = 0;
+        make_terms<2>(v2, ct, 64, 0, S.ba, S.sca, S.faca);
+        store_term_scales(S.sca, 64, 0, 8, tmem + lane_base + kSfba, lane);
+        fence_proxy_async();
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (ct == 0) *S.hold = 1;
+        if (lane == 0) mbar_arrive(S.aready);
+        const bool got = mbar_wait_bounded(S.dfull, jd & 1, a.budget);
+        jd++;
+        if (!got && lane == 0) fsflag(fs_timeout(l, 49));
+        alive = chain_sync_and(got);
+        if (!alive) break;
+        tc_fence_after();
+        const float wseg = d_seg < a.k ? S.wts[l * 16 + d_seg] * a.scaling : 1.0f;
+        // tile t of this CTA's half of H: rows gu_p * H / 2 + 128 t + r; every
+        // tile's accumulator row read before one wait
+        float* Yb = Yout + ((size_t)d_seg * nb + gu_b) * H + gu_p * (H / 2);
+        uint32_t dt[8][4];
+#pragma unroll
+        for (int t = 0; t < 8; t++)
+          if (t < DT)
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(dt[t][0]), "=r"(dt[t][1]), "=r"(dt[t][2]), "=r"(dt[t][3])
+                         : "r"(tmem + lane_base + kAccD + 16u * (uint32_t)t)
+                         : "memory");
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 8; t++)
+          if (t < DT) {
+            float y = 0.f;
+#pragma unroll
+            for (int tt = 0; tt < kT; tt++) y += S.faca[tt] * __uint_as_float(dt[t][tt]);
+            __stcg(Yb + t * 128 + r, y * wseg);
+          }
+        tc_fence_before();
+        named_sync(kBarChain, kChain);
+        if (ct < DT) red_release_add_fs(&cnt2[gu_p * DT + ct], 1u);  // the half's row blocks
+      } else if (has_d) {
         if (!wait_count(&cnt1[d_seg], (unsigned)(l + 1) * per_seg, l, 50)) {
           alive = false;
           break;
@@ -1212,25 +1418,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float y = fold_runs(tmem + lane_base + kAccD, S.faca) * wseg;
         tc_fence_before();
         __stcg(Yout + (size_t)d_seg * H + d_rb * 128 + r, y);
-        signal_count(ROUTED ? &cnt2[d_rb] : &cnt2[d_rb / rb_per_part]);
+        signal_count(&cnt2[d_rb / rb_per_part]);
       }
 
       // ---- routed stack, reducer: h_{l+1} for its rows, then layer l+1's input ----
       if (is_red) {
-        if (!wait_count(&cnt2[red_r0 / 128], (unsigned)(l + 1) * a.kk, l, 54)) {
+        // every (segment, I block) partial of the reducer's rows: thread ct
+        // sums row ct % 32 over the segments and the I blocks of quarter
+        // ct / 32 (in that order, all loads in flight), the four quarters then
+        // in order
+        if (!wait_count(&cnt2[red_r0 / 128], (unsigned)(l + 1) * a.kk * nb, l, 54)) {
           alive = false;
           break;
         }
+        {
+          constexpr int BQ = VA / 2;  // I blocks of a quarter (nb / 4)
+          const int qq = ct >> 5;
+          const float* src = Yout + (size_t)(qq * BQ) * H + red_r0 + (ct & 31);
+          float part[kFsMaxSeg][BQ];
+#pragma unroll
+          for (int sg = 0; sg < kFsMaxSeg; sg++)
+#pragma unroll
+            for (int bb = 0; bb < BQ; bb++)
+              part[sg][bb] = sg < a.kk ? __ldcg(src + ((size_t)sg * nb + bb) * H) : 0.f;
+          float acc = 0.f;
+#pragma unroll
+          for (int sg = 0; sg < kFsMaxSeg; sg++)
+#pragma unroll
+            for (int bb = 0; bb < BQ; bb++)
+              if (sg < a.kk) acc += part[sg][bb];
+          S.red[ct] = acc;
+        }
+        named_sync(kBarChain, kChain);
         if (ct < kFsRedRows) {
           const int row = red_r0 + ct;
-          float part[16];
-#pragma unroll
-          for (int sg = 0; sg < 16; sg++)
-            part[sg] = sg < a.kk ? __ldcg(Yout + (size_t)sg * H + row) : 0.f;
-          float v = 0.f;
-#pragma unroll
-          for (int sg = 0; sg < 16; sg++)
-            if (sg < a.kk) v += part[sg];
+          float v = ((S.red[ct] + S.red[32 + ct]) + S.red[64 + ct]) + S.red[96 + ct];
           if (a.residual) v += hrow;
           hrow = round_to(v, a.dtype);
           if (l == a.L - 1) {
@@ -1258,6 +1480,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
+  // the partner may still write into this CTA's shared memory until it is done
+  if constexpr (ROUTED) cluster_sync_fs();
   if (warp == kWarpMma) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -1304,8 +1528,17 @@ bool decode_stack_fp4_supported(int H, int I, int kk, int sms, bool routed) {
   if (I != 512 && I != 1024 && I != 2048) return false;
   if (kk < 1 || kk > 16 || kk * (H / 128) > sms) return false;  // one down item per CTA
   if (decode_stack_fp4_nks(I, kk, sms) == 0) return false;      // one gate/up item per CTA
-  if (routed && H / kFsRedRows > sms - 1) return false;  // one reducer per CTA, the router apart
-  if (kSfbx + (uint32_t)(H / 16 + I / 16) > kTmemCols) return false;
+  if (routed) {
+    // CTA pairs: both K halves of every (segment, I block), the last pair of
+    // the grid (the router's) without an item; one reducer per CTA
+    const int G = sms & ~1;
+    if (kk > kFsMaxSeg || decode_stack_fp4_nks(I, kk, sms) != 2 || 2 * kk * (I / 64) > G - 2 ||
+        H / kFsRedRows > G - 1)
+      return false;
+    if (sfbx_of(true) + (uint32_t)(H / 16 + 32) > kTmemCols) return false;
+  } else if (sfbx_of(false) + (uint32_t)(H / 16 + I / 16) > kTmemCols) {
+    return false;
+  }
   return decode_stack_fp4_smem_bytes(H, I, kFsMaxLayers, routed) <= 227 * 1024;
 }
 
@@ -1327,14 +1560,37 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
   if (decode_stack_fp4_nks(a.I, a.kk, sms) != a.nks || a.kk * (a.H / 128) > sms ||
-      (a.routed && a.H / kFsRedRows > sms - 1))
+      !decode_stack_fp4_supported(a.H, a.I, a.kk, sms, a.routed != 0))
     return cudaErrorInvalidValue;
+  // The routed stack runs as CTA pairs (clusters of 2) over an even grid.
+  const int grid = a.routed ? (sms & ~1) : sms;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.routed ? 2 : 1;
   // Every CTA must be resident (CTAs wait on one another's counters): one per
-  // SM, cooperative launch.
-  int per_sm = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
-  if (e != cudaSuccess) return e;
-  if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+  // SM (every pair co-scheduled), cooperative launch.
+  if (a.routed) {
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess) return e;
+    if (2 * clusters < grid) return cudaErrorCooperativeLaunchTooLarge;
+  } else {
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+  }
   // dependency counters, and (routed) the exchange area behind them
   const size_t zero = kFsCounters * sizeof(unsigned) +
                       (a.routed ? fs_xchg_u64(a.H, a.E, a.L) * sizeof(unsigned long long) : 0);
@@ -1343,16 +1599,6 @@ cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   e = cudaMemsetAsync(a.bar, 0, zero, stream);
   if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)sms);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeCooperative;
-  attr.val.cooperative = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
   void* args[] = {const_cast<FsArgs*>(&a)};
   e = cudaLaunchKernelExC(&cfg, kern, args);
   if (e != cudaSuccess) return e;

@@ -101,6 +101,9 @@ struct alignas(64) GemmArgs {
 // driver entry point).  rows: rows of the whole bank / activation matrix.
 cudaError_t map_codes(CUtensorMap* m, const void* w, int64_t rows, int64_t K, int box_rows);
 cudaError_t map_scales(CUtensorMap* m, const void* s, int64_t rows, int64_t K, int box_rows);
+// Codes of K = 64 steps (32-byte rows, 32-byte swizzle): the routed decode
+// stack's down tiles.
+cudaError_t map_codes_k64(CUtensorMap* m, const void* w, int64_t rows, int64_t K, int box_rows);
 cudaError_t map_rows16(CUtensorMap* m, const void* b, bool bf16, int64_t rows, int64_t K,
                        int64_t ld);
 
@@ -165,6 +168,7 @@ constexpr int kFsRedRows = 32;
 constexpr int kFsLgStride = 16;  // u64 per logit accumulator (one 128-byte line)
 constexpr int kFsCounters = 64;  // cnt1[16] gate/up items per segment, cnt2[16] down items
 constexpr int kFsMaxReducers = 64;
+constexpr int kFsMaxSeg = 9;  // routed stack: top_k <= 8 routed segments + the shared expert
 // Routed stack exchange area, zeroed at every launch (its values carry their
 // own completion: counts or layer tags), laid out after the counters:
 //   routing lines  [kFsMaxLayers][8] u64

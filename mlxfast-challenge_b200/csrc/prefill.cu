@@ -814,6 +814,11 @@ cudaError_t map_codes(CUtensorMap* m, const void* w, int64_t rows, int64_t K, in
                    (uint64_t)K / 2, 128, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+cudaError_t map_codes_k64(CUtensorMap* m, const void* w, int64_t rows, int64_t K, int box_rows) {
+  return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)rows,
+                   (uint64_t)K / 2, 32, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
 cudaError_t map_scales(CUtensorMap* m, const void* s, int64_t rows, int64_t K, int box_rows) {
   return encode_2d(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, s, (uint64_t)K / 16, (uint64_t)rows,
                    (uint64_t)K / 16, 16, (uint32_t)box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);

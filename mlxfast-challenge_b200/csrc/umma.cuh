@@ -45,6 +45,16 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
          ((uint64_t)(1024u >> 4) << 32) | ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
 
+// K-major operand tile in the 32-byte swizzle layout: rows of 32 bytes (one
+// K = 64 step of E2M1 codes), 8-row x 32-byte atoms (16-byte chunk index XOR
+// bit 2 of the row, the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_32B),
+// atoms stacked along M every 256 bytes: SBO>>4 = 256>>4, LBO ignored (1),
+// version 1, base offset 0 (atoms 256-byte aligned), layout type 6 (SWIZZLE_32B).
+__device__ __forceinline__ uint64_t smem_desc_sw32(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) |
+         ((uint64_t)(256u >> 4) << 32) | ((uint64_t)1u << 46) | ((uint64_t)6u << 61);
+}
+
 // Instruction descriptor, kind::f16: D f32, A and B f16, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) |
@@ -138,6 +148,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
       "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
+}
+
+// 32 lanes x 32 bits, 4 consecutive columns.  Completion: tmem_wait_st().
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const uint32_t (&v)[4]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3])
+               : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_st() {

@@ -76,6 +76,21 @@ def assert_close(got, want, max_abs=MAX_ABS, rel_l2=REL_L2, what=""):
     assert ma <= max_abs and rl <= rel_l2, f"{what}: max_abs={ma:.3e} rel_l2={rl:.3e}"
 
 
+def assert_close_bf16_out(got, want, max_abs=MAX_ABS, rel_l2=REL_L2, what=""):
+    """assert_close for an output the path rounds to bf16 (the residual stream
+    of the decode stacks, |y| up to ~10): the max-abs bar plus one bf16 ulp of
+    the oracle value (2^-7 |want|), the rounding of an f32 result to bf16; the
+    relative-L2 bar unchanged."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    err = np.abs(got - want)
+    bound = max_abs + np.abs(want) * 2.0 ** -7
+    worst = float((err - bound).max(initial=-1.0))
+    _, rl = close_report(got, want)
+    assert worst <= 0 and rl <= rel_l2, (f"{what}: max excess over the bound {worst:.3e}, "
+                                         f"max_abs={err.max(initial=0.0):.3e} rel_l2={rl:.3e}")
+
+
 def check_routing(orc, x_bits, G_bits, bias, inds, wts, k):
     """GPU routing [T, k] against the oracle router (Laguna.swift:165-180) on the
     same x (bf16 bits [T, H]).  The GPU sums the logits in another order than

@@ -24,7 +24,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import PKG, assert_close, check_routing
+from conftest import PKG, assert_close, assert_close_bf16_out, check_routing
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -38,10 +38,11 @@ def bf16_bits(t):
     return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-def make_layers(nv, n, n_experts=256, with_shared=True, seed=700, hidden=2048, inter=512):
+def make_layers(nv, n, n_experts=256, with_shared=True, seed=700, hidden=2048, inter=512,
+                top_k=8):
     lag = importlib.import_module(PKG + ".laguna")
     cfg = lag.LagunaMoEConfig(n_experts=n_experts, hidden=hidden, inter=inter,
-                              shared_inter=inter)
+                              shared_inter=inter, top_k=top_k)
     made = [lag.random_sparse_layer(nv, seed=seed + l, device=DEV, cfg=cfg, n_experts=n_experts,
                                     with_shared=with_shared) for l in range(n)]
     return [m[0] for m in made], [m[1] for m in made]
@@ -109,7 +110,7 @@ def check_stack(nv, orc, blocks, raws, x0, residual=True, norm=True):
                                       banks_np(raws[l]["routed"]),
                                       banks_np(raws[l]["shared"]) if raws[l]["shared"] else None,
                                       scaling=2.5, residual=hl if residual else None)
-        assert_close(hs[l + 1].float().cpu().numpy(), want, what=f"layer {l}")
+        assert_close_bf16_out(hs[l + 1].float().cpu().numpy(), want, what=f"layer {l}")
     nv.device_status()  # raises on a latched index error or expired wait
     return y_full, routing
 
@@ -150,10 +151,13 @@ def test_routed_stack_across_launches_plain(nv, orc):
     check_stack(nv, orc, blocks, raws, x0, residual=False, norm=False)
 
 
-@pytest.mark.parametrize("hidden,inter,shared", [(1024, 512, False), (2048, 1024, True)])
-def test_routed_stack_other_shapes(nv, orc, hidden, inter, shared):
+@pytest.mark.parametrize("hidden,inter,shared,top_k", [(1024, 512, False, 8),
+                                                       (2048, 1024, True, 3)])
+def test_routed_stack_other_shapes(nv, orc, hidden, inter, shared, top_k):
+    """Shapes the routed stack's CTA pairs take besides Laguna's: hidden 1024
+    (4 row tiles per CTA of a pair), inter 1024 (16 I blocks per segment)."""
     blocks, raws = make_layers(nv, 3, n_experts=128, with_shared=shared, seed=1100,
-                               hidden=hidden, inter=inter)
+                               hidden=hidden, inter=inter, top_k=top_k)
     g = torch.Generator(device=DEV).manual_seed(3)
     x0 = torch.randn(1, hidden, generator=g, device=DEV).to(torch.bfloat16)
     check_stack(nv, orc, blocks, raws, x0)
@@ -226,3 +230,7 @@ def test_routed_stack_rejects(nv):
     with nv.launch_flags(exact_decode=True):
         assert lib.moe_decode_stack_routed_launches(
             (nv._lib.MoeLayerDesc * 1)(blocks[0].desc), 1) == 0
+    # inter 1024 with top-8 and a shared expert: 9 x 16 I blocks do not fit
+    # the grid as CTA pairs (the per-layer calls run it)
+    wide, _ = make_layers(nv, 1, n_experts=64, seed=1600, inter=1024)
+    assert lib.moe_decode_stack_routed_launches((nv._lib.MoeLayerDesc * 1)(wide[0].desc), 1) == 0
