@@ -454,6 +454,7 @@ struct Xchg {
   unsigned long long* rt;   // [kFsMaxLayers][8]: layer l's routing, slot j tagged l + 1
   unsigned long long* xin;  // [2][H / 2]: the layer inputs, two values per word, tagged
   unsigned long long* sq;   // [kFsMaxLayers][kFsMaxReducers]: sums of squares, tagged
+  unsigned long long* ys;   // [L][H][kFsYsStride]: counted layer-output sums (norm on)
   unsigned long long* lg;   // [L][E][kFsLgStride]: counted logit sums
 };
 __device__ __forceinline__ Xchg xchg(const FsArgs& a) {
@@ -461,7 +462,8 @@ __device__ __forceinline__ Xchg xchg(const FsArgs& a) {
   x.rt = a.XG;
   x.xin = x.rt + (size_t)kFsMaxLayers * 8;
   x.sq = x.xin + (size_t)a.H;
-  x.lg = x.sq + (size_t)kFsMaxLayers * kFsMaxReducers;
+  x.ys = x.sq + (size_t)kFsMaxLayers * kFsMaxReducers;
+  x.lg = x.ys + (size_t)a.L * a.H * kFsYsStride;
   return x;
 }
 
@@ -487,21 +489,30 @@ __device__ __forceinline__ unsigned long long tagged(uint32_t tag, uint32_t payl
 }
 __device__ __forceinline__ uint32_t tag_of(unsigned long long w) { return (uint32_t)(w >> 48); }
 
-// Counted logit partials: each reducer adds (q << 16) + (bad << 8) + 1 with q
-// its partial in 2^-28 units; bits 7..0 count the adds (complete at nR), bits
-// 15..8 the partials that were not finite or beyond 2^13 in magnitude (the
-// logit is then NaN), bits 63..16 the sum of q (|sum| < 2^47 for nR <= 64).
-// Integer sums do not depend on the order of the adds.
-constexpr float kLogitUnitInv = 268435456.0f, kLogitUnit = 3.7252902984619141e-09f;  // 2^28
-__device__ __forceinline__ void add_counted_logit(unsigned long long* line, float p) {
-  const bool ok = fabsf(p) < 8192.0f;
-  const long long q = ok ? __float2ll_rn(p * kLogitUnitInv) : 0ll;
+// Counted sums: each contributor adds (q << 16) + (bad << 8) + 1 with q its
+// value in 2^-F units; bits 7..0 count the adds, bits 15..8 the values that
+// were not finite or beyond 2^B in magnitude (the sum is then NaN), bits
+// 63..16 the sum of q (|sum| < 2^47 for fewer than 2^(47 - F - B) adds).
+// Integer sums do not depend on the order of the adds, so every run gives the
+// same bits.  Logits: F = 28, B = 13, 64 reducers; the routed stack's layer
+// outputs: F = 24, B = 16, kk * I / 64 <= 127 down items per row.
+template <int F, int B>
+__device__ __forceinline__ void add_counted(unsigned long long* p, float x) {
+  const bool ok = fabsf(x) < (float)(1 << B);
+  const long long q = ok ? __float2ll_rn(x * (float)(1ull << F)) : 0ll;
   const unsigned long long v = ((unsigned long long)q << 16) + (ok ? 1ull : 0x101ull);
-  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(line), "l"(v) : "memory");
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+template <int F>
+__device__ __forceinline__ float decode_counted(unsigned long long v) {
+  if ((v >> 8) & 0xFF) return __int_as_float(0x7fc00000);
+  return __ll2float_rn((long long)v >> 16) * (1.0f / (float)(1ull << F));
+}
+__device__ __forceinline__ void add_counted_logit(unsigned long long* line, float p) {
+  add_counted<28, 13>(line, p);
 }
 __device__ __forceinline__ float decode_counted_logit(unsigned long long v) {
-  if ((v >> 8) & 0xFF) return __int_as_float(0x7fc00000);
-  return __ll2float_rn((long long)v >> 16) * kLogitUnit;
+  return decode_counted<28>(v);
 }
 
 // Bounded poll by a whole warp: every lane's `n` words (in its registers
@@ -1358,17 +1369,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                          : "r"(tmem + lane_base + kAccD + 16u * (uint32_t)t)
                          : "memory");
         tmem_wait_ld();
+        // With the norm: each row's counted sum of the 2^-24 fixed-point
+        // partials (the count completes it, no counter hop); without: f32
+        // partials per (segment, I block) behind the row blocks' counters.
+        unsigned long long* ysl =
+            XC.ys + ((size_t)l * H + gu_p * (H / 2) + r) * kFsYsStride;
 #pragma unroll
         for (int t = 0; t < 8; t++)
           if (t < DT) {
             float y = 0.f;
 #pragma unroll
             for (int tt = 0; tt < kT; tt++) y += S.faca[tt] * __uint_as_float(dt[t][tt]);
-            __stcg(Yb + t * 128 + r, y * wseg);
+            if (a.has_norm) add_counted<24, 16>(ysl + (size_t)t * 128 * kFsYsStride, y * wseg);
+            else __stcg(Yb + t * 128 + r, y * wseg);
           }
         tc_fence_before();
         named_sync(kBarChain, kChain);
-        if (ct < DT) red_release_add_fs(&cnt2[gu_p * DT + ct], 1u);  // the half's row blocks
+        if (!a.has_norm && ct < DT) red_release_add_fs(&cnt2[gu_p * DT + ct], 1u);
       } else if (has_d) {
         if (!wait_count(&cnt1[d_seg], (unsigned)(l + 1) * per_seg, l, 50)) {
           alive = false;
@@ -1422,7 +1439,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // ---- routed stack, reducer: h_{l+1} for its rows, then layer l+1's input ----
-      if (is_red) {
+      if (is_red && a.has_norm) {
+        // the counted sums of the reducer's rows: complete when all kk * nb
+        // down items have added
+        bool got = true;
+        float vsum = 0.f;
+        if (ct < 32) {
+          const unsigned long long* p[1] = {XC.ys + ((size_t)l * H + red_r0 + ct) * kFsYsStride};
+          unsigned long long w[1] = {0ull};
+          const unsigned want = (unsigned)(a.kk * nb);
+          got = poll_words<1>(p, w, a.budget,
+                              [&](unsigned long long v) { return (unsigned)(v & 0xFF) == want; });
+          if (!got && lane == 0) fsflag(fs_timeout(l, 54));
+          vsum = decode_counted<24>(w[0]);
+        }
+        alive = chain_sync_and(got);
+        if (!alive) break;
+        if (ct < kFsRedRows) {
+          const int row = red_r0 + ct;
+          float v = vsum;
+          if (a.residual) v += hrow;
+          hrow = round_to(v, a.dtype);
+          if (l == a.L - 1) {
+            if (a.last) store_from_f32(a.y, a.dtype, row, hrow);
+            else __stcg(a.Hres + (size_t)((lg + 1) & 1) * H + row, hrow);  // next launch's h_0
+          }
+        }
+        if (l + 1 < a.L && !route_rows(l + 1)) {
+          alive = false;
+          break;
+        }
+      } else if (is_red) {
         // every (segment, I block) partial of the reducer's rows: thread ct
         // sums row ct % 32 over the segments and the I blocks of quarter
         // ct / 32 (in that order, all loads in flight), the four quarters then
@@ -1532,7 +1579,9 @@ bool decode_stack_fp4_supported(int H, int I, int kk, int sms, bool routed) {
     // CTA pairs: both K halves of every (segment, I block), the last pair of
     // the grid (the router's) without an item; one reducer per CTA
     const int G = sms & ~1;
+    // (kk * I / 64 <= 127: the counted layer-output sums stay below 2^47)
     if (kk > kFsMaxSeg || decode_stack_fp4_nks(I, kk, sms) != 2 || 2 * kk * (I / 64) > G - 2 ||
+        kk * (I / 64) > 127 ||
         H / kFsRedRows > G - 1)
       return false;
     if (sfbx_of(true) + (uint32_t)(H / 16 + 32) > kTmemCols) return false;

@@ -166,6 +166,7 @@ struct FsLayer {
 // adds their share of every expert's router logit.
 constexpr int kFsRedRows = 32;
 constexpr int kFsLgStride = 16;  // u64 per logit accumulator (one 128-byte line)
+constexpr int kFsYsStride = 4;   // u64 per layer-output accumulator (a 32-byte sector)
 constexpr int kFsCounters = 64;  // cnt1[16] gate/up items per segment, cnt2[16] down items
 constexpr int kFsMaxReducers = 64;
 constexpr int kFsMaxSeg = 9;  // routed stack: top_k <= 8 routed segments + the shared expert
@@ -174,10 +175,11 @@ constexpr int kFsMaxSeg = 9;  // routed stack: top_k <= 8 routed segments + the 
 //   routing lines  [kFsMaxLayers][8] u64
 //   layer inputs   [2][H / 2] u64 (by stack-layer parity)
 //   squares        [kFsMaxLayers][kFsMaxReducers] u64
+//   layer outputs  [L][H][kFsYsStride] u64: counted sums of the down partials (norm on)
 //   logits         [L][E][kFsLgStride] u64
 __host__ __device__ constexpr size_t fs_xchg_u64(int H, int E, int L) {
   return (size_t)kFsMaxLayers * 8 + (size_t)H + (size_t)kFsMaxLayers * kFsMaxReducers +
-         (size_t)L * E * kFsLgStride;
+         (size_t)L * H * kFsYsStride + (size_t)L * E * kFsLgStride;
 }
 struct alignas(64) FsArgs {
   CUtensorMap maps[kFsMaxMaps];  // layer l: maps[l * mpl + j]; j >= 6: the shared expert's
