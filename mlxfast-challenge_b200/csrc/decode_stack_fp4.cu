@@ -48,23 +48,33 @@
 // decoder layer's residual stream and RMSNorm around the block
 // (Laguna.swift:242-246: h_{l+1} = h_l + block_l(RMSNorm_l(h_l))).  Only the
 // shared expert's weights can stream ahead of the chain; a routed expert's
-// slabs go out the moment its layer's top-k is known.  The layer's output
-// reduction, the norm and the router's logits are the reducers' step:
-// reducer j (CTA j < H / 32) waits for the down items of its 32 rows, sums
-// their segment partials in segment order (+ the residual h_l), rounds to
-// the activation dtype -- h_{l+1} for those rows -- and, with the norm,
-// publishes the rows' f32 sum of squares as its tagged word of the layer,
-// reads every reducer's word and sums them in reducer order (the same bits on
-// every reducer), and forms x = dtype(dtype(h * rsqrt(mean + eps)) * w), the
-// reference's RMSNorm fallback (mlx/fast.cpp:90-108); x goes out as tagged
-// words (the gate/up items' input); then it adds x[rows] . G[e, rows] for
-// every expert e into the expert's counted logit sum (64-bit fixed point,
-// 2^-28 units, with an add count: integer sums do not depend on the order of
-// the adds, so every run gives the same bits).  The router CTA (the last
-// one) waits for the counts, rounds each logit to the activation dtype as the
-// reference's bf16 matmul does, selects the top-k (topk.cuh) and publishes the
-// layer's routing line; every CTA with an item of the layer reads it.  The
-// reducers' router rows are prefetched two layers ahead with cp.async.
+// slabs go out the moment its layer's top-k is known.
+//   Items: CTA pairs (clusters of 2).  The pair of (segment, I block b)
+// computes gate/up over its two K halves (one per CTA), swaps the partials
+// through distributed shared memory (remote stores and a remote mbarrier
+// arrival), and each CTA computes the down projection of the block's 64 act
+// values for its half of H: row tiles of 128 rows x K 64 (32-byte rows,
+// 32-byte swizzle), one MMA each.  A row of the layer output is then the sum
+// of kk * I / 64 partials.
+//   Reducers (CTA j < H / 32, 32 rows each): with the norm, every down item
+// adds its partials to one counted 64-bit fixed-point word per row (2^-24
+// units, with an add count: integer sums do not depend on the order of the
+// adds, so every run gives the same bits) and the reducer polls the word until
+// it is complete; without the norm, f32 partials per (segment, I block)
+// behind per-row-block counters, summed in a fixed order.  The reducer adds
+// the residual h_l and rounds to the activation dtype -- h_{l+1} for its rows
+// -- and, with the norm, publishes the rows' f32 sum of squares as its tagged
+// word of the layer, reads every reducer's word and sums them in reducer order
+// (the same bits on every reducer), and forms x = dtype(dtype(h * rsqrt(mean +
+// eps)) * w), the reference's RMSNorm fallback (mlx/fast.cpp:90-108); x goes
+// out as tagged words (the gate/up items' input); then it adds x[rows] .
+// G[e, rows] for every expert e into the expert's counted logit sum (2^-28
+// units).  The reducers' router rows are prefetched two layers ahead with
+// cp.async.
+//   Router: the last CTA, all its warps, no item: waits for the counts,
+// rounds each logit to the activation dtype as the reference's bf16 matmul
+// does, selects the top-k (topk.cuh) and publishes the layer's routing line;
+// every CTA with an item of the layer reads it.
 //
 // Roles (320 threads): warp 0 TMA (this CTA's weight slabs of layer l, l+1,
 // ... in consumption order into a 10-stage ring -- 8 in the routed stack, one
@@ -568,94 +578,80 @@ __device__ __forceinline__ void router_partials(const FsArgs& a, const FsSmem& S
     if (ct + 128 * h < a.E) add_counted_logit(lg + (size_t)(ct + 128 * h) * kFsLgStride, p[h]);
 }
 
-// The router CTA (no reducer: its router-row buffer is the scratch), all four
-// chain warps: warp w waits until all nR reducers have added to the logit
-// sums of experts 64 w + lane and 64 w + 32 + lane, rounds each logit to the
-// activation dtype as the reference's bf16 matmul returns it, scores it, and
-// ranks its two keys among the warp's 64 (the number of larger keys: keys are
-// distinct apart from 0, topk.cuh); keys of rank < k form the warp's sorted
-// list.  Warp 0 ranks the 32 list entries the same way, which gives the top k
-// in slot order, and publishes slot j (lane j < k) as tagged (expert id << 32
-// | weight bits) words of layer l's routing line, and into the layer's routing
-// outputs; weights / their sum in slot order.  Counting compares shared-memory
-// words instead of exchanging keys between lanes: no dependent chain of warp
-// shuffles.  Lanes of warp 0 end with their slot.
-__device__ __forceinline__ bool route_and_publish(const FsArgs& a, const FsSmem& S,
-                                                  const Xchg& X, int l, int ct, int nR,
-                                                  uint32_t& isel, float& wsel) {
-  const int w = ct >> 5, lane = ct & 31;
-  uint64_t* wkeys = reinterpret_cast<uint64_t*>(S.rsl) + w * 64;        // [4][64]
-  uint64_t* lists = reinterpret_cast<uint64_t*>(S.rsl + 2048);           // [4][8]
-  float* lscore = reinterpret_cast<float*>(S.rsl + 2048 + 256);          // [4][8]
-  uint64_t* skey = reinterpret_cast<uint64_t*>(S.rsl + 2048 + 384);      // [8] slots
-  float* sscore = reinterpret_cast<float*>(S.rsl + 2048 + 384 + 64);     // [8]
+// The router CTA, all its warps (it has no expert item): thread t < 256
+// waits until all nR reducers have added to the logit sum of expert t, rounds
+// the logit to the activation dtype as the reference's bf16 matmul returns
+// it, scores it and ranks its key among its warp's 32 (the number of larger
+// keys: keys are distinct apart from 0, topk.cuh); keys of rank < k form the
+// warp's sorted list.  Warps 0-1 rank the 8 warps' list entries (one each)
+// among all 64, which gives the top k in slot order; warp 0 publishes slot j
+// (lane j < k) as tagged (expert id << 32 | weight bits) words of layer l's
+// routing line, and into the layer's routing outputs; weights / their sum in
+// slot order.  Counting compares shared-memory words instead of exchanging
+// keys between lanes: no dependent chain of warp shuffles.
+__device__ __forceinline__ bool route_and_publish_cta(const FsArgs& a, const FsSmem& S,
+                                                      const Xchg& X, int l, int nR) {
+  constexpr int kW = 8;  // warps holding one expert per lane
+  const int t = threadIdx.x, w = t >> 5, lane = t & 31;
+  uint64_t* wkeys = reinterpret_cast<uint64_t*>(S.rsl);                 // [8][32]
+  uint64_t* lists = reinterpret_cast<uint64_t*>(S.rsl + 2048);          // [8][8]
+  float* lscore = reinterpret_cast<float*>(S.rsl + 2048 + 512);         // [8][8]
+  uint64_t* skey = reinterpret_cast<uint64_t*>(S.rsl + 2048 + 768);     // [8] slots
+  float* sscore = reinterpret_cast<float*>(S.rsl + 2048 + 768 + 64);    // [8]
+  int* okf = reinterpret_cast<int*>(S.rsl + 2048 + 768 + 96);
   const unsigned long long* lg = X.lg + (size_t)l * a.E * kFsLgStride;
   const float* b = a.layer[l].router_b;
-  const int e[2] = {64 * w + lane, 64 * w + 32 + lane};
-  float bias[2];
-  const unsigned long long* p[2];
-#pragma unroll
-  for (int i = 0; i < 2; i++) {
-    bias[i] = (b && e[i] < a.E) ? __ldg(b + e[i]) : 0.f;
-    p[i] = e[i] < a.E ? lg + (size_t)e[i] * kFsLgStride : nullptr;
-  }
-  if (lane < 8) {  // empty list entries and slots: no expert, score 0
-    lists[w * 8 + lane] = 0ull;
-    lscore[w * 8 + lane] = 0.f;
-    if (w == 0) {
-      skey[lane] = 0ull;
-      sscore[lane] = 0.f;
+  bool ok = true;
+  if (w < kW) {
+    if (lane < 8) {  // empty list entries and slots: no expert, score 0
+      lists[w * 8 + lane] = 0ull;
+      lscore[w * 8 + lane] = 0.f;
+      if (w == 0) {
+        skey[lane] = 0ull;
+        sscore[lane] = 0.f;
+      }
     }
-  }
-  unsigned long long wv[2] = {0ull, 0ull};
-  const bool ok =
-      poll_words<2>(p, wv, a.budget, [&](unsigned long long v) { return (int)(v & 0xFF) == nR; });
-  uint64_t t[2];
-  float sc[2];
-#pragma unroll
-  for (int i = 0; i < 2; i++) {
-    sc[i] = 0.f;
-    t[i] = 0ull;
-    if (p[i]) {
-      sc[i] = sigmoid_ref(round_to_dtype(decode_counted_logit(wv[i]), a.dtype));
-      t[i] = choice_key(sc[i] + bias[i], (uint32_t)e[i]);
+    if (t == 0) *okf = 1;
+    const bool live = t < a.E;
+    const float bias = (b && live) ? __ldg(b + t) : 0.f;
+    const unsigned long long* p[1] = {live ? lg + (size_t)t * kFsLgStride : nullptr};
+    unsigned long long wv[1] = {0ull};
+    ok = poll_words<1>(p, wv, a.budget, [&](unsigned long long v) { return (int)(v & 0xFF) == nR; });
+    float sc = 0.f;
+    uint64_t key = 0ull;
+    if (live) {
+      sc = sigmoid_ref(round_to_dtype(decode_counted_logit(wv[0]), a.dtype));
+      key = choice_key(sc + bias, (uint32_t)t);
     }
-  }
-  wkeys[lane] = t[0];
-  wkeys[32 + lane] = t[1];
-  __syncwarp();
-  int rc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};  // four counts per key: short add chains
-  const ulonglong2* wk = reinterpret_cast<const ulonglong2*>(wkeys);
+    wkeys[t] = key;
+    __syncwarp();
+    int rc[4] = {0, 0, 0, 0};
+    const ulonglong2* wk = reinterpret_cast<const ulonglong2*>(wkeys + w * 32);
 #pragma unroll
-  for (int j = 0; j < 32; j += 2) {
-    const ulonglong2 q0 = wk[j], q1 = wk[j + 1];
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-      rc[i][0] += (int)(q0.x > t[i]);
-      rc[i][1] += (int)(q0.y > t[i]);
-      rc[i][2] += (int)(q1.x > t[i]);
-      rc[i][3] += (int)(q1.y > t[i]);
+    for (int j = 0; j < 16; j += 2) {
+      const ulonglong2 q0 = wk[j], q1 = wk[j + 1];
+      rc[0] += (int)(q0.x > key);
+      rc[1] += (int)(q0.y > key);
+      rc[2] += (int)(q1.x > key);
+      rc[3] += (int)(q1.y > key);
     }
+    const int r = (rc[0] + rc[1]) + (rc[2] + rc[3]);
+    __syncwarp();  // the list entries' zeroing before the writes
+    if (key && r < a.k) {  // a key of 0 (no expert) leaves its entry empty
+      lists[w * 8 + r] = key;
+      lscore[w * 8 + r] = sc;
+    }
+    if (!ok && lane == 0) *okf = 0;
   }
-  const int r0 = (rc[0][0] + rc[0][1]) + (rc[0][2] + rc[0][3]);
-  const int r1 = (rc[1][0] + rc[1][1]) + (rc[1][2] + rc[1][3]);
-  // a key of 0 (no expert) ranks after every real key; its entry stays empty
-  if (t[0] && r0 < a.k) {
-    lists[w * 8 + r0] = t[0];
-    lscore[w * 8 + r0] = sc[0];
-  }
-  if (t[1] && r1 < a.k) {
-    lists[w * 8 + r1] = t[1];
-    lscore[w * 8 + r1] = sc[1];
-  }
-  const bool all_ok = chain_sync_and(ok);  // the lists visible to warp 0
-  if (w == 0) {
-    const uint64_t u = lists[lane];
-    const float us = lscore[lane];
+  __syncthreads();  // the eight lists visible to warps 0-1
+  const bool all_ok = *okf != 0;
+  if (w < 2) {
+    const uint64_t u = lists[t];
+    const float us = lscore[t];
     const ulonglong2* lk = reinterpret_cast<const ulonglong2*>(lists);
     int rq[4] = {0, 0, 0, 0};
 #pragma unroll
-    for (int j = 0; j < 16; j += 2) {
+    for (int j = 0; j < 32; j += 2) {
       const ulonglong2 q0 = lk[j], q1 = lk[j + 1];
       rq[0] += (int)(q0.x > u);
       rq[1] += (int)(q0.y > u);
@@ -667,31 +663,32 @@ __device__ __forceinline__ bool route_and_publish(const FsArgs& a, const FsSmem&
       skey[r] = u;
       sscore[r] = us;
     }
-    __syncwarp();
-    // slot scores for every lane (two vector loads), summed in slot order
-    const float4 s0 = reinterpret_cast<const float4*>(sscore)[0];
-    const float4 s1 = reinterpret_cast<const float4*>(sscore)[1];
-    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    float wsum = 0.f;
+    named_sync(2, 64);  // the slots written
+    if (w == 0) {
+      const float4 s0 = reinterpret_cast<const float4*>(sscore)[0];
+      const float4 s1 = reinterpret_cast<const float4*>(sscore)[1];
+      const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      float wsum = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) wsum += j < a.k ? sv[j] : 0.f;
-    const uint64_t key = lane < 8 ? skey[lane] : 0ull;
-    isel = key ? 0xFFFFFFFFu - (uint32_t)key : 0x7fffffffu;
-    wsel = lane < 8 ? sv[0] : 0.f;
+      for (int j = 0; j < 8; j++) wsum += j < a.k ? sv[j] : 0.f;
+      const uint64_t kk = lane < 8 ? skey[lane] : 0ull;
+      const uint32_t isel = kk ? 0xFFFFFFFFu - (uint32_t)kk : 0x7fffffffu;
+      float wsel = lane < 8 ? sv[0] : 0.f;
 #pragma unroll
-    for (int j = 1; j < 8; j++)
-      if (lane == j) wsel = sv[j];
-    if (a.norm) wsel = wsel / wsum;
-    if (lane < a.k) {
-      const uint32_t id16 = isel < 0xFFFFu ? isel : 0xFFFFu;
-      publish_u64(X.rt + (size_t)l * 8 + lane, tagged((uint32_t)(l + 1), 0u) |
-                                                   ((unsigned long long)id16 << 32) |
-                                                   __float_as_uint(wsel));
-      if (a.layer[l].inds) a.layer[l].inds[lane] = isel;
-      if (a.layer[l].wts) a.layer[l].wts[lane] = wsel;
+      for (int j = 1; j < 8; j++)
+        if (lane == j) wsel = sv[j];
+      if (a.norm) wsel = wsel / wsum;
+      if (lane < a.k) {
+        const uint32_t id16 = isel < 0xFFFFu ? isel : 0xFFFFu;
+        publish_u64(X.rt + (size_t)l * 8 + lane, tagged((uint32_t)(l + 1), 0u) |
+                                                     ((unsigned long long)id16 << 32) |
+                                                     __float_as_uint(wsel));
+        if (a.layer[l].inds) a.layer[l].inds[lane] = isel;
+        if (a.layer[l].wts) a.layer[l].wts[lane] = wsel;
+      }
     }
   }
-  named_sync(kBarChain, kChain);  // the scratch is free again
+  __syncthreads();  // the scratch is free again
   return all_ok;
 }
 
@@ -780,7 +777,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (ROUTED) cluster_sync_fs();  // the partner's barriers exist before any arrival
   const uint32_t tmem = *S.tslot;
 
-  if (warp == kWarpTma) {
+  if (ROUTED && c == G - 1) {
+    // ------------------ the router CTA: every warp routes ------------------
+    const Xchg XR = xchg(a);
+    const int nR = H / kFsRedRows;
+    for (int l = 0; l < a.L; l++) {
+      const bool got = route_and_publish_cta(a, S, XR, l, nR);
+      if (!got) {
+        if (threadIdx.x == 0) fsflag(fs_timeout(l, 53));
+        break;
+      }
+    }
+  } else if (warp == kWarpTma) {
     // ------------------------------ TMA producer ------------------------------
     const uint32_t el = elect_one_fs();
     uint32_t g = 0;
@@ -1115,7 +1123,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // thread ct < 32 (the chain's first warp); the router: the last CTA.
     const int nR = H / kFsRedRows;
     const bool is_red = ROUTED && c < nR;
-    const bool is_router = ROUTED && c == G - 1;
     const int red_r0 = c * kFsRedRows;
     const Xchg XC = ROUTED ? xchg(a) : Xchg{};
     float hrow = 0.f;  // reducer thread ct < 32: h_j at its row (the residual)
@@ -1191,8 +1198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t isel = 0;
         float wsel = 0.f;
         bool got = true;
-        if (is_router) got = route_and_publish(a, S, XC, l, ct, nR, isel, wsel);
-        else if (ct < 32) got = read_routing(a, XC, l, lane, isel, wsel);
+        if (ct < 32) got = read_routing(a, XC, l, lane, isel, wsel);
         if (ct < 32) {
           if (!got && lane == 0) fsflag(fs_timeout(l, 53));
           if (lane < a.k) {
@@ -1209,7 +1215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_sync(kBarChain, kChain);
         return *S.bar_ok != 0;
       };
-      if (ROUTED && !has_gu && (has_d || is_router) && !take_routing()) {
+      if (ROUTED && !has_gu && has_d && !take_routing()) {
         alive = false;
         break;
       }
