@@ -477,6 +477,8 @@ def stack_traffic(layers, kind="routed", launches=1):
     try:
         with open(os.path.join(ROOT, "profiles", name)) as f:
             d = json.load(f)
+        if d.get("dram_bytes_per_layer") is None:
+            return None
         return d["dram_bytes_per_layer"] * layers / launches
     except Exception:
         return None
@@ -678,6 +680,9 @@ def main():
                           f"{chain.launches_per_step()} persistent launches",
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "peak_source": peak_src, "traffic": tr,
+                "traffic_note": (None if tr is not None else
+                                 "ncu cannot launch this cooperative cluster kernel "
+                                 "(profiles/moe_decode_stack_routed_traffic.json)"),
                 "algorithmic_bytes_per_launch": bytes_step / chain.launches_per_step(),
                 "algorithmic_bytes_per_step": bytes_step, "us_per_step": k_ms * 1e3,
                 "us_per_layer": k_ms * 1e3 / args.layers}
