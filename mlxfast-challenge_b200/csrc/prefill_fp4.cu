@@ -468,17 +468,30 @@ __global__ void __launch_bounds__(kFThreads, 1)
       if (!sync_and(2, 128, got)) break;
       tc_fence_after();
       const int r = 32 * q + lane;  // accumulator row = TMEM lane
+      // every slot of a chunk folded unconditionally (straight-line code: the
+      // factors of slots past the tile are zero), then the guarded stores;
+      // a slot's four factors in one 16-byte shared-memory read
+      const float4* fac4 = reinterpret_cast<const float4*>(sFac);
       for (int c0 = 0; c0 < ti.N; c0 += 32) {
         uint32_t v[32];
         tmem_ld32_nowait(tmem + lane_base + (uint32_t)(buf * kFAcc + c0), v);
         tmem_wait_ld();
+        float yy[8];
+#pragma unroll
+        for (int jj = 0; jj < 8; jj++) {
+          const float4 f = fac4[c0 / kT + jj];
+          float y = 0.f;
+          y += f.x * __uint_as_float(v[kT * jj]);
+          y += f.y * __uint_as_float(v[kT * jj + 1]);
+          y += f.z * __uint_as_float(v[kT * jj + 2]);
+          y += f.w * __uint_as_float(v[kT * jj + 3]);
+          yy[jj] = y;
+        }
 #pragma unroll
         for (int jj = 0; jj < 8; jj++) {
           const int sidx = c0 / kT + jj;  // slot within the tile
           if (sidx >= ti.count) continue;
-          float y = 0.f;
-#pragma unroll
-          for (int t = 0; t < kT; t++) y += sFac[sidx * kT + t] * __uint_as_float(v[kT * jj + t]);
+          const float y = yy[jj];
           if (a.mode == 2) {
             const int row = ti.m_tile * 128 + r;
             if (row < ti.Mrows) a.out[(int64_t)(ti.start + sidx) * a.out_ld + row] = y;
