@@ -244,6 +244,9 @@ __device__ __forceinline__ float silu_f(float x) {
   return x * (x < 0.0f ? y : 1.0f - y);
 }
 
+// MODE (1 gate/up + SwiGLU, 2 down) as a template parameter: each launch runs
+// only its own epilogue code.
+template <int MODE>
 __global__ void __launch_bounds__(kFThreads, 1)
     nvfp4_gemm_fp4_kernel(const __grid_constant__ GemmFp4Args a) {
   extern __shared__ __align__(1024) unsigned char fsmem_raw[];
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
   }
   pdl_wait_f();  // tiles and term rows come from the preceding kernels
   pdl_trigger_f();
-  const int m_tiles = a.mode == 1 ? (max(a.Mrows, a.Mrows_shared) + 63) / 64
+  const int m_tiles = MODE == 1 ? (max(a.Mrows, a.Mrows_shared) + 63) / 64
                                   : (max(a.Mrows, a.Mrows_shared) + 127) / 128;
   const int ntot = f_total(a, m_tiles);
   if ((int)blockIdx.x >= ntot) return;  // uniform per CTA, before any barrier use
@@ -316,7 +319,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       const CUtensorMap* s0 = ti.is_shared ? &a.mss0 : &a.ms0;
       const CUtensorMap* c1 = ti.is_shared ? &a.mcs1 : &a.mc1;
       const CUtensorMap* s1 = ti.is_shared ? &a.mss1 : &a.ms1;
-      const int row0 = (ti.is_shared ? 0 : ti.grp * a.Mrows) + ti.m_tile * (a.mode == 1 ? 64 : 128);
+      const int row0 = (ti.is_shared ? 0 : ti.grp * a.Mrows) + ti.m_tile * (MODE == 1 ? 64 : 128);
       const int brow = ti.start * kT;
       const int hb = (ti.N + 31) / 32 - 1;  // term rows loaded: 32 (hb + 1) >= N
       const uint32_t tx = (uint32_t)(kFA + kFSA) +
@@ -331,7 +334,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
         if (el) {
           uint8_t* st = sStage + s * kFStage;
           mbar_arrive_expect_tx(&full[s], tx);
-          if (a.mode == 1) {
+          if (MODE == 1) {
             tma_load_2d(st, c0, sl * 128, row0, &full[s]);
             tma_load_2d(st + kFA / 2, c1, sl * 128, row0, &full[s]);
             tma_load_2d(st + kFA + kFB, s0, sl * 16, row0, &full[s]);
@@ -492,7 +495,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
           const int sidx = c0 / kT + jj;  // slot within the tile
           if (sidx >= ti.count) continue;
           const float y = yy[jj];
-          if (a.mode == 2) {
+          if (MODE == 2) {
             const int row = ti.m_tile * 128 + r;
             if (row < ti.Mrows) a.out[(int64_t)(ti.start + sidx) * a.out_ld + row] = y;
           } else if (r < 64) {
@@ -505,7 +508,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      if (a.mode == 1) {
+      if (MODE == 1) {
         named_sync(2, 128);
         const int i = et & 63;
         const int row = ti.m_tile * 64 + i;
@@ -559,7 +562,9 @@ cudaError_t launch_nvfp4_gemm_fp4(const GemmFp4Args& a, int max_tiles, cudaStrea
   if (a.max_tiles != max_tiles) return cudaErrorInvalidValue;
   const size_t smem = gemm_fp4_smem_bytes(max_tiles);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  cudaError_t e = ensure_smem(nvfp4_gemm_fp4_kernel, smem);
+  if (a.mode != 1 && a.mode != 2) return cudaErrorInvalidValue;
+  auto kern = a.mode == 1 ? nvfp4_gemm_fp4_kernel<1> : nvfp4_gemm_fp4_kernel<2>;
+  cudaError_t e = ensure_smem(kern, smem);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 0;
   e = cudaGetDevice(&dev);
@@ -569,7 +574,7 @@ cudaError_t launch_nvfp4_gemm_fp4(const GemmFp4Args& a, int max_tiles, cudaStrea
   const int m_tiles = a.mode == 1 ? (std::max(a.Mrows, a.Mrows_shared) + 63) / 64
                                   : (std::max(a.Mrows, a.Mrows_shared) + 127) / 128;
   const int grid = std::max(1, std::min(sms, max_tiles * m_tiles));
-  return launch_pdl_f(nvfp4_gemm_fp4_kernel, dim3(grid), dim3(kFThreads), smem, stream, a);
+  return launch_pdl_f(kern, dim3(grid), dim3(kFThreads), smem, stream, a);
 }
 
 cudaError_t read_and_clear_fp4_error(int* out) {
