@@ -706,9 +706,12 @@ __device__ __forceinline__ bool read_routing(const FsArgs& a, const Xchg& X, int
   return ok;
 }
 
-template <int VX, int VA, bool ROUTED>
+// RM: 0 given routing, 1 routed stack, 2 routed stack with the norm (a.has_norm
+// as a compile-time constant: each launch holds only its own reducer path).
+template <int VX, int VA, int RM>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_decode_stack_fp4_kernel(const __grid_constant__ FsArgs a) {
+  constexpr bool ROUTED = RM > 0, NORM = RM == 2;
   constexpr int NS = stages(ROUTED);
   extern __shared__ __align__(1024) unsigned char fs_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -1139,7 +1142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tag = (uint32_t)(j + 1);
       float xv = hrow;
       bool ok = true;
-      if (a.has_norm && ct < 32) {
+      if (NORM && ct < 32) {
         const float w = load_as_f32(a.layer[j].norm_w, a.dtype, row);
         const float s2 = warp_sum(hrow * hrow);
         unsigned long long* sq = XC.sq + (size_t)j * kFsMaxReducers;
@@ -1386,12 +1389,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             float y = 0.f;
 #pragma unroll
             for (int tt = 0; tt < kT; tt++) y += S.faca[tt] * __uint_as_float(dt[t][tt]);
-            if (a.has_norm) add_counted<24, 16>(ysl + (size_t)t * 128 * kFsYsStride, y * wseg);
+            if (NORM) add_counted<24, 16>(ysl + (size_t)t * 128 * kFsYsStride, y * wseg);
             else __stcg(Yb + t * 128 + r, y * wseg);
           }
         tc_fence_before();
         named_sync(kBarChain, kChain);
-        if (!a.has_norm && ct < DT) red_release_add_fs(&cnt2[gu_p * DT + ct], 1u);
+        if (!NORM && ct < DT) red_release_add_fs(&cnt2[gu_p * DT + ct], 1u);
       } else if (has_d) {
         if (!wait_count(&cnt1[d_seg], (unsigned)(l + 1) * per_seg, l, 50)) {
           alive = false;
@@ -1445,7 +1448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // ---- routed stack, reducer: h_{l+1} for its rows, then layer l+1's input ----
-      if (is_red && a.has_norm) {
+      if (is_red && NORM) {
         // the counted sums of the reducer's rows: complete when all kk * nb
         // down items have added
         bool got = true;
@@ -1541,7 +1544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int VX, bool R>
+template <int VX, int R>
 const void* pick_va(int va) {
   switch (va) {
     case 4: return reinterpret_cast<const void*>(moe_decode_stack_fp4_kernel<VX, 4, R>);
@@ -1552,7 +1555,7 @@ const void* pick_va(int va) {
 }
 
 // VX: values of x per chain thread (the K part of a gate/up item / 128).
-template <bool R>
+template <int R>
 const void* pick_kernel(int H, int I, int nks) {
   switch (H / nks / 128) {
     case 4: return pick_va<4, R>(I / 128);
@@ -1599,8 +1602,9 @@ bool decode_stack_fp4_supported(int H, int I, int kk, int sms, bool routed) {
 
 cudaError_t launch_decode_stack_fp4(const FsArgs& a, cudaStream_t stream) {
   const void* kern = a.nks <= 0 ? nullptr
-                     : a.routed ? pick_kernel<true>(a.H, a.I, a.nks)
-                                : pick_kernel<false>(a.H, a.I, a.nks);
+                     : !a.routed  ? pick_kernel<0>(a.H, a.I, a.nks)
+                     : a.has_norm ? pick_kernel<2>(a.H, a.I, a.nks)
+                                  : pick_kernel<1>(a.H, a.I, a.nks);
   if (!kern || a.L < 1 || a.L > kFsMaxLayers || a.L * a.mpl > kFsMaxMaps)
     return cudaErrorInvalidValue;
   if (a.routed && (a.E < 1 || a.E > 256 || a.k > 8 || a.dtype == kF32 ||
