@@ -34,7 +34,8 @@
 //                    byte j);
 //     MMA thread     4 tcgen05.mma per slab (M=128, N = 4 x slots, K=64) into
 //                    one of three TMEM accumulators;
-//     epilogue       (4 warps) accumulator column 4 j + t holds term t of slot
+//     epilogue       (8 warps, two per TMEM lane quarter, alternate 32-column
+//                    chunks) accumulator column 4 j + t holds term t of slot
 //                    j: y = sum_t fac * D.  Mode 2 writes Y[slot][row]; mode 1
 //                    passes gate and up values through shared memory (the
 //                    gate rows sit in lane quarters 0-1, the up rows in 2-3)
@@ -61,8 +62,11 @@ constexpr int kFSA = kFBM * 16;            // weight scales: 2 KB
 constexpr int kFSB = kFRows * 16;          // term-row scales: 2 KB
 constexpr int kFStage = kFA + kFB + kFSA + kFSB;  // 36 KB, 1 KB multiple
 static_assert(kFStage % 1024 == 0, "stage alignment");
-constexpr int kFThreads = 320;             // 0 TMA, 1 MMA, 2-5 scales, 6-9 epilogue
+constexpr int kFThreads = 448;             // 0 TMA, 1 MMA, 2-5 scales, 6-13 epilogue
 constexpr int kWarpTma = 0, kWarpMma = 1, kWarpEpi0 = 6;  // warps 2-5: scale factors
+// Epilogue: two warps per tensor-memory lane quarter (warp w reads lanes
+// 32 (w % 4) ..), each taking every other 32-column chunk of a tile.
+constexpr int kEpiT = kFThreads - 32 * kWarpEpi0;  // 256
 constexpr int kFAcc = 128;                 // accumulator columns (one buffer)
 constexpr int kFSf = 32;                   // scale columns per stage: 16 A + 16 B
 constexpr int kFTmem = 512;
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     }
     for (int i = 0; i < kFBufs; i++) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], kEpiT / 32);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -443,7 +447,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
   } else {
     // ------------------------------ epilogue ------------------------------
     const int q = warp & 3;  // TMEM lane quarter: rows 32 q .. 32 q + 31
-    const int et = threadIdx.x - 32 * kWarpEpi0;  // 0..127
+    const int eh = (warp - kWarpEpi0) >> 2;       // chunks eh, eh + 2, ... of a tile
+    const int et = threadIdx.x - 32 * kWarpEpi0;  // 0 .. kEpiT - 1
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
     int j = 0;
     // The tile's term factors (column 4 s + t <- slot s, term t), loaded one
@@ -463,19 +468,19 @@ __global__ void __launch_bounds__(kFThreads, 1)
       un = next_tile(u + gridDim.x, tn);
       fnext = (un < ntot && et < kT * tn.count) ? a.bfac[(int64_t)tn.start * kT + et] : 0.f;
       const int buf = j % kFBufs;
-      named_sync(2, 128);
-      sFac[et] = fcur;
-      named_sync(2, 128);
+      named_sync(2, kEpiT);
+      if (et < kFRows) sFac[et] = fcur;
+      named_sync(2, kEpiT);
       const bool got = mbar_wait_bounded(&acc_full[buf], (j / kFBufs) & 1);
       if (!got && lane == 0) fflag(kErrTimeout);
-      if (!sync_and(2, 128, got)) break;
+      if (!sync_and(2, kEpiT, got)) break;
       tc_fence_after();
       const int r = 32 * q + lane;  // accumulator row = TMEM lane
       // every slot of a chunk folded unconditionally (straight-line code: the
       // factors of slots past the tile are zero), then the guarded stores;
       // a slot's four factors in one 16-byte shared-memory read
       const float4* fac4 = reinterpret_cast<const float4*>(sFac);
-      for (int c0 = 0; c0 < ti.N; c0 += 32) {
+      for (int c0 = 32 * eh; c0 < ti.N; c0 += 64) {
         uint32_t v[32];
         tmem_ld32_nowait(tmem + lane_base + (uint32_t)(buf * kFAcc + c0), v);
         tmem_wait_ld();
@@ -509,11 +514,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       if (MODE == 1) {
-        named_sync(2, 128);
+        named_sync(2, kEpiT);
         const int i = et & 63;
         const int row = ti.m_tile * 64 + i;
         if (row < ti.Mrows)
-          for (int sidx = et >> 6; sidx < ti.count; sidx += 2)
+          for (int sidx = et >> 6; sidx < ti.count; sidx += kEpiT / 64)
             a.out[(int64_t)(ti.start + sidx) * a.out_ld + row] =
                 silu_f(sG[i * kGuPitch + sidx]) * sU[i * kGuPitch + sidx];
       }
