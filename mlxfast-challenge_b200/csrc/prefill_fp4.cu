@@ -11,10 +11,11 @@
 // term t being the NVFP4 quantisation (UE4M3 scale per group of 16, E2M1
 // codes rounded to nearest even) of the row's residual after terms 0..t-1,
 // under a power-of-two factor per (row, term): the row's max places its largest
-// term-0 group scale in [171, 352], term t's factor is 4^-t times that (each
-// term's scales stay in E4M3's normal range).  Each term cuts the residual by at least 6x per
-// group; four terms reproduce the W4A16 product to a relative-L2 of ~5e-5
-// (N(0,1) rows and SwiGLU outputs, measured on the CPU), 100x inside the
+// term-0 group scale in [171, 352], term t's factor is 4^-t times that (no
+// term's scales overflow E4M3; groups far below the row max get subnormal
+// scales in the later terms).  Each term cuts the residual by at least 6x per
+// group; four terms reproduce the W4A16 product to a relative-L2 of ~1e-4
+// (N(0,1) rows and SwiGLU outputs, a numpy restatement), 50x inside the
 // path's 5e-3 tolerance.  The weight operand is the checkpoint's NVFP4 data as
 // is (codes and E4M3 group scales used as UE4M3: the quantizer never emits a
 // sign bit or 0x7F).  Every product is exact and sums in f32.
