@@ -84,10 +84,14 @@ NVFP4MOE_API int nvfp4_version(void);
 /* The grouped GEMMs of moe_block_forward (T >= 2: expert sort, each distinct
  * expert streamed once) run by default on the
  * block-scaled FP4 tensor cores (tcgen05 kind::mxf4nvf4): activations as a sum
- * of four NVFP4 terms (relative-L2 ~5e-5 from the W4A16 product, 20x below
+ * of four NVFP4 terms (relative-L2 ~1e-4 from the W4A16 product, 10x below
  * bf16 output rounding), weights as stored.  NVFP4_LAUNCH_EXACT_PREFILL
  * selects the exact path instead (weights dequantised to 16-bit, kind::f16;
- * ~1.7x slower at T = 512). */
+ * ~2.1x slower at T = 512).  The FP4 GEMMs hold the batch's tile list
+ * (E + T * top_k / 32 + T / 32 entries) in shared memory; a batch whose list
+ * does not fit (above ~13.8k tokens at E = 256, top-8, with a shared expert)
+ * runs on the exact path.  moe_ep_partial_forward has no exact path and
+ * returns NVFP4_ERR_UNSUPPORTED there. */
 #define NVFP4_LAUNCH_EXACT_PREFILL 4
 /* moe_decode_stack_forward runs by default on the block-scaled FP4 tensor
  * cores where the shape allows (hidden 1024 or 2048, inter 512 / 1024 / 2048,

@@ -142,7 +142,11 @@ BlockLayout block_layout(const moe_layer_desc* L, int64_t T,
     B.y_off = align_up(B.ascale_off + (size_t)B.S * sizeof(float), 256);
     B.total = align_up(B.y_off + (size_t)B.S * L->hidden * sizeof(float), 256);
     auto k_ok = [](int64_t K) { return K == 512 || K == 1024 || K == 2048; };
-    B.fp4 = k_ok(L->hidden) && k_ok(L->inter);
+    // The FP4 GEMMs stage the whole tile list in shared memory: beyond
+    // ~13.8k tokens at Laguna sizes it does not fit, and the exact path
+    // (no such list) takes the batch.
+    B.fp4 = k_ok(L->hidden) && k_ok(L->inter) && B.max_tiles < (1 << 20) &&
+            nvfp4::gemm_fp4_smem_bytes((int)B.max_tiles) <= (size_t)227 * 1024;
     if (B.fp4) {
       const size_t rows = (size_t)B.S * nvfp4::kFp4Terms;
       B.xtc_off = B.total;
@@ -1149,7 +1153,8 @@ int moe_ep_partial_forward_typed(void* y_partial, int partial_dtype, const void*
   const int esz = dtype == NVFP4_F32 ? 4 : 2;
   if (!B.prefill || !B.fp4 || !aligned16(x) || (x_ld * esz) % 16 || !aligned16(y_partial))
     return fail(NVFP4_ERR_UNSUPPORTED,
-                "[%s] needs T > 8 tokens, Laguna-sized layers and 16-byte aligned rows.", op);
+                "[%s] needs T > 8 tokens, Laguna-sized layers, 16-byte aligned rows and a tile "
+                "list (E + T * top_k / 32 + T / 32 entries) that fits in shared memory.", op);
   if (!workspace || workspace_bytes < B.total)
     return fail(NVFP4_ERR_WORKSPACE, "[%s] workspace of %zu bytes required.", op, B.total);
   char* ws = static_cast<char*>(workspace);

@@ -136,6 +136,26 @@ def test_prefill_fp4_terms_close_to_exact_path(nv, layer):
                  what="fp4 terms vs exact")
 
 
+def test_long_prompt_takes_the_exact_path(nv, orc, layer):
+    """T = 14336 at Laguna sizes: the FP4 GEMMs' tile list (E + T*k/32 + T/32
+    entries) no longer fits in shared memory, so the block runs on the exact
+    path -- the same bits as the exact path on the two halves (tokens are
+    independent), and within tolerance of the oracle on sampled tokens."""
+    lag, block, raw = layer
+    T, h = 14336, 7168
+    g = torch.Generator(device=DEV).manual_seed(14)
+    x = torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16)
+    res = torch.randn(T, 2048, generator=g, device=DEV).to(torch.bfloat16)
+    y, inds, wts = block(x, residual=res, return_routing=True)
+    with nv.launch_flags(exact_prefill=True):
+        halves = [block(x[i:i + h], residual=res[i:i + h]) for i in (0, h)]
+    nv.device_status()
+    assert torch.equal(y, torch.cat(halves))
+    tokens = np.array([0, 4097, 9000, T - 1])
+    want = oracle_tokens(orc, raw, x, inds, wts, tokens, residual=res)
+    assert_close(y.float().cpu().numpy()[tokens], want, what="T=14336 vs oracle")
+
+
 @pytest.mark.parametrize("exact", [False, True])
 def test_prefill_non_finite_rows_propagate(nv, layer, exact):
     """A token whose activations hold NaN or inf gives a non-finite output row,
