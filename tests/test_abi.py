@@ -144,3 +144,36 @@ def test_stacks_reject_layers_of_another_shape(nv, field, value):
     assert L.moe_decode_stack_routed_forward(None, None, 0, 2, descs, 1, None, 1e-6, None, None,
                                              None, 0, None) == nv._lib.NVFP4_ERR_UNSUPPORTED
     assert "[moe_decode_stack_routed]" in _last(L)
+
+
+def _laguna_desc(nv):
+    d = nv._lib.MoeLayerDesc()
+    d.hidden, d.inter, d.n_experts, d.top_k, d.shared_inter = 2048, 512, 256, 8, 512
+    d.routed_scaling, d.norm_topk_prob = 2.5, 1
+    return d
+
+
+def test_long_batches_leave_the_fp4_gemms(nv):
+    """The FP4 prefill GEMMs hold the tile list (E + T k / 32 + T / 32 entries)
+    in shared memory; past ~13.8k tokens at Laguna sizes the block's workspace
+    no longer carries the FP4 term buffers (the exact path takes the batch)."""
+    L = nv._lib.lib()
+    d = _laguna_desc(nv)
+    fits, over = 13824, 13840
+    w_fits = L.moe_block_workspace_size(ctypes.byref(d), fits)
+    w_over = L.moe_block_workspace_size(ctypes.byref(d), over)
+    # the four term rows per slot (codes, scales, factors of x and act) drop out
+    assert w_over < w_fits - 9 * fits * 4 * (1024 + 256)
+
+
+def test_ep_partial_refuses_a_tile_list_that_does_not_fit(nv):
+    """moe_ep_partial_forward has no exact path: a batch whose FP4 tile list
+    does not fit is refused on the host with NVFP4_ERR_UNSUPPORTED."""
+    L = nv._lib.lib()
+    d = _laguna_desc(nv)
+    p = ctypes.c_void_p(256)
+    T = 16384
+    st = L.moe_ep_partial_forward(p, p, 2048, 0, T, ctypes.byref(d), p, p, 0, 0, T, p, 1 << 40,
+                                  None)
+    assert st == nv._lib.NVFP4_ERR_UNSUPPORTED
+    assert "[moe_ep_partial]" in _last(L) and "tile" in _last(L)
