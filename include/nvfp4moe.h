@@ -91,7 +91,8 @@ NVFP4MOE_API int nvfp4_version(void);
  * (E + T * top_k / 32 + T / 32 entries) in shared memory; a batch whose list
  * does not fit (above ~13.8k tokens at E = 256, top-8, with a shared expert)
  * runs on the exact path.  moe_ep_partial_forward has no exact path and
- * returns NVFP4_ERR_UNSUPPORTED there. */
+ * returns NVFP4_ERR_UNSUPPORTED there: call it over row ranges of the
+ * gathered batch (tokens are independent), as ep.py's gather form does. */
 #define NVFP4_LAUNCH_EXACT_PREFILL 4
 /* moe_decode_stack_forward runs by default on the block-scaled FP4 tensor
  * cores where the shape allows (hidden 1024 or 2048, inter 512 / 1024 / 2048,

@@ -309,24 +309,60 @@ class CudaGatherEPOps:
         from . import moe_router_topk
         return moe_router_topk(x, self.router_w, self.router_b, self.top_k, self.norm)
 
+    # moe_ep_partial_forward's FP4 GEMMs hold the batch's tile list
+    # (E + ceil(T k / 32) + ceil(T / 32) entries) in shared memory; this many
+    # entries always fit.  A longer gathered batch runs as several calls over
+    # consecutive row ranges (tokens are independent).
+    MAX_TILES = 4096
+
+    def chunk_tokens(self, Tt: int) -> int:
+        """Rows per moe_ep_partial_forward call for a gathered batch of Tt."""
+        sh = self.local.desc.shared_inter > 0
+        n = 1
+        while True:
+            c = -(-Tt // n)
+            tiles = self.epr + -(-c * self.top_k // 32) + (-(-c // 32) if sh else 0)
+            if tiles <= self.MAX_TILES or c <= 1:
+                return c
+            n += 1
+
+    def _routed_only_desc(self):
+        # the layer without its shared expert, for a row range holding none of
+        # this rank's own tokens
+        d = getattr(self, "_desc_routed", None)
+        if d is None:
+            d = type(self.local.desc).from_buffer_copy(self.local.desc)
+            d.shared_inter = 0
+            for f in ("shared_gate", "shared_up", "shared_down"):
+                setattr(d, f, type(d.shared_gate)())
+            self._desc_routed = d
+        return d
+
     def partial(self, rows, dtype, row0, nrows):
         from . import _dtype_code
         H, k = self.H, self.top_k
         xb, ids, wts = unpack_tokens(rows, H, k, dtype)
         Tt = rows.shape[0]
         esz = torch.empty(0, dtype=dtype).element_size()
-        nbytes = int(lib().moe_ep_partial_workspace_size(ctypes.byref(self.local.desc), Tt))
-        ws = self._ws.get(Tt)
+        c = self.chunk_tokens(Tt)
+        nbytes = int(lib().moe_ep_partial_workspace_size(ctypes.byref(self.local.desc), c))
+        ws = self._ws.get(c)
         if ws is None or ws.numel() < nbytes:
             ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=rows.device)
-            self._ws[Tt] = ws
+            self._ws[c] = ws
         y = torch.empty(Tt, H, dtype=self.partial_dtype, device=rows.device)
         probe = torch.empty(0, dtype=dtype, device=rows.device)
-        check(lib().moe_ep_partial_forward_typed(
-            y.data_ptr(), _dtype_code(y, "moe_ep"), rows.data_ptr(), rows.shape[1] // esz,
-            _dtype_code(probe, "moe_ep"),
-            Tt, ctypes.byref(self.local.desc), ids.data_ptr(), wts.data_ptr(),
-            self.rank * self.epr, row0, nrows, ws.data_ptr(), ws.numel(), self._stream(rows)))
+        sh = self.local.desc.shared_inter > 0
+        for c0 in range(0, Tt, c):
+            c1 = min(Tt, c0 + c)
+            s0, s1 = max(row0, c0), min(row0 + nrows, c1)  # own rows in this range
+            desc = self.local.desc if (not sh or s1 > s0) else self._routed_only_desc()
+            r0, rn = (s0 - c0, s1 - s0) if (sh and s1 > s0) else (0, 0)
+            check(lib().moe_ep_partial_forward_typed(
+                y[c0:].data_ptr(), _dtype_code(y, "moe_ep"), rows[c0:].data_ptr(),
+                rows.shape[1] // esz, _dtype_code(probe, "moe_ep"),
+                c1 - c0, ctypes.byref(desc), ids[c0:].data_ptr(), wts[c0:].data_ptr(),
+                self.rank * self.epr, r0, rn, ws.data_ptr(), ws.numel(), self._stream(rows)))
         return y
 
     def finish(self, mine, shared, residual, dtype):

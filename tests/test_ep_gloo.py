@@ -197,3 +197,33 @@ def test_ep_gather_two_gloo_ranks_matches_single_block(orc):
         want = orc.port.moe_block_f32(x, inds.astype(np.uint32), wts, routed, shared,
                                       scaling=SCALING, residual=res)
         assert_close(y, want, what=f"rank {r}")
+
+
+@pytest.mark.parametrize("Tt,epr,k,shared,want", [
+    (4096, 32, 8, True, 4096),      # BASELINE config[3] at 8 GPUs: one call
+    (16384, 32, 8, True, 8192),     # 8 x 2048 tokens: two calls
+    (16384, 256, 8, False, 8192),   # one rank, no shared expert
+    (100000, 32, 16, True, 7143),   # 14 calls (13 would need 4120 entries)
+])
+def test_gather_partial_chunk_rule(Tt, epr, k, shared, want):
+    """CudaGatherEPOps.partial splits a gathered batch into the fewest equal
+    row ranges whose FP4 tile list (E + ceil(T k / 32) + ceil(T / 32) with a
+    shared expert) stays within MAX_TILES."""
+    ep = importlib.import_module(PKG + ".ep")
+
+    class Desc:
+        shared_inter = 512 if shared else 0
+
+    class Local:
+        desc = Desc()
+
+    class Ops:
+        MAX_TILES = ep.CudaGatherEPOps.MAX_TILES
+        local = Local()
+
+    o = Ops()
+    o.epr, o.top_k = epr, k
+    c = ep.CudaGatherEPOps.chunk_tokens(o, Tt)
+    assert c == want
+    tiles = epr + -(-c * k // 32) + (-(-c // 32) if shared else 0)
+    assert tiles <= ep.CudaGatherEPOps.MAX_TILES

@@ -106,13 +106,15 @@ def test_simulated_ranks_match_single_block(nv, world, T):
 
 @pytest.mark.parametrize("world,T,pdt", [(2, 64, torch.float32), (4, 100, torch.float32),
                                          (8, 512, torch.float32), (2, 64, torch.bfloat16),
-                                         (8, 512, torch.bfloat16)])
+                                         (8, 512, torch.bfloat16), (8, 2048, torch.bfloat16)])
 def test_gather_form_simulated_ranks_match_single_block(nv, world, T, pdt):
     """GatherEPBlock's steps for `world` ranks in one process: every rank's
     partial over all gathered tokens (moe_ep_partial_forward_typed, foreign
     experts skipped; f32 or bf16 partials), the reduce-scatter as a sum in the
     partials' dtype, moe_ep_finish_typed with the shared expert and the
-    residual -- against the single-GPU block."""
+    residual -- against the single-GPU block.  At 8 x 2048 the gathered
+    batch (16384 tokens) runs as two partial calls per rank, one of them
+    without the rank's own rows (no shared expert)."""
     ep = importlib.import_module(PKG + ".ep")
     lag = importlib.import_module(PKG + ".laguna")
     block, raw = lag.random_sparse_layer(nv, seed=37, device=DEV)
