@@ -317,6 +317,8 @@ class CudaGatherEPOps:
 
     def chunk_tokens(self, Tt: int) -> int:
         """Rows per moe_ep_partial_forward call for a gathered batch of Tt."""
+        if Tt <= 1:
+            return 1
         sh = self.local.desc.shared_inter > 0
         n = 1
         while True:

@@ -204,6 +204,7 @@ def test_ep_gather_two_gloo_ranks_matches_single_block(orc):
     (16384, 32, 8, True, 8192),     # 8 x 2048 tokens: two calls
     (16384, 256, 8, False, 8192),   # one rank, no shared expert
     (100000, 32, 16, True, 7143),   # 14 calls (13 would need 4120 entries)
+    (0, 32, 8, True, 1),            # an empty batch: no call, an empty partial
 ])
 def test_gather_partial_chunk_rule(Tt, epr, k, shared, want):
     """CudaGatherEPOps.partial splits a gathered batch into the fewest equal
