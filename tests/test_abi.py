@@ -177,3 +177,56 @@ def test_ep_partial_refuses_a_tile_list_that_does_not_fit(nv):
                                   None)
     assert st == nv._lib.NVFP4_ERR_UNSUPPORTED
     assert "[moe_ep_partial]" in _last(L) and "tile" in _last(L)
+
+
+@pytest.mark.parametrize("epr,k,shared", [(32, 8, True), (256, 8, True), (64, 16, False)])
+def test_ep_chunk_rule_stays_inside_the_fp4_limit(nv, epr, k, shared):
+    """ep.py's row-range rule (MAX_TILES entries) never asks the library for a
+    batch its FP4 GEMMs would refuse: the largest range the rule allows is
+    below the size at which the workspace stops carrying the FP4 buffers."""
+    ep = importlib.import_module(PKG + ".ep")
+    L = nv._lib.lib()
+    d = _laguna_desc(nv)
+    d.n_experts, d.top_k = epr, k
+    d.shared_inter = 512 if shared else 0
+
+    def ws(T):
+        return L.moe_ep_partial_workspace_size(ctypes.byref(d), T)
+
+    # Past the limit the layout is the exact path's, whose size per token is
+    # the asymptote below; the FP4 term buffers add >= 4 terms x H/2 bytes of
+    # codes per slot on top, so "FP4 included" is a per-token size well above it.
+    big = 1 << 18
+    exact_per_token = ws(big) / big
+    slots = k + (1 if shared else 0)
+    margin = slots * 4 * (2048 // 2) / 2
+
+    def has_fp4(T):
+        return ws(T) / T > exact_per_token + margin
+
+    lo, hi = 16, big  # a prefill-sized batch (below 2 tokens there is no prefill layout)
+    assert has_fp4(lo) and not has_fp4(hi)
+    while hi - lo > 1:
+        mid = (lo + hi) // 2
+        if has_fp4(mid):
+            lo = mid
+        else:
+            hi = mid
+    limit = lo  # largest T whose layout still carries the FP4 buffers
+
+    class Ops:
+        MAX_TILES = ep.CudaGatherEPOps.MAX_TILES
+
+        class local:
+            desc = d
+
+    o = Ops()
+    o.epr, o.top_k = epr, k
+    c_max = 1
+    while True:  # the largest single range the rule accepts
+        t = epr + -(-(c_max + 1) * k // 32) + (-(-(c_max + 1) // 32) if shared else 0)
+        if t > o.MAX_TILES:
+            break
+        c_max += 1
+    assert ep.CudaGatherEPOps.chunk_tokens(o, c_max) == c_max
+    assert c_max <= limit
